@@ -1,0 +1,448 @@
+#!/usr/bin/env python
+"""Training-step benchmark of the tinygs hot path on B200.
+
+Workload (N = 1): BASELINE config 2 -- 3M Gaussians, SH degree 3, fp16
+rasterizer with fp32 parameters/gradients/Adam, 1920x1080, cameras from a
+seeded 60-view orbit of radius 4, seeded U[0,1] targets (synthetic stand-ins:
+no dataset is named and the reference's scenes are absent).  One step =
+forward render -> 0.8 L1 + 0.2 (1-SSIM) (x grad_scaler 10) -> backward ->
+Adam (max_grad_1 0.3), i.e. Orchestrator::train_step with
+record_trajectory off and the data loader replaced by resident targets.
+
+N > 1 (torchrun, one process per GPU, NCCL): every rank renders its own orbit
+view of the same replicated model each step, the gradient arena (236 B per
+Gaussian) is summed with one NCCL all-reduce and every rank applies the same
+Adam step with gradient scale 1/(grad_scaler*N) -- the reference's
+accumulate_grad_steps=N semantics (orchestrator.cu:343-403).  Weak scaling:
+`value` counts view-steps of all ranks per second.
+
+Reported: `value` (device-resident inputs, CUDA events, max over ranks),
+`e2e` (target uploaded from pinned host memory and the loss scalar read back
+every step, through the public API), per-stage times, the roofline of the
+fused Adam kernel (the HBM-bound kernel whose time is measured live), clocks
+sampled during the timed region, and a CPU baseline (the oracle restatement,
+timed on a bounded sample on the host cores).
+
+`--impl reference` times the CPU restatement of the reference's algorithm
+(the reference itself has no CPU implementation and its CUDA build cannot be
+reproduced here) on the same workload and prints it in the same format.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "train iters/s (fwd+bwd+SSIM+Adam) @3M Gaussians 1080p; render Mpix/s"
+GRAD_SCALER = 10.0
+ADAM_BYTES_PER_GAUSSIAN = 7 * 59 * 4  # read theta, g, m, v; write theta, m, v
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=25.0, help="seconds of CPU work for the baseline sample")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = Path(f"/tmp/tgs_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "power_w_max": max(power), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU oracle
+
+def cpu_oracle_step_time(cfg_name: str, budget_s: float, fp32_math: bool = True) -> dict:
+    """Time one oracle training step of the workload on the host cores.
+    Per-Gaussian and per-pixel stages run in full; the two blend stages run on
+    every k-th tile (k chosen from a probe so the sample fits the budget) and
+    their time is scaled by k."""
+    import numpy as np
+
+    from oracle import pyoracle as O
+    from tinygs_b200 import scenes
+
+    cfg = scenes.CONFIGS[cfg_name]
+    params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
+    cam = scenes.cameras(cfg)[0]
+    W, H = cfg.width, cfg.height
+    target = scenes.target_image(W, H, cfg.seed + 100).reshape(-1)
+    fp16 = False if fp32_math else cfg.dtype == "float16"
+    lib = O.load()
+    gw, gh = O.grid(cam)
+    n_tiles = gw * gh
+    t = {}
+    t0 = time.perf_counter()
+    prims = O.preprocess(params, cfg.sh_degree, cam, fp16)
+    t["preprocess"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    bins = O.binning(prims, cam, fp16)
+    t["binning"] = time.perf_counter() - t0
+    # probe the blend cost on 1/256 of the tiles, then pick the stride
+    lib.orc_set_tile_stride(256)
+    t0 = time.perf_counter()
+    O.blend_forward(prims, bins, cam, fp16)
+    probe = max(time.perf_counter() - t0, 1e-4)
+    remaining = max(budget_s - sum(t.values()), 2.0)
+    est_full_fwd = probe * 256
+    stride = int(min(256, max(1, (3.0 * est_full_fwd) / remaining)))
+    lib.orc_set_tile_stride(stride)
+    t0 = time.perf_counter()
+    fwd = O.blend_forward(prims, bins, cam, fp16)
+    t["blend_forward"] = (time.perf_counter() - t0) * stride
+    lib.orc_set_tile_stride(1)
+    dt = np.float16 if fp16 else np.float32
+    img = fwd["image"]
+    loss_map = np.zeros(img.shape, dt)
+    grad_img = np.zeros(img.shape, dt)
+    t0 = time.perf_counter()
+    O.l1(img, target.astype(dt), loss_map, grad_img, W, H, 0.8 * GRAD_SCALER)
+    O.ssim(img, target.astype(dt), loss_map, grad_img, W, H, 0.2 * GRAD_SCALER)
+    t["loss"] = time.perf_counter() - t0
+    lib.orc_set_tile_stride(stride)
+    t0 = time.perf_counter()
+    screen = O.blend_backward(prims, bins, fwd, grad_img, cam, fp16)
+    t["blend_backward"] = (time.perf_counter() - t0) * stride
+    lib.orc_set_tile_stride(1)
+    t0 = time.perf_counter()
+    grads = O.preprocess_backward(params, cfg.sh_degree, cam, prims["n_touched"], screen)
+    t["preprocess_backward"] = time.perf_counter() - t0
+    from types import SimpleNamespace
+    acfg = SimpleNamespace(beta1=0.9, beta2=0.999, epsilon=1e-8, max_grad_1=0.3, means_lr=1.6e-4, shs_lr=2.5e-3,
+                           opacities_lr=5e-2, scales_lr=5e-3, rotations_lr=1e-3, opacities_l1=0.0, scales_l1=0.0,
+                           scene_scale=1.0, global_lr=1.0, decay_reduction_mean=True)
+    m = {k: np.zeros_like(v) for k, v in params.items()}
+    v = {k: np.zeros_like(x) for k, x in params.items()}
+    t0 = time.perf_counter()
+    O.adam_step(params, grads, m, v, acfg, 1, 1.0 / GRAD_SCALER)
+    t["adam"] = time.perf_counter() - t0
+    total = sum(t.values())
+    return {"seconds_per_step": total, "stages_s": {k: round(x, 4) for k, x in t.items()}, "tile_stride": stride,
+            "threads": O.threads(), "fp16_emulated": fp16, "n_instances": bins["n_instances"]}
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the reference algorithm."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from tinygs_b200 import scenes
+
+    cfg = scenes.CONFIGS[args.config]
+    steps_run, times = 0, []
+    budget = 150.0
+    start = time.perf_counter()
+    for k in range(max(1, args.steps)):
+        r = cpu_oracle_step_time(args.config, args.cpu_budget)
+        times.append(r["seconds_per_step"])
+        steps_run += 1
+        if time.perf_counter() - start > budget:
+            break
+    sec = statistics.median(times)
+    value = 1.0 / sec
+    cores = r["threads"]
+    sample = (f"one oracle training step of {args.config} per step ({cfg.n} Gaussians, {cfg.width}x{cfg.height}, "
+              f"fp32 arithmetic); blend stages on every {r['tile_stride']}th tile, time scaled by the stride; "
+              f"{steps_run} of {args.steps} steps run (budget)")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "iters/s", "n_gpus": 0,
+            "steps": steps_run, "warmup": 0, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config}", "gaussians": cfg.n, "width": cfg.width, "height": cfg.height,
+                       "sh_degree": cfg.sh_degree, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "iters/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "stages_s": r["stages_s"]}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours
+
+def kernels_per_step(n_tiles: int, world: int) -> int:
+    tile_bits = max(1, (n_tiles - 1).bit_length())
+    tile_passes = (tile_bits + 7) // 8
+    forward = 1 + 2 + 4 * 3 + 3 + 3 * tile_passes + 2 + 1  # preprocess, compaction, sorts, instances, ranges, blend
+    return forward + 2 + 2 + 1  # loss fwd/bwd, blend bwd + preprocess bwd, adam
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    cfg = scenes.CONFIGS[args.config]
+    W, H = cfg.width, cfg.height
+    fp16 = cfg.dtype == "float16"
+    dt = torch.float16 if fp16 else torch.float32
+    params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
+    g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+    del params
+    grads = g.zeros_like()
+    opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
+    cams = scenes.cameras(cfg)
+    n_targets = 4
+    host_targets = [torch.from_numpy(scenes.target_image(W, H, cfg.seed + 100 + k).reshape(-1)).to(dt).pin_memory()
+                    for k in range(n_targets)]
+    dev_targets = [t.cuda() for t in host_targets]
+    tgt_upload = torch.empty_like(dev_targets[0])
+    numel = rt.image_numel(W, H)
+    image = torch.zeros(numel, dtype=dt, device="cuda")
+    grad_image = torch.zeros_like(image)
+    loss_map = torch.zeros_like(image)
+    loss_sum = torch.zeros(1, device="cuda")
+    loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
+    loss = rt.FusedLoss(W, H)
+    stream = torch.cuda.current_stream()
+
+    def make_raster(cap_inst):
+        r = rt.FastGSB200Rasterizer(cfg.n, W, H, cap_inst)
+        r.set_gaussians(g)
+        return r
+
+    # size the instance capacity from the views this rank will render
+    rast = make_raster(24 * cfg.n)
+    ctx = rt.RasterizeContext(stream=stream, grad_scaler=GRAD_SCALER, fwd_output_image=image,
+                              grad_output_image=grad_image, gaussians_grad=grads, accumulate=False)
+    max_inst = 0
+    for v in range(0, len(cams), max(1, len(cams) // 8)):
+        ctx.fwd_input = cams[v]
+        rast.forward(ctx)
+        c = rast.counts()
+        max_inst = max(max_inst, c.n_instances)
+        if c.overflow:
+            raise SystemExit("instance capacity too small for the sizing pass")
+    rast.close()
+    rast = make_raster(int(max_inst * 1.5) + 1024)
+
+    def view_of(step):
+        return cams[(step * world + rank) % len(cams)]
+
+    stage_events = None
+
+    def step(k, e2e=False, record=None):
+        ctx.fwd_input = view_of(k)
+        if e2e:
+            tgt_upload.copy_(host_targets[k % n_targets], non_blocking=True)
+            tgt = tgt_upload
+        else:
+            tgt = dev_targets[k % n_targets]
+        ev = record
+        if ev is not None:
+            ev[0].record(stream)
+        loss_map.zero_()
+        grad_image.zero_()
+        rast.forward(ctx)
+        if ev is not None:
+            ev[1].record(stream)
+        loss.evaluate(image, tgt, loss_map, grad_image, W, H, grad_scaler=GRAD_SCALER, loss_sum=loss_sum,
+                      stream=stream)
+        if ev is not None:
+            ev[2].record(stream)
+        rast.backward(ctx)
+        if ev is not None:
+            ev[3].record(stream)
+        if world > 1:
+            dist.all_reduce(grads.storage)
+        if ev is not None:
+            ev[4].record(stream)
+        opt.step(1.0 / (GRAD_SCALER * world), stream=stream)
+        if ev is not None:
+            ev[5].record(stream)
+        if e2e:
+            loss_host[k % 2].copy_(loss_sum[0], non_blocking=True)
+
+    def timed(n_steps, e2e, offset):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(n_steps):
+            step(offset + k, e2e)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    counts = rast.counts()
+    if counts.overflow:
+        raise SystemExit("capacity overflow during warm-up")
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms_dev = timed(args.steps, False, args.warmup)
+    clocks = sampler.stop()
+    ms_e2e = timed(args.steps, True, args.warmup + args.steps)
+    torch.cuda.synchronize()
+    if not np.isfinite(float(loss_host[0])):
+        raise SystemExit("non-finite loss")
+
+    # per-stage times on a separate pass (not part of the headline)
+    n_stage = max(3, min(args.steps, 10))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n_stage)]
+    for k in range(n_stage):
+        step(args.warmup + 2 * args.steps + k, False, evs[k])
+    torch.cuda.synchronize()
+    names = ["forward", "loss", "backward", "allreduce", "adam"]
+    stages = {nm: statistics.median(e[i].elapsed_time(e[i + 1]) for e in evs) for i, nm in enumerate(names)}
+
+    # forward-only render throughput (render Mpix/s)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    for k in range(args.steps):
+        ctx.fwd_input = view_of(k)
+        rast.forward(ctx)
+    r1.record(stream)
+    torch.cuda.synchronize()
+    render_ms = r0.elapsed_time(r1) / args.steps
+
+    counts = rast.counts()
+    ms_step = ms_dev / args.steps
+    value = world * 1e3 / ms_step
+    e2e_ms = ms_e2e / args.steps
+    adam_ms = stages["adam"]
+    adam_gbs = ADAM_BYTES_PER_GAUSSIAN * cfg.n / (adam_ms * 1e-3) / 1e9
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        hbm_peak, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        hbm_peak, peak_src = 6650.0, "fallback"
+    tile_count = ((W + 15) // 16) * ((H + 15) // 16)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_oracle_step_time(args.config, args.cpu_budget)
+        cpu = {"value": 1.0 / r["seconds_per_step"], "unit": "iters/s", "cores": r["threads"], "kind": "port",
+               "sample": (f"one oracle step of {args.config} ({cfg.n} Gaussians, {W}x{H}, fp32 arithmetic); "
+                          f"blend stages on every {r['tile_stride']}th tile, scaled by the stride"),
+               "stages_s": r["stages_s"]}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "iters/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 raster / f32 params+grads+Adam" if fp16 else "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{args.config}: {cfg.n} Gaussians SH{cfg.sh_degree}, {cfg.dtype} rasterizer, "
+                                   f"{W}x{H}, {len(cams)}-view orbit r={cfg.cam_distance}",
+                       "gaussians": cfg.n, "width": W, "height": H, "sh_degree": cfg.sh_degree,
+                       "views_per_gpu_step": 1, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (parameters+gradients+moments 2.8 GB per step)"},
+            "e2e": {"value": world * 1e3 / e2e_ms, "unit": "iters/s",
+                    "h2d_bytes_per_step": int(tgt_upload.numel() * tgt_upload.element_size()),
+                    "d2h_bytes_per_step": 4},
+            "render_mpix_s": W * H / (render_ms * 1e-3) / 1e6,
+            "stages_ms": {k: round(v, 4) for k, v in stages.items()},
+            "roofline": {"bound": "hbm", "kernel": "k_adam (fused Adam over the 59-float arena)",
+                         "achieved": adam_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": adam_gbs / hbm_peak,
+                         "peak_source": peak_src, "traffic": None,
+                         "bytes_per_gaussian": ADAM_BYTES_PER_GAUSSIAN},
+            "counts": {"visible": counts.n_visible, "instances": counts.n_instances, "buckets": counts.n_buckets},
+            "gpu_launches": kernels_per_step(tile_count, world) * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    rast.close()
+    loss.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,282 @@
+/*
+ * tgs_abi.h -- C ABI of the B200-native tinygs training hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes and
+ * returns an int status (TGS_OK == 0).  No exception and no C++ type crosses
+ * this boundary.  All device work is enqueued on the caller's stream; no
+ * entry point synchronises the host unless its comment says so.
+ *
+ * Reference interfaces replaced (paths inside Adversarr/tinygs):
+ *   rasterizer  RasterizerBase::forward/backward
+ *                 tinygs/include/tinygs/rasterizer/rasterizer.hpp:38-58
+ *               raw API fast_gs::rasterization::forward/backward
+ *                 tinygs/src/rasterizer/fastgs_ours/forward.h:13-45,
+ *                 tinygs/src/rasterizer/fastgs_ours/backward.h:13-53,
+ *                 tinygs/src/rasterizer/fastgs.cu:89-384 (fp32/fp16 dispatch)
+ *   loss        LossBase::evaluate(LossContext, float scale)
+ *                 tinygs/include/tinygs/loss/loss.hpp:6-28,
+ *                 tinygs/src/loss/l1.cu:109-151,
+ *                 tinygs/src/loss/fused_ssim.cu:797-916
+ *   optimizer   OptimizerBase::step(float scale, cudaStream_t)
+ *                 tinygs/include/tinygs/optim/optim.hpp:39-92,
+ *                 tinygs/src/optim/simple_adam.cu:457-580
+ *   model state GPUGaussian3d (SoA parameter arrays)
+ *                 tinygs/include/tinygs/core/gpu_gaussian.hpp:9-73
+ *
+ * Image buffers use the reference's physical layout: CHW planes, each plane
+ * padded to multiples of 8 in x and y and stored as 8x8 tiles,
+ *   idx = ((y>>3)*(Wp>>3) + (x>>3))*64 + (y&7)*8 + (x&7),  plane stride Wp*Hp
+ * (tinygs/include/tinygs/common.hpp:389-408, core/image.hpp:51-59).
+ */
+#ifndef TGS_ABI_H
+#define TGS_ABI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TGS_API __attribute__((visibility("default")))
+#else
+#define TGS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define TGS_OK                    0
+#define TGS_ERR_INVALID_ARGUMENT  1  /* null pointer, bad size, bad dtype     */
+#define TGS_ERR_CUDA              2  /* a CUDA runtime call failed            */
+#define TGS_ERR_CAPACITY          3  /* a device buffer bound was exceeded    */
+#define TGS_ERR_OUT_OF_MEMORY     4  /* cudaMalloc failed at handle creation  */
+#define TGS_ERR_NO_FORWARD        5  /* backward called without a forward     */
+#define TGS_ERR_UNSUPPORTED       6  /* combination not implemented           */
+#define TGS_ERR_DEVICE_TIMEOUT    7  /* a bounded device wait gave up         */
+
+/* Image / rasterizer arithmetic type (reference tinygs::DataType, image.hpp:6-11). */
+#define TGS_FLOAT32 0
+#define TGS_FLOAT16 1
+
+/* Opaque stream handle: a cudaStream_t passed through as a pointer. */
+typedef void* tgs_stream_t;
+
+/* SoA parameter (or gradient, or moment) arrays of one Gaussian model, all
+ * device pointers of fp32, exactly the reference GPUGaussian3d layout:
+ *   means     [n][3]   world position
+ *   opacities [n]      logit of opacity
+ *   rotations [n][4]   quaternion stored (w, x, y, z)
+ *   scales    [n][3]   log of the axis scales
+ *   sh0       [n][3]   SH band-0 coefficients (RGB)
+ *   sh_rest   [n][15][3] SH bands 1..3, always 15 per Gaussian
+ * `sh_degree` (0..3) selects the active bands; storage is always 15.  */
+typedef struct TgsGaussians {
+    float* means;
+    float* opacities;
+    float* rotations;
+    float* scales;
+    float* sh0;
+    float* sh_rest;
+    int64_t n;
+    int32_t sh_degree;
+    int32_t _pad;
+} TgsGaussians;
+
+/* One pinhole view.  `w2c` is the 4x4 world-to-camera matrix in row-major
+ * order (row r at w2c[4r..4r+3]); OpenCV convention (z forward, y down).
+ * The reference takes glm matrices K (column-major, fx=K[0][0], fy=K[1][1],
+ * cx=K[2][0], cy=K[2][1]) and w2c and uploads transpose(w2c)
+ * (tinygs/src/rasterizer/fastgs.cu:95-126); this struct carries the same
+ * numbers by value, so no pose upload is needed.  */
+typedef struct TgsCamera {
+    int32_t width;
+    int32_t height;
+    float fx, fy, cx, cy;
+    float near_plane;   /* reference default 0.01 (orchestrator.hpp:45) */
+    float far_plane;    /* reference default 100  (orchestrator.hpp:46) */
+    float w2c[16];
+} TgsCamera;
+
+/* Per-Gaussian densification statistics, 16 B, reference
+ * tinygs::DensificationInfo (tinygs/include/tinygs/core/gaussian.hpp:18-23). */
+typedef struct TgsDensificationInfo {
+    float accum_counter;
+    float accum_grad_mean2d;
+    float accum_absgrad_mean2d;
+    float max_radii_screen;
+} TgsDensificationInfo;
+
+/* ------------------------------------------------------------- rasterizer */
+
+/* Capacity bounds fixed at creation.  All scratch is allocated once from
+ * these; no step allocates.  max_instances == 0 selects 16 * max_gaussians. */
+typedef struct TgsRasterCaps {
+    int64_t max_gaussians;
+    int32_t max_width;
+    int32_t max_height;
+    int64_t max_instances;
+} TgsRasterCaps;
+
+/* Counts of the last forward.  Written on the device; read by
+ * tgs_raster_counts().  `overflow` != 0 means a capacity bound was hit and
+ * the outputs of that forward are invalid (grow the caps and rerun). */
+typedef struct TgsRasterCounts {
+    uint32_t n_visible;
+    uint32_t n_instances;
+    uint32_t n_buckets;
+    uint32_t overflow;
+} TgsRasterCounts;
+
+typedef struct TgsRaster TgsRaster;
+
+/* Replaces FastGSRasterizer construction + its scratch blobs
+ * (tinygs/src/rasterizer/fastgs.cu:26-87).  Uses the current CUDA device. */
+TGS_API int tgs_raster_create(const TgsRasterCaps* caps, TgsRaster** out);
+TGS_API int tgs_raster_destroy(TgsRaster* r);
+
+/* Device bytes held by the handle (all scratch, allocated at creation). */
+TGS_API int tgs_raster_workspace_bytes(const TgsRaster* r, size_t* bytes);
+
+/* Forward render.  Replaces RasterizerBase::forward / FastGSRasterizer::forward
+ * (tinygs/src/rasterizer/fastgs.cu:89-236) and the kernels of
+ * fastgs_ours/forward.cu:20-292 (dtype TGS_FLOAT32) or
+ * fastgs_ours_fp16/forward.cu:20-290 (dtype TGS_FLOAT16).
+ *   image  [3][Hp*Wp] of dtype, written
+ *   alpha  [Hp*Wp] of dtype, written; may be NULL
+ *   dens   [n] densification info, max_radii_screen updated; may be NULL
+ * The handle keeps the per-view state the backward needs.  No host sync. */
+TGS_API int tgs_raster_forward(TgsRaster* r, const TgsGaussians* params,
+                       const TgsCamera* cam, int32_t dtype, void* image,
+                       void* alpha, TgsDensificationInfo* dens,
+                       tgs_stream_t stream);
+
+/* Backward.  Replaces RasterizerBase::backward / FastGSRasterizer::backward
+ * (tinygs/src/rasterizer/fastgs.cu:238-384) and the kernels of
+ * fastgs_ours/backward.cu:211-349 or fastgs_ours_fp16/backward.cu:211-342.
+ *   image       the image written by the matching forward
+ *   grad_image  dL/dimage, same layout and dtype
+ *   grads       gradient arrays (same layout as params)
+ *   accumulate  1: grads += dL/dparams (reference semantics, grads must be
+ *               zeroed by the caller at the start of an accumulation cycle);
+ *               0: grads = dL/dparams for every Gaussian (no zeroing needed)
+ *   dens        densification accumulators updated; may be NULL  */
+TGS_API int tgs_raster_backward(TgsRaster* r, const TgsGaussians* params,
+                        const TgsCamera* cam, int32_t dtype, const void* image,
+                        const void* grad_image, TgsGaussians* grads,
+                        int32_t accumulate, TgsDensificationInfo* dens,
+                        tgs_stream_t stream);
+
+/* Copies the counts of the last forward to the host.  Synchronises `stream`. */
+TGS_API int tgs_raster_counts(TgsRaster* r, TgsRasterCounts* out, tgs_stream_t stream);
+
+/* Debug / parity access to the intermediate state of the last forward
+ * (device pointers owned by the handle, valid until the next forward):
+ *   which = 0 n_touched_tiles   uint32[n]
+ *         = 1 instance tile ids  uint32[n_instances]   (sorted)
+ *         = 2 instance prim ids  uint32[n_instances]   (sorted)
+ *         = 3 tile ranges        uint32[2*n_tiles]      [start, end)
+ *         = 4 per-pixel contribution counts  uint32[Hp*Wp] (fp32 path)
+ *                                            uint16[Hp*Wp] (fp16 path)
+ *         = 5 mean2d             float[2*n]
+ *         = 6 conic_opacity      float[4*n]  (fp32 path)
+ *         = 7 color              float[3*n]  (fp32 path)
+ *         = 8 primitive info     16 B * n    (fp16 path, packed record)
+ *         = 9 screen bounds      uint16[4*n]
+ *         =10 depth-sorted visible prim ids  uint32[n_visible]
+ *         =11 backward scratch   float[12*n]  (dL/dmean2d, |dL/dmean2d|,
+ *                                dL/dconic, dL/dopacity, dL/dcolor, pad)
+ *         =12 per-tile max contribution count  uint32[n_tiles]
+ *         =13 per-tile inclusive bucket offsets uint32[n_tiles]
+ *         =14 depth keys (float bits)          uint32[n]
+ *         =15 bucket checkpoints [n_buckets][256] float4 (fp32 path) or
+ *             4 x fp16 (r, g, b, 255*T) (fp16 path)  */
+TGS_API int tgs_raster_debug_buffer(TgsRaster* r, int32_t which, void** dev_ptr,
+                            size_t* bytes);
+
+/* ------------------------------------------------------------------- loss */
+
+/* L1 term.  Replaces L1Loss::evaluate (tinygs/src/loss/l1.cu:109-151):
+ *   loss_map += s*|sat(pred)-target|, grad += s*sign(sat(pred)-target),
+ *   s = scale / (3*W*H), over every physical element (padding included).
+ * loss_map and grad may each be NULL. dtype TGS_FLOAT32 or TGS_FLOAT16. */
+TGS_API int tgs_loss_l1(int32_t dtype, int32_t width, int32_t height, const void* pred,
+                const void* target, void* loss_map, void* grad, float scale,
+                tgs_stream_t stream);
+
+typedef struct TgsLoss TgsLoss;
+
+/* Scratch for the SSIM partial-derivative maps, sized for max_w x max_h. */
+TGS_API int tgs_loss_create(int32_t max_width, int32_t max_height, TgsLoss** out);
+TGS_API int tgs_loss_destroy(TgsLoss* l);
+
+/* Fused SSIM term.  Replaces FusedSSIMLoss::evaluate
+ * (tinygs/src/loss/fused_ssim.cu:797-916): 11-tap Gaussian window
+ * (sigma 1.5), C1 = 1e-4, C2 = 9e-4, zero padding,
+ *   loss_map += s*(1-ssim), grad -= s*dssim/dpred,  s = scale/(W*H).
+ * grad may be NULL (forward only); loss_map must not be NULL. */
+TGS_API int tgs_loss_fused_ssim(TgsLoss* l, int32_t dtype, int32_t width,
+                        int32_t height, const void* pred, const void* target,
+                        void* loss_map, void* grad, float scale,
+                        tgs_stream_t stream);
+
+/* Both terms of the reference's default loss mix in one call, equal to
+ * tgs_loss_l1(scale_l1) followed by tgs_loss_fused_ssim(scale_ssim), plus an
+ * optional device scalar: if loss_sum != NULL, *loss_sum (fp32, device) is
+ * set to the sum of this call's loss contributions (no host sync). */
+TGS_API int tgs_loss_l1_ssim(TgsLoss* l, int32_t dtype, int32_t width, int32_t height,
+                     const void* pred, const void* target, void* loss_map,
+                     void* grad, float scale_l1, float scale_ssim,
+                     float* loss_sum, tgs_stream_t stream);
+
+/* -------------------------------------------------------------- optimizer */
+
+/* Hyper-parameters, reference GaussianOptimizationParams + SimpleAdamParameters
+ * (tinygs/include/tinygs/optim/optim.hpp:8-37, simple_adam.hpp:8-27). */
+typedef struct TgsAdamConfig {
+    float beta1;          /* 0.9   */
+    float beta2;          /* 0.999 */
+    float epsilon;        /* 1e-8  */
+    float max_grad_1;     /* |g| clip per element, 0 disables (ref default 1) */
+    float means_lr;       /* times scene_scale * global_lr                    */
+    float shs_lr;         /* sh0: shs_lr*global_lr; sh_rest: *0.05 in addition */
+    float opacities_lr;
+    float scales_lr;
+    float rotations_lr;
+    float opacities_l1;   /* L1 decay on opacity (ref default 0)             */
+    float scales_l1;      /* L1 decay on scale   (ref default 0)             */
+    float scene_scale;
+    float global_lr;
+    int32_t decay_reduction_mean; /* 1: decay weights divided by n ("mean") */
+} TgsAdamConfig;
+
+/* One Adam step over all six parameter arrays in one launch.  Replaces
+ * SimpleAdam::step_adam (tinygs/src/optim/simple_adam.cu:457-580):
+ *   g = gradient_scale*grad (+ decay), clipped to +-max_grad_1,
+ *   m = lerp(m, g, 1-b1), v = lerp(v, g^2, 1-b2),
+ *   theta -= (m/bc1)*lr / (sqrt(v)/sqrt(bc2) + eps),
+ * with bc1 = 1-b1^step and bc2 = 1-b2^step computed in double on the host.
+ * `step` is the 1-based step count after increment (reference
+ * m_global_steps).  m and v use the TgsGaussians layout.  If zero_grads != 0
+ * the gradient arrays are zeroed in the same pass. */
+TGS_API int tgs_adam_step(const TgsGaussians* params, const TgsGaussians* grads,
+                  const TgsGaussians* exp_avg, const TgsGaussians* exp_avg_sq,
+                  const TgsAdamConfig* cfg, uint32_t step,
+                  float gradient_scale, int32_t zero_grads,
+                  tgs_stream_t stream);
+
+/* ------------------------------------------------------------------ misc */
+
+/* Zero a Gaussian array set (the reference's m_gradients->memset(0),
+ * tinygs/src/orchestrator.cu:351-353). */
+TGS_API int tgs_gaussians_zero(const TgsGaussians* g, tgs_stream_t stream);
+
+/* Human-readable text for a status code (static storage). */
+TGS_API const char* tgs_status_string(int status);
+
+/* Library version string, e.g. "tinygs-b200 0.1 sm_100a". */
+TGS_API const char* tgs_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TGS_ABI_H */

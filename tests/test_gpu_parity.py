@@ -1,0 +1,385 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Each stage is checked in isolation by feeding the GPU's own intermediate
+state into the oracle's restatement of the next stage, then the whole
+training step is checked end to end.  Tolerances (from the benchmark spec):
+tile counts, instance lists and ranges bit-exact; fp32 images within 1e-5
+absolute, fp16 images within 2e-3; gradients within 1e-3 relative (plus a
+1e-4-of-max floor for entries that are near zero).
+
+Decisions the oracle marks "fragile" (a cull, bound or tile test within the
+tolerance of its threshold, where the GPU's fast-math log/sqrt/divide and
+the CPU's IEEE ones may legitimately disagree) are excluded from the exact
+comparisons and counted.
+"""
+import numpy as np
+import pytest
+import torch
+
+from tinygs_b200 import runtime as rt
+from tinygs_b200 import scenes
+
+from gpu_helpers import GpuRun, close_rel, scene
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=[False, True], ids=["fp32", "fp16"])
+def fp16(request):
+    return request.param
+
+
+# ------------------------------------------------------------- preprocess
+
+def test_preprocess_matches_oracle(oracle, cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0")
+    run = GpuRun(params, sh, cam, fp16).forward()
+    gp = run.prims()
+    op = oracle.preprocess(params, sh, cam, fp16)
+    stable = op["fragile"] == 0
+    assert (~stable).sum() < 0.005 * cfg.n
+    np.testing.assert_array_equal(gp["n_touched"][stable], op["n_touched"][stable])
+    vis = stable & (op["n_touched"] > 0)
+    assert vis.sum() > 0.9 * cfg.n
+    np.testing.assert_array_equal(gp["bounds"][vis], op["bounds"][vis])
+    assert close_rel(gp["mean2d"][vis], op["mean2d"][vis], 1e-5, 1e-6)[0]
+    assert close_rel(gp["depth_key"][vis].view(np.float32), op["depth_key"][vis].view(np.float32), 1e-6, 0)[0]
+    if fp16:
+        gh = gp["prim_info"][vis][:, :8].view(np.float16).astype(np.float32)
+        oh = op["prim_info"][vis][:, :8].view(np.float16).astype(np.float32)
+        assert close_rel(gh, oh, 2e-3, 1e-6)[0]  # one fp16 ulp
+        drgb = np.abs(gp["prim_info"][vis][:, 8:11].astype(int) - op["prim_info"][vis][:, 8:11].astype(int))
+        assert drgb.max() <= 1
+    else:
+        assert close_rel(gp["conic_opacity"][vis], op["conic_opacity"][vis], 1e-4, 1e-6)[0]
+        assert close_rel(gp["color"][vis], op["color"][vis], 1e-5, 1e-6)[0]
+
+
+def test_preprocess_sh3_color(oracle, cuda_lib):
+    cfg, params, sh, cam = scene("cfg1", n=20000)
+    run = GpuRun(params, sh, cam, False).forward()
+    gp, op = run.prims(), oracle.preprocess(params, sh, cam, False)
+    vis = (op["fragile"] == 0) & (op["n_touched"] > 0)
+    assert vis.sum() > 1000
+    np.testing.assert_array_equal(gp["n_touched"][vis], op["n_touched"][vis])
+    assert close_rel(gp["color"][vis], op["color"][vis], 1e-5, 1e-6)[0]
+
+
+# ---------------------------------------------------------------- binning
+
+def _check_instance_lists(gb, gp, ob, fragile):
+    """GPU lists are sorted by (tile, depth, index) and hold the same
+    (tile, prim) pairs as the oracle outside fragile Gaussians."""
+    tiles, prims = gb["inst_tile"], gb["inst_prim"]
+    assert gb["n_instances"] == int(gp["n_touched"].astype(np.int64).sum())
+    assert np.all(np.diff(tiles.astype(np.int64)) >= 0)
+    depth = gp["depth_key"][prims].astype(np.uint64)
+    key = (tiles.astype(np.uint64) << np.uint64(40)) | (depth << np.uint64(8))
+    same = tiles[1:] == tiles[:-1]
+    d0, d1 = gp["depth_key"][prims[:-1]], gp["depth_key"][prims[1:]]
+    assert np.all((d0 <= d1) | ~same)
+    tie = same & (d0 == d1)
+    assert np.all(prims[1:][tie] > prims[:-1][tie])
+    del key
+    # ranges agree with the sorted list
+    r = gb["ranges"]
+    cnt = (r[:, 1] - r[:, 0]).astype(np.int64)
+    assert cnt.sum() == gb["n_instances"]
+    nz = cnt > 0
+    assert np.all(tiles[r[nz, 0]] == np.nonzero(nz)[0])
+    # pairs equal to the oracle's outside fragile Gaussians
+    keep_g = fragile[prims] == 0
+    keep_o = fragile[ob["inst_prim"]] == 0
+    pg = set(zip(tiles[keep_g].tolist(), prims[keep_g].tolist()))
+    po = set(zip(ob["inst_tile"][keep_o].tolist(), ob["inst_prim"][keep_o].tolist()))
+    assert pg == po
+
+
+def test_binning_sorted_and_exact(oracle, cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0")
+    run = GpuRun(params, sh, cam, fp16).forward()
+    assert run.counts.overflow == 0
+    gp, gb = run.prims(), run.bins()
+    op = oracle.preprocess(params, sh, cam, fp16)
+    ob = oracle.binning(op, cam, fp16)
+    _check_instance_lists(gb, gp, ob, op["fragile"])
+    # the oracle binning over the GPU's own primitives reproduces the GPU
+    # lists exactly, order included
+    gp2 = dict(gp)
+    gp2["fragile"] = np.zeros(cfg.n, np.uint8)
+    ob2 = oracle.binning(gp2, cam, fp16)
+    stable = op["fragile"] == 0
+    if stable.all():
+        np.testing.assert_array_equal(ob2["inst_prim"], gb["inst_prim"])
+        np.testing.assert_array_equal(ob2["inst_tile"], gb["inst_tile"])
+    assert gb["n_visible"] == int((gp["n_touched"] > 0).sum())
+    np.testing.assert_array_equal(gb["sorted_visible"], ob2["sorted_visible"])
+
+
+def test_binning_large_footprints_use_warp_path(oracle, cuda_lib):
+    """Big Gaussians (more than 8 candidate tiles) take the warp-cooperative
+    counting and emission path."""
+    cfg, params, sh, cam = scene("cfg0", n=3000)
+    params["scales"] = params["scales"] + 2.5  # ~12x larger
+    run = GpuRun(params, sh, cam, False).forward()
+    gp, gb = run.prims(), run.bins()
+    big = (gp["bounds"][:, 1] - gp["bounds"][:, 0]).astype(int) * (gp["bounds"][:, 3] - gp["bounds"][:, 2])
+    assert (big > 8).sum() > 100
+    op = oracle.preprocess(params, sh, cam, False)
+    ob = oracle.binning(op, cam, False)
+    stable = op["fragile"] == 0
+    np.testing.assert_array_equal(gp["n_touched"][stable], op["n_touched"][stable])
+    _check_instance_lists(gb, gp, ob, op["fragile"])
+
+
+# ---------------------------------------------------------- blend forward
+
+def test_blend_forward_matches_oracle(oracle, cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0")
+    run = GpuRun(params, sh, cam, fp16).forward()
+    gp, gb, gf = run.prims(), run.bins(), run.fwd_state()
+    of = oracle.blend_forward(gp, gb, cam, fp16)
+    img_g = gf["image"].astype(np.float32)
+    img_o = of["image"].astype(np.float32)
+    err = np.abs(img_g - img_o)
+    if fp16:
+        assert err.max() <= 2e-3, err.max()
+        assert np.mean(gf["n_contrib"] == of["n_contrib"]) > 0.999
+    else:
+        # 1e-5 absolute; a decision on the alpha or transmittance threshold
+        # evaluated within one ulp may flip for a handful of pixels
+        assert np.mean(err <= 1e-5) >= 0.9999, (err.max(), np.mean(err <= 1e-5))
+        assert err.max() <= 5e-3
+        assert np.mean(gf["n_contrib"] == of["n_contrib"]) >= 0.9999
+        a_err = np.abs(gf["alpha"] - of["alpha"])
+        assert np.mean(a_err <= 1e-5) >= 0.9999
+    assert np.mean(gf["tile_max"] == of["tile_max"]) >= 0.99
+
+
+def test_blend_forward_odd_sizes(oracle, cuda_lib, fp16):
+    """Image sizes that are not multiples of 16 (partial render tiles) or of 8
+    (padded storage tiles)."""
+    for (w, h) in [(200, 136), (250, 130)]:
+        cfg, params, sh, _ = scene("cfg0", n=4000)
+        cam = scenes.camera_dict(cfg, scenes.look_at_w2c((0.0, 0.0, -3.0)))
+        cam.update(width=w, height=h, cx=w / 2, cy=h / 2)
+        run = GpuRun(params, sh, cam, fp16).forward()
+        gp, gb, gf = run.prims(), run.bins(), run.fwd_state()
+        of = oracle.blend_forward(gp, gb, cam, fp16)
+        err = np.abs(gf["image"].astype(np.float32) - of["image"].astype(np.float32))
+        tol = 2e-3 if fp16 else 1e-5
+        assert np.mean(err <= tol) >= 0.9999, (w, h, err.max())
+
+
+# --------------------------------------------------------- blend backward
+
+def _grad_image(run, seed=3):
+    rng = np.random.default_rng(seed)
+    g = rng.normal(0.0, 1e-3, size=run.image.numel()).astype(np.float32)
+    return g.astype(np.float16) if run.fp16 else g
+
+
+def test_blend_backward_matches_oracle(oracle, cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0")
+    run = GpuRun(params, sh, cam, fp16).forward()
+    gimg = _grad_image(run)
+    run.backward(gimg)
+    gp, gb, gf = run.prims(), run.bins(), run.fwd_state()
+    ob = oracle.blend_backward(gp, gb, gf, gimg, cam, fp16)
+    gh = run.helpers()
+    vis = gp["n_touched"] > 0
+    for k in ("grad_mean2d", "absgrad_mean2d", "grad_conic", "grad_opacity", "grad_color"):
+        ok, worst, nbad = close_rel(gh[k][vis], ob[k][vis], 1e-3, 1e-4)
+        assert ok, (k, worst, nbad)
+
+
+# ----------------------------------------------------- preprocess backward
+
+def test_preprocess_backward_matches_oracle(oracle, cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg1", n=20000)
+    run = GpuRun(params, sh, cam, fp16).forward()
+    gimg = _grad_image(run, 4)
+    run.backward(gimg, accumulate=True)
+    gp = run.prims()
+    screen = run.helpers()
+    og = oracle.preprocess_backward(params, sh, cam, gp["n_touched"], screen)
+    gg = run.grads_np()
+    for k in ("means", "opacities", "rotations", "scales", "sh0", "sh_rest"):
+        ok, worst, nbad = close_rel(gg[k], og[k], 1e-3, 1e-4)
+        assert ok, (k, worst, nbad)
+
+
+def test_backward_overwrite_equals_accumulate_into_zero(cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0", n=5000)
+    a = GpuRun(params, sh, cam, fp16).forward()
+    g = _grad_image(a, 9)
+    a.backward(g, accumulate=True)
+    b = GpuRun(params, sh, cam, fp16).forward()
+    b.grads.storage.fill_(123.0)  # overwrite mode must not read these
+    b.backward(g, accumulate=False)
+    ga, gb_ = a.grads_np(), b.grads_np()
+    for k in ga:
+        ok, worst, nbad = close_rel(gb_[k], ga[k], 1e-5, 1e-6)
+        assert ok, (k, worst)
+
+
+# ------------------------------------------------------------------ losses
+
+@pytest.mark.parametrize("size", [(256, 256), (200, 136)])
+def test_l1_ssim_matches_oracle(oracle, cuda_lib, fp16, size):
+    w, h = size
+    rng = np.random.default_rng(11)
+    pred = scenes.target_image(w, h, 1).reshape(-1) * 1.2 - 0.1
+    tgt = scenes.target_image(w, h, 2).reshape(-1)
+    dt = np.float16 if fp16 else np.float32
+    pred, tgt = pred.astype(dt), tgt.astype(dt)
+    lo, go = np.zeros_like(pred), np.zeros_like(pred)
+    oracle.l1(pred, tgt, lo, go, w, h, 8.0)
+    oracle.ssim(pred, tgt, lo, go, w, h, 2.0)
+    loss = rt.FusedLoss(w, h)
+    tp, tt = torch.from_numpy(pred).cuda(), torch.from_numpy(tgt).cuda()
+    lg, gg = torch.zeros_like(tp), torch.zeros_like(tp)
+    s = torch.zeros(1, device="cuda")
+    loss.evaluate(tp, tt, lg, gg, w, h, grad_scaler=10.0, loss_sum=s)
+    torch.cuda.synchronize()
+    lg, gg = lg.cpu().numpy().astype(np.float64), gg.cpu().numpy().astype(np.float64)
+    if fp16:
+        assert np.abs(lg - lo.astype(np.float64)).max() <= 2e-3 * max(1.0, np.abs(lo).max())
+        assert close_rel(gg, go.astype(np.float64), 2e-3, 2e-3)[0]
+    else:
+        assert close_rel(lg, lo, 1e-4, 1e-5)[0]
+        ok, worst, nbad = close_rel(gg, go, 1e-3, 1e-4)
+        assert ok, (worst, nbad)
+    assert abs(float(s.item()) - float(lo.astype(np.float64).sum())) <= 1e-3 * abs(float(lo.astype(np.float64).sum()))
+    # separate entry points equal the fused one
+    l2, g2 = torch.zeros_like(tp), torch.zeros_like(tp)
+    loss.evaluate_l1(tp, tt, l2, g2, w, h, 8.0)
+    loss.evaluate_ssim(tp, tt, l2, g2, w, h, 2.0)
+    torch.cuda.synchronize()
+    assert close_rel(g2.cpu().numpy(), gg, 1e-3 if fp16 else 1e-6, 1e-6)[0]
+
+
+# -------------------------------------------------------------------- adam
+
+def test_adam_matches_oracle(oracle, cuda_lib):
+    n = 10001  # not a multiple of 4: exercises the element-wise tails
+    rng = np.random.default_rng(5)
+    mk = lambda: {"means": rng.normal(size=(n, 3)).astype(np.float32),
+                  "opacities": rng.normal(size=n).astype(np.float32),
+                  "rotations": rng.normal(size=(n, 4)).astype(np.float32),
+                  "scales": rng.normal(size=(n, 3)).astype(np.float32),
+                  "sh0": rng.normal(size=(n, 3)).astype(np.float32),
+                  "sh_rest": rng.normal(size=(n, 15, 3)).astype(np.float32)}
+    params, grads = mk(), mk()
+    cfg = rt.AdamParams(max_grad_1=0.3, means_lr=1e-3, shs_lr=1e-3, opacities_lr=1e-3, scales_lr=1e-3,
+                        rotations_lr=1e-3, opacities_l1=0.01, scales_l1=0.02, scene_scale=2.0)
+    g = rt.GaussianSet.from_numpy(params, 3)
+    gr = rt.GaussianSet.from_numpy(grads, 3)
+    opt = rt.SimpleAdam(g, gr, cfg)
+    m = {k: np.zeros_like(v) for k, v in params.items()}
+    v = {k: np.zeros_like(v_) for k, v_ in params.items()}
+    ref = {k: a.copy() for k, a in params.items()}
+    for step in (1, 2, 3):
+        opt.step(0.1)
+        oracle.adam_step(ref, grads, m, v, cfg, step, 0.1)
+    torch.cuda.synchronize()
+    out = g.to_numpy()
+    for k in ref:
+        np.testing.assert_allclose(out[k], ref[k], rtol=2e-6, atol=2e-7, err_msg=k)
+    mo = opt.exp_avg.to_numpy()
+    for k in m:
+        np.testing.assert_allclose(mo[k], m[k], rtol=2e-6, atol=1e-9, err_msg=k)
+
+
+def test_adam_zero_grads_fused(cuda_lib):
+    params = scenes.gaussian_params(1000, 3, "normal", 1)
+    g = rt.GaussianSet.from_numpy(params, 3)
+    gr = rt.GaussianSet.from_numpy(scenes.gaussian_params(1000, 3, "normal", 2), 3)
+    opt = rt.SimpleAdam(g, gr)
+    opt.step(1.0, zero_grads=True)
+    torch.cuda.synchronize()
+    assert float(gr.storage.abs().max()) == 0.0
+
+
+# -------------------------------------------------------------- end to end
+
+def test_train_step_end_to_end(oracle, cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0")
+    W, H = cfg.width, cfg.height
+    target = scenes.target_image(W, H, 77).reshape(-1)
+    dt = np.float16 if fp16 else np.float32
+    ref = oracle.train_step({k: v.copy() for k, v in params.items()}, sh, cam, target, fp16, do_adam=False)
+    run = GpuRun(params, sh, cam, fp16).forward()
+    loss = rt.FusedLoss(W, H)
+    tgt = torch.from_numpy(target.astype(dt)).cuda()
+    lmap = torch.zeros_like(run.image)
+    loss.evaluate(run.image, tgt, lmap, run.grad_image, W, H, grad_scaler=10.0)
+    run.rast.backward(run.ctx)
+    torch.cuda.synchronize()
+    img_o = ref["render"]["fwd"]["image"].astype(np.float32)
+    err = np.abs(run.image.cpu().numpy().astype(np.float32) - img_o)
+    tol = 2e-3 if fp16 else 1e-5
+    assert np.mean(err <= tol) >= 0.999, (err.max(), np.mean(err <= tol))
+    gg = run.grads_np()
+    og = ref["grads"]
+    for k in ("means", "opacities", "rotations", "scales", "sh0"):
+        a, b = gg[k].astype(np.float64).ravel(), og[k].astype(np.float64).ravel()
+        cos = float(a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-30))
+        # end to end, rare threshold flips (fragile tile tests, L1 signs
+        # where pred == target) move a few entries; the direction must agree
+        assert cos > (0.99 if fp16 else 0.999), (k, cos)
+        rel = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+        assert rel < (0.1 if fp16 else 0.02), (k, rel)
+
+
+def test_empty_and_degenerate_scenes(cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0", n=64)
+    # everything behind the camera
+    p = {k: v.copy() for k, v in params.items()}
+    p["means"][:, 2] = -10.0
+    run = GpuRun(p, sh, cam, fp16).forward()
+    assert run.counts.n_visible == 0 and run.counts.n_instances == 0
+    assert float(run.image.float().abs().max()) == 0.0
+    run.backward(np.zeros(run.image.numel(), np.float16 if fp16 else np.float32))
+    assert float(run.grads.storage.abs().max()) == 0.0
+    # degenerate quaternions and transparent Gaussians are culled
+    p = {k: v.copy() for k, v in params.items()}
+    p["rotations"][:32] = 0.0
+    p["opacities"][32:] = -20.0
+    run = GpuRun(p, sh, cam, fp16).forward()
+    assert run.counts.n_visible == 0
+
+
+def test_capacity_overflow_is_reported_not_faulted(cuda_lib, fp16):
+    cfg, params, sh, cam = scene("cfg0", n=4000)
+    run = GpuRun(params, sh, cam, fp16, max_instances=500).forward()
+    assert run.counts.overflow != 0
+    assert run.counts.n_instances > 500
+    run.backward(np.ones(run.image.numel(), np.float16 if fp16 else np.float32))
+    assert torch.isfinite(run.grads.storage).all()
+    assert float(run.grads.storage.abs().max()) == 0.0
+
+
+def test_densification_info_accumulates(oracle, cuda_lib):
+    cfg, params, sh, cam = scene("cfg0", n=5000)
+    run = GpuRun(params, sh, cam, False)
+    dens = torch.zeros(5000, 4, device="cuda")
+    run.ctx.densification_info = dens
+    run.forward()
+    gimg = _grad_image(run, 21)
+    run.backward(gimg)
+    d = dens.cpu().numpy()
+    gp = run.prims()
+    vis = gp["n_touched"] > 0
+    np.testing.assert_array_equal(d[vis, 0], 1.0)
+    np.testing.assert_array_equal(d[~vis, 0], 0.0)
+    # the oracle's radii and accumulated gradient norms
+    od = np.zeros((5000, 4), np.float32)
+    oracle.preprocess(params, sh, cam, False, dens=od)
+    ok = (d[:, 3] == od[:, 3]) | (np.abs(d[:, 3] - od[:, 3]) <= 1.0)  # ceil() of an approximate sqrt
+    assert ok.mean() > 0.999
+    screen = run.helpers()
+    ref = np.zeros((5000, 4), np.float32)
+    oracle.preprocess_backward(params, sh, cam, gp["n_touched"], screen, dens=ref)
+    assert close_rel(d[:, 1], ref[:, 1], 1e-4, 1e-6)[0]
+    assert close_rel(d[:, 2], ref[:, 2], 1e-4, 1e-6)[0]

@@ -1,0 +1,121 @@
+"""ctypes binding of ``include/tgs_abi.h``.
+
+This module only describes the C structs and function prototypes and loads
+``libtgs_b200.so``; it never falls back to anything else.  Loading the library
+does not touch the GPU (the CUDA runtime is linked statically and initialised
+lazily), so the export check runs on machines without one.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libtgs_b200.so"
+HEADER = PKG.parent / "include" / "tgs_abi.h"
+
+TGS_OK = 0
+TGS_ERR_INVALID_ARGUMENT = 1
+TGS_ERR_CUDA = 2
+TGS_ERR_CAPACITY = 3
+TGS_ERR_OUT_OF_MEMORY = 4
+TGS_ERR_NO_FORWARD = 5
+TGS_ERR_UNSUPPORTED = 6
+TGS_ERR_DEVICE_TIMEOUT = 7
+
+TGS_FLOAT32 = 0
+TGS_FLOAT16 = 1
+
+
+class TgsGaussians(ctypes.Structure):
+    _fields_ = [("means", c_void_p), ("opacities", c_void_p), ("rotations", c_void_p), ("scales", c_void_p),
+                ("sh0", c_void_p), ("sh_rest", c_void_p), ("n", c_int64), ("sh_degree", c_int32),
+                ("_pad", c_int32)]
+
+
+class TgsCamera(ctypes.Structure):
+    _fields_ = [("width", c_int32), ("height", c_int32), ("fx", c_float), ("fy", c_float), ("cx", c_float),
+                ("cy", c_float), ("near_plane", c_float), ("far_plane", c_float), ("w2c", c_float * 16)]
+
+
+class TgsRasterCaps(ctypes.Structure):
+    _fields_ = [("max_gaussians", c_int64), ("max_width", c_int32), ("max_height", c_int32),
+                ("max_instances", c_int64)]
+
+
+class TgsRasterCounts(ctypes.Structure):
+    _fields_ = [("n_visible", c_uint32), ("n_instances", c_uint32), ("n_buckets", c_uint32),
+                ("overflow", c_uint32)]
+
+
+class TgsAdamConfig(ctypes.Structure):
+    _fields_ = [("beta1", c_float), ("beta2", c_float), ("epsilon", c_float), ("max_grad_1", c_float),
+                ("means_lr", c_float), ("shs_lr", c_float), ("opacities_lr", c_float), ("scales_lr", c_float),
+                ("rotations_lr", c_float), ("opacities_l1", c_float), ("scales_l1", c_float),
+                ("scene_scale", c_float), ("global_lr", c_float), ("decay_reduction_mean", c_int32)]
+
+
+_P = c_void_p
+PROTOTYPES = {
+    "tgs_raster_create": (c_int32, [POINTER(TgsRasterCaps), POINTER(c_void_p)]),
+    "tgs_raster_destroy": (c_int32, [_P]),
+    "tgs_raster_workspace_bytes": (c_int32, [_P, POINTER(c_size_t)]),
+    "tgs_raster_forward": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, _P, _P, _P, _P]),
+    "tgs_raster_backward": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, _P, _P,
+                                      POINTER(TgsGaussians), c_int32, _P, _P]),
+    "tgs_raster_counts": (c_int32, [_P, POINTER(TgsRasterCounts), _P]),
+    "tgs_raster_debug_buffer": (c_int32, [_P, c_int32, POINTER(c_void_p), POINTER(c_size_t)]),
+    "tgs_loss_l1": (c_int32, [c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, _P]),
+    "tgs_loss_create": (c_int32, [c_int32, c_int32, POINTER(c_void_p)]),
+    "tgs_loss_destroy": (c_int32, [_P]),
+    "tgs_loss_fused_ssim": (c_int32, [_P, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, _P]),
+    "tgs_loss_l1_ssim": (c_int32, [_P, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, _P, _P]),
+    "tgs_adam_step": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32, c_float, c_int32, _P]),
+    "tgs_gaussians_zero": (c_int32, [POINTER(TgsGaussians), _P]),
+    "tgs_status_string": (c_char_p, [c_int32]),
+    "tgs_version": (c_char_p, []),
+}
+
+_lib = None
+
+
+def header_symbols(header: Path = HEADER) -> list[str]:
+    """Names of every function ``include/tgs_abi.h`` declares."""
+    text = header.read_text()
+    return sorted(set(re.findall(r"TGS_API\s+[\w\s\*]*?\b(tgs_\w+)\s*\(", text)))
+
+
+def load_library(path: Path | str | None = None) -> ctypes.CDLL:
+    """Load libtgs_b200.so and attach the prototypes.  Raises if it is missing:
+    there is no fallback implementation."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(f"{p} is missing; build it with `python -m tinygs_b200.build` "
+                           "(tinygs_b200 has no non-CUDA fallback)")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in PROTOTYPES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+class TgsError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        lib = _lib
+        msg = lib.tgs_status_string(status).decode() if lib is not None else str(status)
+        super().__init__(f"{where}: {msg} (status {status})")
+        self.status = status
+
+
+def check(status: int, where: str) -> None:
+    if status != TGS_OK:
+        raise TgsError(status, where)

@@ -1,0 +1,130 @@
+// adam.cu -- one fused Adam step over all six Gaussian parameter arrays.
+//
+// The reference launches one kernel per parameter array
+// (tinygs/src/optim/simple_adam.cu:457-580, kernels adam / adam_f32x4 at
+// :105-213).  Here a single grid-stride launch walks the six segments as one
+// virtual array in 16-byte chunks (float4 loads/stores of theta, grad, m, v),
+// with the per-segment learning rate and decay looked up per chunk; segment
+// tails that are not a multiple of four floats are handled element-wise
+// (the reference's f32x4 kernel reads and writes up to three floats past
+// the end there).  Optionally the gradient is zeroed in the same pass.
+#include "kernels.h"
+
+namespace tgs {
+namespace {
+
+constexpr int kMaxSegs = 8;
+
+struct SegTable {
+  float* theta[kMaxSegs];
+  const float* grad[kMaxSegs];
+  float* m[kMaxSegs];
+  float* v[kMaxSegs];
+  int64_t count[kMaxSegs];
+  int64_t chunk_begin[kMaxSegs + 1];  // prefix of ceil(count/4)
+  float lr[kMaxSegs];
+  float decay[kMaxSegs];
+  int decay_kind[kMaxSegs];
+  int vec_ok[kMaxSegs];
+  int n;
+};
+
+struct AdamScalars {
+  float beta1, beta2, eps, gscale, bc1, bc2_sqrt, max_g;
+  int zero_grads;
+};
+
+__device__ __forceinline__ float lerp_ref(float v0, float v1, float t) {
+  // fma form of v0 + t (v1 - v0), simple_adam.cu:24-26
+  return fmaf(t, v1, fmaf(-t, v0, v0));
+}
+
+__device__ __forceinline__ void adam_one(float& th, float g_raw, float& m, float& v, float lr, int kind, float decay,
+                                         const AdamScalars& a) {
+  float g = a.gscale * g_raw;
+  if (kind == 1) {
+    const float s = 1.0f / (1.0f + __expf(-th));
+    g = g + decay * (s * (1.0f - s));
+  } else if (kind == 2) {
+    g = g + decay * __expf(th);
+  }
+  if (a.max_g != 0.0f) g = copysignf(fminf(fabsf(g), a.max_g), g);
+  m = lerp_ref(m, g, 1.0f - a.beta1);
+  v = lerp_ref(v, g * g, 1.0f - a.beta2);
+  const float mh = m / a.bc1;
+  const float den = sqrtf(v) / a.bc2_sqrt + a.eps;
+  th -= mh * lr / den;
+}
+
+__global__ void __launch_bounds__(256) k_adam(SegTable t, AdamScalars a, int64_t total_chunks) {
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total_chunks;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int s = 0;
+#pragma unroll
+    for (int k = 1; k < kMaxSegs; ++k)
+      if (k < t.n && c >= t.chunk_begin[k]) s = k;
+    const int64_t e0 = (c - t.chunk_begin[s]) * 4;
+    const int64_t cnt = t.count[s];
+    const float lr = t.lr[s], decay = t.decay[s];
+    const int kind = t.decay_kind[s];
+    if (t.vec_ok[s] && e0 + 4 <= cnt) {
+      float4 th = *reinterpret_cast<const float4*>(t.theta[s] + e0);
+      const float4 g = *reinterpret_cast<const float4*>(t.grad[s] + e0);
+      float4 m = *reinterpret_cast<const float4*>(t.m[s] + e0);
+      float4 v = *reinterpret_cast<const float4*>(t.v[s] + e0);
+      adam_one(th.x, g.x, m.x, v.x, lr, kind, decay, a);
+      adam_one(th.y, g.y, m.y, v.y, lr, kind, decay, a);
+      adam_one(th.z, g.z, m.z, v.z, lr, kind, decay, a);
+      adam_one(th.w, g.w, m.w, v.w, lr, kind, decay, a);
+      *reinterpret_cast<float4*>(t.theta[s] + e0) = th;
+      *reinterpret_cast<float4*>(t.m[s] + e0) = m;
+      *reinterpret_cast<float4*>(t.v[s] + e0) = v;
+      if (a.zero_grads) *reinterpret_cast<float4*>(const_cast<float*>(t.grad[s]) + e0) = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      for (int64_t e = e0; e < min(e0 + 4, cnt); ++e) {
+        float th = t.theta[s][e], m = t.m[s][e], v = t.v[s][e];
+        adam_one(th, t.grad[s][e], m, v, lr, kind, decay, a);
+        t.theta[s][e] = th;
+        t.m[s][e] = m;
+        t.v[s][e] = v;
+        if (a.zero_grads) const_cast<float*>(t.grad[s])[e] = 0.f;
+      }
+    }
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+void launch_adam(const AdamSegment* segs, int n_segs, float beta1, float beta2, float eps, float gradient_scale,
+                 float bc1, float bc2_sqrt, float max_grad_1, int zero_grads, cudaStream_t stream) {
+  SegTable t{};
+  t.n = n_segs;
+  int64_t chunks = 0;
+  for (int k = 0; k < n_segs && k < kMaxSegs; ++k) {
+    t.theta[k] = segs[k].theta;
+    t.grad[k] = segs[k].grad;
+    t.m[k] = segs[k].m;
+    t.v[k] = segs[k].v;
+    t.count[k] = segs[k].count;
+    t.lr[k] = segs[k].lr;
+    t.decay[k] = segs[k].decay;
+    t.decay_kind[k] = segs[k].decay_kind;
+    t.vec_ok[k] = aligned16(segs[k].theta) && aligned16(segs[k].grad) && aligned16(segs[k].m) &&
+                  aligned16(segs[k].v);
+    t.chunk_begin[k] = chunks;
+    chunks += (segs[k].count + 3) / 4;
+  }
+  for (int k = n_segs; k <= kMaxSegs; ++k) t.chunk_begin[k < kMaxSegs + 1 ? k : kMaxSegs] = chunks;
+  if (chunks == 0) return;
+  AdamScalars a{beta1, beta2, eps, gradient_scale, bc1, bc2_sqrt, max_grad_1, zero_grads};
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (chunks + 255) / 256;
+  const int blocks = static_cast<int>(want < sms * 8 ? want : sms * 8);
+  k_adam<<<blocks, 256, 0, stream>>>(t, a, chunks);
+}
+
+}  // namespace tgs

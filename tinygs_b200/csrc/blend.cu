@@ -1,0 +1,478 @@
+// blend.cu -- per-tile front-to-back alpha blending, forward and backward.
+//
+// Forward (one CTA per 16x16 tile): primitives are staged through shared
+// memory in batches, each pixel composites front to back until its
+// transmittance would drop below 1e-4, and every 32 primitives the running
+// (colour, transmittance) of every pixel is checkpointed so that the
+// backward can restart any 32-primitive bucket independently.
+//   fp32 reference: fastgs_ours/kernels_forward.cuh:569-715
+//   fp16 reference: fastgs_ours_fp16/kernels_forward.cuh:917-1171 (half2
+//   arithmetic, two horizontally adjacent pixels per thread, colour and
+//   transmittance carried scaled by 255)
+// Backward (one warp per bucket, one lane per primitive): the 256 pixels of
+// the tile stream through the warp as a diagonal wavefront (lane l sees
+// pixel i - l at step i), so each pixel's state passes from primitive to
+// primitive in depth order by a one-lane shuffle.  Per-primitive sums are
+// reduced in registers and added to the per-Gaussian scratch with one set of
+// atomics per bucket.
+//   fp32 reference: fastgs_ours/kernels_backward.cuh:675-927
+//   fp16 reference: fastgs_ours_fp16/kernels_backward.cuh:861-1389; its
+//   semantics (no per-pixel contributor mask, alpha capped at fp16(0.99),
+//   255-scaled checkpoints) are evaluated here in fp32 arithmetic.
+#include "kernels.h"
+
+namespace tgs {
+namespace {
+
+// ------------------------------------------------------------ forward fp32
+
+__global__ void __launch_bounds__(kTilePixels)
+    k_blend_forward_f32(const uint2* __restrict__ ranges, const uint32_t* __restrict__ bucket_offsets,
+                        const uint32_t* __restrict__ inst_prim, const float2* __restrict__ mean2d,
+                        const float4* __restrict__ conic_opacity, const float* __restrict__ color,
+                        const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ image,
+                        float* __restrict__ alpha, uint32_t* __restrict__ n_contrib,
+                        uint32_t* __restrict__ tile_max, uint32_t* __restrict__ bucket_tile,
+                        float4* __restrict__ ckpt) {
+  __shared__ float2 s_mean[kTilePixels];
+  __shared__ float4 s_co[kTilePixels];
+  __shared__ float4 s_col[kTilePixels];
+  __shared__ uint32_t s_max[kTilePixels / 32];
+  const uint32_t tid = threadIdx.x;
+  const uint32_t lx = tid & 15u, ly = tid >> 4;
+  const uint32_t tile = blockIdx.y * cam.grid_w + blockIdx.x;
+  const uint32_t px = blockIdx.x * kTile + lx, py = blockIdx.y * kTile + ly;
+  const bool inside = px < cam.width && py < cam.height;
+  const float2 pix = make_float2(static_cast<float>(px) + 0.5f, static_cast<float>(py) + 0.5f);
+  const bool ok = counts->overflow == 0u;
+  const uint2 r = ok ? ranges[tile] : make_uint2(0, 0);
+  const uint32_t count = r.y - r.x;
+  const uint32_t first_bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
+  const uint32_t n_buckets = (count + kBucket - 1) / kBucket;
+  for (uint32_t k = tid; k < n_buckets; k += kTilePixels) bucket_tile[first_bucket + k] = tile;
+  const uint32_t slot = tiled_index(ly, lx, 2);
+  float4* my_ckpt = ckpt + static_cast<size_t>(first_bucket) * kTilePixels + slot;
+
+  float cr = 0.f, cg = 0.f, cb = 0.f, T = 1.f;
+  uint32_t n_seen = 0, n_used = 0;
+  bool done = !inside;
+  for (uint32_t start = 0; start < count; start += kTilePixels) {
+    if (__syncthreads_count(done) == kTilePixels) break;
+    const uint32_t k = start + tid;
+    if (k < count) {
+      const uint32_t p = inst_prim[r.x + k];
+      s_mean[tid] = mean2d[p];
+      s_co[tid] = conic_opacity[p];
+      s_col[tid] = make_float4(fmaxf(color[3 * p], 0.f), fmaxf(color[3 * p + 1], 0.f),
+                               fmaxf(color[3 * p + 2], 0.f), 0.f);
+    }
+    __syncthreads();
+    const uint32_t batch = min(static_cast<uint32_t>(kTilePixels), count - start);
+    uint32_t j = 0;
+    for (; !done && j < batch; ++j) {
+      if ((j & 31u) == 0) my_ckpt[static_cast<size_t>((start + j) >> 5) * kTilePixels] = make_float4(cr, cg, cb, T);
+      ++n_seen;
+      const float4 co = s_co[j];
+      const float2 m = s_mean[j];
+      const float dx = m.x - pix.x, dy = m.y - pix.y;
+      const float power = 0.5f * (co.x * dx * dx + co.z * dy * dy) + co.y * dx * dy;
+      if (power < 0.0f) continue;
+      const float a = fminf(co.w * __expf(-power), kMaxAlphaF32);
+      if (a < kMinAlpha) continue;
+      const float Tn = T * (1.0f - a);
+      if (Tn < kMinTransmittance) {
+        done = true;
+        continue;
+      }
+      const float4 c = s_col[j];
+      const float w = T * a;
+      cr += w * c.x;
+      cg += w * c.y;
+      cb += w * c.z;
+      T = Tn;
+      n_used = n_seen;
+    }
+    // checkpoints of the rest of this batch hold the frozen state
+    for (j = (j + 31u) & ~31u; j < batch; j += 32u)
+      my_ckpt[static_cast<size_t>((start + j) >> 5) * kTilePixels] = make_float4(cr, cg, cb, T);
+  }
+  if (inside) {
+    const uint32_t pi = tiled_index(py, px, cam.tiled_w);
+    image[pi] = cr;
+    image[pi + cam.plane] = cg;
+    image[pi + 2 * cam.plane] = cb;
+    if (alpha != nullptr) alpha[pi] = 1.0f - T;
+    n_contrib[pi] = n_used;
+  }
+  const uint32_t wmax = __reduce_max_sync(0xffffffffu, n_used);
+  if ((tid & 31u) == 0) s_max[tid >> 5] = wmax;
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t mx = 0;
+    for (int w = 0; w < kTilePixels / 32; ++w) mx = max(mx, s_max[w]);
+    tile_max[tile] = mx;
+  }
+}
+
+// ------------------------------------------------------------ forward fp16
+
+__device__ __forceinline__ __half2 h2exp2_approx(__half2 x) {
+  __half2 y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(*reinterpret_cast<uint32_t*>(&y)) : "r"(*reinterpret_cast<uint32_t*>(&x)));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// fp16 rasterizer: 128 threads, thread (tx, ty) owns pixels (2tx, ty) and
+// (2tx+1, ty).  Every arithmetic step is the same fp16 operation as in the
+// reference kernel, so images agree to the bit with it (up to the one
+// hardware exp2 approximation both share).
+constexpr int kF16Threads = kTilePixels / 2;
+
+__global__ void __launch_bounds__(kF16Threads)
+    k_blend_forward_f16(const uint2* __restrict__ ranges, const uint32_t* __restrict__ bucket_offsets,
+                        const uint32_t* __restrict__ inst_prim, const float2* __restrict__ mean2d,
+                        const PrimInfo16* __restrict__ prim_info, const DevCounts* __restrict__ counts,
+                        DevCamera cam, __half* __restrict__ image, __half* __restrict__ alpha,
+                        uint16_t* __restrict__ n_contrib, uint32_t* __restrict__ tile_max,
+                        uint32_t* __restrict__ bucket_tile, uint4* __restrict__ ckpt) {
+  __shared__ __half2 s_mx[kF16Threads], s_my[kF16Threads];
+  __shared__ __half2 s_cx[kF16Threads], s_cy[kF16Threads], s_cz[kF16Threads], s_op[kF16Threads];
+  __shared__ __half2 s_r[kF16Threads], s_g[kF16Threads], s_b[kF16Threads];
+  __shared__ uint32_t s_max[kF16Threads / 32];
+  const uint32_t tid = threadIdx.x;
+  const uint32_t tx = tid & 7u, ty = tid >> 3;
+  const uint32_t lx = 2 * tx, ly = ty;
+  const uint32_t tile = blockIdx.y * cam.grid_w + blockIdx.x;
+  const uint32_t px = blockIdx.x * kTile + lx, py = blockIdx.y * kTile + ly;
+  const uint32_t in0 = (px < cam.width && py < cam.height) ? 1u : 0u;
+  const uint32_t in1 = (px + 1 < cam.width && py < cam.height) ? 1u : 0u;
+  const uint32_t inside = in0 | (in1 << 16);
+
+  const __half2 inv16 = __float2half2_rn(0.0625f);
+  const __half2 h16 = __float2half2_rn(16.0f);
+  const __half2 half_2 = __float2half2_rn(0.5f);
+  const __half2 zero2 = __float2half2_rn(0.0f);
+  const __half2 one2 = __float2half2_rn(1.0f);
+  const __half2 scale2 = __float2half2_rn(255.0f);
+  const __half2 unscale2 = __float2half2_rn(1.0f / 255.0f);
+  const __half2 max_a2 = __float2half2_rn(kMaxAlphaF16);
+  const __half min_t = __float2half_rd(kMinTransmittance * 255.0f);
+  const __half2 min_t2 = __halves2half2(min_t, min_t);
+  const __half2 log2e = __float2half2_rn(1.4426950409f);
+  const __half2 s16_1 = __halves2half2(__float2half_rn(16.0f), __float2half_rn(1.0f));
+  // pixel offsets in tile units: (x + 0.5) / 16 for both pixels, (y + 0.5) / 16
+  const __half2 off0 = __hfma2(inv16, __halves2half2(__uint2half_rn(lx), __uint2half_rn(ly)),
+                               __float2half2_rn(1.0f / 32.0f));
+  const __half2 off_x = __halves2half2(__low2half(off0), __hadd(__low2half(inv16), __low2half(off0)));
+  const __half2 off_y = __highs2half2(off0, off0);
+  const float2 anchor = make_float2(static_cast<float>(blockIdx.x), static_cast<float>(blockIdx.y));
+
+  const bool ok = counts->overflow == 0u;
+  const uint2 r = ok ? ranges[tile] : make_uint2(0, 0);
+  const uint32_t count = r.y - r.x;
+  const uint32_t first_bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
+  const uint32_t n_buckets = (count + kBucket - 1) / kBucket;
+  for (uint32_t k = tid; k < n_buckets; k += kF16Threads) bucket_tile[first_bucket + k] = tile;
+  // checkpoint record of the pixel pair: 2 x (r,g | b,T) halves
+  uint4* my_ckpt = ckpt + (static_cast<size_t>(first_bucket) * kTilePixels + tiled_index(ly, lx, 2)) / 2;
+
+  __half2 cr = zero2, cg = zero2, cb = zero2, T = scale2;
+  uint32_t n_seen = 0;        // two 16-bit counters
+  uint32_t live = inside;     // 1 per unfinished pixel in each 16-bit half
+  auto store_ckpt = [&](uint32_t bucket) {
+    const uint32_t p0x = h2u(__lows2half2(cr, cg)), p0y = h2u(__lows2half2(cb, T));
+    const uint32_t p1x = h2u(__highs2half2(cr, cg)), p1y = h2u(__highs2half2(cb, T));
+    my_ckpt[static_cast<size_t>(bucket) * (kTilePixels / 2)] = make_uint4(p0x, p0y, p1x, p1y);
+  };
+  for (uint32_t start = 0; start < count; start += kF16Threads) {
+    if (__syncthreads_count(live) == 0) break;
+    const uint32_t k = start + tid;
+    if (k < count) {
+      const uint32_t p = inst_prim[r.x + k];
+      const float2 m = mean2d[p];
+      const float mx = m.x / 16.0f - anchor.x, my = m.y / 16.0f - anchor.y;
+      s_mx[tid] = __float2half2_rn(mx);
+      s_my[tid] = __float2half2_rn(my);
+      const PrimInfo16 rec = prim_info[p];
+      const __half2 cxy = __hmul2(rec.conic_xy, h16);
+      const __half2 czo = __hmul2(rec.conic_z_opacity, s16_1);
+      s_cx[tid] = __lows2half2(cxy, cxy);
+      s_cy[tid] = __highs2half2(cxy, cxy);
+      s_cz[tid] = __lows2half2(czo, czo);
+      s_op[tid] = __highs2half2(czo, czo);
+      s_r[tid] = __float2half2_rn(static_cast<float>(rec.rgb_pad.x));
+      s_g[tid] = __float2half2_rn(static_cast<float>(rec.rgb_pad.y));
+      s_b[tid] = __float2half2_rn(static_cast<float>(rec.rgb_pad.z));
+    }
+    __syncthreads();
+    const uint32_t batch = min(static_cast<uint32_t>(kF16Threads), count - start);
+    uint32_t i = 0;
+    while (live && i < batch) {
+      store_ckpt((start + i) >> 5);
+      const uint32_t j_end = min(i + 32u, batch);
+      for (uint32_t j = i; j < j_end && live; ++j) {
+        const __half2 dx = __hsub2(s_mx[j], off_x);
+        const __half2 dy = __hsub2(s_my[j], off_y);
+        const __half2 qx = __hmul2(dx, __hmul2(s_cx[j], dx));
+        const __half2 qz = __hmul2(dy, __hmul2(s_cz[j], dy));
+        const __half2 qy = __hmul2(dx, __hmul2(s_cy[j], dy));
+        const __half2 power = __hmul2(__hfma2(half_2, __hadd2(qx, qz), qy), h16);
+        const __half2 g = h2exp2_approx(__hmul2(__hneg2(power), log2e));
+        const __half2 a = __hmin2(__hmul2(s_op[j], g), max_a2);
+        const __half2 Tn = __hfma2(__hneg2(a), T, T);
+        // positive halves compare like their bit patterns
+        const uint32_t accept = __vsetgeu2(h2u(Tn), h2u(min_t2));
+        const uint32_t on = live & accept;
+        const uint32_t mask = (on << 16) - on;  // 0xffff per enabled pixel
+        const __half2 w = u2h(h2u(__hmul2(__hmul2(T, a), unscale2)) & mask);
+        cr = __hfma2(s_r[j], w, cr);
+        cg = __hfma2(s_g[j], w, cg);
+        cb = __hfma2(s_b[j], w, cb);
+        T = u2h(h2u(T) ^ (mask & (h2u(Tn) ^ h2u(T))));
+        n_seen = __vaddus2(n_seen, live);
+        live &= accept;
+      }
+      live &= __vsetltu2(n_seen, 0xffffffffu);
+      i += 32u;
+    }
+    for (; i < batch; i += 32u) store_ckpt((start + i) >> 5);
+  }
+  const __half2 out_r = __hmul2(cr, unscale2), out_g = __hmul2(cg, unscale2), out_b = __hmul2(cb, unscale2);
+  const __half2 out_t = __hmul2(T, unscale2);
+  if (inside != 0u) {
+    const uint32_t pi = tiled_index(py, px, cam.tiled_w);
+    *reinterpret_cast<__half2*>(image + pi) = out_r;
+    *reinterpret_cast<__half2*>(image + pi + cam.plane) = out_g;
+    *reinterpret_cast<__half2*>(image + pi + 2 * cam.plane) = out_b;
+    if (alpha != nullptr) *reinterpret_cast<__half2*>(alpha + pi) = __hsub2(one2, out_t);
+    *reinterpret_cast<uint32_t*>(n_contrib + pi) = n_seen;
+  }
+  const uint32_t mine = max(n_seen & 0xffffu, n_seen >> 16);
+  const uint32_t wmax = __reduce_max_sync(0xffffffffu, mine);
+  if ((tid & 31u) == 0) s_max[tid >> 5] = wmax;
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t mx = 0;
+    for (int w = 0; w < kF16Threads / 32; ++w) mx = max(mx, s_max[w]);
+    tile_max[tile] = mx;
+  }
+}
+
+// ---------------------------------------------------------------- backward
+
+constexpr int kBwdWarps = 8;
+
+template <int kFp16>
+__global__ void __launch_bounds__(32 * kBwdWarps)
+    k_blend_backward(const uint2* __restrict__ ranges, const uint32_t* __restrict__ bucket_offsets,
+                     const uint32_t* __restrict__ inst_prim, const float2* __restrict__ mean2d,
+                     const float4* __restrict__ conic_opacity, const float* __restrict__ color,
+                     const PrimInfo16* __restrict__ prim_info, const void* __restrict__ image_v,
+                     const void* __restrict__ grad_v, const uint32_t* __restrict__ tile_max,
+                     const void* __restrict__ n_contrib_v, const uint32_t* __restrict__ bucket_tile,
+                     const void* __restrict__ ckpt_v, const DevCounts* __restrict__ counts, DevCamera cam,
+                     float* __restrict__ helpers) {
+  __shared__ float4 s_a[kBwdWarps][32];  // (Ca.r, Ca.g, Ca.b, T)
+  __shared__ float4 s_b[kBwdWarps][32];  // (G.r, G.g, G.b, last as bits)
+  if (counts->overflow != 0u) return;
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const uint32_t n_buckets = counts->n_buckets;
+  const uint32_t gw = gridDim.x * kBwdWarps;
+  const float max_alpha = kFp16 ? __half2float(__float2half_rn(kMaxAlphaF16)) : kMaxAlphaF32;
+
+  for (uint32_t bucket = blockIdx.x * kBwdWarps + warp; bucket < n_buckets; bucket += gw) {
+    const uint32_t tile = bucket_tile[bucket];
+    const uint2 r = ranges[tile];
+    const uint32_t count = r.y - r.x;
+    const uint32_t tb = bucket - (tile == 0 ? 0u : bucket_offsets[tile - 1]);
+    if (tb * kBucket >= tile_max[tile]) continue;
+    const uint32_t tp = tb * kBucket + lane;
+    const bool valid_prim = tp < count && (!kFp16 || tp <= 0xffffu);
+    const uint32_t gx = tile % cam.grid_w, gy = tile / cam.grid_w;
+
+    uint32_t p = 0;
+    float mx = 0.f, my = 0.f, ca = 0.f, cb = 0.f, cc = 0.f, op = 0.f;
+    float col0 = 0.f, col1 = 0.f, col2 = 0.f, f0 = 0.f, f1 = 0.f, f2 = 0.f;
+    if (valid_prim) {
+      p = inst_prim[r.x + tp];
+      const float2 m = mean2d[p];
+      mx = m.x - 0.5f;
+      my = m.y - 0.5f;
+      if constexpr (kFp16) {
+        const PrimInfo16 rec = prim_info[p];
+        ca = __low2float(rec.conic_xy);
+        cb = __high2float(rec.conic_xy);
+        cc = __low2float(rec.conic_z_opacity);
+        op = __high2float(rec.conic_z_opacity);
+        col0 = static_cast<float>(rec.rgb_pad.x);
+        col1 = static_cast<float>(rec.rgb_pad.y);
+        col2 = static_cast<float>(rec.rgb_pad.z);
+        f0 = f1 = f2 = 1.f;
+      } else {
+        const float4 co = conic_opacity[p];
+        ca = co.x;
+        cb = co.y;
+        cc = co.z;
+        op = co.w;
+        const float u0 = color[3 * p], u1 = color[3 * p + 1], u2 = color[3 * p + 2];
+        col0 = fmaxf(u0, 0.f);
+        col1 = fmaxf(u1, 0.f);
+        col2 = fmaxf(u2, 0.f);
+        f0 = u0 >= 0.f ? 1.f : 0.f;
+        f1 = u1 >= 0.f ? 1.f : 0.f;
+        f2 = u2 >= 0.f ? 1.f : 0.f;
+      }
+    }
+    float g_mx = 0.f, g_my = 0.f, a_mx = 0.f, a_my = 0.f;
+    float g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_op = 0.f, g_c0 = 0.f, g_c1 = 0.f, g_c2 = 0.f;
+    // pixel state travelling along the lanes
+    float T = 0.f, A0 = 0.f, A1 = 0.f, A2 = 0.f, G0 = 0.f, G1 = 0.f, G2 = 0.f;
+    uint32_t last = 0;
+
+    for (uint32_t chunk = 0; chunk <= kTilePixels / 32; ++chunk) {
+      if (chunk < kTilePixels / 32) {
+        // stage the next 32 pixels of the walk
+        const uint32_t i = chunk * 32 + lane;
+        uint32_t dx, dy;
+        walk_pixel(i, dx, dy);
+        const uint32_t px = gx * kTile + dx, py = gy * kTile + dy;
+        float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (px < cam.width && py < cam.height) {
+          const uint32_t pi = tiled_index(py, px, cam.tiled_w);
+          if constexpr (kFp16) {
+            const uint2 c = reinterpret_cast<const uint2*>(ckpt_v)[static_cast<size_t>(bucket) * kTilePixels + i];
+            const float2 rg = __half22float2(u2h(c.x));
+            const float2 bt = __half22float2(u2h(c.y));
+            const __half* img = reinterpret_cast<const __half*>(image_v);
+            const __half* gr = reinterpret_cast<const __half*>(grad_v);
+            a4 = make_float4(__half2float(img[pi]) * 255.0f - rg.x, __half2float(img[pi + cam.plane]) * 255.0f - rg.y,
+                             __half2float(img[pi + 2 * cam.plane]) * 255.0f - bt.x, bt.y * (1.0f / 255.0f));
+            b4 = make_float4(__half2float(gr[pi]), __half2float(gr[pi + cam.plane]),
+                             __half2float(gr[pi + 2 * cam.plane]), __uint_as_float(0xffffffffu));
+          } else {
+            const float4 c = reinterpret_cast<const float4*>(ckpt_v)[static_cast<size_t>(bucket) * kTilePixels + i];
+            const float* img = reinterpret_cast<const float*>(image_v);
+            const float* gr = reinterpret_cast<const float*>(grad_v);
+            a4 = make_float4(img[pi] - c.x, img[pi + cam.plane] - c.y, img[pi + 2 * cam.plane] - c.z, c.w);
+            b4 = make_float4(gr[pi], gr[pi + cam.plane], gr[pi + 2 * cam.plane],
+                             __uint_as_float(reinterpret_cast<const uint32_t*>(n_contrib_v)[pi]));
+          }
+        }
+        s_a[warp][lane] = a4;
+        s_b[warp][lane] = b4;
+      }
+      __syncwarp();
+#pragma unroll 4
+      for (uint32_t s = 0; s < 32; ++s) {
+        T = __shfl_up_sync(0xffffffffu, T, 1);
+        A0 = __shfl_up_sync(0xffffffffu, A0, 1);
+        A1 = __shfl_up_sync(0xffffffffu, A1, 1);
+        A2 = __shfl_up_sync(0xffffffffu, A2, 1);
+        G0 = __shfl_up_sync(0xffffffffu, G0, 1);
+        G1 = __shfl_up_sync(0xffffffffu, G1, 1);
+        G2 = __shfl_up_sync(0xffffffffu, G2, 1);
+        last = __shfl_up_sync(0xffffffffu, last, 1);
+        if (lane == 0) {
+          if (chunk < kTilePixels / 32) {
+            const float4 a4 = s_a[warp][s], b4 = s_b[warp][s];
+            A0 = a4.x; A1 = a4.y; A2 = a4.z; T = a4.w;
+            G0 = b4.x; G1 = b4.y; G2 = b4.z; last = __float_as_uint(b4.w);
+          } else {
+            T = A0 = A1 = A2 = G0 = G1 = G2 = 0.f;
+            last = 0;
+          }
+        }
+        const int idx = static_cast<int>(chunk * 32 + s) - static_cast<int>(lane);
+        const bool valid_pix = idx >= 0 && idx < kTilePixels;
+        uint32_t dx, dy;
+        walk_pixel(static_cast<uint32_t>(idx) & 255u, dx, dy);
+        const float ddx = mx - static_cast<float>(gx * kTile + dx);
+        const float ddy = my - static_cast<float>(gy * kTile + dy);
+        const float dxx = ddx * ddx, dxy = ddx * ddy, dyy = ddy * ddy;
+        const float power = fmaxf(0.5f * (ca * dxx + cc * dyy) + cb * dxy, 0.f);
+        const float gau = __expf(-power);
+        bool use = valid_prim && valid_pix;
+        if constexpr (!kFp16) use = use && tp < last;
+        const float a = use ? fminf(op * gau, max_alpha) : 0.f;
+        const float w = T * a;
+        const float om = 1.0f - a;
+        const float cdg = col0 * G0 + col1 * G1 + col2 * G2;
+        g_c0 += w * (G0 * f0);
+        g_c1 += w * (G1 * f1);
+        g_c2 += w * (G2 * f2);
+        A0 -= w * col0;
+        A1 -= w * col1;
+        A2 -= w * col2;
+        const float adg = A0 * G0 + A1 * G1 + A2 * G2;
+        const float dop = a * (T * cdg - adg / om);
+        g_op += dop;
+        g_ca += dop * dxx;
+        g_cb += dop * dxy;
+        g_cc += dop * dyy;
+        const float gmx = dop * (ca * ddx + cb * ddy);
+        const float gmy = dop * (cb * ddx + cc * ddy);
+        g_mx += gmx;
+        g_my += gmy;
+        a_mx += fabsf(gmx);
+        a_my += fabsf(gmy);
+        T = T * om;
+      }
+      __syncwarp();
+    }
+    if (valid_prim) {
+      // scale conventions: fp32 accumulates in [0,1] colour units; the fp16
+      // path carries colour and C_after scaled by 255 (reference lines
+      // 1359-1369 divide by 255 at the end)
+      const float s = kFp16 ? (1.0f / 255.0f) : 1.0f;
+      float* h = helpers + static_cast<size_t>(p) * kHelperFloats;
+      atomicAdd(h + 0, -g_mx * s);
+      atomicAdd(h + 1, -g_my * s);
+      atomicAdd(h + 2, a_mx * s);
+      atomicAdd(h + 3, a_my * s);
+      atomicAdd(h + 4, -0.5f * g_ca * s);
+      atomicAdd(h + 5, -0.5f * g_cb * s);
+      atomicAdd(h + 6, -0.5f * g_cc * s);
+      atomicAdd(h + 7, g_op * s * (1.0f - op));
+      atomicAdd(h + 8, g_c0);
+      atomicAdd(h + 9, g_c1);
+      atomicAdd(h + 10, g_c2);
+    }
+  }
+}
+
+}  // namespace
+
+void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, void* image, void* alpha,
+                          cudaStream_t stream) {
+  const dim3 grid(cam.grid_w, cam.grid_h);
+  const uint32_t* sorted_prim = s.inst_prim[s.tile_result];
+  if (fp16)
+    k_blend_forward_f16<<<grid, kF16Threads, 0, stream>>>(
+        s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.prim_info, s.counts, cam,
+        reinterpret_cast<__half*>(image), reinterpret_cast<__half*>(alpha), reinterpret_cast<uint16_t*>(s.n_contrib),
+        s.tile_max_contrib, s.bucket_tile, reinterpret_cast<uint4*>(s.ckpt));
+  else
+    k_blend_forward_f32<<<grid, kTilePixels, 0, stream>>>(
+        s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.conic_opacity, s.color, s.counts, cam,
+        reinterpret_cast<float*>(image), reinterpret_cast<float*>(alpha), s.n_contrib, s.tile_max_contrib,
+        s.bucket_tile, s.ckpt);
+}
+
+void launch_blend_backward(const RasterState& s, const DevCamera& cam, int fp16, const void* image,
+                           const void* grad_image, cudaStream_t stream) {
+  const uint32_t* sorted_prim = s.inst_prim[s.tile_result];
+  const int blocks = s.num_sms * 8;
+  if (fp16)
+    k_blend_backward<1><<<blocks, 32 * kBwdWarps, 0, stream>>>(
+        s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.conic_opacity, s.color, s.prim_info, image,
+        grad_image, s.tile_max_contrib, s.n_contrib, s.bucket_tile, s.ckpt, s.counts, cam, s.helpers);
+  else
+    k_blend_backward<0><<<blocks, 32 * kBwdWarps, 0, stream>>>(
+        s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.conic_opacity, s.color, s.prim_info, image,
+        grad_image, s.tile_max_contrib, s.n_contrib, s.bucket_tile, s.ckpt, s.counts, cam, s.helpers);
+}
+
+}  // namespace tgs

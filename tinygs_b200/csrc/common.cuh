@@ -1,0 +1,84 @@
+// common.cuh -- device-side definitions shared by every kernel of the library.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace tgs {
+
+// Rendering constants of the reference rasterizer
+// (tinygs/src/rasterizer/fastgs_ours/rasterization_config.h:18-40 and
+//  tinygs/src/rasterizer/fastgs_ours_fp16/rasterization_config.h:21-45).
+constexpr int kTile = 16;                 // 16x16 pixel render tile
+constexpr int kTilePixels = kTile * kTile; // 256
+constexpr int kBucket = 32;               // primitives per backward bucket
+constexpr float kDilation = 0.3f;
+constexpr float kMinAlpha = 1.0f / 255.0f;
+constexpr float kMaxAlphaF32 = 0.999f;
+constexpr float kMaxAlphaF16 = 0.99f;
+constexpr float kMinTransmittance = 1e-4f;
+constexpr uint32_t kSequentialTiles = 8;
+
+// Device-side camera passed by value as a kernel parameter.
+struct DevCamera {
+  float4 r1, r2, r3;  // rows of w2c
+  float3 pos;         // camera centre in world space
+  float fx, fy, cx, cy;
+  float near_plane, far_plane;
+  float w, h;         // image size as float
+  uint32_t width, height;
+  uint32_t grid_w, grid_h;  // 16x16 render tiles
+  uint32_t tiled_w, tiled_h;  // 8x8 storage tiles
+  uint32_t plane;     // channel stride of the tiled image
+};
+
+// Physical index of pixel (y, x) in the reference's 8x8-tiled image plane
+// (tinygs/include/tinygs/common.hpp:389-408).
+__host__ __device__ __forceinline__ uint32_t tiled_index(uint32_t y, uint32_t x, uint32_t tiled_w) {
+  return (((y >> 3) * tiled_w + (x >> 3)) << 6) + ((y & 7u) << 3) + (x & 7u);
+}
+
+// Pixel (dx, dy) of the i-th entry of the 16x16 tile walked as four 8x8
+// sub-tiles, row-major inside each; the same order is used for the bucket
+// checkpoints so that entry i of a checkpoint is pixel i of the walk.
+__device__ __forceinline__ void walk_pixel(uint32_t i, uint32_t& dx, uint32_t& dy) {
+  const uint32_t sub = i >> 6, in = i & 63u;
+  dx = (in & 7u) + (sub & 1u) * 8u;
+  dy = (in >> 3) + (sub >> 1) * 8u;
+}
+
+__device__ __forceinline__ float sat(float x) { return __saturatef(x); }
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+// Per-Gaussian scratch the blend backward accumulates into and the
+// preprocess backward consumes: 12 floats, 48 B, three float4.
+//   [0..1] dL/dmean2d  [2..3] sum |dL/dmean2d|  [4..6] dL/dconic
+//   [7]    dL/dopacity (already times 1-opacity)  [8..10] dL/dcolor  [11] pad
+constexpr int kHelperFloats = 12;
+
+// Packed fp16-path primitive record (16 B), the reference's PrimitiveInfo
+// layout (fastgs_ours_fp16/rasterization_config.h:54-58).
+struct alignas(16) PrimInfo16 {
+  __half2 conic_xy;
+  __half2 conic_z_opacity;
+  uchar4 rgb_pad;
+  uint32_t pad;
+};
+
+// Error word written by device code when a capacity bound is exceeded.
+constexpr uint32_t kOverflowInstances = 1u;
+constexpr uint32_t kOverflowBuckets = 2u;
+// set if instance emission ever disagreed with the preprocess tile count
+constexpr uint32_t kInconsistentTiles = 4u;
+
+// Device counters of one forward, kept in one 16-byte record.
+struct DevCounts {
+  uint32_t n_visible;
+  uint32_t n_instances;
+  uint32_t n_buckets;
+  uint32_t overflow;
+};
+
+}  // namespace tgs

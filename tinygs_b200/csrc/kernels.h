@@ -1,0 +1,114 @@
+// kernels.h -- host-side launchers of the device kernels (internal interface
+// between the C ABI in abi.cu and the kernel translation units).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace tgs {
+
+struct GaussianPtrs {
+  float* means;
+  float* opacities;
+  float* rotations;
+  float* scales;
+  float* sh0;
+  float* sh_rest;
+  int64_t n;
+  int32_t sh_degree;
+};
+
+// Scratch of one rasterizer handle; every pointer is a device allocation
+// sized at creation.
+struct RasterState {
+  int64_t cap_n = 0;        // Gaussians
+  int64_t cap_inst = 0;     // instances
+  int64_t cap_buckets = 0;  // 32-primitive buckets
+  int32_t max_w = 0, max_h = 0;
+  int64_t max_tiles = 0;
+  int64_t max_pixels = 0;   // padded pixels
+
+  // per Gaussian
+  uint32_t* n_touched = nullptr;
+  uint32_t* depth_key = nullptr;
+  ushort4* bounds = nullptr;
+  float2* mean2d = nullptr;
+  float4* conic_opacity = nullptr;  // fp32 path; aliases prim_info storage
+  PrimInfo16* prim_info = nullptr;  // fp16 path
+  float* color = nullptr;           // [n][3] fp32 path
+  float* helpers = nullptr;         // [n][12] backward scratch
+  uint32_t* vis_key[2] = {nullptr, nullptr};
+  uint32_t* vis_idx[2] = {nullptr, nullptr};
+  uint32_t* block_sums = nullptr;   // block partial sums for scans
+  // per instance
+  uint16_t* inst_key[2] = {nullptr, nullptr};
+  uint32_t* inst_prim[2] = {nullptr, nullptr};
+  // radix sort scratch
+  uint32_t* sort_hist = nullptr;    // [256][sort_max_blocks]
+  uint32_t* sort_digit_total = nullptr;  // [256]
+  int64_t sort_max_blocks = 0;
+  // per tile
+  uint2* ranges = nullptr;
+  uint32_t* bucket_offsets = nullptr;
+  uint32_t* tile_max_contrib = nullptr;
+  // per pixel
+  uint32_t* n_contrib = nullptr;    // uint32 (fp32 path) or uint16 (fp16 path)
+  // per bucket
+  uint32_t* bucket_tile = nullptr;
+  float4* ckpt = nullptr;           // [buckets][256] float4 (fp32) or uint2 (fp16)
+  // counts
+  DevCounts* counts = nullptr;
+  uint32_t* bwd_work = nullptr;     // work counter of the persistent backward
+
+  // state of the last forward
+  int have_forward = 0;
+  int last_dtype = 0;
+  int64_t last_n = 0;
+  uint32_t last_tile_passes = 0;  // parity of the tile sort result
+  int depth_result = 0;           // which vis buffer holds the sorted list
+  int tile_result = 0;            // which inst buffer holds the sorted list
+  int num_sms = 148;
+};
+
+DevCamera make_camera(int width, int height, float fx, float fy, float cx, float cy,
+                      float near_plane, float far_plane, const float w2c[16]);
+
+// forward stages (preprocess.cu, binning.cu, blend.cu)
+void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam,
+                       int fp16, float4* dens, cudaStream_t stream);
+void launch_binning(RasterState& s, int64_t n, const DevCamera& cam, int fp16, cudaStream_t stream);
+void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, void* image,
+                          void* alpha, cudaStream_t stream);
+// backward stages
+void launch_blend_backward(const RasterState& s, const DevCamera& cam, int fp16, const void* image,
+                           const void* grad_image, cudaStream_t stream);
+void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g,
+                                const GaussianPtrs& grads, const DevCamera& cam, int accumulate,
+                                float4* dens, cudaStream_t stream);
+
+// losses (loss.cu)
+void launch_l1(int fp16, int width, int height, const void* pred, const void* target,
+               void* loss_map, void* grad, float scale, cudaStream_t stream);
+void launch_ssim(int fp16, int width, int height, const void* pred, const void* target,
+                 void* loss_map, void* grad, float scale_ssim, float scale_l1, float* partials,
+                 float* loss_sum, cudaStream_t stream);
+
+// optimizer (adam.cu)
+struct AdamSegment {
+  float* theta;
+  const float* grad;
+  float* m;
+  float* v;
+  int64_t count;
+  float lr;
+  int decay_kind;  // 0 none, 1 opacity, 2 scale
+  float decay;
+};
+void launch_adam(const AdamSegment* segs, int n_segs, float beta1, float beta2, float eps,
+                 float gradient_scale, float bc1, float bc2_sqrt, float max_grad_1,
+                 int zero_grads, cudaStream_t stream);
+
+}  // namespace tgs

@@ -1,0 +1,99 @@
+// tiles.cuh -- exact Gaussian/tile overlap tests used both when counting the
+// tiles a Gaussian touches (preprocess) and when emitting its instances
+// (binning).  Both call sites use these same functions, so counts and
+// emitted instances always agree.
+#pragma once
+
+#include "common.cuh"
+
+namespace tgs {
+
+// Maximum of the Gaussian's exponent over the pixel rectangle of tile
+// (tx, ty) compared against ln(255 * opacity): the StopThePop test
+// (Radl et al. 2024), as used by tinygs
+// (fastgs_ours/kernels_forward.cuh:49-84).  `mx, my` is the 2D mean shifted
+// by -0.5 so that pixel centres sit on integer coordinates.  The arithmetic
+// order follows the reference so that decisions coincide with it.
+__device__ __forceinline__ bool tile_overlaps_f32(float mx, float my, float ca, float cb, float cc,
+                                                  uint32_t tx, uint32_t ty, float thr) {
+  const float x0 = static_cast<float>(tx * kTile), y0 = static_cast<float>(ty * kTile);
+  const float x1 = static_cast<float>((tx + 1) * kTile - 1), y1 = static_cast<float>((ty + 1) * kTile - 1);
+  const float dx0 = x0 - mx, dy0 = y0 - my;
+  const float left = static_cast<float>(dx0 > 0.0f);
+  const float above = static_cast<float>(dy0 > 0.0f);
+  const float outx = left + static_cast<float>(mx > x1);
+  const float outy = above + static_cast<float>(my > y1);
+  if (outy + outx == 0.0f) return true;  // mean inside the tile
+  // nearest corner, then slide along the tile edges towards the maximum
+  const float cx = x1 + left * (x0 - x1);
+  const float cy = y1 + above * (y0 - y1);
+  const float ex = mx - cx, ey = my - cy;
+  const float sx = copysignf(static_cast<float>(kTile - 1), dx0);
+  const float sy = copysignf(static_cast<float>(kTile - 1), dy0);
+  const float t0 = outy * __saturatef((sx * ca * ex + sx * cb * ey) / (sx * ca * sx));
+  const float t1 = outx * __saturatef((sy * cb * ex + sy * cc * ey) / (sy * cc * sy));
+  const float px = cx + t0 * sx, py = cy + t1 * sy;
+  const float qx = mx - px, qy = my - py;
+  const float power = 0.5f * (ca * qx * qx + cc * qy * qy) + cb * qx * qy;
+  return power <= thr;
+}
+
+// Half-precision variant of the same test used by the fp16 rasterizer
+// (fastgs_ours_fp16/kernels_forward.cuh:123-169): the tile-relative
+// distances and the edge parameter are evaluated in fp16 on the packed
+// conic, the final exponent in fp32.  Same operation sequence as the
+// reference so that instance lists coincide.
+__device__ __forceinline__ bool tile_overlaps_f16(float mx, float my, __half2 conic_xy, __half2 conic_zw,
+                                                  uint32_t tx, uint32_t ty, float thr) {
+  const __half2 one = __float2half2_rn(1.0f);
+  const __half2 zero = __float2half2_rn(0.0f);
+  const __half span_h = __float2half_rd(static_cast<float>(kTile - 1) / static_cast<float>(kTile));
+  const __half2 span = __halves2half2(span_h, span_h);
+  const __half2 lo = __halves2half2(__float2half_rd(static_cast<float>(tx) - mx * (1.0f / kTile)),
+                                    __float2half_rd(static_cast<float>(ty) - my * (1.0f / kTile)));
+  const __half2 hi = __hadd2(lo, span);
+  const __half2 before = __hgtu2(lo, zero);  // 1.0 where the mean lies before the tile
+  const __half2 after = __hltu2(hi, zero);   // 1.0 where it lies after it
+  const __half2 outside = __hadd2(before, after);
+  if (__hbeq2(outside, zero)) return true;
+  (void)one;
+  // step sign from the sign of lo
+  const uint32_t lo_bits = *reinterpret_cast<const uint32_t*>(&lo);
+  const uint32_t span_bits = *reinterpret_cast<const uint32_t*>(&span);
+  const uint32_t step_bits = (span_bits & 0x7fff7fffu) | (lo_bits & 0x80008000u);
+  const __half2 step = *reinterpret_cast<const __half2*>(&step_bits);
+  // distance from the nearest edge: -(lerp(hi, lo, before))
+  const __half2 nb = __hneg2(before);
+  const __half2 dist = __hneg2(__hfma2(before, lo, __hfma2(nb, hi, hi)));
+  const __half2 dist_xx = __lows2half2(dist, dist);
+  const __half2 dist_yy = __highs2half2(dist, dist);
+  const __half2 c_xy = conic_xy;
+  const __half2 c_yz = __halves2half2(__high2half(conic_xy), __low2half(conic_zw));
+  const __half2 c_xz = __halves2half2(__low2half(conic_xy), __low2half(conic_zw));
+  const __half2 num = __hadd2(__hmul2(__hmul2(step, c_xy), dist_xx), __hmul2(__hmul2(step, c_yz), dist_yy));
+  const __half2 den = __hmul2(__hmul2(step, step), c_xz);
+  const __half2 t = __hmul2_sat(__h2div(num, den), __lowhigh2highlow(outside));
+  const float2 q = __half22float2(__hsub2(dist, __hmul2(t, step)));
+  const float qx = q.x * static_cast<float>(kTile), qy = q.y * static_cast<float>(kTile);
+  const float fa = __low2float(conic_xy), fb = __high2float(conic_xy), fc = __low2float(conic_zw);
+  const float power = 0.5f * (fa * qx * qx + fc * qy * qy) + fb * qx * qy;
+  return power <= thr;
+}
+
+// Per-primitive tile-test inputs in one register bundle.
+struct TileTest {
+  float mx, my;   // mean2d - 0.5
+  float ca, cb, cc;
+  __half2 h_xy, h_zw;
+  float thr;
+};
+
+template <int kFp16>
+__device__ __forceinline__ bool overlaps(const TileTest& p, uint32_t tx, uint32_t ty) {
+  if constexpr (kFp16)
+    return tile_overlaps_f16(p.mx, p.my, p.h_xy, p.h_zw, tx, ty, p.thr);
+  else
+    return tile_overlaps_f32(p.mx, p.my, p.ca, p.cb, p.cc, tx, ty, p.thr);
+}
+
+}  // namespace tgs

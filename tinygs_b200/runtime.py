@@ -1,0 +1,305 @@
+"""Python mirror of the reference's plugin interfaces over the C ABI.
+
+PyTorch is used only for device memory and streams; every computation goes
+through ``libtgs_b200.so``.  Names and argument meaning follow the reference:
+
+  GaussianSet            GPUGaussian3d (tinygs/include/tinygs/core/gpu_gaussian.hpp)
+  RasterizeContext       tinygs/include/tinygs/rasterizer/rasterizer.hpp:9-29
+  FastGSB200Rasterizer   RasterizerBase::forward/backward (rasterizer.hpp:38-58)
+  L1Loss, FusedSSIMLoss  LossBase::evaluate(ctx, scale) (loss/loss.hpp:15-28)
+  SimpleAdam             OptimizerBase::step(scale, stream) (optim/optim.hpp:39-92)
+
+Errors surface as exceptions (the reference throws std::runtime_error);
+the C ABI underneath returns status codes.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _abi
+from ._abi import TgsAdamConfig, TgsCamera, TgsGaussians, TgsRasterCaps, TgsRasterCounts, check, load_library
+
+SEGMENTS = ("means", "opacities", "rotations", "scales", "sh0", "sh_rest")
+WIDTHS = {"means": 3, "opacities": 1, "rotations": 4, "scales": 3, "sh0": 3, "sh_rest": 45}
+FLOATS_PER_GAUSSIAN = sum(WIDTHS.values())  # 59
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+class GaussianSet:
+    """One SoA set of Gaussian arrays (parameters, gradients or a moment) in a
+    single device allocation: 59 floats per Gaussian, segments padded to a
+    multiple of four Gaussians so every segment starts 16-byte aligned."""
+
+    def __init__(self, n: int, sh_degree: int, device="cuda", storage: torch.Tensor | None = None):
+        self.n = int(n)
+        self.sh_degree = int(sh_degree)
+        npad = (self.n + 3) // 4 * 4
+        self.npad = npad
+        total = FLOATS_PER_GAUSSIAN * npad
+        self.storage = storage if storage is not None else torch.zeros(total, dtype=torch.float32, device=device)
+        off = 0
+        self.views: dict[str, torch.Tensor] = {}
+        for name in SEGMENTS:
+            w = WIDTHS[name]
+            self.views[name] = self.storage[off:off + w * npad].view(npad, w)[: self.n]
+            off += w * npad
+
+    def __getattr__(self, name):
+        views = self.__dict__.get("views")
+        if views is not None and name in views:
+            return views[name]
+        raise AttributeError(name)
+
+    @classmethod
+    def from_numpy(cls, arrays: dict[str, np.ndarray], sh_degree: int, device="cuda") -> "GaussianSet":
+        n = arrays["means"].shape[0]
+        g = cls(n, sh_degree, device)
+        g.copy_from_numpy(arrays)
+        return g
+
+    def copy_from_numpy(self, arrays: dict[str, np.ndarray]) -> None:
+        for name in SEGMENTS:
+            a = np.asarray(arrays[name], dtype=np.float32).reshape(self.n, WIDTHS[name])
+            self.views[name].copy_(torch.from_numpy(a))
+
+    def to_numpy(self) -> dict[str, np.ndarray]:
+        out = {}
+        for name in SEGMENTS:
+            v = self.views[name].detach().cpu().numpy()
+            out[name] = v.reshape(self.n, 15, 3) if name == "sh_rest" else (v[:, 0] if name == "opacities" else v)
+        return out
+
+    def zeros_like(self) -> "GaussianSet":
+        return GaussianSet(self.n, self.sh_degree, self.storage.device)
+
+    def abi(self) -> TgsGaussians:
+        s = TgsGaussians()
+        for name in SEGMENTS:
+            setattr(s, name, self.views[name].data_ptr() if self.n > 0 else None)
+        s.n = self.n
+        s.sh_degree = self.sh_degree
+        return s
+
+
+def make_camera(cam: dict) -> TgsCamera:
+    c = TgsCamera()
+    c.width, c.height = int(cam["width"]), int(cam["height"])
+    c.fx, c.fy, c.cx, c.cy = float(cam["fx"]), float(cam["fy"]), float(cam["cx"]), float(cam["cy"])
+    c.near_plane, c.far_plane = float(cam.get("near", 0.01)), float(cam.get("far", 100.0))
+    w = np.asarray(cam["w2c"], dtype=np.float32).reshape(16)
+    for k in range(16):
+        c.w2c[k] = float(w[k])
+    return c
+
+
+def image_numel(width: int, height: int, channels: int = 3) -> int:
+    return channels * ((width + 7) // 8 * 8) * ((height + 7) // 8 * 8)
+
+
+@dataclass
+class RasterizeContext:
+    """Mirror of tinygs::RasterizeContext (rasterizer.hpp:9-29)."""
+    stream: object = None
+    grad_scaler: float = 1.0
+    fwd_input: dict | None = None          # camera: width, height, fx, fy, cx, cy, near, far, w2c
+    fwd_output_image: torch.Tensor | None = None
+    grad_output_image: torch.Tensor | None = None
+    gaussians_grad: GaussianSet | None = None
+    densification_info: torch.Tensor | None = None  # [n][4] float32
+    alpha: torch.Tensor | None = None
+    accumulate: bool = True
+
+
+class FastGSB200Rasterizer:
+    """RasterizerBase implementation backed by the sm_100a kernels."""
+
+    def __init__(self, max_gaussians: int, max_width: int, max_height: int, max_instances: int = 0,
+                 data_type: str = "float32"):
+        self.lib = load_library()
+        caps = TgsRasterCaps(int(max_gaussians), int(max_width), int(max_height), int(max_instances))
+        h = ctypes.c_void_p()
+        check(self.lib.tgs_raster_create(ctypes.byref(caps), ctypes.byref(h)), "tgs_raster_create")
+        self.handle = h
+        self.caps = caps
+        self.gaussians: GaussianSet | None = None
+        self.data_type = data_type
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.tgs_raster_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_gaussians(self, g: GaussianSet) -> None:
+        self.gaussians = g
+
+    def _dtype(self, img: torch.Tensor) -> int:
+        if img.dtype == torch.float32:
+            return _abi.TGS_FLOAT32
+        if img.dtype == torch.float16:
+            return _abi.TGS_FLOAT16
+        raise RuntimeError(f"unsupported image dtype {img.dtype}")
+
+    def forward(self, ctx: RasterizeContext) -> None:
+        if self.gaussians is None:
+            raise RuntimeError("Gaussians not set")
+        g = self.gaussians.abi()
+        cam = make_camera(ctx.fwd_input)
+        check(self.lib.tgs_raster_forward(self.handle, ctypes.byref(g), ctypes.byref(cam),
+                                          self._dtype(ctx.fwd_output_image), _ptr(ctx.fwd_output_image),
+                                          _ptr(ctx.alpha), _ptr(ctx.densification_info),
+                                          _stream_handle(ctx.stream)), "tgs_raster_forward")
+
+    def backward(self, ctx: RasterizeContext) -> None:
+        if self.gaussians is None or ctx.gaussians_grad is None:
+            raise RuntimeError("Gaussians or gradient gaussians not set")
+        g = self.gaussians.abi()
+        gg = ctx.gaussians_grad.abi()
+        cam = make_camera(ctx.fwd_input)
+        check(self.lib.tgs_raster_backward(self.handle, ctypes.byref(g), ctypes.byref(cam),
+                                           self._dtype(ctx.fwd_output_image), _ptr(ctx.fwd_output_image),
+                                           _ptr(ctx.grad_output_image), ctypes.byref(gg),
+                                           1 if ctx.accumulate else 0, _ptr(ctx.densification_info),
+                                           _stream_handle(ctx.stream)), "tgs_raster_backward")
+
+    def counts(self, stream=None) -> TgsRasterCounts:
+        c = TgsRasterCounts()
+        check(self.lib.tgs_raster_counts(self.handle, ctypes.byref(c), _stream_handle(stream)), "tgs_raster_counts")
+        return c
+
+    def debug_buffer(self, which: int) -> tuple[int, int]:
+        p = ctypes.c_void_p()
+        n = ctypes.c_size_t()
+        check(self.lib.tgs_raster_debug_buffer(self.handle, which, ctypes.byref(p), ctypes.byref(n)),
+              "tgs_raster_debug_buffer")
+        return p.value, n.value
+
+    def debug_array(self, which: int, dtype: torch.dtype, count: int) -> torch.Tensor:
+        """Copy the first `count` elements of an internal buffer (tests only)."""
+        ptr, nbytes = self.debug_buffer(which)
+        elem = torch.tensor([], dtype=dtype).element_size()
+        if count * elem > nbytes:
+            raise ValueError("debug buffer smaller than requested")
+        if count == 0:
+            return torch.empty(0, dtype=dtype, device="cuda")
+        typestr = {torch.float32: "<f4", torch.float16: "<f2", torch.int32: "<i4", torch.int16: "<i2",
+                   torch.uint8: "|u1"}[dtype]
+        view = _DeviceView(ptr, count, typestr)
+        return torch.as_tensor(view, device="cuda").clone()
+
+
+class _DeviceView:
+    """Minimal __cuda_array_interface__ exporter for a raw device pointer."""
+
+    def __init__(self, ptr: int, count: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class FusedLoss:
+    """The reference's default loss mix (configs/default.json:30-39):
+    0.8 * L1 + 0.2 * (1 - SSIM), each term scaled by grad_scaler, evaluated
+    in one call that accumulates into `loss` and `grad` like
+    LossBase::evaluate and also reduces the step's loss to a device scalar."""
+
+    def __init__(self, max_width: int, max_height: int, w_l1: float = 0.8, w_ssim: float = 0.2):
+        self.lib = load_library()
+        h = ctypes.c_void_p()
+        check(self.lib.tgs_loss_create(int(max_width), int(max_height), ctypes.byref(h)), "tgs_loss_create")
+        self.handle = h
+        self.w_l1, self.w_ssim = w_l1, w_ssim
+
+    def close(self):
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.tgs_loss_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def _dtype(t: torch.Tensor) -> int:
+        return _abi.TGS_FLOAT16 if t.dtype == torch.float16 else _abi.TGS_FLOAT32
+
+    def evaluate(self, pred, target, loss_map, grad, width, height, grad_scaler=1.0, loss_sum=None, stream=None):
+        check(self.lib.tgs_loss_l1_ssim(self.handle, self._dtype(pred), int(width), int(height), _ptr(pred),
+                                        _ptr(target), _ptr(loss_map), _ptr(grad),
+                                        float(self.w_l1 * grad_scaler), float(self.w_ssim * grad_scaler),
+                                        _ptr(loss_sum), _stream_handle(stream)), "tgs_loss_l1_ssim")
+
+    def evaluate_l1(self, pred, target, loss_map, grad, width, height, scale, stream=None):
+        check(self.lib.tgs_loss_l1(self._dtype(pred), int(width), int(height), _ptr(pred), _ptr(target),
+                                   _ptr(loss_map), _ptr(grad), float(scale), _stream_handle(stream)), "tgs_loss_l1")
+
+    def evaluate_ssim(self, pred, target, loss_map, grad, width, height, scale, stream=None):
+        check(self.lib.tgs_loss_fused_ssim(self.handle, self._dtype(pred), int(width), int(height), _ptr(pred),
+                                           _ptr(target), _ptr(loss_map), _ptr(grad), float(scale),
+                                           _stream_handle(stream)), "tgs_loss_fused_ssim")
+
+
+@dataclass
+class AdamParams:
+    """GaussianOptimizationParams + SimpleAdamParameters (optim.hpp:8-37,
+    simple_adam.hpp:8-27) with the reference defaults."""
+    beta1: float = 0.9
+    beta2: float = 0.999
+    epsilon: float = 1e-8
+    max_grad_1: float = 1.0
+    means_lr: float = 1.6e-4
+    shs_lr: float = 2.5e-3
+    opacities_lr: float = 5.0e-2
+    scales_lr: float = 5.0e-3
+    rotations_lr: float = 1.0e-3
+    opacities_l1: float = 0.0
+    scales_l1: float = 0.0
+    scene_scale: float = 1.0
+    global_lr: float = 1.0
+    decay_reduction_mean: bool = True
+
+    def abi(self) -> TgsAdamConfig:
+        return TgsAdamConfig(self.beta1, self.beta2, self.epsilon, self.max_grad_1, self.means_lr, self.shs_lr,
+                             self.opacities_lr, self.scales_lr, self.rotations_lr, self.opacities_l1,
+                             self.scales_l1, self.scene_scale, self.global_lr, 1 if self.decay_reduction_mean else 0)
+
+
+class SimpleAdam:
+    """OptimizerBase::step over a GaussianSet; owns the two moment sets."""
+
+    def __init__(self, params: GaussianSet, grads: GaussianSet, cfg: AdamParams | None = None):
+        self.lib = load_library()
+        self.params, self.grads = params, grads
+        self.cfg = cfg or AdamParams()
+        self.exp_avg = params.zeros_like()
+        self.exp_avg_sq = params.zeros_like()
+        self.global_steps = 0
+
+    def step(self, scale: float, stream=None, zero_grads: bool = False) -> None:
+        self.global_steps += 1
+        p, g, m, v = self.params.abi(), self.grads.abi(), self.exp_avg.abi(), self.exp_avg_sq.abi()
+        cfg = self.cfg.abi()
+        check(self.lib.tgs_adam_step(ctypes.byref(p), ctypes.byref(g), ctypes.byref(m), ctypes.byref(v),
+                                     ctypes.byref(cfg), self.global_steps, float(scale), 1 if zero_grads else 0,
+                                     _stream_handle(stream)), "tgs_adam_step")

@@ -76,7 +76,7 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.fh,
+                                          "-lms", "50", "-i", str(self.gpu)], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -343,18 +343,19 @@ def run_ours(args):
             ms = float(t.item())
         return ms
 
+    # clocks are sampled from the start of the warm-up to the end of both
+    # timed regions (a 50 ms sampling period would miss a short timed region)
+    sampler = ClockSampler(local)
+    sampler.start()
     for k in range(args.warmup):
         step(k)
     torch.cuda.synchronize()
     counts = rast.counts()
     if counts.overflow:
         raise SystemExit("capacity overflow during warm-up")
-
-    sampler = ClockSampler(local)
-    sampler.start()
     ms_dev = timed(args.steps, False, args.warmup)
-    clocks = sampler.stop()
     ms_e2e = timed(args.steps, True, args.warmup + args.steps)
+    clocks = sampler.stop()
     torch.cuda.synchronize()
     if not np.isfinite(float(loss_host[0])):
         raise SystemExit("non-finite loss")

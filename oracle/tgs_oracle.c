@@ -26,6 +26,12 @@
 static int g_tile_stride = 1;
 void orc_set_tile_stride(int32_t stride) { g_tile_stride = stride > 0 ? stride : 1; }
 
+/* Finite-difference checks only: a smooth variant of the fp32 forward (every
+ * tile of the grid is touched, no alpha < 1/255 cut, no early termination),
+ * of which the restated backward is the exact derivative. */
+static int g_smooth = 0;
+void orc_set_smooth_forward(int32_t on) { g_smooth = on != 0; }
+
 /* ---------------------------------------------------------------- helpers */
 
 static inline float satf(float x) { return x > 0.f ? (x < 1.f ? x : 1.f) : 0.f; }
@@ -431,6 +437,7 @@ void orc_preprocess(int64_t n, const float* means, const float* opacities,
         if (fabsf(bx0 - roundf(bx0)) < 1e-4f || fabsf(bx1 - roundf(bx1)) < 1e-4f ||
             fabsf(by0 - roundf(by0)) < 1e-4f || fabsf(by1 - roundf(by1)) < 1e-4f)
             fragile = 1;
+        if (g_smooth) { b0 = 0; b1 = gw; b2 = 0; b3 = gh; }
         uint32_t tile_count = (b1 - b0) * (b3 - b2);
         if (tile_count == 0) active = 0;
         if (!active) continue;
@@ -442,7 +449,7 @@ void orc_preprocess(int64_t n, const float* means, const float* opacities,
             float margin;
             int c = fp16 ? tile_test_f16(smx, smy, hcx, hcy, hcz, tx_, ty_, thr, &margin)
                          : tile_test_f32(smx, smy, conic, tx_, ty_, thr, &margin);
-            if (c) touched++;
+            if (c || g_smooth) touched++;
             float tol = fp16 ? 2e-2f * fmaxf(fabsf(thr), 1.f) : FRAGILE_REL * fmaxf(fabsf(thr), 1.f);
             if (isfinite(margin) && fabsf(margin) <= tol) fragile = 1;
         }
@@ -569,7 +576,7 @@ int64_t orc_binning(int64_t n, const OrcPrimitives* prim, const OrcCamera* cam,
             float margin;
             int c = fp16 ? tile_test_f16(smx, smy, hc[0], hc[1], hc[2], tx, ty, thr, &margin)
                          : tile_test_f32(smx, smy, conic, tx, ty, thr, &margin);
-            if (c && emitted < prim->n_touched[i]) {
+            if ((c || g_smooth) && emitted < prim->n_touched[i]) {
                 tmp_tile[o + emitted] = ty * gw + tx;
                 tmp_prim[o + emitted] = i;
                 ++emitted;
@@ -672,9 +679,9 @@ void orc_blend_forward_f32(const OrcCamera* cam, const uint32_t* ranges,
                     if (s < 0.f) continue;
                     float g = expf(-s);
                     float a = fminf(co[3] * g, 0.999f);
-                    if (a < 1.0f / 255.0f) continue;
+                    if (a < 1.0f / 255.0f && !g_smooth) continue;
                     float Tn = T * (1.0f - a);
-                    if (Tn < 1e-4f) {
+                    if (Tn < 1e-4f && !g_smooth) {
                         done = 1;
                         continue;
                     }

@@ -157,6 +157,9 @@ void orc_adam(int64_t count, float* theta, const float* grad, float* m,
 /* Timing samples only: blend stages process every `stride`-th tile. */
 void orc_set_tile_stride(int32_t stride);
 
+/* Finite-difference checks only: smooth fp32 forward (see tgs_oracle.c). */
+void orc_set_smooth_forward(int32_t on);
+
 /* IEEE binary16 helpers used by the fp16 emulation. */
 uint16_t orc_f2h(float f);
 float orc_h2f(uint16_t h);

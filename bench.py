@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="cfg2")
+    ap.add_argument("--n", type=int, default=0, help="override the Gaussian count (profiling small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0, help="seconds of CPU work for the baseline sample")
     return ap.parse_args()
@@ -114,7 +115,16 @@ class ClockSampler:
 
 # ------------------------------------------------------------ CPU oracle
 
-def cpu_oracle_step_time(cfg_name: str, budget_s: float, fp32_math: bool = True) -> dict:
+def scene_config(name: str, n: int = 0):
+    import dataclasses
+
+    from tinygs_b200 import scenes
+
+    cfg = scenes.CONFIGS[name]
+    return dataclasses.replace(cfg, n=n) if n else cfg
+
+
+def cpu_oracle_step_time(cfg_name: str, budget_s: float, fp32_math: bool = True, n: int = 0) -> dict:
     """Time one oracle training step of the workload on the host cores.
     Per-Gaussian and per-pixel stages run in full; the two blend stages run on
     every k-th tile (k chosen from a probe so the sample fits the budget) and
@@ -124,7 +134,7 @@ def cpu_oracle_step_time(cfg_name: str, budget_s: float, fp32_math: bool = True)
     from oracle import pyoracle as O
     from tinygs_b200 import scenes
 
-    cfg = scenes.CONFIGS[cfg_name]
+    cfg = scene_config(cfg_name, n)
     params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
     cam = scenes.cameras(cfg)[0]
     W, H = cfg.width, cfg.height
@@ -190,12 +200,12 @@ def run_reference(args):
         return
     from tinygs_b200 import scenes
 
-    cfg = scenes.CONFIGS[args.config]
+    cfg = scene_config(args.config, args.n)
     steps_run, times = 0, []
     budget = 150.0
     start = time.perf_counter()
     for k in range(max(1, args.steps)):
-        r = cpu_oracle_step_time(args.config, args.cpu_budget)
+        r = cpu_oracle_step_time(args.config, args.cpu_budget, n=args.n)
         times.append(r["seconds_per_step"])
         steps_run += 1
         if time.perf_counter() - start > budget:
@@ -243,7 +253,7 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    cfg = scenes.CONFIGS[args.config]
+    cfg = scene_config(args.config, args.n)
     W, H = cfg.width, cfg.height
     fp16 = cfg.dtype == "float16"
     dt = torch.float16 if fp16 else torch.float32
@@ -398,7 +408,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_oracle_step_time(args.config, args.cpu_budget)
+        r = cpu_oracle_step_time(args.config, args.cpu_budget, n=args.n)
         cpu = {"value": 1.0 / r["seconds_per_step"], "unit": "iters/s", "cores": r["threads"], "kind": "port",
                "sample": (f"one oracle step of {args.config} ({cfg.n} Gaussians, {W}x{H}, fp32 arithmetic); "
                           f"blend stages on every {r['tile_stride']}th tile, scaled by the stride"),

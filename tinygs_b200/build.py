@@ -23,6 +23,9 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 BUILD = HERE / "_build"
 LIB = HERE / "libtgs_b200.so"
+HOST_DIR = HERE / "host"
+DRIVER = HERE / "tgs_train_step"
+CUDA_HOME = Path("/usr/local/cuda")
 
 SOURCES = ["abi.cu", "preprocess.cu", "binning.cu", "blend.cu", "loss.cu", "adam.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -81,6 +84,25 @@ def build(verbose: bool = False, force: bool = False, extra_flags: list[str] | N
     return LIB
 
 
+def build_host(verbose: bool = False, force: bool = False) -> Path:
+    """Compile the C++20 driver of the plugin adapters (host code only, g++),
+    linked against libtgs_b200.so (found next to it at run time)."""
+    src = HOST_DIR / "train_step_main.cpp"
+    deps = [src, HOST_DIR / "tgs_plugins.hpp", INCLUDE / "tgs_abi.h", LIB]
+    if not force and not _stale(DRIVER, deps):
+        return DRIVER
+    cmd = ["g++", "-std=c++20", "-O2", "-Wall", "-Wextra", "-I", str(INCLUDE), "-I", str(CUDA_HOME / "include"),
+           str(src), "-o", str(DRIVER), "-L", str(HERE), "-ltgs_b200", "-L", str(CUDA_HOME / "lib64"),
+           "-lcudart_static", "-ldl", "-lrt", "-lpthread", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("host driver build failed:\n" + r.stdout + r.stderr)
+    return DRIVER
+
+
 if __name__ == "__main__":
     build(verbose=True, force="--force" in sys.argv)
+    build_host(verbose=True, force="--force" in sys.argv)
     print(LIB)

@@ -1,0 +1,403 @@
+// tgs_plugins.hpp -- C++20 implementations of tinygs's plugin interfaces on
+// top of the C ABI (include/tgs_abi.h).
+//
+// The classes mirror the reference's interfaces so that the B200 kernels
+// drop in behind its training loop:
+//   RasterizerBase / FastGSB200Rasterizer   tinygs/include/tinygs/rasterizer/rasterizer.hpp:9-63
+//   LossBase / L1Loss / FusedSSIMLoss        tinygs/include/tinygs/loss/loss.hpp:6-28
+//   OptimizerBase / SimpleAdam               tinygs/include/tinygs/optim/optim.hpp:8-92,
+//                                            tinygs/include/tinygs/optim/simple_adam.hpp:8-89
+//   GPUGaussian3d                            tinygs/include/tinygs/core/gpu_gaussian.hpp:9-73
+//   train_step()                             tinygs/src/orchestrator.cu:335-439
+// Camera matrices are taken in the reference's glm convention (column-major
+// K and w2c, fx = K[0][0], fy = K[1][1], cx = K[2][0], cy = K[2][1]).
+// Errors are reported as std::runtime_error, as the reference does; the C
+// ABI underneath returns status codes.  Everything runs on the caller's
+// stream; the only host synchronisation is the optional capacity check of
+// the rasterizer (one per forward, cheaper than the reference's four).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/tgs_abi.h"
+
+namespace tgs_b200 {
+
+inline void check(int status, const char* where) {
+  if (status != TGS_OK) throw std::runtime_error(std::string(where) + ": " + tgs_status_string(status));
+}
+
+inline void check_cuda(cudaError_t e, const char* where) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+enum class DataType { Float32 = TGS_FLOAT32, Float16 = TGS_FLOAT16 };
+
+// tinygs::ImageShape / tinygs::Image (tinygs/include/tinygs/core/image.hpp:35-85)
+struct ImageShape {
+  uint32_t width = 0, height = 0, channel = 3;
+  uint32_t size() const { return width * height * channel; }
+  uint32_t padded_width() const { return (width + 7u) / 8u * 8u; }
+  uint32_t padded_height() const { return (height + 7u) / 8u * 8u; }
+  uint32_t padded_size() const { return padded_width() * padded_height() * channel; }
+};
+
+struct Image {
+  ImageShape shape;
+  DataType data_type = DataType::Float32;
+  void* data = nullptr;
+  size_t bytes() const { return size_t(shape.padded_size()) * (data_type == DataType::Float16 ? 2u : 4u); }
+};
+
+// SoA parameter arrays in one device allocation: 59 floats per Gaussian,
+// every segment padded to a multiple of four Gaussians (16-byte aligned).
+class GPUGaussian3d {
+ public:
+  static constexpr int kWidths[6] = {3, 1, 4, 3, 3, 45};
+
+  GPUGaussian3d(int64_t n, int sh_degree) : m_n(n), m_sh_degree(sh_degree) {
+    m_npad = (n + 3) / 4 * 4;
+    check_cuda(cudaMalloc(&m_arena, sizeof(float) * 59 * static_cast<size_t>(m_npad > 0 ? m_npad : 1)),
+               "GPUGaussian3d: cudaMalloc");
+    check_cuda(cudaMemset(m_arena, 0, sizeof(float) * 59 * static_cast<size_t>(m_npad > 0 ? m_npad : 1)),
+               "GPUGaussian3d: cudaMemset");
+  }
+  ~GPUGaussian3d() { cudaFree(m_arena); }
+  GPUGaussian3d(const GPUGaussian3d&) = delete;
+  GPUGaussian3d& operator=(const GPUGaussian3d&) = delete;
+
+  int64_t size() const { return m_n; }
+  int get_sh_degree() const { return m_sh_degree; }
+  void set_sh_degree(int d) { m_sh_degree = d; }
+  float* segment(int k) const {
+    size_t off = 0;
+    for (int i = 0; i < k; ++i) off += size_t(kWidths[i]) * static_cast<size_t>(m_npad);
+    return m_arena + off;
+  }
+  float* means() const { return segment(0); }
+  float* opacities() const { return segment(1); }
+  float* rotations() const { return segment(2); }
+  float* scales() const { return segment(3); }
+  float* sh_coefficient_0() const { return segment(4); }
+  float* sh_coefficients_rest() const { return segment(5); }
+  float* arena() const { return m_arena; }
+  size_t arena_floats() const { return 59 * static_cast<size_t>(m_npad); }
+
+  TgsGaussians abi() const {
+    TgsGaussians g{};
+    g.means = means();
+    g.opacities = opacities();
+    g.rotations = rotations();
+    g.scales = scales();
+    g.sh0 = sh_coefficient_0();
+    g.sh_rest = sh_coefficients_rest();
+    g.n = m_n;
+    g.sh_degree = m_sh_degree;
+    return g;
+  }
+
+  // host data per segment in the reference layout (means [n][3], ...)
+  void copy_from_host(int k, const float* src, cudaStream_t s = nullptr) {
+    check_cuda(cudaMemcpyAsync(segment(k), src, sizeof(float) * kWidths[k] * static_cast<size_t>(m_n),
+                               cudaMemcpyHostToDevice, s),
+               "GPUGaussian3d::copy_from_host");
+  }
+  void copy_to_host(int k, float* dst, cudaStream_t s = nullptr) const {
+    check_cuda(cudaMemcpyAsync(dst, segment(k), sizeof(float) * kWidths[k] * static_cast<size_t>(m_n),
+                               cudaMemcpyDeviceToHost, s),
+               "GPUGaussian3d::copy_to_host");
+  }
+  void memset(int value, cudaStream_t s = nullptr) {
+    check_cuda(cudaMemsetAsync(m_arena, value, sizeof(float) * arena_floats(), s), "GPUGaussian3d::memset");
+  }
+
+ private:
+  int64_t m_n = 0, m_npad = 0;
+  int m_sh_degree = 0;
+  float* m_arena = nullptr;
+};
+
+// tinygs::GPUBatchInput (tinygs/include/tinygs/dataloader/dataloader.hpp:8-14)
+struct GPUBatchInput {
+  uint32_t width = 0, height = 0;
+  float near_plane = 0.01f, far_plane = 100.0f;
+  float K[9] = {};    // glm::mat3, column-major
+  float w2c[16] = {}; // glm::mat4, column-major
+};
+
+inline TgsCamera to_camera(const GPUBatchInput& in) {
+  TgsCamera c{};
+  c.width = static_cast<int32_t>(in.width);
+  c.height = static_cast<int32_t>(in.height);
+  c.fx = in.K[0];
+  c.fy = in.K[4];
+  c.cx = in.K[6];
+  c.cy = in.K[7];
+  c.near_plane = in.near_plane;
+  c.far_plane = in.far_plane;
+  for (int r = 0; r < 4; ++r)
+    for (int col = 0; col < 4; ++col) c.w2c[4 * r + col] = in.w2c[4 * col + r];
+  return c;
+}
+
+// tinygs::RasterizeContext (rasterizer.hpp:9-29)
+struct RasterizeContext {
+  cudaStream_t stream = nullptr;
+  float grad_scaler = 1.0f;
+  GPUBatchInput fwd_input;
+  Image fwd_output_image;
+  Image grad_output_image;
+  std::shared_ptr<GPUGaussian3d> gaussians_grad;
+  TgsDensificationInfo* densification_info = nullptr;  // [n], optional
+};
+
+class RasterizerBase {
+ public:
+  virtual ~RasterizerBase() = default;
+  virtual void forward(const RasterizeContext& ctx) = 0;
+  virtual void backward(RasterizeContext& ctx) = 0;
+  virtual void set_gaussians(std::shared_ptr<GPUGaussian3d> g) { m_gaussians = std::move(g); }
+
+ protected:
+  std::shared_ptr<GPUGaussian3d> m_gaussians;
+};
+
+// Rasterizer backed by the sm_100a kernels.  The handle and its scratch are
+// created on the first forward from the model size and image size and
+// re-created (larger) only when a capacity bound is hit.
+class FastGSB200Rasterizer final : public RasterizerBase {
+ public:
+  // check_capacity: read the device counts after each forward (one host
+  // sync) and re-render with larger scratch on overflow.
+  explicit FastGSB200Rasterizer(bool check_capacity = true) : m_check(check_capacity) {}
+  ~FastGSB200Rasterizer() override {
+    if (m_handle) tgs_raster_destroy(m_handle);
+  }
+
+  // `accumulate`: 1 = grads += (reference semantics), 0 = grads overwritten
+  void set_accumulate(bool a) { m_accumulate = a; }
+
+  void forward(const RasterizeContext& ctx) override {
+    if (!m_gaussians) throw std::runtime_error("Gaussians not set");
+    const TgsCamera cam = to_camera(ctx.fwd_input);
+    ensure(m_gaussians->size(), cam.width, cam.height, m_inst_cap);
+    for (int attempt = 0; attempt < 4; ++attempt) {
+      const TgsGaussians g = m_gaussians->abi();
+      check(tgs_raster_forward(m_handle, &g, &cam, static_cast<int32_t>(ctx.fwd_output_image.data_type),
+                               ctx.fwd_output_image.data, nullptr, ctx.densification_info, ctx.stream),
+            "FastGSB200Rasterizer::forward");
+      if (!m_check) return;
+      TgsRasterCounts c{};
+      check(tgs_raster_counts(m_handle, &c, ctx.stream), "FastGSB200Rasterizer::forward (counts)");
+      m_counts = c;
+      if (c.overflow == 0) return;
+      ensure(m_gaussians->size(), cam.width, cam.height, int64_t(c.n_instances) * 3 / 2 + 1024, true);
+    }
+    throw std::runtime_error("FastGSB200Rasterizer::forward: capacity could not be met");
+  }
+
+  void backward(RasterizeContext& ctx) override {
+    if (!m_gaussians || !ctx.gaussians_grad) throw std::runtime_error("Gaussians or gradient gaussians not set");
+    const TgsCamera cam = to_camera(ctx.fwd_input);
+    const TgsGaussians g = m_gaussians->abi();
+    TgsGaussians gg = ctx.gaussians_grad->abi();
+    check(tgs_raster_backward(m_handle, &g, &cam, static_cast<int32_t>(ctx.fwd_output_image.data_type),
+                              ctx.fwd_output_image.data, ctx.grad_output_image.data, &gg, m_accumulate ? 1 : 0,
+                              ctx.densification_info, ctx.stream),
+          "FastGSB200Rasterizer::backward");
+  }
+
+  TgsRasterCounts last_counts() const { return m_counts; }
+
+ private:
+  void ensure(int64_t n, int w, int h, int64_t inst, bool force = false) {
+    if (!force && m_handle && n <= m_caps.max_gaussians && w <= m_caps.max_width && h <= m_caps.max_height) return;
+    if (m_handle) tgs_raster_destroy(m_handle);
+    m_handle = nullptr;
+    m_caps.max_gaussians = std::max<int64_t>(n, 1);
+    m_caps.max_width = w;
+    m_caps.max_height = h;
+    m_caps.max_instances = inst;
+    m_inst_cap = inst;
+    check(tgs_raster_create(&m_caps, &m_handle), "FastGSB200Rasterizer: tgs_raster_create");
+  }
+
+  TgsRaster* m_handle = nullptr;
+  TgsRasterCaps m_caps{};
+  TgsRasterCounts m_counts{};
+  int64_t m_inst_cap = 0;
+  bool m_check = true;
+  bool m_accumulate = true;
+};
+
+// tinygs::LossContext / LossBase (loss.hpp:6-28)
+struct LossContext {
+  Image pred, target, loss, grad;
+  cudaStream_t stream = nullptr;
+};
+
+class LossBase {
+ public:
+  virtual ~LossBase() = default;
+  virtual void evaluate(LossContext ctx, float scale) = 0;
+  virtual std::string name() const = 0;
+};
+
+class L1Loss final : public LossBase {
+ public:
+  void evaluate(LossContext ctx, float scale) override {
+    check(tgs_loss_l1(static_cast<int32_t>(ctx.pred.data_type), int32_t(ctx.pred.shape.width),
+                      int32_t(ctx.pred.shape.height), ctx.pred.data, ctx.target.data, ctx.loss.data, ctx.grad.data,
+                      scale, ctx.stream),
+          "L1Loss::evaluate");
+  }
+  std::string name() const override { return "l1"; }
+};
+
+class FusedSSIMLoss final : public LossBase {
+ public:
+  ~FusedSSIMLoss() override {
+    if (m_handle) tgs_loss_destroy(m_handle);
+  }
+  void evaluate(LossContext ctx, float scale) override {
+    ensure(int32_t(ctx.pred.shape.width), int32_t(ctx.pred.shape.height));
+    check(tgs_loss_fused_ssim(m_handle, static_cast<int32_t>(ctx.pred.data_type), int32_t(ctx.pred.shape.width),
+                              int32_t(ctx.pred.shape.height), ctx.pred.data, ctx.target.data, ctx.loss.data,
+                              ctx.grad.data, scale, ctx.stream),
+          "FusedSSIMLoss::evaluate");
+  }
+  std::string name() const override { return "fused_ssim"; }
+
+ protected:
+  void ensure(int32_t w, int32_t h) {
+    if (m_handle && w <= m_w && h <= m_h) return;
+    if (m_handle) tgs_loss_destroy(m_handle);
+    m_handle = nullptr;
+    check(tgs_loss_create(w, h, &m_handle), "FusedSSIMLoss: tgs_loss_create");
+    m_w = w;
+    m_h = h;
+  }
+  TgsLoss* m_handle = nullptr;
+  int32_t m_w = 0, m_h = 0;
+};
+
+// GaussianOptimizationParams + SimpleAdamParameters (optim.hpp:8-37,
+// simple_adam.hpp:8-27) with the reference defaults.
+struct SimpleAdamParameters {
+  float beta1 = 0.9f, beta2 = 0.999f, epsilon = 1e-8f;
+  bool decay_reduction_mean = true;
+};
+struct GaussianOptimizationParams {
+  float max_grad_1 = 1.0f;
+  float means_lr = 1.6e-4f, shs_lr = 2.5e-3f, opacities_lr = 5.0e-2f, scales_lr = 5.0e-3f, rotations_lr = 1.0e-3f;
+  float opacities_l1 = 0.0f, scales_l1 = 0.0f;
+};
+
+class OptimizerBase {
+ public:
+  OptimizerBase(std::shared_ptr<GPUGaussian3d> g, std::shared_ptr<GPUGaussian3d> grad)
+      : m_gaussians(std::move(g)), m_gaussians_grad(std::move(grad)) {}
+  virtual ~OptimizerBase() = default;
+  virtual void step(float scale, cudaStream_t stream) = 0;
+  void set_lr(float lr) { m_global_lr = lr; }
+  float get_lr() const { return m_global_lr; }
+  GaussianOptimizationParams& params() { return m_params; }
+
+ protected:
+  std::shared_ptr<GPUGaussian3d> m_gaussians, m_gaussians_grad;
+  float m_global_lr = 1.0f;
+  GaussianOptimizationParams m_params;
+};
+
+class SimpleAdam final : public OptimizerBase {
+ public:
+  SimpleAdam(std::shared_ptr<GPUGaussian3d> g, std::shared_ptr<GPUGaussian3d> grad)
+      : OptimizerBase(g, grad),
+        m_first(std::make_shared<GPUGaussian3d>(g->size(), g->get_sh_degree())),
+        m_second(std::make_shared<GPUGaussian3d>(g->size(), g->get_sh_degree())) {}
+
+  SimpleAdamParameters& adam_params() { return m_adam; }
+  void set_scene_scale(float s) { m_scene_scale = s; }
+  void set_zero_grads_after_step(bool z) { m_zero_grads = z; }
+
+  void step(float scale, cudaStream_t stream) override {
+    ++m_global_steps;
+    const TgsAdamConfig cfg{m_adam.beta1,          m_adam.beta2,         m_adam.epsilon,   m_params.max_grad_1,
+                            m_params.means_lr,     m_params.shs_lr,      m_params.opacities_lr,
+                            m_params.scales_lr,    m_params.rotations_lr, m_params.opacities_l1,
+                            m_params.scales_l1,    m_scene_scale,        m_global_lr,
+                            m_adam.decay_reduction_mean ? 1 : 0};
+    const TgsGaussians p = m_gaussians->abi(), g = m_gaussians_grad->abi(), m = m_first->abi(),
+                       v = m_second->abi();
+    check(tgs_adam_step(&p, &g, &m, &v, &cfg, m_global_steps, scale, m_zero_grads ? 1 : 0, stream),
+          "SimpleAdam::step");
+  }
+
+ private:
+  SimpleAdamParameters m_adam;
+  std::shared_ptr<GPUGaussian3d> m_first, m_second;
+  uint32_t m_global_steps = 0;
+  float m_scene_scale = 1.0f;
+  bool m_zero_grads = false;
+};
+
+// One Orchestrator::train_step (orchestrator.cu:335-439) without the data
+// loader, pose optimisation and strategy: zero the gradient and image
+// buffers, forward, each loss with weight * grad_scaler, backward, and the
+// optimizer step with gradient scale 1 / (grad_scaler * accumulate_steps).
+struct WeightedLoss {
+  std::unique_ptr<LossBase> loss;
+  float weight;
+};
+
+class TrainStep {
+ public:
+  TrainStep(std::shared_ptr<GPUGaussian3d> g, std::shared_ptr<GPUGaussian3d> grad, RasterizerBase& rast,
+            OptimizerBase& opt, float grad_scaler = 10.0f)
+      : m_g(std::move(g)), m_grad(std::move(grad)), m_rast(rast), m_opt(opt), m_grad_scaler(grad_scaler) {}
+
+  void add_loss(std::unique_ptr<LossBase> l, float w) { m_losses.push_back({std::move(l), w}); }
+
+  void run(RasterizeContext& ctx, const Image& target, const Image& loss_map) {
+    m_grad->memset(0, ctx.stream);
+    check_cuda(cudaMemsetAsync(loss_map.data, 0, loss_map.bytes(), ctx.stream), "TrainStep: loss memset");
+    check_cuda(cudaMemsetAsync(ctx.grad_output_image.data, 0, ctx.grad_output_image.bytes(), ctx.stream),
+               "TrainStep: grad memset");
+    ctx.gaussians_grad = m_grad;
+    m_rast.forward(ctx);
+    LossContext lc{ctx.fwd_output_image, target, loss_map, ctx.grad_output_image, ctx.stream};
+    for (auto& wl : m_losses) wl.loss->evaluate(lc, wl.weight * m_grad_scaler);
+    m_rast.backward(ctx);
+    m_opt.step(1.0f / m_grad_scaler, ctx.stream);
+  }
+
+ private:
+  std::shared_ptr<GPUGaussian3d> m_g, m_grad;
+  RasterizerBase& m_rast;
+  OptimizerBase& m_opt;
+  float m_grad_scaler;
+  std::vector<WeightedLoss> m_losses;
+};
+
+// Factory in the shape of create_rasterizer (rasterizer.cpp:44-53).
+inline std::unique_ptr<RasterizerBase> create_rasterizer(const std::string& type) {
+  if (type == "fastgs_b200") return std::make_unique<FastGSB200Rasterizer>();
+  throw std::runtime_error("unknown rasterizer type: " + type);
+}
+
+inline std::unique_ptr<LossBase> create_loss(const std::string& type) {
+  if (type == "l1") return std::make_unique<L1Loss>();
+  if (type == "fused_ssim") return std::make_unique<FusedSSIMLoss>();
+  throw std::runtime_error("unknown loss type: " + type);
+}
+
+}  // namespace tgs_b200

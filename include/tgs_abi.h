@@ -228,6 +228,29 @@ TGS_API int tgs_loss_l1_ssim(TgsLoss* l, int32_t dtype, int32_t width, int32_t h
                      void* grad, float scale_l1, float scale_ssim,
                      float* loss_sum, tgs_stream_t stream);
 
+/* Largest padded image (Wp * Hp pixels, e.g. 512 x 512) that
+ * tgs_loss_l1_ssim_noalloc accepts. */
+#define TGS_NOALLOC_MAX_PIXELS 262144
+
+/* tgs_loss_l1_ssim for callers that cannot allocate device memory -- hosts
+ * whose memory pool owns all device memory, or code that must not allocate
+ * where it runs.  No counterpart in the reference.  It takes no TgsLoss
+ * handle: the SSIM partial-derivative maps live in a fixed array inside the
+ * library (9 MiB held by every GPU that loads it, until exit) instead of
+ * memory the caller allocates; the caller still passes inputs and outputs.
+ * Same arguments and results as tgs_loss_l1_ssim without its first argument.
+ * Returns TGS_ERR_CAPACITY if Wp * Hp exceeds TGS_NOALLOC_MAX_PIXELS.  The
+ * first call on a device looks up the array's device address (make it
+ * before any stream capture).  Every call on a device shares the array:
+ * calls whose GPU work may overlap race on it and must be serialised.
+ * Calls no cudaMalloc or cudaFree. */
+TGS_API int tgs_loss_l1_ssim_noalloc(int32_t dtype, int32_t width,
+                                     int32_t height, const void* pred,
+                                     const void* target, void* loss_map,
+                                     void* grad, float scale_l1,
+                                     float scale_ssim, float* loss_sum,
+                                     tgs_stream_t stream);
+
 /* -------------------------------------------------------------- optimizer */
 
 /* Hyper-parameters, reference GaussianOptimizationParams + SimpleAdamParameters

@@ -27,6 +27,7 @@ TGS_ERR_DEVICE_TIMEOUT = 7
 
 TGS_FLOAT32 = 0
 TGS_FLOAT16 = 1
+TGS_NOALLOC_MAX_PIXELS = 262144
 
 
 class TgsGaussians(ctypes.Structure):
@@ -72,6 +73,7 @@ PROTOTYPES = {
     "tgs_loss_destroy": (c_int32, [_P]),
     "tgs_loss_fused_ssim": (c_int32, [_P, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, _P]),
     "tgs_loss_l1_ssim": (c_int32, [_P, c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, _P, _P]),
+    "tgs_loss_l1_ssim_noalloc": (c_int32, [c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, c_float, _P, _P]),
     "tgs_adam_step": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
                                 POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32, c_float, c_int32, _P]),
     "tgs_gaussians_zero": (c_int32, [POINTER(TgsGaussians), _P]),

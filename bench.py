@@ -233,7 +233,9 @@ def kernels_per_step(n_tiles: int, world: int) -> int:
     tile_bits = max(1, (n_tiles - 1).bit_length())
     tile_passes = (tile_bits + 7) // 8
     forward = 1 + 2 + 4 * 3 + 3 + 3 * tile_passes + 2 + 1  # preprocess, compaction, sorts, instances, ranges, blend
-    return forward + 2 + 2 + 1  # loss fwd/bwd, blend bwd + preprocess bwd, adam
+    # loss fwd/bwd; blend bwd; per-Gaussian backward fused with Adam (one GPU)
+    # or per-Gaussian backward + Adam (several GPUs; NCCL's kernel not counted)
+    return forward + 2 + 1 + (1 if world == 1 else 2)
 
 
 def run_ours(args):
@@ -300,37 +302,38 @@ def run_ours(args):
     def view_of(step):
         return cams[(step * world + rank) % len(cams)]
 
-    stage_events = None
+    # one GPU: backward and Adam in one pass (tgs_raster_backward_adam); with
+    # several GPUs the gradients must be all-reduced between the two
+    fused = world == 1
 
-    def step(k, e2e=False, record=None):
+    def step(k, e2e=False, ev=None):
         ctx.fwd_input = view_of(k)
         if e2e:
             tgt_upload.copy_(host_targets[k % n_targets], non_blocking=True)
             tgt = tgt_upload
         else:
             tgt = dev_targets[k % n_targets]
-        ev = record
-        if ev is not None:
-            ev[0].record(stream)
         loss_map.zero_()
         grad_image.zero_()
         rast.forward(ctx)
         if ev is not None:
-            ev[1].record(stream)
+            ev[0].record(stream)
         loss.evaluate(image, tgt, loss_map, grad_image, W, H, grad_scaler=GRAD_SCALER, loss_sum=loss_sum,
                       stream=stream)
         if ev is not None:
-            ev[2].record(stream)
-        rast.backward(ctx)
-        if ev is not None:
-            ev[3].record(stream)
-        if world > 1:
+            ev[1].record(stream)
+        if fused:
+            opt.fused_backward_step(rast, ctx, 1.0 / GRAD_SCALER)
+        else:
+            rast.backward(ctx)
+            if ev is not None:
+                ev[2].record(stream)
             dist.all_reduce(grads.storage)
-        if ev is not None:
-            ev[4].record(stream)
-        opt.step(1.0 / (GRAD_SCALER * world), stream=stream)
-        if ev is not None:
-            ev[5].record(stream)
+            if ev is not None:
+                ev[3].record(stream)
+            opt.step(1.0 / (GRAD_SCALER * world), stream=stream)
+            if ev is not None:
+                ev[4].record(stream)
         if e2e:
             loss_host[k % 2].copy_(loss_sum[0], non_blocking=True)
 
@@ -370,14 +373,28 @@ def run_ours(args):
     if not np.isfinite(float(loss_host[0])):
         raise SystemExit("non-finite loss")
 
-    # per-stage times on a separate pass (not part of the headline)
+    # per-stage times on a separate pass (not part of the headline): the
+    # handle records CUDA events between its stages on the stream, the bench
+    # brackets the loss (and, with several GPUs, the all-reduce and Adam)
     n_stage = max(3, min(args.steps, 10))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(n_stage)]
+    rast.set_stage_timing(True)
+    rows = []
     for k in range(n_stage):
-        step(args.warmup + 2 * args.steps + k, False, evs[k])
-    torch.cuda.synchronize()
-    names = ["forward", "loss", "backward", "allreduce", "adam"]
-    stages = {nm: statistics.median(e[i].elapsed_time(e[i + 1]) for e in evs) for i, nm in enumerate(names)}
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        step(args.warmup + 2 * args.steps + k, False, evs)
+        torch.cuda.synchronize()
+        t = rast.stage_times()
+        row = {"preprocess": t[0], "binning": t[1], "blend_forward": t[2], "loss": evs[0].elapsed_time(evs[1]),
+               "blend_backward": t[3]}
+        if fused:
+            row["gaussian_backward_adam"] = t[4]
+        else:
+            row["gaussian_backward"] = t[4]
+            row["allreduce"] = evs[2].elapsed_time(evs[3])
+            row["adam"] = evs[3].elapsed_time(evs[4])
+        rows.append(row)
+    rast.set_stage_timing(False)
+    stages = {nm: statistics.median(r[nm] for r in rows) for nm in rows[0]}
 
     # forward-only render throughput (render Mpix/s)
     if world > 1:
@@ -393,11 +410,22 @@ def run_ours(args):
     render_ms = r0.elapsed_time(r1) / args.steps
 
     counts = rast.counts()
+    counts_v = int(counts.n_visible)
     ms_step = ms_dev / args.steps
     value = world * 1e3 / ms_step
     e2e_ms = ms_e2e / args.steps
-    adam_ms = stages["adam"]
-    adam_gbs = ADAM_BYTES_PER_GAUSSIAN * cfg.n / (adam_ms * 1e-3) / 1e9
+    if fused:
+        # k_preprocess_backward<true>: parameters, both moments read and
+        # written, the touched-tile counts, and the 48-byte screen-space
+        # gradients of the visible Gaussians
+        kernel = "k_preprocess_backward<true> (per-Gaussian backward fused with Adam)"
+        kernel_bytes = cfg.n * (6 * 236 + 4) + counts_v * 48
+        kernel_ms = stages["gaussian_backward_adam"]
+    else:
+        kernel = "k_adam (fused Adam over the 59-float arena)"
+        kernel_bytes = ADAM_BYTES_PER_GAUSSIAN * cfg.n
+        kernel_ms = stages["adam"]
+    kernel_gbs = kernel_bytes / (kernel_ms * 1e-3) / 1e9
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -430,10 +458,9 @@ def run_ours(args):
                     "d2h_bytes_per_step": 4},
             "render_mpix_s": W * H / (render_ms * 1e-3) / 1e6,
             "stages_ms": {k: round(v, 4) for k, v in stages.items()},
-            "roofline": {"bound": "hbm", "kernel": "k_adam (fused Adam over the 59-float arena)",
-                         "achieved": adam_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": adam_gbs / hbm_peak,
-                         "peak_source": peak_src, "traffic": None,
-                         "bytes_per_gaussian": ADAM_BYTES_PER_GAUSSIAN},
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": kernel_gbs, "peak": hbm_peak,
+                         "unit": "GB/s", "frac": kernel_gbs / hbm_peak, "peak_source": peak_src, "traffic": None,
+                         "algorithmic_bytes_per_launch": kernel_bytes, "avg_launch_ms": kernel_ms},
             "counts": {"visible": counts.n_visible, "instances": counts.n_instances, "buckets": counts.n_buckets},
             "gpu_launches": kernels_per_step(tile_count, world) * args.steps,
             "clocks": clocks,

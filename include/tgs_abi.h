@@ -193,6 +193,16 @@ TGS_API int tgs_raster_counts(TgsRaster* r, TgsRasterCounts* out, tgs_stream_t s
 TGS_API int tgs_raster_debug_buffer(TgsRaster* r, int32_t which, void** dev_ptr,
                             size_t* bytes);
 
+/* Stage timing for profiling.  When enabled, forward and backward record a
+ * CUDA event between their stages on the caller's stream (no host sync).
+ * tgs_raster_stage_times() waits for those events and returns the elapsed
+ * milliseconds of the stages of the last forward and backward:
+ *   [0] preprocess  [1] binning (compaction, sorts, instances, ranges)
+ *   [2] blend forward  [3] blend backward
+ *   [4] per-Gaussian backward (with the Adam update when fused). */
+TGS_API int tgs_raster_set_stage_timing(TgsRaster* r, int32_t enable);
+TGS_API int tgs_raster_stage_times(TgsRaster* r, float* out_ms5);
+
 /* ------------------------------------------------------------------- loss */
 
 /* L1 term.  Replaces L1Loss::evaluate (tinygs/src/loss/l1.cu:109-151):
@@ -286,6 +296,26 @@ TGS_API int tgs_adam_step(const TgsGaussians* params, const TgsGaussians* grads,
                   const TgsAdamConfig* cfg, uint32_t step,
                   float gradient_scale, int32_t zero_grads,
                   tgs_stream_t stream);
+
+/* Backward and optimizer step in one pass: equal to
+ *   tgs_raster_backward(accumulate = 0) into a gradient arena, followed by
+ *   tgs_adam_step(..., zero_grads = 0)
+ * (the reference's FastGSRasterizer::backward then SimpleAdam::step with a
+ * single view per step, orchestrator.cu:373-403), but each Gaussian's 59
+ * gradients go from the backward straight into its Adam update without being
+ * stored and re-read.  `grads` may be NULL (no gradient output) or receive
+ * the gradients as tgs_raster_backward would write them.  For several views
+ * per step (accumulation or multi-GPU all-reduce) use the separate calls. */
+TGS_API int tgs_raster_backward_adam(TgsRaster* r, const TgsGaussians* params,
+                                     const TgsCamera* cam, int32_t dtype,
+                                     const void* image, const void* grad_image,
+                                     TgsGaussians* grads,
+                                     const TgsGaussians* exp_avg,
+                                     const TgsGaussians* exp_avg_sq,
+                                     const TgsAdamConfig* cfg, uint32_t step,
+                                     float gradient_scale,
+                                     TgsDensificationInfo* dens,
+                                     tgs_stream_t stream);
 
 /* ------------------------------------------------------------------ misc */
 

@@ -1473,6 +1473,8 @@ void orc_adam(int64_t count, float* theta, const float* grad, float* m,
               float gradient_scale, float bias_correction1,
               float bias_correction2_sqrt, float max_grad_1,
               int32_t decay_kind, float decay) {
+    /* element-wise, so the thread count does not change the result */
+#pragma omp parallel for schedule(static) if (count > 65536)
     for (int64_t i = 0; i < count; ++i) {
         float th = theta[i];
         float g = gradient_scale * grad[i];

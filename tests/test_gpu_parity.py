@@ -185,16 +185,26 @@ def _grad_image(run, seed=3):
     return g.astype(np.float16) if run.fp16 else g
 
 
-def test_blend_backward_matches_oracle(oracle, cuda_lib, fp16):
+@pytest.mark.parametrize("with_dens", [True, False], ids=["dens", "nodens"])
+def test_blend_backward_matches_oracle(oracle, cuda_lib, fp16, with_dens):
+    """Screen-space gradients; sum |dL/dmean2d| is accumulated only when
+    densification statistics are requested (it feeds nothing else)."""
     cfg, params, sh, cam = scene("cfg0")
     run = GpuRun(params, sh, cam, fp16).forward()
+    if with_dens:
+        run.ctx.densification_info = torch.zeros((run.n, 4), dtype=torch.float32, device="cuda")
     gimg = _grad_image(run)
     run.backward(gimg)
     gp, gb, gf = run.prims(), run.bins(), run.fwd_state()
     ob = oracle.blend_backward(gp, gb, gf, gimg, cam, fp16)
     gh = run.helpers()
     vis = gp["n_touched"] > 0
-    for k in ("grad_mean2d", "absgrad_mean2d", "grad_conic", "grad_opacity", "grad_color"):
+    keys = ["grad_mean2d", "grad_conic", "grad_opacity", "grad_color"]
+    if with_dens:
+        keys.append("absgrad_mean2d")
+    else:
+        assert not np.any(gh["absgrad_mean2d"])
+    for k in keys:
         ok, worst, nbad = close_rel(gh[k][vis], ob[k][vis], 1e-3, 1e-4)
         assert ok, (k, worst, nbad)
 
@@ -390,3 +400,49 @@ def test_densification_info_accumulates(oracle, cuda_lib):
     oracle.preprocess_backward(params, sh, cam, gp["n_touched"], screen, dens=ref)
     assert close_rel(d[:, 1], ref[:, 1], 1e-4, 1e-6)[0]
     assert close_rel(d[:, 2], ref[:, 2], 1e-4, 1e-6)[0]
+
+
+# ----------------------------------------------------- fused backward + Adam
+
+def test_fused_backward_adam_equals_separate_calls(cuda_lib, fp16):
+    """tgs_raster_backward_adam == tgs_raster_backward(accumulate=0) followed
+    by tgs_adam_step.  The blend backward adds with float atomics, so two runs
+    differ in the last bits of the gradients; Adam normalises each step, so a
+    coordinate whose gradient is at that noise level can take a different
+    step -- those must be rare."""
+    cfg, params, sh, cam = scene("cfg1", n=20000)
+    gimg = None
+    results = []
+    for fused in (False, True):
+        run = GpuRun(params, sh, cam, fp16).forward()
+        if gimg is None:
+            gimg = _grad_image(run, 31)
+        run.grad_image.copy_(torch.from_numpy(gimg).to(run.dt))
+        run.ctx.accumulate = False
+        opt = rt.SimpleAdam(run.g, run.grads, rt.AdamParams(max_grad_1=0.3))
+        if fused:
+            opt.fused_backward_step(run.rast, run.ctx, 0.1, write_grads=True)
+        else:
+            run.rast.backward(run.ctx)
+            opt.step(0.1)
+        torch.cuda.synchronize()
+        results.append((run.g.to_numpy(), run.grads_np(), opt.exp_avg.to_numpy()))
+    (p0, g0, m0), (p1, g1, m1) = results
+    for k in p0:
+        # float-atomic order noise; the gradient tolerance of the path is 1e-3
+        ok, worst, nbad = close_rel(g1[k], g0[k], 1e-3, 1e-5)
+        assert ok, ("grad", k, worst)
+        close = np.abs(p1[k] - p0[k]) <= 1e-6 + 1e-6 * np.abs(p0[k])
+        assert close.mean() > 0.999, (k, close.mean())
+        assert close_rel(m1[k], m0[k], 1e-3, 1e-4)[0], k
+
+
+def test_stage_times_are_reported(cuda_lib):
+    cfg, params, sh, cam = scene("cfg0", n=5000)
+    run = GpuRun(params, sh, cam, False)
+    run.rast.set_stage_timing(True)
+    run.forward()
+    run.backward(_grad_image(run, 5))
+    t = run.rast.stage_times()
+    assert len(t) == 5 and all(x > 0 for x in t), t
+    run.rast.set_stage_timing(False)

@@ -66,7 +66,12 @@ PROTOTYPES = {
     "tgs_raster_forward": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, _P, _P, _P, _P]),
     "tgs_raster_backward": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, _P, _P,
                                       POINTER(TgsGaussians), c_int32, _P, _P]),
+    "tgs_raster_backward_adam": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, _P, _P,
+                                           POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                           POINTER(TgsAdamConfig), c_uint32, c_float, _P, _P]),
     "tgs_raster_counts": (c_int32, [_P, POINTER(TgsRasterCounts), _P]),
+    "tgs_raster_set_stage_timing": (c_int32, [_P, c_int32]),
+    "tgs_raster_stage_times": (c_int32, [_P, POINTER(c_float)]),
     "tgs_raster_debug_buffer": (c_int32, [_P, c_int32, POINTER(c_void_p), POINTER(c_size_t)]),
     "tgs_loss_l1": (c_int32, [c_int32, c_int32, c_int32, _P, _P, _P, _P, c_float, _P]),
     "tgs_loss_create": (c_int32, [c_int32, c_int32, POINTER(c_void_p)]),

@@ -70,7 +70,17 @@ struct TgsRaster {
   void* arena = nullptr;
   size_t arena_bytes = 0;
   int device = 0;
+  // stage timing (profiling only): events between the stages
+  bool timing = false;
+  cudaEvent_t ev[7] = {};
+  bool fwd_timed = false, bwd_timed = false;
 };
+
+namespace {
+void mark(TgsRaster* r, int k, cudaStream_t st) {
+  if (r->timing) cudaEventRecord(r->ev[k], st);
+}
+}  // namespace
 
 struct TgsLoss {
   float* partials = nullptr;
@@ -128,6 +138,8 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   const size_t np = static_cast<size_t>(s.max_pixels);
   s.n_touched = c.take<uint32_t>(n);
   s.depth_key = c.take<uint32_t>(n);
+  s.tile_mask = c.take<uint64_t>(n);
+  s.big_list = c.take<uint4>(n);
   s.bounds = c.take<ushort4>(n);
   s.mean2d = c.take<float2>(n);
   s.conic_opacity = c.take<float4>(n);
@@ -143,18 +155,50 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   s.inst_key[1] = c.take<uint16_t>(ni);
   s.inst_prim[0] = c.take<uint32_t>(ni);
   s.inst_prim[1] = c.take<uint32_t>(ni);
-  s.sort_max_blocks = static_cast<int64_t>((std::max(n, ni) + 4095) / 4096);
+  s.sort_max_blocks = static_cast<int64_t>((std::max(n, ni) + kSortTileItems - 1) / kSortTileItems);
   s.sort_hist = c.take<uint32_t>(256 * static_cast<size_t>(s.sort_max_blocks));
   s.sort_digit_total = c.take<uint32_t>(256);
   s.ranges = c.take<uint2>(nt);
   s.bucket_offsets = c.take<uint32_t>(nt);
   s.tile_max_contrib = c.take<uint32_t>(nt);
   s.n_contrib = c.take<uint32_t>(np);
-  s.bucket_tile = c.take<uint32_t>(nb);
+  s.live_buckets = c.take<uint2>(nb);
   s.ckpt = c.take<float4>(nb * kTilePixels);
   s.counts = c.take<DevCounts>(1);
   s.bwd_work = c.take<uint32_t>(4);
   bytes = c.off + 256;
+}
+
+// Per-segment learning rates and decays of SimpleAdam::step_adam
+// (simple_adam.cu:468-577), segment order means, opacities, rotations,
+// scales, sh0, sh_rest; the higher SH bands use 0.05 * shs_lr (line 19, 571).
+void adam_segments(const TgsAdamConfig* cfg, int64_t n, uint32_t step, float gradient_scale, AdamStepArgs* out) {
+  const float g_scale = cfg->decay_reduction_mean ? 1.0f / static_cast<float>(n) : 1.0f;
+  const float op_decay = cfg->opacities_l1 * g_scale, sc_decay = cfg->scales_l1 * g_scale;
+  const float lr[6] = {cfg->means_lr * cfg->scene_scale * cfg->global_lr, cfg->opacities_lr * cfg->global_lr,
+                       cfg->rotations_lr * cfg->global_lr,               cfg->scales_lr * cfg->global_lr,
+                       cfg->shs_lr * cfg->global_lr,                     cfg->shs_lr * 0.05f * cfg->global_lr};
+  for (int k = 0; k < 6; ++k) {
+    out->lr[k] = lr[k];
+    out->decay[k] = 0.f;
+    out->kind[k] = 0;
+  }
+  if (op_decay != 0.f) {
+    out->kind[1] = 1;
+    out->decay[1] = op_decay;
+  }
+  if (sc_decay != 0.f) {
+    out->kind[3] = 2;
+    out->decay[3] = sc_decay;
+  }
+  out->beta1 = cfg->beta1;
+  out->beta2 = cfg->beta2;
+  out->eps = cfg->epsilon;
+  out->gradient_scale = gradient_scale;
+  out->bc1 = static_cast<float>(1.0 - std::pow(static_cast<double>(cfg->beta1), static_cast<double>(step)));
+  out->bc2_sqrt =
+      static_cast<float>(std::sqrt(1.0 - std::pow(static_cast<double>(cfg->beta2), static_cast<double>(step))));
+  out->max_grad_1 = cfg->max_grad_1;
 }
 
 }  // namespace
@@ -221,6 +265,8 @@ int tgs_raster_create(const TgsRasterCaps* caps, TgsRaster** out) {
 int tgs_raster_destroy(TgsRaster* r) {
   if (r == nullptr) return TGS_ERR_INVALID_ARGUMENT;
   int st = TGS_OK;
+  for (cudaEvent_t e : r->ev)
+    if (e != nullptr) cudaEventDestroy(e);
   if (r->arena != nullptr) st = cuda_status(cudaFree(r->arena));
   delete r;
   return st;
@@ -244,9 +290,14 @@ int tgs_raster_forward(TgsRaster* r, const TgsGaussians* params, const TgsCamera
   const GaussianPtrs g = to_ptrs(params);
   cudaMemsetAsync(s.counts, 0, sizeof(DevCounts), st);
   s.have_forward = 0;
+  mark(r, 0, st);
   if (g.n > 0) launch_preprocess(s, g, dc, dtype == TGS_FLOAT16, reinterpret_cast<float4*>(dens), st);
+  mark(r, 1, st);
   launch_binning(s, g.n, dc, dtype == TGS_FLOAT16, st);
+  mark(r, 2, st);
   launch_blend_forward(s, dc, dtype == TGS_FLOAT16, image, alpha, st);
+  mark(r, 3, st);
+  r->fwd_timed = r->timing;
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return TGS_ERR_CUDA;
   s.have_forward = 1;
@@ -267,11 +318,72 @@ int tgs_raster_backward(TgsRaster* r, const TgsGaussians* params, const TgsCamer
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const DevCamera dc = make_camera(cam->width, cam->height, cam->fx, cam->fy, cam->cx, cam->cy, cam->near_plane,
                                    cam->far_plane, cam->w2c);
-  launch_blend_backward(s, dc, dtype == TGS_FLOAT16, image, grad_image, st);
+  mark(r, 4, st);
+  launch_blend_backward(s, dc, dtype == TGS_FLOAT16, image, grad_image, dens != nullptr, st);
+  mark(r, 5, st);
   if (params->n > 0)
     launch_preprocess_backward(s, to_ptrs(params), to_ptrs(grads), dc, accumulate, reinterpret_cast<float4*>(dens),
                                st);
+  mark(r, 6, st);
+  r->bwd_timed = r->timing;
   return cuda_status(cudaGetLastError());
+}
+
+int tgs_raster_backward_adam(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cam, int32_t dtype,
+                             const void* image, const void* grad_image, TgsGaussians* grads,
+                             const TgsGaussians* exp_avg, const TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg,
+                             uint32_t step, float gradient_scale, TgsDensificationInfo* dens, tgs_stream_t stream) {
+  if (r == nullptr || !gaussians_ok(params) || !camera_ok(cam) || image == nullptr || grad_image == nullptr ||
+      !gaussians_ok(exp_avg) || !gaussians_ok(exp_avg_sq) || cfg == nullptr || step == 0 ||
+      (grads != nullptr && !gaussians_ok(grads)))
+    return TGS_ERR_INVALID_ARGUMENT;
+  RasterState& s = r->s;
+  if (!s.have_forward || s.last_dtype != dtype || s.last_n != params->n || exp_avg->n != params->n ||
+      exp_avg_sq->n != params->n || (grads != nullptr && grads->n != params->n))
+    return TGS_ERR_NO_FORWARD;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const DevCamera dc = make_camera(cam->width, cam->height, cam->fx, cam->fy, cam->cx, cam->cy, cam->near_plane,
+                                   cam->far_plane, cam->w2c);
+  mark(r, 4, st);
+  launch_blend_backward(s, dc, dtype == TGS_FLOAT16, image, grad_image, dens != nullptr, st);
+  mark(r, 5, st);
+  if (params->n > 0) {
+    AdamStepArgs a{};
+    adam_segments(cfg, params->n, step, gradient_scale, &a);
+    GaussianPtrs none{};
+    none.n = params->n;
+    const GaussianPtrs gp = grads != nullptr ? to_ptrs(grads) : none;
+    const GaussianPtrs m = to_ptrs(exp_avg), v = to_ptrs(exp_avg_sq);
+    launch_preprocess_backward(s, to_ptrs(params), gp, dc, 0, reinterpret_cast<float4*>(dens), st, &m, &v, &a);
+  }
+  mark(r, 6, st);
+  r->bwd_timed = r->timing;
+  return cuda_status(cudaGetLastError());
+}
+
+int tgs_raster_set_stage_timing(TgsRaster* r, int32_t enable) {
+  if (r == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  if (enable && r->ev[0] == nullptr)
+    for (cudaEvent_t& e : r->ev)
+      if (cudaEventCreate(&e) != cudaSuccess) return TGS_ERR_CUDA;
+  r->timing = enable != 0;
+  r->fwd_timed = r->bwd_timed = false;
+  return TGS_OK;
+}
+
+int tgs_raster_stage_times(TgsRaster* r, float* out) {
+  if (r == nullptr || out == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  for (int k = 0; k < 5; ++k) out[k] = 0.f;
+  if (r->fwd_timed) {
+    if (cudaEventSynchronize(r->ev[3]) != cudaSuccess) return TGS_ERR_CUDA;
+    for (int k = 0; k < 3; ++k) cudaEventElapsedTime(&out[k], r->ev[k], r->ev[k + 1]);
+  }
+  if (r->bwd_timed) {
+    if (cudaEventSynchronize(r->ev[6]) != cudaSuccess) return TGS_ERR_CUDA;
+    cudaEventElapsedTime(&out[3], r->ev[4], r->ev[5]);
+    cudaEventElapsedTime(&out[4], r->ev[5], r->ev[6]);
+  }
+  return TGS_OK;
 }
 
 int tgs_raster_counts(TgsRaster* r, TgsRasterCounts* out, tgs_stream_t stream) {

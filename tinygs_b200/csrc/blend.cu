@@ -24,6 +24,16 @@
 namespace tgs {
 namespace {
 
+// The buckets of a tile that start before its deepest contributor are the
+// ones the backward runs; the forward appends them to a list (in no
+// particular order) so that the backward's warps only see live work.
+__device__ __forceinline__ void publish_live_buckets(uint32_t tile, uint32_t deepest, DevCounts* counts,
+                                                     uint32_t* s_live) {
+  const uint32_t nl = (deepest + kBucket - 1) / kBucket;
+  s_live[0] = nl > 0 ? atomicAdd(&counts->n_live_buckets, nl) : 0u;
+  s_live[1] = nl;
+}
+
 // ------------------------------------------------------------ forward fp32
 
 __global__ void __launch_bounds__(kTilePixels)
@@ -32,12 +42,13 @@ __global__ void __launch_bounds__(kTilePixels)
                         const float4* __restrict__ conic_opacity, const float* __restrict__ color,
                         const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ image,
                         float* __restrict__ alpha, uint32_t* __restrict__ n_contrib,
-                        uint32_t* __restrict__ tile_max, uint32_t* __restrict__ bucket_tile,
-                        float4* __restrict__ ckpt) {
+                        uint32_t* __restrict__ tile_max, uint2* __restrict__ live_buckets,
+                        DevCounts* __restrict__ live_count, float4* __restrict__ ckpt) {
   __shared__ float2 s_mean[kTilePixels];
   __shared__ float4 s_co[kTilePixels];
   __shared__ float4 s_col[kTilePixels];
   __shared__ uint32_t s_max[kTilePixels / 32];
+  __shared__ uint32_t s_live[2];
   const uint32_t tid = threadIdx.x;
   const uint32_t lx = tid & 15u, ly = tid >> 4;
   const uint32_t tile = blockIdx.y * cam.grid_w + blockIdx.x;
@@ -48,8 +59,6 @@ __global__ void __launch_bounds__(kTilePixels)
   const uint2 r = ok ? ranges[tile] : make_uint2(0, 0);
   const uint32_t count = r.y - r.x;
   const uint32_t first_bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
-  const uint32_t n_buckets = (count + kBucket - 1) / kBucket;
-  for (uint32_t k = tid; k < n_buckets; k += kTilePixels) bucket_tile[first_bucket + k] = tile;
   const uint32_t slot = tiled_index(ly, lx, 2);
   float4* my_ckpt = ckpt + static_cast<size_t>(first_bucket) * kTilePixels + slot;
 
@@ -111,7 +120,10 @@ __global__ void __launch_bounds__(kTilePixels)
     uint32_t mx = 0;
     for (int w = 0; w < kTilePixels / 32; ++w) mx = max(mx, s_max[w]);
     tile_max[tile] = mx;
+    publish_live_buckets(tile, mx, live_count, s_live);
   }
+  __syncthreads();
+  for (uint32_t j = tid; j < s_live[1]; j += kTilePixels) live_buckets[s_live[0] + j] = make_uint2(tile, j);
 }
 
 // ------------------------------------------------------------ forward fp16
@@ -137,11 +149,13 @@ __global__ void __launch_bounds__(kF16Threads)
                         const PrimInfo16* __restrict__ prim_info, const DevCounts* __restrict__ counts,
                         DevCamera cam, __half* __restrict__ image, __half* __restrict__ alpha,
                         uint16_t* __restrict__ n_contrib, uint32_t* __restrict__ tile_max,
-                        uint32_t* __restrict__ bucket_tile, uint4* __restrict__ ckpt) {
+                        uint2* __restrict__ live_buckets, DevCounts* __restrict__ live_count,
+                        uint4* __restrict__ ckpt) {
   __shared__ __half2 s_mx[kF16Threads], s_my[kF16Threads];
   __shared__ __half2 s_cx[kF16Threads], s_cy[kF16Threads], s_cz[kF16Threads], s_op[kF16Threads];
   __shared__ __half2 s_r[kF16Threads], s_g[kF16Threads], s_b[kF16Threads];
   __shared__ uint32_t s_max[kF16Threads / 32];
+  __shared__ uint32_t s_live[2];
   const uint32_t tid = threadIdx.x;
   const uint32_t tx = tid & 7u, ty = tid >> 3;
   const uint32_t lx = 2 * tx, ly = ty;
@@ -174,8 +188,6 @@ __global__ void __launch_bounds__(kF16Threads)
   const uint2 r = ok ? ranges[tile] : make_uint2(0, 0);
   const uint32_t count = r.y - r.x;
   const uint32_t first_bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
-  const uint32_t n_buckets = (count + kBucket - 1) / kBucket;
-  for (uint32_t k = tid; k < n_buckets; k += kF16Threads) bucket_tile[first_bucket + k] = tile;
   // checkpoint record of the pixel pair: 2 x (r,g | b,T) halves
   uint4* my_ckpt = ckpt + (static_cast<size_t>(first_bucket) * kTilePixels + tiled_index(ly, lx, 2)) / 2;
 
@@ -258,189 +270,284 @@ __global__ void __launch_bounds__(kF16Threads)
     uint32_t mx = 0;
     for (int w = 0; w < kF16Threads / 32; ++w) mx = max(mx, s_max[w]);
     tile_max[tile] = mx;
+    publish_live_buckets(tile, mx, live_count, s_live);
   }
+  __syncthreads();
+  for (uint32_t j = tid; j < s_live[1]; j += kF16Threads) live_buckets[s_live[0] + j] = make_uint2(tile, j);
 }
 
 // ---------------------------------------------------------------- backward
 
 constexpr int kBwdWarps = 8;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Per-pixel inputs of one bucket, fetched a chunk of 32 pixels ahead.
+template <int kFp16>
+struct PixelRaw {
+  float ck[4];   // checkpoint (colour so far, T) at the start of the bucket
+  float img[3];  // final colour
+  float grad[3];
+  uint32_t last;
+  bool inside;
+};
 
 template <int kFp16>
+__device__ __forceinline__ PixelRaw<kFp16> fetch_pixel(uint32_t i, uint32_t bucket, uint32_t gx, uint32_t gy,
+                                                       const DevCamera& cam, const void* image_v,
+                                                       const void* grad_v, const void* n_contrib_v,
+                                                       const void* ckpt_v) {
+  PixelRaw<kFp16> r{};
+  uint32_t dx, dy;
+  walk_pixel(i, dx, dy);
+  const uint32_t px = gx * kTile + dx, py = gy * kTile + dy;
+  r.inside = px < cam.width && py < cam.height;
+  if (!r.inside) return r;
+  const uint32_t pi = tiled_index(py, px, cam.tiled_w);
+  if constexpr (kFp16) {
+    const uint2 c = reinterpret_cast<const uint2*>(ckpt_v)[static_cast<size_t>(bucket) * kTilePixels + i];
+    const float2 rg = __half22float2(u2h(c.x));
+    const float2 bt = __half22float2(u2h(c.y));
+    r.ck[0] = rg.x;
+    r.ck[1] = rg.y;
+    r.ck[2] = bt.x;
+    r.ck[3] = bt.y;
+    const __half* img = reinterpret_cast<const __half*>(image_v);
+    const __half* gr = reinterpret_cast<const __half*>(grad_v);
+#pragma unroll
+    for (int c3 = 0; c3 < 3; ++c3) {
+      r.img[c3] = __half2float(img[pi + c3 * cam.plane]);
+      r.grad[c3] = __half2float(gr[pi + c3 * cam.plane]);
+    }
+  } else {
+    const float4 c = reinterpret_cast<const float4*>(ckpt_v)[static_cast<size_t>(bucket) * kTilePixels + i];
+    r.ck[0] = c.x;
+    r.ck[1] = c.y;
+    r.ck[2] = c.z;
+    r.ck[3] = c.w;
+    const float* img = reinterpret_cast<const float*>(image_v);
+    const float* gr = reinterpret_cast<const float*>(grad_v);
+#pragma unroll
+    for (int c3 = 0; c3 < 3; ++c3) {
+      r.img[c3] = img[pi + c3 * cam.plane];
+      r.grad[c3] = gr[pi + c3 * cam.plane];
+    }
+    r.last = reinterpret_cast<const uint32_t*>(n_contrib_v)[pi];
+  }
+  return r;
+}
+
+// The state a pixel enters the bucket with: transmittance T, the colour
+// still to come behind the current primitive dotted with dL/dpixel (adg),
+// the pixel centre, dL/dpixel and (fp32 path) its contributor count.  fp16
+// path: colour and the colour-behind are on the 0..255 scale.
+template <int kFp16>
+__device__ __forceinline__ void pixel_state(const PixelRaw<kFp16>& r, uint32_t i, uint32_t gx, uint32_t gy,
+                                            float4& a4, float4& b4) {
+  uint32_t dx, dy;
+  walk_pixel(i, dx, dy);
+  const float px = static_cast<float>(gx * kTile + dx), py = static_cast<float>(gy * kTile + dy);
+  if (!r.inside) {
+    a4 = make_float4(0.f, 0.f, px, py);
+    b4 = make_float4(0.f, 0.f, 0.f, __uint_as_float(0u));
+    return;
+  }
+  const float s = kFp16 ? 255.0f : 1.0f;
+  const float a0 = r.img[0] * s - r.ck[0], a1 = r.img[1] * s - r.ck[1], a2 = r.img[2] * s - r.ck[2];
+  const float adg = a0 * r.grad[0] + a1 * r.grad[1] + a2 * r.grad[2];
+  const float T = kFp16 ? r.ck[3] * (1.0f / 255.0f) : r.ck[3];
+  a4 = make_float4(T, adg, px, py);
+  b4 = make_float4(r.grad[0], r.grad[1], r.grad[2], __uint_as_float(kFp16 ? 0xffffffffu : r.last));
+}
+
+template <int kFp16>
+__device__ __forceinline__ void load_conic(uint32_t p, const float4* __restrict__ conic_opacity,
+                                           const PrimInfo16* __restrict__ prim_info, float4& co) {
+  if constexpr (kFp16) {
+    const PrimInfo16 rec = prim_info[p];
+    co = make_float4(__low2float(rec.conic_xy), __high2float(rec.conic_xy), __low2float(rec.conic_z_opacity),
+                     __high2float(rec.conic_z_opacity));
+  } else {
+    co = conic_opacity[p];
+  }
+}
+
+// kAbs: also accumulate sum |dL/dmean2d| (consumed only by densification).
+template <int kFp16, bool kAbs>
 __global__ void __launch_bounds__(32 * kBwdWarps)
     k_blend_backward(const uint2* __restrict__ ranges, const uint32_t* __restrict__ bucket_offsets,
-                     const uint32_t* __restrict__ inst_prim, const float2* __restrict__ mean2d,
-                     const float4* __restrict__ conic_opacity, const float* __restrict__ color,
-                     const PrimInfo16* __restrict__ prim_info, const void* __restrict__ image_v,
-                     const void* __restrict__ grad_v, const uint32_t* __restrict__ tile_max,
-                     const void* __restrict__ n_contrib_v, const uint32_t* __restrict__ bucket_tile,
-                     const void* __restrict__ ckpt_v, const DevCounts* __restrict__ counts, DevCamera cam,
-                     float* __restrict__ helpers) {
-  __shared__ float4 s_a[kBwdWarps][32];  // (Ca.r, Ca.g, Ca.b, T)
+                     const uint2* __restrict__ live_buckets, const uint32_t* __restrict__ inst_prim,
+                     const float2* __restrict__ mean2d, const float4* __restrict__ conic_opacity,
+                     const float* __restrict__ color, const PrimInfo16* __restrict__ prim_info,
+                     const void* __restrict__ image_v, const void* __restrict__ grad_v,
+                     const void* __restrict__ n_contrib_v, const void* __restrict__ ckpt_v,
+                     const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ helpers) {
+  __shared__ float4 s_a[kBwdWarps][32];  // (T, adg, px, py)
   __shared__ float4 s_b[kBwdWarps][32];  // (G.r, G.g, G.b, last as bits)
   if (counts->overflow != 0u) return;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  const uint32_t n_buckets = counts->n_buckets;
-  const uint32_t gw = gridDim.x * kBwdWarps;
+  const uint32_t n_live = counts->n_live_buckets;
+  const uint32_t stride = gridDim.x * kBwdWarps;
   const float max_alpha = kFp16 ? __half2float(__float2half_rn(kMaxAlphaF16)) : kMaxAlphaF32;
+  constexpr uint32_t kChunks = kTilePixels / 32;
 
-  for (uint32_t bucket = blockIdx.x * kBwdWarps + warp; bucket < n_buckets; bucket += gw) {
-    const uint32_t tile = bucket_tile[bucket];
+  for (uint32_t item = blockIdx.x * kBwdWarps + warp; item < n_live; item += stride) {
+    const uint2 lb = live_buckets[item];
+    const uint32_t tile = lb.x, tb = lb.y;
     const uint2 r = ranges[tile];
+    const uint32_t bucket = (tile == 0 ? 0u : bucket_offsets[tile - 1]) + tb;
     const uint32_t count = r.y - r.x;
-    const uint32_t tb = bucket - (tile == 0 ? 0u : bucket_offsets[tile - 1]);
-    if (tb * kBucket >= tile_max[tile]) continue;
     const uint32_t tp = tb * kBucket + lane;
     const bool valid_prim = tp < count && (!kFp16 || tp <= 0xffffu);
     const uint32_t gx = tile % cam.grid_w, gy = tile / cam.grid_w;
 
+
     uint32_t p = 0;
-    float mx = 0.f, my = 0.f, ca = 0.f, cb = 0.f, cc = 0.f, op = 0.f;
-    float col0 = 0.f, col1 = 0.f, col2 = 0.f, f0 = 0.f, f1 = 0.f, f2 = 0.f;
+    float mx = 0.f, my = 0.f, op = 0.f, ka = 0.f, kb = 0.f, kc = 0.f;
+    float col0 = 0.f, col1 = 0.f, col2 = 0.f;
     if (valid_prim) {
       p = inst_prim[r.x + tp];
       const float2 m = mean2d[p];
       mx = m.x - 0.5f;
       my = m.y - 0.5f;
+      float4 co;
+      load_conic<kFp16>(p, conic_opacity, prim_info, co);
+      op = co.w;
+      // exponent in base 2: exp(-q) = 2^(-q log2 e)
+      ka = 0.5f * kLog2e * co.x;
+      kb = kLog2e * co.y;
+      kc = 0.5f * kLog2e * co.z;
       if constexpr (kFp16) {
-        const PrimInfo16 rec = prim_info[p];
-        ca = __low2float(rec.conic_xy);
-        cb = __high2float(rec.conic_xy);
-        cc = __low2float(rec.conic_z_opacity);
-        op = __high2float(rec.conic_z_opacity);
-        col0 = static_cast<float>(rec.rgb_pad.x);
-        col1 = static_cast<float>(rec.rgb_pad.y);
-        col2 = static_cast<float>(rec.rgb_pad.z);
-        f0 = f1 = f2 = 1.f;
+        const uchar4 c = prim_info[p].rgb_pad;
+        col0 = static_cast<float>(c.x);
+        col1 = static_cast<float>(c.y);
+        col2 = static_cast<float>(c.z);
       } else {
-        const float4 co = conic_opacity[p];
-        ca = co.x;
-        cb = co.y;
-        cc = co.z;
-        op = co.w;
-        const float u0 = color[3 * p], u1 = color[3 * p + 1], u2 = color[3 * p + 2];
-        col0 = fmaxf(u0, 0.f);
-        col1 = fmaxf(u1, 0.f);
-        col2 = fmaxf(u2, 0.f);
-        f0 = u0 >= 0.f ? 1.f : 0.f;
-        f1 = u1 >= 0.f ? 1.f : 0.f;
-        f2 = u2 >= 0.f ? 1.f : 0.f;
+        col0 = fmaxf(color[3 * p], 0.f);
+        col1 = fmaxf(color[3 * p + 1], 0.f);
+        col2 = fmaxf(color[3 * p + 2], 0.f);
       }
     }
+    float g_op = 0.f, g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_c0 = 0.f, g_c1 = 0.f, g_c2 = 0.f;
+    float s_x = 0.f, s_y = 0.f;  // sums of dop * (mean - pixel)
     float g_mx = 0.f, g_my = 0.f, a_mx = 0.f, a_my = 0.f;
-    float g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_op = 0.f, g_c0 = 0.f, g_c1 = 0.f, g_c2 = 0.f;
-    // pixel state travelling along the lanes
-    float T = 0.f, A0 = 0.f, A1 = 0.f, A2 = 0.f, G0 = 0.f, G1 = 0.f, G2 = 0.f;
+    // pixel state travelling along the lanes (zero: no contribution)
+    float T = 0.f, adg = 0.f, G0 = 0.f, G1 = 0.f, G2 = 0.f, px = 0.f, py = 0.f;
     uint32_t last = 0;
 
-    for (uint32_t chunk = 0; chunk <= kTilePixels / 32; ++chunk) {
-      if (chunk < kTilePixels / 32) {
-        // stage the next 32 pixels of the walk
+    for (uint32_t chunk = 0; chunk <= kChunks; ++chunk) {
+      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (chunk < kChunks) {
         const uint32_t i = chunk * 32 + lane;
-        uint32_t dx, dy;
-        walk_pixel(i, dx, dy);
-        const uint32_t px = gx * kTile + dx, py = gy * kTile + dy;
-        float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (px < cam.width && py < cam.height) {
-          const uint32_t pi = tiled_index(py, px, cam.tiled_w);
-          if constexpr (kFp16) {
-            const uint2 c = reinterpret_cast<const uint2*>(ckpt_v)[static_cast<size_t>(bucket) * kTilePixels + i];
-            const float2 rg = __half22float2(u2h(c.x));
-            const float2 bt = __half22float2(u2h(c.y));
-            const __half* img = reinterpret_cast<const __half*>(image_v);
-            const __half* gr = reinterpret_cast<const __half*>(grad_v);
-            a4 = make_float4(__half2float(img[pi]) * 255.0f - rg.x, __half2float(img[pi + cam.plane]) * 255.0f - rg.y,
-                             __half2float(img[pi + 2 * cam.plane]) * 255.0f - bt.x, bt.y * (1.0f / 255.0f));
-            b4 = make_float4(__half2float(gr[pi]), __half2float(gr[pi + cam.plane]),
-                             __half2float(gr[pi + 2 * cam.plane]), __uint_as_float(0xffffffffu));
-          } else {
-            const float4 c = reinterpret_cast<const float4*>(ckpt_v)[static_cast<size_t>(bucket) * kTilePixels + i];
-            const float* img = reinterpret_cast<const float*>(image_v);
-            const float* gr = reinterpret_cast<const float*>(grad_v);
-            a4 = make_float4(img[pi] - c.x, img[pi + cam.plane] - c.y, img[pi + 2 * cam.plane] - c.z, c.w);
-            b4 = make_float4(gr[pi], gr[pi + cam.plane], gr[pi + 2 * cam.plane],
-                             __uint_as_float(reinterpret_cast<const uint32_t*>(n_contrib_v)[pi]));
-          }
-        }
-        s_a[warp][lane] = a4;
-        s_b[warp][lane] = b4;
+        const PixelRaw<kFp16> raw = fetch_pixel<kFp16>(i, bucket, gx, gy, cam, image_v, grad_v, n_contrib_v, ckpt_v);
+        pixel_state<kFp16>(raw, i, gx, gy, a4, b4);
       }
+      s_a[warp][lane] = a4;
+      s_b[warp][lane] = b4;
       __syncwarp();
-#pragma unroll 4
-      for (uint32_t s = 0; s < 32; ++s) {
+#pragma unroll 8
+      for (uint32_t st = 0; st < 32; ++st) {
         T = __shfl_up_sync(0xffffffffu, T, 1);
-        A0 = __shfl_up_sync(0xffffffffu, A0, 1);
-        A1 = __shfl_up_sync(0xffffffffu, A1, 1);
-        A2 = __shfl_up_sync(0xffffffffu, A2, 1);
+        adg = __shfl_up_sync(0xffffffffu, adg, 1);
         G0 = __shfl_up_sync(0xffffffffu, G0, 1);
         G1 = __shfl_up_sync(0xffffffffu, G1, 1);
         G2 = __shfl_up_sync(0xffffffffu, G2, 1);
-        last = __shfl_up_sync(0xffffffffu, last, 1);
+        px = __shfl_up_sync(0xffffffffu, px, 1);
+        py = __shfl_up_sync(0xffffffffu, py, 1);
+        if constexpr (!kFp16) last = __shfl_up_sync(0xffffffffu, last, 1);
         if (lane == 0) {
-          if (chunk < kTilePixels / 32) {
-            const float4 a4 = s_a[warp][s], b4 = s_b[warp][s];
-            A0 = a4.x; A1 = a4.y; A2 = a4.z; T = a4.w;
-            G0 = b4.x; G1 = b4.y; G2 = b4.z; last = __float_as_uint(b4.w);
-          } else {
-            T = A0 = A1 = A2 = G0 = G1 = G2 = 0.f;
-            last = 0;
-          }
+          const float4 na = s_a[warp][st], nb = s_b[warp][st];
+          T = na.x;
+          adg = na.y;
+          px = na.z;
+          py = na.w;
+          G0 = nb.x;
+          G1 = nb.y;
+          G2 = nb.z;
+          if constexpr (!kFp16) last = __float_as_uint(nb.w);
         }
-        const int idx = static_cast<int>(chunk * 32 + s) - static_cast<int>(lane);
-        const bool valid_pix = idx >= 0 && idx < kTilePixels;
-        uint32_t dx, dy;
-        walk_pixel(static_cast<uint32_t>(idx) & 255u, dx, dy);
-        const float ddx = mx - static_cast<float>(gx * kTile + dx);
-        const float ddy = my - static_cast<float>(gy * kTile + dy);
+        const float ddx = mx - px, ddy = my - py;
         const float dxx = ddx * ddx, dxy = ddx * ddy, dyy = ddy * ddy;
-        const float power = fmaxf(0.5f * (ca * dxx + cc * dyy) + cb * dxy, 0.f);
-        const float gau = __expf(-power);
-        bool use = valid_prim && valid_pix;
-        if constexpr (!kFp16) use = use && tp < last;
-        const float a = use ? fminf(op * gau, max_alpha) : 0.f;
+        const float q2 = fmaxf(ka * dxx + kc * dyy + kb * dxy, 0.f);
+        float a = fminf(op * exp2f(-q2), max_alpha);
+        if constexpr (!kFp16) a = tp < last ? a : 0.f;
         const float w = T * a;
         const float om = 1.0f - a;
         const float cdg = col0 * G0 + col1 * G1 + col2 * G2;
-        g_c0 += w * (G0 * f0);
-        g_c1 += w * (G1 * f1);
-        g_c2 += w * (G2 * f2);
-        A0 -= w * col0;
-        A1 -= w * col1;
-        A2 -= w * col2;
-        const float adg = A0 * G0 + A1 * G1 + A2 * G2;
+        g_c0 += w * G0;
+        g_c1 += w * G1;
+        g_c2 += w * G2;
+        adg -= w * cdg;  // what lies behind this primitive
         const float dop = a * (T * cdg - adg / om);
         g_op += dop;
         g_ca += dop * dxx;
         g_cb += dop * dxy;
         g_cc += dop * dyy;
-        const float gmx = dop * (ca * ddx + cb * ddy);
-        const float gmy = dop * (cb * ddx + cc * ddy);
-        g_mx += gmx;
-        g_my += gmy;
-        a_mx += fabsf(gmx);
-        a_my += fabsf(gmy);
-        T = T * om;
+        if constexpr (kAbs) {
+          // (ca, cb, cc) = (2 ka, kb, 2 kc) / log2 e
+          const float gmx = dop * (2.0f * ka * ddx + kb * ddy) * (1.0f / kLog2e);
+          const float gmy = dop * (kb * ddx + 2.0f * kc * ddy) * (1.0f / kLog2e);
+          g_mx += gmx;
+          g_my += gmy;
+          a_mx += fabsf(gmx);
+          a_my += fabsf(gmy);
+        } else {
+          s_x += dop * ddx;
+          s_y += dop * ddy;
+        }
+        T *= om;
       }
       __syncwarp();
     }
     if (valid_prim) {
+      if constexpr (!kAbs) {
+        float4 co;
+        load_conic<kFp16>(p, conic_opacity, prim_info, co);
+        g_mx = co.x * s_x + co.y * s_y;
+        g_my = co.y * s_x + co.z * s_y;
+      }
+      if constexpr (!kFp16) {
+        // colour clamped at zero passes no gradient
+        if (color[3 * p] < 0.f) g_c0 = 0.f;
+        if (color[3 * p + 1] < 0.f) g_c1 = 0.f;
+        if (color[3 * p + 2] < 0.f) g_c2 = 0.f;
+      }
       // scale conventions: fp32 accumulates in [0,1] colour units; the fp16
-      // path carries colour and C_after scaled by 255 (reference lines
-      // 1359-1369 divide by 255 at the end)
-      const float s = kFp16 ? (1.0f / 255.0f) : 1.0f;
+      // path carries colour and the colour-behind scaled by 255 (reference
+      // lines 1359-1369 divide by 255 at the end)
+      const float sc = kFp16 ? (1.0f / 255.0f) : 1.0f;
       float* h = helpers + static_cast<size_t>(p) * kHelperFloats;
-      atomicAdd(h + 0, -g_mx * s);
-      atomicAdd(h + 1, -g_my * s);
-      atomicAdd(h + 2, a_mx * s);
-      atomicAdd(h + 3, a_my * s);
-      atomicAdd(h + 4, -0.5f * g_ca * s);
-      atomicAdd(h + 5, -0.5f * g_cb * s);
-      atomicAdd(h + 6, -0.5f * g_cc * s);
-      atomicAdd(h + 7, g_op * s * (1.0f - op));
+      atomicAdd(h + 0, -g_mx * sc);
+      atomicAdd(h + 1, -g_my * sc);
+      if constexpr (kAbs) {
+        atomicAdd(h + 2, a_mx * sc);
+        atomicAdd(h + 3, a_my * sc);
+      }
+      atomicAdd(h + 4, -0.5f * g_ca * sc);
+      atomicAdd(h + 5, -0.5f * g_cb * sc);
+      atomicAdd(h + 6, -0.5f * g_cc * sc);
+      atomicAdd(h + 7, g_op * sc * (1.0f - op));
       atomicAdd(h + 8, g_c0);
       atomicAdd(h + 9, g_c1);
       atomicAdd(h + 10, g_c2);
     }
   }
+}
+
+template <int kFp16, bool kAbs>
+void run_blend_backward(const RasterState& s, const DevCamera& cam, const void* image, const void* grad_image,
+                        cudaStream_t stream) {
+  // persistent: as many blocks as are resident at once
+  static int per_sm[64] = {};  // per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& bps = per_sm[dev & 63];
+  if (bps == 0) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, k_blend_backward<kFp16, kAbs>, 32 * kBwdWarps, 0);
+    if (bps <= 0) bps = 1;
+  }
+  k_blend_backward<kFp16, kAbs><<<s.num_sms * bps, 32 * kBwdWarps, 0, stream>>>(
+      s.ranges, s.bucket_offsets, s.live_buckets, s.inst_prim[s.tile_result], s.mean2d, s.conic_opacity, s.color,
+      s.prim_info, image, grad_image, s.n_contrib, s.ckpt, s.counts, cam, s.helpers);
 }
 
 }  // namespace
@@ -453,26 +560,27 @@ void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, 
     k_blend_forward_f16<<<grid, kF16Threads, 0, stream>>>(
         s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.prim_info, s.counts, cam,
         reinterpret_cast<__half*>(image), reinterpret_cast<__half*>(alpha), reinterpret_cast<uint16_t*>(s.n_contrib),
-        s.tile_max_contrib, s.bucket_tile, reinterpret_cast<uint4*>(s.ckpt));
+        s.tile_max_contrib, s.live_buckets, s.counts, reinterpret_cast<uint4*>(s.ckpt));
   else
     k_blend_forward_f32<<<grid, kTilePixels, 0, stream>>>(
         s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.conic_opacity, s.color, s.counts, cam,
         reinterpret_cast<float*>(image), reinterpret_cast<float*>(alpha), s.n_contrib, s.tile_max_contrib,
-        s.bucket_tile, s.ckpt);
+        s.live_buckets, s.counts, s.ckpt);
 }
 
 void launch_blend_backward(const RasterState& s, const DevCamera& cam, int fp16, const void* image,
-                           const void* grad_image, cudaStream_t stream) {
-  const uint32_t* sorted_prim = s.inst_prim[s.tile_result];
-  const int blocks = s.num_sms * 8;
-  if (fp16)
-    k_blend_backward<1><<<blocks, 32 * kBwdWarps, 0, stream>>>(
-        s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.conic_opacity, s.color, s.prim_info, image,
-        grad_image, s.tile_max_contrib, s.n_contrib, s.bucket_tile, s.ckpt, s.counts, cam, s.helpers);
-  else
-    k_blend_backward<0><<<blocks, 32 * kBwdWarps, 0, stream>>>(
-        s.ranges, s.bucket_offsets, sorted_prim, s.mean2d, s.conic_opacity, s.color, s.prim_info, image,
-        grad_image, s.tile_max_contrib, s.n_contrib, s.bucket_tile, s.ckpt, s.counts, cam, s.helpers);
+                           const void* grad_image, int abs_grad, cudaStream_t stream) {
+  if (fp16) {
+    if (abs_grad)
+      run_blend_backward<1, true>(s, cam, image, grad_image, stream);
+    else
+      run_blend_backward<1, false>(s, cam, image, grad_image, stream);
+  } else {
+    if (abs_grad)
+      run_blend_backward<0, true>(s, cam, image, grad_image, stream);
+    else
+      run_blend_backward<0, false>(s, cam, image, grad_image, stream);
+  }
 }
 
 }  // namespace tgs

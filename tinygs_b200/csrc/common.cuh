@@ -18,7 +18,11 @@ constexpr float kMinAlpha = 1.0f / 255.0f;
 constexpr float kMaxAlphaF32 = 0.999f;
 constexpr float kMaxAlphaF16 = 0.99f;
 constexpr float kMinTransmittance = 1e-4f;
-constexpr uint32_t kSequentialTiles = 8;
+constexpr int kSortTileItems = 2048;  // items per radix-sort block
+// the count pass records which of the first kMaskTiles tiles of a
+// rectangle (row-major) a Gaussian touches; instance emission expands those
+// bits and tests only the tiles past them
+constexpr uint32_t kMaskTiles = 64;
 
 // Device-side camera passed by value as a kernel parameter.
 struct DevCamera {
@@ -79,6 +83,9 @@ struct DevCounts {
   uint32_t n_instances;
   uint32_t n_buckets;
   uint32_t overflow;
+  uint32_t n_live_buckets;  // buckets the backward runs (forward appends them)
+  uint32_t n_big;           // Gaussians whose rectangle extends past kMaskTiles tiles
+  uint32_t pad[2];
 };
 
 }  // namespace tgs

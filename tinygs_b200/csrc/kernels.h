@@ -34,6 +34,8 @@ struct RasterState {
   // per Gaussian
   uint32_t* n_touched = nullptr;
   uint32_t* depth_key = nullptr;
+  uint64_t* tile_mask = nullptr;     // hit bits of the first kMaskTiles tiles
+  uint4* big_list = nullptr;         // (Gaussian, first slot, end) with tiles past kMaskTiles
   ushort4* bounds = nullptr;
   float2* mean2d = nullptr;
   float4* conic_opacity = nullptr;  // fp32 path; aliases prim_info storage
@@ -57,7 +59,7 @@ struct RasterState {
   // per pixel
   uint32_t* n_contrib = nullptr;    // uint32 (fp32 path) or uint16 (fp16 path)
   // per bucket
-  uint32_t* bucket_tile = nullptr;
+  uint2* live_buckets = nullptr;    // (tile, bucket in tile) of the buckets the backward runs
   float4* ckpt = nullptr;           // [buckets][256] float4 (fp32) or uint2 (fp16)
   // counts
   DevCounts* counts = nullptr;
@@ -83,11 +85,24 @@ void launch_binning(RasterState& s, int64_t n, const DevCamera& cam, int fp16, c
 void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, void* image,
                           void* alpha, cudaStream_t stream);
 // backward stages
+// abs_grad: also accumulate sum |dL/dmean2d| (densification statistics)
 void launch_blend_backward(const RasterState& s, const DevCamera& cam, int fp16, const void* image,
-                           const void* grad_image, cudaStream_t stream);
+                           const void* grad_image, int abs_grad, cudaStream_t stream);
+// Optimizer step fused into the preprocess backward (per-segment learning
+// rate, decay kind and weight in the reference's segment order).
+struct AdamStepArgs {
+  float lr[6];
+  float decay[6];
+  int kind[6];
+  float beta1, beta2, eps, gradient_scale, bc1, bc2_sqrt, max_grad_1;
+};
+// adam == nullptr: gradients written to `grads` (+= if accumulate).
+// adam != nullptr: Adam applied to g/exp_avg/exp_avg_sq; grads written only
+// where its pointers are non-null.
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g,
                                 const GaussianPtrs& grads, const DevCamera& cam, int accumulate,
-                                float4* dens, cudaStream_t stream);
+                                float4* dens, cudaStream_t stream, const GaussianPtrs* exp_avg = nullptr,
+                                const GaussianPtrs* exp_avg_sq = nullptr, const AdamStepArgs* adam = nullptr);
 
 // losses (loss.cu)
 void launch_l1(int fp16, int width, int height, const void* pred, const void* target,

@@ -116,46 +116,69 @@ __device__ __forceinline__ uint32_t clamp_bound(int v, uint32_t hi) {
   return min(hi, static_cast<uint32_t>(max(0, v)));
 }
 
-// Exact tile count with warp cooperation for large rectangles: the first
-// kSequentialTiles tiles are tested by the owning lane, the rest by the
-// whole warp, one Gaussian at a time.  Every lane must call this.
+// Exact tile count, the warp's (Gaussian, tile) pairs tested 32 at a time:
+// the rectangles of the 32 lanes are laid end to end (row-major inside each)
+// and lane j of a round tests pair base + j for whichever Gaussian owns it,
+// so lanes stay busy whatever the mix of rectangle sizes.  Every lane must
+// call this.  The hit pattern of the first kMaskTiles tiles of the lane's
+// rectangle is returned in `mask`, so that instance emission can expand it
+// instead of testing those tiles again.
 template <int kFp16>
-__device__ uint32_t count_tiles(const TileTest& p, uint4 b, bool active) {
+__device__ uint32_t count_tiles(const TileTest& p, uint4 b, bool active, uint64_t& mask) {
+  const unsigned full = 0xffffffffu;
+  const uint32_t lane = lane_id();
   const uint32_t width = b.y - b.x;
   const uint32_t total = active ? width * (b.w - b.z) : 0u;
-  uint32_t count = 0;
-  const uint32_t seq = min(total, kSequentialTiles);
-  for (uint32_t k = 0; k < seq; ++k) {
-    const uint32_t ty = b.z + k / width, tx = b.x + k % width;
-    count += overlaps<kFp16>(p, tx, ty) ? 1u : 0u;
+  const float inv_w = width > 0 ? 1.0f / static_cast<float>(width) : 0.f;
+  uint32_t incl = total;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(full, incl, o);
+    if (lane >= static_cast<uint32_t>(o)) incl += y;
   }
-  uint32_t big = __ballot_sync(0xffffffffu, total > kSequentialTiles);
-  const uint32_t lane = lane_id();
-  while (big) {
-    const int src = __ffs(big) - 1;
-    big &= big - 1;
-    TileTest q;
-    q.mx = __shfl_sync(0xffffffffu, p.mx, src);
-    q.my = __shfl_sync(0xffffffffu, p.my, src);
-    q.ca = __shfl_sync(0xffffffffu, p.ca, src);
-    q.cb = __shfl_sync(0xffffffffu, p.cb, src);
-    q.cc = __shfl_sync(0xffffffffu, p.cc, src);
-    q.h_xy = __shfl_sync(0xffffffffu, p.h_xy, src);
-    q.h_zw = __shfl_sync(0xffffffffu, p.h_zw, src);
-    q.thr = __shfl_sync(0xffffffffu, p.thr, src);
-    const uint32_t x0 = __shfl_sync(0xffffffffu, b.x, src);
-    const uint32_t w = __shfl_sync(0xffffffffu, width, src);
-    const uint32_t y0 = __shfl_sync(0xffffffffu, b.z, src);
-    const uint32_t n = __shfl_sync(0xffffffffu, total, src);
-    // n, w, x0, y0 are warp-uniform, so every lane runs the same rounds
-    const uint32_t rounds = (n - kSequentialTiles + 31u) / 32u;
-    uint32_t hits = 0;
-    for (uint32_t r = 0; r < rounds; ++r) {
-      const uint32_t k = kSequentialTiles + r * 32u + lane;
-      const bool hit = k < n && overlaps<kFp16>(q, x0 + k % w, y0 + k / w);
-      hits += __popc(__ballot_sync(0xffffffffu, hit));
+  const uint32_t start = incl - total;  // this lane's first pair
+  const uint32_t pairs = __shfl_sync(full, incl, 31);
+  uint32_t count = 0;
+  mask = 0;
+  for (uint32_t base = 0; base < pairs; base += 32u) {
+    const uint32_t slot = base + lane;
+    uint32_t owner = 0;
+#pragma unroll
+    for (uint32_t step = 16; step >= 1; step >>= 1) {
+      const uint32_t o = __shfl_sync(full, start, owner + step);
+      if (o <= slot) owner += step;
     }
-    if (lane == static_cast<uint32_t>(src)) count += hits;
+    TileTest q;
+    q.mx = __shfl_sync(full, p.mx, owner);
+    q.my = __shfl_sync(full, p.my, owner);
+    if constexpr (kFp16) {
+      q.h_xy = __shfl_sync(full, p.h_xy, owner);
+      q.h_zw = __shfl_sync(full, p.h_zw, owner);
+    } else {
+      q.ca = __shfl_sync(full, p.ca, owner);
+      q.cb = __shfl_sync(full, p.cb, owner);
+      q.cc = __shfl_sync(full, p.cc, owner);
+    }
+    q.thr = __shfl_sync(full, p.thr, owner);
+    const uint32_t o_start = __shfl_sync(full, start, owner);
+    const uint32_t o_x = __shfl_sync(full, b.x, owner), o_y = __shfl_sync(full, b.z, owner);
+    const uint32_t o_w = __shfl_sync(full, width, owner);
+    const float o_inv = __shfl_sync(full, inv_w, owner);
+    const uint32_t t = slot - o_start;
+    // row = floor(t / w), exact for t < 2^21 with the half-step offset
+    const uint32_t row = __float2uint_rz((static_cast<float>(t) + 0.5f) * o_inv);
+    const uint32_t col = t - row * o_w;
+    const bool hit = slot < pairs && overlaps<kFp16>(q, o_x + col, o_y + row);
+    const uint32_t m = __ballot_sync(full, hit);
+    // this lane's pairs within the round
+    const uint32_t lo = max(start, base), hi = min(start + total, base + 32u);
+    if (lo < hi) {
+      const uint32_t len = hi - lo;
+      const uint32_t bits = (m >> (lo - base)) & (len == 32u ? full : ((1u << len) - 1u));
+      count += __popc(bits);
+      const uint32_t at = lo - start;  // first tile index of these bits
+      if (at < kMaskTiles) mask |= static_cast<uint64_t>(bits) << at;
+    }
   }
   return count;
 }
@@ -169,7 +192,11 @@ __global__ void __launch_bounds__(kPreBlock)
                  uint32_t* __restrict__ depth_key, ushort4* __restrict__ bounds,
                  float2* __restrict__ mean2d, float4* __restrict__ conic_opacity,
                  PrimInfo16* __restrict__ prim_info, float* __restrict__ color,
-                 uint32_t* __restrict__ block_visible) {
+                 uint64_t* __restrict__ tile_mask, float4* __restrict__ helpers,
+                 uint32_t* __restrict__ block_visible, int rest_vec) {
+  // higher-order SH rows of the warp's 32 Gaussians, loaded coalesced (one
+  // row per lane would touch 32 cache lines per load instruction)
+  __shared__ __align__(16) float s_rest[kPreBlock / 32][32 * 45];
   const uint32_t i = blockIdx.x * kPreBlock + threadIdx.x;
   const bool in_range = i < n;
   const uint32_t gi = in_range ? i : (n > 0 ? n - 1 : 0);
@@ -198,6 +225,7 @@ __global__ void __launch_bounds__(kPreBlock)
   const bool warp_alive = __ballot_sync(0xffffffffu, active) != 0u;
 
   uint32_t touched = 0;
+  uint64_t hits = 0;
   uint4 rect = make_uint4(0, 0, 0, 0);
   float2 m2 = make_float2(0.f, 0.f);
   float3 conic = make_float3(0.f, 0.f, 0.f);
@@ -252,14 +280,35 @@ __global__ void __launch_bounds__(kPreBlock)
     tt.h_xy = hxy;
     tt.h_zw = hzw;
     tt.thr = thr;
-    if (__ballot_sync(0xffffffffu, active) != 0u) touched = count_tiles<kFp16>(tt, rect, active);
+    if (__ballot_sync(0xffffffffu, active) != 0u) touched = count_tiles<kFp16>(tt, rect, active, hits);
     if (!active) touched = 0;
+  }
+
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  if (active_bases > 1 && __ballot_sync(0xffffffffu, in_range && touched > 0) != 0u) {
+    const uint32_t first = i - lane;  // < n: some lane is in range
+    const uint32_t cnt = min(32u, n - first);
+    const float* src = sh_rest + 45 * static_cast<size_t>(first);
+    float* dst = s_rest[warp];
+    if (rest_vec && cnt == 32u) {
+      for (uint32_t e = lane; e < 32u * 45u / 4u; e += 32u)
+        reinterpret_cast<float4*>(dst)[e] = reinterpret_cast<const float4*>(src)[e];
+    } else {
+      for (uint32_t e = lane; e < cnt * 45u; e += 32u) dst[e] = src[e];
+    }
+    __syncwarp();
   }
 
   if (in_range) {
     n_touched[i] = touched;
     if (touched > 0) {
       depth_key[i] = __float_as_uint(depth);
+      tile_mask[i] = hits;
+      // the blend backward accumulates into these
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      helpers[3 * i] = z;
+      helpers[3 * i + 1] = z;
+      helpers[3 * i + 2] = z;
       bounds[i] = make_ushort4(static_cast<unsigned short>(rect.x), static_cast<unsigned short>(rect.y),
                                static_cast<unsigned short>(rect.z), static_cast<unsigned short>(rect.w));
       mean2d[i] = m2;
@@ -270,13 +319,16 @@ __global__ void __launch_bounds__(kPreBlock)
       if (active_bases > 1) {
         const float dx = mx3 - cam.pos.x, dy = my3 - cam.pos.y, dz = mz3 - cam.pos.z;
         const float inv = rsqrtf(dx * dx + dy * dy + dz * dz);
-        float b[15];
+        float b[15] = {};
         const int nb = sh_basis(dx * inv, dy * inv, dz * inv, active_bases, b);
-        const float* rest = sh_rest + 45 * static_cast<size_t>(i);
-        for (int k = 0; k < nb; ++k) {
-          col.x += b[k] * rest[3 * k];
-          col.y += b[k] * rest[3 * k + 1];
-          col.z += b[k] * rest[3 * k + 2];
+        const float* rest = s_rest[warp] + 45 * lane;  // 45 words apart: no bank conflicts
+#pragma unroll
+        for (int k = 0; k < 15; ++k) {
+          if (k < nb) {
+            col.x += b[k] * rest[3 * k];
+            col.y += b[k] * rest[3 * k + 1];
+            col.z += b[k] * rest[3 * k + 2];
+          }
         }
       }
       if constexpr (kFp16) {
@@ -303,21 +355,57 @@ __global__ void __launch_bounds__(kPreBlock)
 
 // --------------------------------------------------------------- backward
 
-// dL/d(direction) contributions of each SH basis function (derivatives of the
-// real SH basis written out per band; fastgs_ours/kernels_backward.cuh:22-86).
-__device__ __forceinline__ float3 sh_backward(const float* __restrict__ rest, float* __restrict__ g_rest,
-                                              float3 gc, float3 dir_raw, int active_bases, bool accumulate,
-                                              float3& g_dc_out) {
-  g_dc_out = make_float3(0.28209479177387814f * gc.x, 0.28209479177387814f * gc.y,
-                         0.28209479177387814f * gc.z);
+// The backward works on one warp's 32 consecutive Gaussians at a time.  The
+// 59 parameter floats of those Gaussians are staged in shared memory by
+// coalesced asynchronous copies (slice layout per warp, in floats: means 96,
+// opacity 32, rotation 128, log-scale 96, sh0 96, sh1..3 1440).  Each lane
+// computes its Gaussian's gradients: the 14 geometry and sh0 floats go to a
+// shared gradient slice; the 45 higher-band SH gradients are the outer
+// product of the 15 basis values and dL/dcolour, so only those 18 floats are
+// kept.  The write-out (gradients, or the Adam step) then streams every
+// segment with coalesced, 16-byte accesses.
+constexpr int kWarpGaussians = 32;
+constexpr int kSliceFloats = 59 * kWarpGaussians;  // 1888
+constexpr int kGeomFloats = 14 * kWarpGaussians;   // 448: segments 0..4
+constexpr int kShStride = 19;                      // 15 basis + 3 dL/dcolour, odd: no bank conflicts
+constexpr int kShFloats = kShStride * kWarpGaussians;
+constexpr int kWarpFloats = kSliceFloats + kGeomFloats + kShFloats;  // 2944
+constexpr int kBwdWarps = 4;
+__host__ __device__ constexpr int seg_width(int k) {
+  return k == 0 ? 3 : k == 1 ? 1 : k == 2 ? 4 : k == 3 ? 3 : k == 4 ? 3 : 45;
+}
+__host__ __device__ constexpr int seg_off(int k) {
+  return k == 0 ? 0 : k == 1 ? 96 : k == 2 ? 128 : k == 3 ? 256 : k == 4 ? 352 : 448;
+}
+
+struct SegPtrs {
+  float* p[6];
+};
+
+struct AdamArgs {
+  float lr[6];
+  float decay[6];
+  int kind[6];
+  float beta1, beta2, eps, gscale, bc1, bc2_sqrt, max_g;
+};
+
+// SH colour backward (fastgs_ours/kernels_backward.cuh:22-86): writes the 45
+// higher-band gradients and returns dL/dposition through the view direction.
+__device__ __forceinline__ float3 sh_backward_slice(const float* __restrict__ rest, float* __restrict__ sb,
+                                                    float3 gc, float3 dir_raw, int active_bases) {
+  // sb: 15 basis values (zero past the active band) then dL/dcolour; the
+  // gradient of rest[k][c] is sb[k] * sb[15 + c]
+  sb[15] = gc.x;
+  sb[16] = gc.y;
+  sb[17] = gc.z;
   if (active_bases <= 1) {
-    if (!accumulate)
-      for (int k = 0; k < 45; ++k) g_rest[k] = 0.f;
+#pragma unroll
+    for (int k = 0; k < 15; ++k) sb[k] = 0.f;
     return make_float3(0.f, 0.f, 0.f);
   }
   const float inv = rsqrtf(dir_raw.x * dir_raw.x + dir_raw.y * dir_raw.y + dir_raw.z * dir_raw.z);
   const float x = dir_raw.x * inv, y = dir_raw.y * inv, z = dir_raw.z * inv;
-  float b[15];
+  float b[15] = {};
   const int nb = sh_basis(x, y, z, active_bases, b);
   float dbx[15], dby[15], dbz[15];
 #pragma unroll
@@ -345,21 +433,16 @@ __device__ __forceinline__ float3 sh_backward(const float* __restrict__ rest, fl
     dbx[14] = -1.7701307697799304f * xx + 1.7701307697799304f * yy; dby[14] = 3.5402615395598609f * xy;
   }
   float3 gd = make_float3(0.f, 0.f, 0.f);
+#pragma unroll
   for (int k = 0; k < 15; ++k) {
     if (k < nb) {
-      const float r0 = rest[3 * k], r1 = rest[3 * k + 1], r2 = rest[3 * k + 2];
-      const float g0 = b[k] * gc.x, g1 = b[k] * gc.y, g2 = b[k] * gc.z;
-      if (accumulate) {
-        g_rest[3 * k] += g0; g_rest[3 * k + 1] += g1; g_rest[3 * k + 2] += g2;
-      } else {
-        g_rest[3 * k] = g0; g_rest[3 * k + 1] = g1; g_rest[3 * k + 2] = g2;
-      }
-      const float d = r0 * gc.x + r1 * gc.y + r2 * gc.z;
+      sb[k] = b[k];
+      const float d = rest[3 * k] * gc.x + rest[3 * k + 1] * gc.y + rest[3 * k + 2] * gc.z;
       gd.x += dbx[k] * d;
       gd.y += dby[k] * d;
       gd.z += dbz[k] * d;
-    } else if (!accumulate) {
-      g_rest[3 * k] = 0.f; g_rest[3 * k + 1] = 0.f; g_rest[3 * k + 2] = 0.f;
+    } else {
+      sb[k] = 0.f;
     }
   }
   // through the normalisation of the view direction
@@ -372,62 +455,43 @@ __device__ __forceinline__ float3 sh_backward(const float* __restrict__ rest, fl
                      (-xz * gd.x - yz * gd.y + (xx + yy) * gd.z) * r);
 }
 
-__device__ __forceinline__ void put(float* p, float v, bool acc) {
-  if (acc) *p += v; else *p = v;
-}
-
-// Preprocess backward: conic -> 2D covariance -> 3D covariance -> (log-scale,
-// quaternion); mean2d (+ frustum clamp mask) -> mean3d; colour -> SH (+ view
-// direction) -> mean3d; densification accumulators.  Reference:
-// fastgs_ours/kernels_backward.cuh:88-352 (including its 2D-covariance
-// off-diagonal term without the factor 2, lines 210-214).
-__global__ void __launch_bounds__(128)
-    k_preprocess_backward(const float* __restrict__ means, const float4* __restrict__ rotations,
-                          const float* __restrict__ scales, const float* __restrict__ sh_rest,
-                          int active_bases, uint32_t n, DevCamera cam,
-                          const uint32_t* __restrict__ n_touched, const float4* __restrict__ helpers,
-                          float* __restrict__ g_means, float* __restrict__ g_opac,
-                          float4* __restrict__ g_rot, float* __restrict__ g_scales,
-                          float* __restrict__ g_sh0, float* __restrict__ g_sh_rest, int accumulate,
-                          float4* __restrict__ dens, const DevCounts* __restrict__ counts) {
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const bool acc = accumulate != 0;
-  // an overflowed forward left no valid backward scratch: treat as untouched
-  if (n_touched[i] == 0 || counts->overflow != 0u) {
-    if (!acc) {
-      for (int k = 0; k < 3; ++k) {
-        g_means[3 * i + k] = 0.f; g_scales[3 * i + k] = 0.f; g_sh0[3 * i + k] = 0.f;
-      }
-      g_opac[i] = 0.f;
-      g_rot[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      float* gr = g_sh_rest + 45 * static_cast<size_t>(i);
-      for (int k = 0; k < 45; ++k) gr[k] = 0.f;
-    }
-    return;
-  }
-  const float4 h0 = helpers[3 * i], h1 = helpers[3 * i + 1], h2 = helpers[3 * i + 2];
+// All parameter gradients of one Gaussian from its screen-space gradients:
+// conic -> 2D covariance -> 3D covariance -> (log-scale, quaternion);
+// mean2d (+ frustum clamp mask) -> mean3d; colour -> SH (+ view direction)
+// -> mean3d.  Reference: fastgs_ours/kernels_backward.cuh:88-352, including
+// its 2D-covariance off-diagonal term without the factor 2 (lines 210-214,
+// consistent with its halved dL/dconic.y) and its raw-quaternion gradient
+// divided by |q|^3 (lines 328-332).  th / g are the warp's parameter and
+// geometry-gradient slices (stride per segment: its width times 32), sb the
+// lane's basis / dL/dcolour row.
+__device__ __forceinline__ void gaussian_backward(const float* __restrict__ th, float* __restrict__ g,
+                                                  float* __restrict__ sb, int lane, const float4 h0,
+                                                  const float4 h1, const float4 h2, int active_bases,
+                                                  const DevCamera& cam) {
   const float gmx = h0.x, gmy = h0.y;
   const float gca = h1.x, gcb = h1.y, gcc = h1.z;
-  const float gop = h1.w;
   const float3 gcol = make_float3(h2.x, h2.y, h2.z);
-
-  const float m0 = means[3 * i], m1 = means[3 * i + 1], m2 = means[3 * i + 2];
-  float3 g_dc;
-  const float3 dmc = sh_backward(sh_rest + 45 * static_cast<size_t>(i), g_sh_rest + 45 * static_cast<size_t>(i),
-                                 gcol, make_float3(m0 - cam.pos.x, m1 - cam.pos.y, m2 - cam.pos.z),
-                                 active_bases, acc, g_dc);
-  put(&g_sh0[3 * i], g_dc.x, acc);
-  put(&g_sh0[3 * i + 1], g_dc.y, acc);
-  put(&g_sh0[3 * i + 2], g_dc.z, acc);
-  put(&g_opac[i], gop, acc);
+  const float* tm = th + 3 * lane;
+  const float m0 = tm[0], m1 = tm[1], m2 = tm[2];
+  const float* tr = th + 128 + 4 * lane;
+  const float4 q = make_float4(tr[0], tr[1], tr[2], tr[3]);
+  const float* ts = th + 256 + 3 * lane;
+  float* g_means = g + 3 * lane;
+  float* g_rot = g + 128 + 4 * lane;
+  float* g_scales = g + 256 + 3 * lane;
+  float* g_sh0 = g + 352 + 3 * lane;
+  const float3 dmc = sh_backward_slice(th + 448 + 45 * lane, sb, gcol,
+                                       make_float3(m0 - cam.pos.x, m1 - cam.pos.y, m2 - cam.pos.z), active_bases);
+  g_sh0[0] = 0.28209479177387814f * gcol.x;
+  g_sh0[1] = 0.28209479177387814f * gcol.y;
+  g_sh0[2] = 0.28209479177387814f * gcol.z;
+  g[96 + lane] = h1.w;  // opacity: already times (1 - opacity)
 
   const float depth = cam.r3.x * m0 + cam.r3.y * m1 + cam.r3.z * m2 + cam.r3.w;
   const float x = (cam.r1.x * m0 + cam.r1.y * m1 + cam.r1.z * m2 + cam.r1.w) / depth;
   const float y = (cam.r2.x * m0 + cam.r2.y * m1 + cam.r2.z * m2 + cam.r2.w) / depth;
-  const float e0 = __expf(scales[3 * i]), e1 = __expf(scales[3 * i + 1]), e2 = __expf(scales[3 * i + 2]);
+  const float e0 = __expf(ts[0]), e1 = __expf(ts[1]), e2 = __expf(ts[2]);
   const float var[3] = {e0 * e0, e1 * e1, e2 * e2};
-  const float4 q = rotations[i];
   const float qn = q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
   const Rot R = make_rotation(q.x, q.y, q.z, q.w, qn);
   float rs[3][3];
@@ -465,10 +529,9 @@ __global__ void __launch_bounds__(128)
   const float dc0 = e.j11 * (gmx - dj13c / depth);
   const float dc1 = e.j22 * (gmy - dj23c / depth);
   const float dc2 = -e.j11 * (x * gmx + h1z / depth) - e.j22 * (y * gmy + h2z / depth);
-  put(&g_means[3 * i], (cam.r1.x * dc0 + cam.r2.x * dc1 + cam.r3.x * dc2) + dmc.x, acc);
-  put(&g_means[3 * i + 1], (cam.r1.y * dc0 + cam.r2.y * dc1 + cam.r3.y * dc2) + dmc.y, acc);
-  put(&g_means[3 * i + 2], (cam.r1.z * dc0 + cam.r2.z * dc1 + cam.r3.z * dc2) + dmc.z, acc);
-
+  g_means[0] = (cam.r1.x * dc0 + cam.r2.x * dc1 + cam.r3.x * dc2) + dmc.x;
+  g_means[1] = (cam.r1.y * dc0 + cam.r2.y * dc1 + cam.r3.y * dc2) + dmc.y;
+  g_means[2] = (cam.r1.z * dc0 + cam.r2.z * dc1 + cam.r3.z * dc2) + dmc.z;
   const float es[3] = {e0, e1, e2};
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
@@ -476,7 +539,7 @@ __global__ void __launch_bounds__(128)
                      R.r[2][k] * R.r[2][k] * d3[5] +
                      2.0f * (R.r[0][k] * R.r[1][k] * d3[1] + R.r[0][k] * R.r[2][k] * d3[2] +
                              R.r[1][k] * R.r[2][k] * d3[4]);
-    put(&g_scales[3 * i + k], 2.0f * es[k] * es[k] * dv, acc);
+    g_scales[k] = 2.0f * es[k] * es[k] * dv;
   }
   float dR[3][3];
 #pragma unroll
@@ -491,25 +554,220 @@ __global__ void __launch_bounds__(128)
   const float hn = R.qxx * dqxx + R.qyy * dqyy + R.qzz * dqzz + R.qxy * dqxy + R.qxz * dqxz + R.qyz * dqyz +
                    R.qrx * dqrx + R.qry * dqry + R.qrz * dqrz;
   const float den = qn * __fsqrt_rn(qn);
-  const float4 gq = make_float4(2.0f * (q.y * dqrx + q.z * dqry + q.w * dqrz - q.x * hn) / den,
-                                2.0f * (2.0f * q.y * dqxx + q.z * dqxy + q.w * dqxz + q.x * dqrx - q.y * hn) / den,
-                                2.0f * (2.0f * q.z * dqyy + q.y * dqxy + q.w * dqyz + q.x * dqry - q.z * hn) / den,
-                                2.0f * (2.0f * q.w * dqzz + q.y * dqxz + q.z * dqyz + q.x * dqrz - q.w * hn) / den);
-  if (acc) {
-    float4 o = g_rot[i];
-    g_rot[i] = make_float4(o.x + gq.x, o.y + gq.y, o.z + gq.z, o.w + gq.w);
+  g_rot[0] = 2.0f * (q.y * dqrx + q.z * dqry + q.w * dqrz - q.x * hn) / den;
+  g_rot[1] = 2.0f * (2.0f * q.y * dqxx + q.z * dqxy + q.w * dqxz + q.x * dqrx - q.y * hn) / den;
+  g_rot[2] = 2.0f * (2.0f * q.z * dqyy + q.y * dqxy + q.w * dqyz + q.x * dqry - q.z * hn) / den;
+  g_rot[3] = 2.0f * (2.0f * q.w * dqzz + q.y * dqxz + q.z * dqyz + q.x * dqrz - q.w * hn) / den;
+}
+
+__device__ __forceinline__ float lerp_adam(float v0, float v1, float t) {
+  // fma form of v0 + t (v1 - v0), simple_adam.cu:24-26
+  return fmaf(t, v1, fmaf(-t, v0, v0));
+}
+
+// Adam update of one element (simple_adam.cu:105-152).
+__device__ __forceinline__ void adam_element(float& th, float g_raw, float& m, float& v, float lr, int kind,
+                                             float decay, const AdamArgs& a) {
+  float g = a.gscale * g_raw;
+  if (kind == 1) {
+    const float sg = 1.0f / (1.0f + __expf(-th));
+    g = g + decay * (sg * (1.0f - sg));
+  } else if (kind == 2) {
+    g = g + decay * __expf(th);
+  }
+  if (a.max_g != 0.0f) g = copysignf(fminf(fabsf(g), a.max_g), g);
+  m = lerp_adam(m, g, 1.0f - a.beta1);
+  v = lerp_adam(v, g * g, 1.0f - a.beta2);
+  const float mh = m / a.bc1;
+  const float den = sqrtf(v) / a.bc2_sqrt + a.eps;
+  th -= mh * lr / den;
+}
+
+// 16-byte (or 4-byte) asynchronous global -> shared copies (cp.async), so
+// that the loads of a whole warp slice are in flight at once.
+__device__ __forceinline__ void cp_async16(float* smem_dst, const float* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kPending));
+}
+
+// Copy the warp's slice of six segments (rows of `cnt` Gaussians) into
+// shared memory.  Full slices of 16-byte aligned segments move in 16-byte
+// chunks; anything else in 4-byte ones.
+__device__ __forceinline__ void stage_slice(const SegPtrs& src, float* dst, uint32_t first, uint32_t cnt,
+                                            uint32_t lane, bool vec) {
+#pragma unroll
+  for (int k = 0; k < 6; ++k) {
+    const int w = seg_width(k);
+    const float* s = src.p[k] + static_cast<size_t>(first) * w;
+    float* d = dst + seg_off(k);
+    const uint32_t count = cnt * w;
+    if (vec) {
+      for (uint32_t e = 4 * lane; e < count; e += 128) cp_async16(d + e, s + e);
+    } else {
+      for (uint32_t e = lane; e < count; e += 32) cp_async4(d + e, s + e);
+    }
+  }
+}
+
+// Gradient of element e of segment k of the warp slice.
+template <int k>
+__device__ __forceinline__ float slice_grad(const float* __restrict__ g, const float* __restrict__ sb, uint32_t e) {
+  if constexpr (k < 5) {
+    return g[seg_off(k) + e];
   } else {
-    g_rot[i] = gq;
+    const uint32_t gl = e / 45u, r = e - 45u * gl, band = r / 3u, c = r - 3u * band;
+    return sb[gl * kShStride + band] * sb[gl * kShStride + 15 + c];
   }
-  if (dens != nullptr) {
-    float4 d = dens[i];
-    d.x += 1.0f;
-    const float ux = gmx * (0.5f * cam.w), uy = gmy * (0.5f * cam.h);
-    d.y += sqrtf(ux * ux + uy * uy);
-    const float vx = h0.z * (0.5f * cam.w), vy = h0.w * (0.5f * cam.h);
-    d.z += sqrtf(vx * vx + vy * vy);
-    dens[i] = d;
+}
+
+// Write-out of segment k: gradients (=, or += when accumulate) or, when
+// kAdam, the Adam step on (params, exp_avg, exp_avg_sq) plus the optional
+// gradient store.
+template <bool kAdam, int k>
+__device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
+                                              const SegPtrs& exp_avg_sq, const AdamArgs& adam, int accumulate,
+                                              const float* __restrict__ th, const float* __restrict__ g,
+                                              const float* __restrict__ sb, uint32_t first, uint32_t cnt,
+                                              uint32_t lane, bool v16) {
+  constexpr int w = seg_width(k);
+  const size_t base = static_cast<size_t>(first) * w;
+  const uint32_t count = cnt * w;
+  float* G = grads.p[k] != nullptr ? grads.p[k] + base : nullptr;
+  if constexpr (kAdam) {
+    const float* ts = th + seg_off(k);
+    float* P = params.p[k] + base;
+    float* M = exp_avg.p[k] + base;
+    float* V = exp_avg_sq.p[k] + base;
+    const float lr = adam.lr[k], decay = adam.decay[k];
+    const int kind = adam.kind[k];
+    if (v16) {
+#pragma unroll 2
+      for (uint32_t e4 = lane; e4 < count / 4; e4 += 32) {
+        float4 t = reinterpret_cast<const float4*>(ts)[e4];
+        float4 m = reinterpret_cast<const float4*>(M)[e4];
+        float4 v = reinterpret_cast<const float4*>(V)[e4];
+        const float4 gv = make_float4(slice_grad<k>(g, sb, 4 * e4), slice_grad<k>(g, sb, 4 * e4 + 1),
+                                      slice_grad<k>(g, sb, 4 * e4 + 2), slice_grad<k>(g, sb, 4 * e4 + 3));
+        adam_element(t.x, gv.x, m.x, v.x, lr, kind, decay, adam);
+        adam_element(t.y, gv.y, m.y, v.y, lr, kind, decay, adam);
+        adam_element(t.z, gv.z, m.z, v.z, lr, kind, decay, adam);
+        adam_element(t.w, gv.w, m.w, v.w, lr, kind, decay, adam);
+        reinterpret_cast<float4*>(P)[e4] = t;
+        reinterpret_cast<float4*>(M)[e4] = m;
+        reinterpret_cast<float4*>(V)[e4] = v;
+        if (G != nullptr) reinterpret_cast<float4*>(G)[e4] = gv;
+      }
+    } else {
+      for (uint32_t e = lane; e < count; e += 32) {
+        float t = ts[e], m = M[e], v = V[e];
+        const float gv = slice_grad<k>(g, sb, e);
+        adam_element(t, gv, m, v, lr, kind, decay, adam);
+        P[e] = t;
+        M[e] = m;
+        V[e] = v;
+        if (G != nullptr) G[e] = gv;
+      }
+    }
+  } else {
+    if (v16) {
+      for (uint32_t e4 = lane; e4 < count / 4; e4 += 32) {
+        float4 gv = make_float4(slice_grad<k>(g, sb, 4 * e4), slice_grad<k>(g, sb, 4 * e4 + 1),
+                                slice_grad<k>(g, sb, 4 * e4 + 2), slice_grad<k>(g, sb, 4 * e4 + 3));
+        if (accumulate) {
+          // untouched Gaussians keep their gradient (+= 0)
+          const float4 o = reinterpret_cast<const float4*>(G)[e4];
+          gv = make_float4(o.x + gv.x, o.y + gv.y, o.z + gv.z, o.w + gv.w);
+        }
+        reinterpret_cast<float4*>(G)[e4] = gv;
+      }
+    } else {
+      for (uint32_t e = lane; e < count; e += 32) {
+        const float gv = slice_grad<k>(g, sb, e);
+        G[e] = accumulate ? G[e] + gv : gv;
+      }
+    }
   }
+}
+
+// kAdam == false: gradients written (or added, accumulate) to `grads`.
+// kAdam == true: the Adam step is applied to params / exp_avg / exp_avg_sq
+// directly from the shared-memory gradients (the gradient arena is written
+// only if `grads` is given), which is tgs_raster_backward(accumulate = 0)
+// followed by tgs_adam_step without the gradient round trip through HBM.
+// The moments of the warp's Gaussians are prefetched into L2 (bulk
+// prefetch) at the start, so their reads in the write-out hit L2.
+template <bool kAdam>
+__global__ void __launch_bounds__(32 * kBwdWarps)
+    k_preprocess_backward(SegPtrs params, SegPtrs grads, SegPtrs exp_avg, SegPtrs exp_avg_sq, AdamArgs adam,
+                          int accumulate, int vec, int active_bases, uint32_t n, DevCamera cam,
+                          const uint32_t* __restrict__ n_touched, const float4* __restrict__ helpers,
+                          float4* __restrict__ dens, const DevCounts* __restrict__ counts) {
+  __shared__ __align__(16) float smem[kBwdWarps * kWarpFloats];
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const uint32_t first = (blockIdx.x * kBwdWarps + warp) * kWarpGaussians;
+  if (first >= n) return;
+  const uint32_t cnt = min(static_cast<uint32_t>(kWarpGaussians), n - first);
+  const bool v16 = vec != 0 && cnt == kWarpGaussians;
+  float* th = smem + warp * kWarpFloats;
+  float* g = th + kSliceFloats;
+  float* sb = g + kGeomFloats;
+  if constexpr (kAdam) {
+    if (v16) {
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        if (lane == static_cast<uint32_t>(k) || lane == static_cast<uint32_t>(k + 6)) {
+          const float* ptr = (lane < 6u ? exp_avg.p[k] : exp_avg_sq.p[k]) + static_cast<size_t>(first) * seg_width(k);
+          const uint32_t bytes = 4u * kWarpGaussians * seg_width(k);
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(ptr), "r"(bytes) : "memory");
+        }
+      }
+    }
+  }
+  stage_slice(params, th, first, cnt, lane, v16);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncwarp();
+  const bool ok = counts->overflow == 0u;
+  const uint32_t i = first + lane;
+  const bool touched = ok && lane < cnt && n_touched[i] > 0;
+  float* my_sb = sb + kShStride * lane;
+  if (touched) {
+    const float4 h0 = helpers[3 * i], h1 = helpers[3 * i + 1], h2 = helpers[3 * i + 2];
+    gaussian_backward(th, g, my_sb, lane, h0, h1, h2, active_bases, cam);
+    if (dens != nullptr) {
+      float4 d = dens[i];
+      d.x += 1.0f;
+      const float ux = h0.x * (0.5f * cam.w), uy = h0.y * (0.5f * cam.h);
+      d.y += sqrtf(ux * ux + uy * uy);
+      const float vx = h0.z * (0.5f * cam.w), vy = h0.w * (0.5f * cam.h);
+      d.z += sqrtf(vx * vx + vy * vy);
+      dens[i] = d;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+#pragma unroll
+      for (int c = 0; c < seg_width(k); ++c) g[seg_off(k) + seg_width(k) * lane + c] = 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < 18; ++c) my_sb[c] = 0.f;
+  }
+  __syncwarp();
+  write_segment<kAdam, 0>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
+  write_segment<kAdam, 1>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
+  write_segment<kAdam, 2>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
+  write_segment<kAdam, 3>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
+  write_segment<kAdam, 4>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
+  write_segment<kAdam, 5>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
 }
 
 }  // namespace
@@ -520,28 +778,64 @@ void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCam
   const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
   const uint32_t blocks = (n + kPreBlock - 1) / kPreBlock;
   if (blocks == 0) return;
+  const int rest_vec = (reinterpret_cast<uintptr_t>(g.sh_rest) & 15u) == 0;
   if (fp16)
     k_preprocess<1><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, s.block_sums);
+        s.prim_info, s.color, s.tile_mask, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
   else
     k_preprocess<0><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, s.block_sums);
+        s.prim_info, s.color, s.tile_mask, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
 }
 
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, const GaussianPtrs& grads,
-                                const DevCamera& cam, int accumulate, float4* dens, cudaStream_t stream) {
+                                const DevCamera& cam, int accumulate, float4* dens, cudaStream_t stream,
+                                const GaussianPtrs* exp_avg, const GaussianPtrs* exp_avg_sq,
+                                const AdamStepArgs* adam) {
   const uint32_t n = static_cast<uint32_t>(g.n);
+  if (n == 0) return;
   const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
-  const uint32_t blocks = (n + 127) / 128;
-  if (blocks == 0) return;
-  k_preprocess_backward<<<blocks, 128, 0, stream>>>(
-      g.means, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh_rest, active_bases, n, cam,
-      s.n_touched, reinterpret_cast<const float4*>(s.helpers), grads.means, grads.opacities,
-      reinterpret_cast<float4*>(grads.rotations), grads.scales, grads.sh0, grads.sh_rest, accumulate, dens, s.counts);
+  const uint32_t per_block = kBwdWarps * kWarpGaussians;
+  const uint32_t blocks = (n + per_block - 1) / per_block;
+  auto segs = [](const GaussianPtrs& x) {
+    SegPtrs p{{x.means, x.opacities, x.rotations, x.scales, x.sh0, x.sh_rest}};
+    return p;
+  };
+  auto aligned = [](const SegPtrs& p) {
+    for (float* q : p.p)
+      if (q != nullptr && (reinterpret_cast<uintptr_t>(q) & 15u) != 0) return false;
+    return true;
+  };
+  AdamArgs a{};
+  SegPtrs m{}, v{};
+  if (adam != nullptr) {
+    for (int k = 0; k < 6; ++k) {
+      a.lr[k] = adam->lr[k];
+      a.decay[k] = adam->decay[k];
+      a.kind[k] = adam->kind[k];
+    }
+    a.beta1 = adam->beta1;
+    a.beta2 = adam->beta2;
+    a.eps = adam->eps;
+    a.gscale = adam->gradient_scale;
+    a.bc1 = adam->bc1;
+    a.bc2_sqrt = adam->bc2_sqrt;
+    a.max_g = adam->max_grad_1;
+    m = segs(*exp_avg);
+    v = segs(*exp_avg_sq);
+    const int vec = aligned(segs(g)) && aligned(m) && aligned(v) && aligned(segs(grads));
+    k_preprocess_backward<true><<<blocks, 32 * kBwdWarps, 0, stream>>>(
+        segs(g), segs(grads), m, v, a, 0, vec, active_bases, n, cam, s.n_touched,
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts);
+  } else {
+    const int vec = aligned(segs(g)) && aligned(segs(grads));
+    k_preprocess_backward<false><<<blocks, 32 * kBwdWarps, 0, stream>>>(
+        segs(g), segs(grads), m, v, a, accumulate, vec, active_bases, n, cam, s.n_touched,
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts);
+  }
 }
 
 }  // namespace tgs

@@ -182,6 +182,16 @@ class FastGSB200Rasterizer:
                                            1 if ctx.accumulate else 0, _ptr(ctx.densification_info),
                                            _stream_handle(ctx.stream)), "tgs_raster_backward")
 
+    def set_stage_timing(self, enable: bool) -> None:
+        check(self.lib.tgs_raster_set_stage_timing(self.handle, 1 if enable else 0), "tgs_raster_set_stage_timing")
+
+    def stage_times(self) -> list[float]:
+        """ms of [preprocess, binning, blend forward, blend backward,
+        per-Gaussian backward (+Adam when fused)] of the last forward/backward."""
+        out = (ctypes.c_float * 5)()
+        check(self.lib.tgs_raster_stage_times(self.handle, out), "tgs_raster_stage_times")
+        return list(out)
+
     def counts(self, stream=None) -> TgsRasterCounts:
         c = TgsRasterCounts()
         check(self.lib.tgs_raster_counts(self.handle, ctypes.byref(c), _stream_handle(stream)), "tgs_raster_counts")
@@ -295,6 +305,22 @@ class SimpleAdam:
         self.exp_avg = params.zeros_like()
         self.exp_avg_sq = params.zeros_like()
         self.global_steps = 0
+
+    def fused_backward_step(self, rast: "FastGSB200Rasterizer", ctx: RasterizeContext, scale: float,
+                            write_grads: bool = False) -> None:
+        """rast.backward(ctx) with accumulate=False followed by step(scale),
+        in one pass over the Gaussians (tgs_raster_backward_adam)."""
+        self.global_steps += 1
+        p, m, v = self.params.abi(), self.exp_avg.abi(), self.exp_avg_sq.abi()
+        g = self.grads.abi() if write_grads else None
+        cam = make_camera(ctx.fwd_input)
+        cfg = self.cfg.abi()
+        check(self.lib.tgs_raster_backward_adam(rast.handle, ctypes.byref(p), ctypes.byref(cam),
+                                                rast._dtype(ctx.fwd_output_image), _ptr(ctx.fwd_output_image),
+                                                _ptr(ctx.grad_output_image), ctypes.byref(g) if g else None,
+                                                ctypes.byref(m), ctypes.byref(v), ctypes.byref(cfg),
+                                                self.global_steps, float(scale), _ptr(ctx.densification_info),
+                                                _stream_handle(ctx.stream)), "tgs_raster_backward_adam")
 
     def step(self, scale: float, stream=None, zero_grads: bool = False) -> None:
         self.global_steps += 1

@@ -118,8 +118,11 @@ typedef struct TgsRasterCaps {
 } TgsRasterCaps;
 
 /* Counts of the last forward.  Written on the device; read by
- * tgs_raster_counts().  `overflow` != 0 means a capacity bound was hit and
- * the outputs of that forward are invalid (grow the caps and rerun). */
+ * tgs_raster_counts().  n_visible counts the Gaussians that passed culling
+ * with a non-empty tile rectangle (a superset of those that touch a tile,
+ * whose per-Gaussian tile counts are debug buffer 0).  `overflow` != 0 means
+ * a capacity bound was hit and the outputs of that forward are invalid (grow
+ * the caps and rerun). */
 typedef struct TgsRasterCounts {
     uint32_t n_visible;
     uint32_t n_instances;

@@ -113,8 +113,12 @@ def test_binning_sorted_and_exact(oracle, cuda_lib, fp16):
     if stable.all():
         np.testing.assert_array_equal(ob2["inst_prim"], gb["inst_prim"])
         np.testing.assert_array_equal(ob2["inst_tile"], gb["inst_tile"])
-    assert gb["n_visible"] == int((gp["n_touched"] > 0).sum())
-    np.testing.assert_array_equal(gb["sorted_visible"], ob2["sorted_visible"])
+    # the depth-sorted candidates (non-empty tile rectangle) include the
+    # Gaussians that touch no tile; without them the list is the oracle's
+    touched = gp["n_touched"] > 0
+    assert gb["n_visible"] >= int(touched.sum())
+    sv = gb["sorted_visible"]
+    np.testing.assert_array_equal(sv[touched[sv]], ob2["sorted_visible"])
 
 
 def test_binning_large_footprints_use_warp_path(oracle, cuda_lib):

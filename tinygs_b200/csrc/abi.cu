@@ -138,8 +138,6 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   const size_t np = static_cast<size_t>(s.max_pixels);
   s.n_touched = c.take<uint32_t>(n);
   s.depth_key = c.take<uint32_t>(n);
-  s.tile_mask = c.take<uint64_t>(n);
-  s.big_list = c.take<uint4>(n);
   s.bounds = c.take<ushort4>(n);
   s.mean2d = c.take<float2>(n);
   s.conic_opacity = c.take<float4>(n);
@@ -152,10 +150,21 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   s.vis_idx[1] = c.take<uint32_t>(n);
   s.block_sums = c.take<uint32_t>((n + 255) / 256 + 1);
   s.inst_key[0] = c.take<uint16_t>(ni);
-  s.inst_key[1] = c.take<uint16_t>(ni);
   s.inst_prim[0] = c.take<uint32_t>(ni);
-  s.inst_prim[1] = c.take<uint32_t>(ni);
-  s.sort_max_blocks = static_cast<int64_t>((std::max(n, ni) + kSortTileItems - 1) / kSortTileItems);
+  const size_t ne = static_cast<size_t>(s.cap_entries > 0 ? s.cap_entries : 1);
+  const size_t ns = static_cast<size_t>(s.max_super);
+  s.ent_key[0] = c.take<uint16_t>(ne);
+  s.ent_key[1] = c.take<uint16_t>(ne);
+  s.ent_prim[0] = c.take<uint32_t>(ne);
+  s.ent_prim[1] = c.take<uint32_t>(ne);
+  s.masks = c.take<uint32_t>(ne);
+  s.super_ranges = c.take<uint2>(ns);
+  s.super_chunk = c.take<uint32_t>(ns);
+  s.cap_chunks = static_cast<int64_t>(ne / kChunk + ns + 1);
+  s.chunks = c.take<uint4>(static_cast<size_t>(s.cap_chunks));
+  s.chunk_counts = c.take<uint32_t>(static_cast<size_t>(s.cap_chunks) * kSuperTiles);
+  s.tile_total = c.take<uint32_t>(nt);
+  s.sort_max_blocks = static_cast<int64_t>((std::max(n, ne) + kSortTileItems - 1) / kSortTileItems);
   s.sort_hist = c.take<uint32_t>(256 * static_cast<size_t>(s.sort_max_blocks));
   s.sort_digit_total = c.take<uint32_t>(256);
   s.ranges = c.take<uint2>(nt);
@@ -239,6 +248,10 @@ int tgs_raster_create(const TgsRasterCaps* caps, TgsRaster** out) {
   s.max_h = caps->max_height;
   s.max_tiles = gw * gh;
   s.cap_buckets = s.cap_inst / kBucket + s.max_tiles;
+  // (Gaussian, super-tile) entries: at least one per Gaussian, about 1.5 in
+  // typical scenes; each entry with a hit carries at least one instance
+  s.cap_entries = std::min<int64_t>(0x7fffffffLL, 2 * std::max<int64_t>(s.cap_n, 1) + s.cap_inst / 2);
+  s.max_super = ((gw + kSuperW - 1) / kSuperW) * ((gh + kSuperH - 1) / kSuperH);
   s.max_pixels = static_cast<int64_t>((caps->max_width + 7) / 8 * 8) * ((caps->max_height + 7) / 8 * 8);
   cudaGetDevice(&r->device);
   cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, r->device);

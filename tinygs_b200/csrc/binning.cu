@@ -1,20 +1,30 @@
 // binning.cu -- from per-Gaussian screen footprints to per-tile, depth-ordered
 // primitive lists.
 //
-// Stages (reference: tinygs/src/rasterizer/fastgs_ours/forward.cu:133-260,
-// kernels_forward.cuh:414-567, and the fp16 twins):
-//   1. compaction of visible Gaussians in index order (scan of the per-block
-//      counts the preprocess kernel published),
-//   2. stable LSD radix sort of the visible list by the depth key (float bits),
-//   3. per-Gaussian instance offsets (scan of touched-tile counts in depth
-//      order) and instance emission (tile id, Gaussian id),
-//   4. stable LSD radix sort of the instances by tile id (only the bits the
-//      tile count needs),
-//   5. per-tile [start, end) ranges and bucket offsets.
-// Stable sorts over an index-ordered input give (tile, depth, index) order,
-// a deterministic member of the reference's order set (its ties among equal
-// depths follow atomic arrival order).  All counts stay on the device: the
-// launches are sized from capacities and each kernel reads the live count.
+// Reference: tinygs/src/rasterizer/fastgs_ours/forward.cu:133-260 and
+// kernels_forward.cuh:414-567 (and the fp16 twins): per-Gaussian tile counts,
+// a depth sort, instance emission and a sort of all instances by tile.  The
+// lists produced here are the same -- every tile holds the Gaussians that pass
+// the exact tile test, in (depth, index) order -- built in two levels so that
+// no sort runs over the ~10 instances per Gaussian:
+//   1. compaction of the candidate Gaussians (culling passed, non-empty tile
+//      rectangle) in index order,
+//   2. stable LSD radix sort of the candidates by the depth key (float bits),
+//   3. one entry per (Gaussian, super-tile of 8x4 tiles) its rectangle
+//      overlaps, emitted in depth order, and a stable sort of the entries by
+//      super-tile (one 8-bit pass for up to 256 super-tiles),
+//   4. the entry list of each super-tile is cut into chunks of 1024 entries;
+//      per chunk, the exact tile tests of each entry give a 32-bit hit mask
+//      and per-tile counts (and each Gaussian's touched-tile total),
+//   5. scans give every (chunk, tile) its first slot: tiles in index order,
+//      chunks in depth order inside a tile; the per-tile [start, end) ranges
+//      and bucket offsets fall out of the same scan,
+//   6. per chunk, stable ranks of the entries in each tile (ballots over the
+//      hit masks) place every instance at its final slot.
+// Ties among equal depths follow the index order, a deterministic member of
+// the reference's order set (its ties follow atomic arrival order).  All
+// counts stay on the device: the launches are sized from capacities and each
+// kernel reads the live count.
 #include <cstring>
 
 #include "kernels.h"
@@ -111,13 +121,17 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// 1. visible list in index order
+// 1. candidate list in index order
 __global__ void __launch_bounds__(kScanBlock)
-    k_compact_visible(const uint32_t* __restrict__ n_touched, const uint32_t* __restrict__ depth_key,
+    k_compact_visible(const ushort4* __restrict__ bounds, const uint32_t* __restrict__ depth_key,
                       const uint32_t* __restrict__ block_offsets, uint32_t n, uint32_t* __restrict__ out_key,
                       uint32_t* __restrict__ out_idx) {
   const uint32_t i = blockIdx.x * kScanBlock + threadIdx.x;
-  const bool vis = i < n && n_touched[i] > 0;
+  bool vis = false;
+  if (i < n) {
+    const ushort4 b = bounds[i];
+    vis = b.x < b.y && b.z < b.w;
+  }
   uint32_t total;
   const uint32_t pos = block_exclusive_scan(vis ? 1u : 0u, total) + block_offsets[blockIdx.x];
   if (vis) {
@@ -286,12 +300,32 @@ __global__ void __launch_bounds__(kSortThreads)
   }
 }
 
-// 3a. per-block sums of touched-tile counts over the depth-sorted list
+// Super-tile geometry: 8x4 tiles (128x64 pixels), one bit per tile in a
+// 32-bit hit mask (bit = row * 8 + column inside the super-tile).
+struct SuperRect {
+  uint32_t sx0, sy0, nsx, nsy;
+};
+__device__ __forceinline__ SuperRect super_rect(ushort4 b) {
+  SuperRect r{0, 0, 0, 0};
+  if (b.x < b.y && b.z < b.w) {
+    r.sx0 = b.x / kSuperW;
+    r.sy0 = b.z / kSuperH;
+    r.nsx = (b.y - 1u) / kSuperW - r.sx0 + 1u;
+    r.nsy = (b.w - 1u) / kSuperH - r.sy0 + 1u;
+  }
+  return r;
+}
+
+// 3a. per-block sums of super-tile entry counts over the depth-sorted list
 __global__ void __launch_bounds__(kScanBlock)
-    k_instance_block_sums(const uint32_t* __restrict__ sorted_idx, const uint32_t* __restrict__ n_touched,
-                          const DevCounts* __restrict__ counts, uint32_t* __restrict__ sums) {
+    k_entry_block_sums(const uint32_t* __restrict__ sorted_idx, const ushort4* __restrict__ bounds,
+                       const DevCounts* __restrict__ counts, uint32_t* __restrict__ sums) {
   const uint32_t k = blockIdx.x * kScanBlock + threadIdx.x;
-  const uint32_t v = k < counts->n_visible ? n_touched[sorted_idx[k]] : 0u;
+  uint32_t v = 0;
+  if (k < counts->n_visible) {
+    const SuperRect r = super_rect(bounds[sorted_idx[k]]);
+    v = r.nsx * r.nsy;
+  }
   const uint32_t s = __reduce_add_sync(0xffffffffu, v);
   __shared__ uint32_t ws[kScanBlock / 32];
   if ((threadIdx.x & 31u) == 0) ws[threadIdx.x >> 5] = s;
@@ -303,230 +337,54 @@ __global__ void __launch_bounds__(kScanBlock)
   }
 }
 
-// 3b. instance emission in depth order.  The preprocess pass recorded the
-// hit bits of the first kMaskTiles tiles of every rectangle (row-major), which
-// are all of them for the small rectangles that make up most of a scene.  A
-// warp emits those instances together: it walks its contiguous output range
-// 32 slots at a time, each lane finding the Gaussian that owns its slot and
-// the matching set bit, so the stores are coalesced.  Tiles past the first
-// kMaskTiles of a larger rectangle are queued for k_emit_big: the depth
-// order puts the largest (nearest) Gaussians next to each other, so testing
-// them here would leave a few warps working long after the rest.
-__device__ __forceinline__ uint32_t select_bit(uint64_t m, uint32_t r) {
-  // index of the r-th (0-based) set bit of m; r < popc(m)
-  const uint32_t lo = static_cast<uint32_t>(m);
-  const uint32_t c = __popc(lo);
-  uint32_t word = r < c ? lo : static_cast<uint32_t>(m >> 32);
-  uint32_t rr = r < c ? r : r - c;
-  uint32_t pos = 0;
-#pragma unroll
-  for (uint32_t step = 16; step >= 1; step >>= 1) {
-    const uint32_t below = __popc((word >> pos) & ((1u << step) - 1u));
-    if (rr >= below) {
-      rr -= below;
-      pos += step;
-    }
-  }
-  return (r < c ? 0u : 32u) + pos;
-}
-
-template <int kFp16>
+// 3b. entry emission in depth order: (super-tile id, Gaussian id)
 __global__ void __launch_bounds__(kScanBlock)
-    k_create_instances(const uint32_t* __restrict__ sorted_idx, const uint32_t* __restrict__ n_touched,
-                       const uint64_t* __restrict__ tile_mask, const uint32_t* __restrict__ block_offsets,
-                       const ushort4* __restrict__ bounds, const float2* __restrict__ mean2d,
-                       const float4* __restrict__ conic_opacity, const PrimInfo16* __restrict__ prim_info,
-                       const DevCounts* __restrict__ counts, uint32_t cap, uint32_t grid_w,
-                       uint16_t* __restrict__ inst_key, uint32_t* __restrict__ inst_prim,
-                       uint4* __restrict__ big_list) {
+    k_create_entries(const uint32_t* __restrict__ sorted_idx, const ushort4* __restrict__ bounds,
+                     const uint32_t* __restrict__ block_offsets, const DevCounts* __restrict__ counts,
+                     uint32_t super_w, uint16_t* __restrict__ ent_key, uint32_t* __restrict__ ent_prim) {
   const uint32_t k = blockIdx.x * kScanBlock + threadIdx.x;
-  const bool overflow = counts->overflow != 0u;
-  const bool active = k < counts->n_visible && !overflow;
-  uint32_t prim = 0, cnt = 0;
+  const bool active = k < counts->n_visible && counts->overflow == 0u;
+  uint32_t prim = 0;
+  SuperRect r{0, 0, 0, 0};
   if (active) {
     prim = sorted_idx[k];
-    cnt = n_touched[prim];
+    r = super_rect(bounds[prim]);
   }
   uint32_t total;
-  const uint32_t off = block_exclusive_scan(cnt, total) + block_offsets[blockIdx.x];
-  if (!active) cnt = 0;
-  if (active && off + cnt > cap) cnt = 0;  // cannot happen without overflow
-  // writes stay inside [off, end) whatever happens below
-  const uint32_t end = off + cnt;
-  ushort4 b = make_ushort4(0, 0, 0, 0);
-  uint32_t width = 0, n_tiles = 0, n_mask = 0;
-  uint64_t mask = 0;
-  if (cnt > 0) {
-    b = bounds[prim];
-    width = b.y - b.x;
-    n_tiles = width * static_cast<uint32_t>(b.w - b.z);
-    mask = tile_mask[prim];
-    n_mask = min(static_cast<uint32_t>(__popcll(mask)), cnt);
-  }
-  const float inv_w = width > 0 ? 1.0f / static_cast<float>(width) : 0.f;
-  const uint32_t lane = threadIdx.x & 31u;
-  const unsigned full = 0xffffffffu;
-  // (1) instances from the hit bits; offsets are non-decreasing over lanes
-  const uint32_t w0 = __shfl_sync(full, off, 0), w1 = __shfl_sync(full, end, 31);
-  for (uint32_t base = w0; base < w1; base += 32u) {
-    const uint32_t slot = base + lane;
-    uint32_t owner = 0;
-#pragma unroll
-    for (uint32_t step = 16; step >= 1; step >>= 1) {
-      const uint32_t o = __shfl_sync(full, off, owner + step);
-      if (o <= slot) owner += step;
+  const uint32_t off = block_exclusive_scan(r.nsx * r.nsy, total) + block_offsets[blockIdx.x];
+  if (!active) return;
+  uint32_t o = off;
+  for (uint32_t y = 0; y < r.nsy; ++y)
+    for (uint32_t x = 0; x < r.nsx; ++x, ++o) {
+      ent_key[o] = static_cast<uint16_t>((r.sy0 + y) * super_w + r.sx0 + x);
+      ent_prim[o] = prim;
     }
-    const uint32_t o_off = __shfl_sync(full, off, owner);
-    const uint32_t o_n = __shfl_sync(full, n_mask, owner);
-    const uint32_t o_lo = __shfl_sync(full, static_cast<uint32_t>(mask), owner);
-    const uint32_t o_hi = __shfl_sync(full, static_cast<uint32_t>(mask >> 32), owner);
-    const uint32_t o_x = __shfl_sync(full, static_cast<uint32_t>(b.x), owner);
-    const uint32_t o_y = __shfl_sync(full, static_cast<uint32_t>(b.z), owner);
-    const uint32_t o_w = __shfl_sync(full, width, owner);
-    const float o_inv = __shfl_sync(full, inv_w, owner);
-    const uint32_t o_p = __shfl_sync(full, prim, owner);
-    const uint32_t r = slot - o_off;
-    if (slot < w1 && r < o_n) {
-      const uint32_t q = select_bit((static_cast<uint64_t>(o_hi) << 32) | o_lo, r);
-      // row = floor(q / w), exact with the half-step offset (q < 64)
-      const uint32_t row = __float2uint_rz((static_cast<float>(q) + 0.5f) * o_inv);
-      inst_key[slot] = static_cast<uint16_t>((o_y + row) * grid_w + o_x + (q - row * o_w));
-      inst_prim[slot] = o_p;
-    }
-  }
-  // (2) tiles past the recorded bits: queue (Gaussian, first slot, end)
-  const bool queue = cnt > 0 && n_tiles > kMaskTiles && off + n_mask < end;
-  const uint32_t qm = __ballot_sync(full, queue);
-  uint32_t qbase = 0;
-  if (lane == 0 && qm != 0u) qbase = atomicAdd(const_cast<uint32_t*>(&counts->n_big), __popc(qm));
-  qbase = __shfl_sync(full, qbase, 0);
-  if (queue) big_list[qbase + __popc(qm & lanemask_lt())] = make_uint4(prim, off + n_mask, end, 0u);
-  // a small rectangle with fewer recorded hits than counted (never
-  // expected): pad with a tile id past the grid and report
-  if (cnt > 0 && n_tiles <= kMaskTiles && n_mask < cnt) {
-    atomicOr(const_cast<uint32_t*>(&counts->overflow), kInconsistentTiles);
-    for (uint32_t j = off + n_mask; j < end; ++j) {
-      inst_key[j] = 0xffffu;
-      inst_prim[j] = prim;
-    }
+}
+
+// 4a. [start, end) of each super-tile in the sorted entry list
+__global__ void k_super_ranges(const uint16_t* __restrict__ keys, const DevCounts* __restrict__ counts,
+                               uint2* __restrict__ ranges) {
+  const uint32_t n = counts->overflow ? 0u : counts->n_entries;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint16_t k = keys[i];
+    if (i == 0 || keys[i - 1] != k) ranges[k].x = i;
+    if (i + 1 == n || keys[i + 1] != k) ranges[k].y = i + 1;
   }
 }
 
-// 3c. the tiles past kMaskTiles of the queued Gaussians, one block per
-// Gaussian: each round the block tests 256 consecutive tiles of the
-// rectangle and writes the hits in row-major order at the running slot.
-template <int kFp16>
-__global__ void __launch_bounds__(kScanBlock)
-    k_emit_big(const uint4* __restrict__ big_list, const ushort4* __restrict__ bounds,
-               const float2* __restrict__ mean2d, const float4* __restrict__ conic_opacity,
-               const PrimInfo16* __restrict__ prim_info, DevCounts* __restrict__ counts, uint32_t grid_w,
-               uint16_t* __restrict__ inst_key, uint32_t* __restrict__ inst_prim) {
-  __shared__ uint32_t s_warp[kScanBlock / 32];
-  const uint32_t n_big = counts->overflow ? 0u : counts->n_big;
-  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  for (uint32_t item = blockIdx.x; item < n_big; item += gridDim.x) {
-    const uint4 it = big_list[item];
-    const uint32_t prim = it.x, end = it.z;
-    const ushort4 b = bounds[prim];
-    const uint32_t w = b.y - b.x, nt = w * static_cast<uint32_t>(b.w - b.z);
-    TileTest q{};
-    const float2 mm = mean2d[prim];
-    q.mx = mm.x - 0.5f;
-    q.my = mm.y - 0.5f;
-    if constexpr (kFp16) {
-      const PrimInfo16 rec = prim_info[prim];
-      q.h_xy = rec.conic_xy;
-      q.h_zw = rec.conic_z_opacity;
-      q.thr = __logf(__high2float(rec.conic_z_opacity) * 255.0f);
-    } else {
-      const float4 co = conic_opacity[prim];
-      q.ca = co.x;
-      q.cb = co.y;
-      q.cc = co.z;
-      q.thr = __logf(co.w * 255.0f);
-    }
-    uint32_t cursor = it.y;
-    for (uint32_t t0 = kMaskTiles; t0 < nt; t0 += kScanBlock) {
-      const uint32_t t = t0 + threadIdx.x;
-      const uint32_t ty = b.z + t / w, tx = b.x + t % w;
-      const bool hit = t < nt && overlaps<kFp16>(q, tx, ty);
-      const uint32_t m = __ballot_sync(0xffffffffu, hit);
-      if (lane == 0) s_warp[warp] = __popc(m);
-      __syncthreads();
-      uint32_t before = 0, total = 0;
-#pragma unroll
-      for (int k = 0; k < kScanBlock / 32; ++k) {
-        const uint32_t c = s_warp[k];
-        before += static_cast<uint32_t>(k) < warp ? c : 0u;
-        total += c;
-      }
-      const uint32_t pos = cursor + before + __popc(m & lanemask_lt());
-      if (hit && pos < end) {
-        inst_key[pos] = static_cast<uint16_t>(ty * grid_w + tx);
-        inst_prim[pos] = prim;
-      }
-      cursor += total;
-      __syncthreads();
-    }
-    // a shortfall (never expected) is padded with a tile id past the grid,
-    // which the range pass ignores, and reported
-    if (cursor < end) {
-      if (threadIdx.x == 0) atomicOr(&counts->overflow, kInconsistentTiles);
-      for (uint32_t j = cursor + threadIdx.x; j < end; j += kScanBlock) {
-        inst_key[j] = 0xffffu;
-        inst_prim[j] = prim;
-      }
-    }
-  }
-}
-
-// 5a. tile ranges from the sorted tile ids, 8 keys (16 bytes) per thread
-__global__ void k_tile_ranges(const uint16_t* __restrict__ keys, const DevCounts* __restrict__ counts,
-                              uint32_t n_tiles, uint2* __restrict__ ranges) {
-  const uint32_t n = counts->overflow ? 0u : counts->n_instances;
-  const uint32_t groups = (n + 7u) / 8u;
-  for (uint32_t gi = blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += gridDim.x * blockDim.x) {
-    const uint32_t i0 = gi * 8u;
-    uint16_t k[8];
-    if (i0 + 8u <= n) {
-      const uint4 v = *reinterpret_cast<const uint4*>(keys + i0);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        k[2 * j] = static_cast<uint16_t>(w[j] & 0xffffu);
-        k[2 * j + 1] = static_cast<uint16_t>(w[j] >> 16);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) k[j] = i0 + j < n ? keys[i0 + j] : static_cast<uint16_t>(0xffffu);
-    }
-    // 0xffff is never a tile id in range (the range check below drops it)
-    const uint16_t prev = i0 == 0 ? static_cast<uint16_t>(0xffffu) : keys[i0 - 1];
-    const uint16_t next = i0 + 8u < n ? keys[i0 + 8] : static_cast<uint16_t>(0xffffu);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint16_t kk = k[j];
-      if (kk >= n_tiles) continue;
-      const uint16_t before = j == 0 ? prev : k[j - 1];
-      const uint16_t after = j == 7 ? next : k[j + 1];
-      if (before != kk) ranges[kk].x = i0 + j;
-      if (after != kk) ranges[kk].y = i0 + j + 1;
-    }
-  }
-}
-
-// 5b. bucket offsets (inclusive scan of ceil(count/32) over tiles)
+// 4b. chunk table: each super-tile's entries cut into chunks of kChunk
+// (one block of 1024 threads; thread t owns a contiguous run of super-tiles)
 __global__ void __launch_bounds__(1024)
-    k_bucket_offsets(const uint2* __restrict__ ranges, uint32_t n_tiles, uint32_t* __restrict__ offsets,
-                     DevCounts* __restrict__ counts, uint32_t cap_buckets) {
+    k_chunk_table(const uint2* __restrict__ super_ranges, uint32_t n_super, uint4* __restrict__ chunks,
+                  uint32_t* __restrict__ super_chunk, DevCounts* __restrict__ counts) {
   __shared__ uint32_t warp_sums[32];
   const uint32_t t = threadIdx.x;
-  const uint32_t per = (n_tiles + 1023u) / 1024u;
-  const uint32_t begin = min(n_tiles, t * per), end = min(n_tiles, begin + per);
+  const uint32_t per = (n_super + 1023u) / 1024u;
+  const uint32_t begin = min(n_super, t * per), end = min(n_super, begin + per);
   uint32_t local = 0;
   for (uint32_t k = begin; k < end; ++k) {
-    const uint2 r = ranges[k];
-    local += (r.y - r.x + 31u) / 32u;
+    const uint2 r = super_ranges[k];
+    local += (r.y - r.x + kChunk - 1u) / kChunk;
   }
   const uint32_t lane = t & 31u, warp = t >> 5;
   uint32_t x = local;
@@ -547,16 +405,289 @@ __global__ void __launch_bounds__(1024)
     warp_sums[lane] = w;
   }
   __syncthreads();
-  uint32_t run = (warp == 0 ? 0u : warp_sums[warp - 1]) + x - local;
+  uint32_t c = (warp == 0 ? 0u : warp_sums[warp - 1]) + x - local;
   for (uint32_t k = begin; k < end; ++k) {
-    const uint2 r = ranges[k];
-    run += (r.y - r.x + 31u) / 32u;
-    offsets[k] = run;
+    const uint2 r = super_ranges[k];
+    super_chunk[k] = c;
+    for (uint32_t st = r.x; st < r.y; st += kChunk, ++c) chunks[c] = make_uint4(k, st, min(r.y, st + kChunk), 0u);
+  }
+  if (t == 1023) counts->n_chunks = warp_sums[31];
+}
+
+// Tile-test inputs of Gaussian p, as the preprocess pass derived them.
+template <int kFp16>
+__device__ __forceinline__ TileTest tile_test_of(uint32_t p, const float2* __restrict__ mean2d,
+                                                 const float4* __restrict__ conic_opacity,
+                                                 const PrimInfo16* __restrict__ prim_info) {
+  TileTest q{};
+  const float2 m = mean2d[p];
+  q.mx = m.x - 0.5f;
+  q.my = m.y - 0.5f;
+  if constexpr (kFp16) {
+    const PrimInfo16 rec = prim_info[p];
+    q.h_xy = rec.conic_xy;
+    q.h_zw = rec.conic_z_opacity;
+    q.thr = __logf(__high2float(rec.conic_z_opacity) * 255.0f);
+  } else {
+    const float4 co = conic_opacity[p];
+    q.ca = co.x;
+    q.cb = co.y;
+    q.cc = co.z;
+    q.thr = __logf(co.w * 255.0f);
+  }
+  return q;
+}
+
+// 5a. per chunk: hit mask of every entry (exact tile tests of its rectangle
+// inside the super-tile, the warp's (entry, tile) pairs tested 32 at a time),
+// per-tile hit counts of the chunk, and each Gaussian's touched-tile total.
+template <int kFp16>
+__global__ void __launch_bounds__(kScanBlock)
+    k_chunk_hits(const uint4* __restrict__ chunks, const uint32_t* __restrict__ ent_prim,
+                 const ushort4* __restrict__ bounds, const float2* __restrict__ mean2d,
+                 const float4* __restrict__ conic_opacity, const PrimInfo16* __restrict__ prim_info,
+                 const DevCounts* __restrict__ counts, uint32_t super_w, uint32_t* __restrict__ masks,
+                 uint32_t* __restrict__ chunk_counts, uint32_t* __restrict__ n_touched) {
+  __shared__ uint32_t s_cnt[kSuperTiles];
+  const unsigned full = 0xffffffffu;
+  const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
+  const uint32_t lane = threadIdx.x & 31u;
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const uint4 ch = chunks[c];
+    const uint32_t tx0 = (ch.x % super_w) * kSuperW, ty0 = (ch.x / super_w) * kSuperH;
+    if (threadIdx.x < kSuperTiles) s_cnt[threadIdx.x] = 0;
+    __syncthreads();
+    for (uint32_t e0 = ch.y; e0 < ch.z; e0 += kScanBlock) {
+      const uint32_t e = e0 + threadIdx.x;
+      const bool valid = e < ch.z;
+      uint32_t prim = 0, x0 = 0, y0 = 0, w = 0, h = 0, magic = 0;
+      TileTest tt{};
+      if (valid) {
+        prim = ent_prim[e];
+        const ushort4 b = bounds[prim];
+        x0 = max(static_cast<uint32_t>(b.x), tx0);
+        y0 = max(static_cast<uint32_t>(b.z), ty0);
+        w = min(static_cast<uint32_t>(b.y), tx0 + kSuperW) - x0;
+        h = min(static_cast<uint32_t>(b.w), ty0 + kSuperH) - y0;
+        magic = 255u / w + 1u;  // t / w == (t * magic) >> 8 for t < 33, w <= 8
+        tt = tile_test_of<kFp16>(prim, mean2d, conic_opacity, prim_info);
+      }
+      const uint32_t total = w * h;  // <= 32
+      // lay the lanes' rectangles end to end; lane j tests pair base + j
+      uint32_t incl = total;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(full, incl, o);
+        if (lane >= static_cast<uint32_t>(o)) incl += y;
+      }
+      const uint32_t start = incl - total;
+      const uint32_t pairs = __shfl_sync(full, incl, 31);
+      uint32_t local = 0;  // hits in rectangle order (bit t = row t / w, column t % w)
+      for (uint32_t base = 0; base < pairs; base += 32u) {
+        const uint32_t slot = base + lane;
+        uint32_t owner = 0;
+#pragma unroll
+        for (uint32_t step = 16; step >= 1; step >>= 1) {
+          const uint32_t o = __shfl_sync(full, start, owner + step);
+          if (o <= slot) owner += step;
+        }
+        TileTest q;
+        q.mx = __shfl_sync(full, tt.mx, owner);
+        q.my = __shfl_sync(full, tt.my, owner);
+        if constexpr (kFp16) {
+          q.h_xy = __shfl_sync(full, tt.h_xy, owner);
+          q.h_zw = __shfl_sync(full, tt.h_zw, owner);
+        } else {
+          q.ca = __shfl_sync(full, tt.ca, owner);
+          q.cb = __shfl_sync(full, tt.cb, owner);
+          q.cc = __shfl_sync(full, tt.cc, owner);
+        }
+        q.thr = __shfl_sync(full, tt.thr, owner);
+        const uint32_t o_start = __shfl_sync(full, start, owner);
+        const uint32_t o_x = __shfl_sync(full, x0, owner), o_y = __shfl_sync(full, y0, owner);
+        const uint32_t o_w = __shfl_sync(full, w, owner), o_magic = __shfl_sync(full, magic, owner);
+        const uint32_t t = slot - o_start;
+        const uint32_t row = (t * o_magic) >> 8;
+        const bool hit = slot < pairs && overlaps<kFp16>(q, o_x + (t - row * o_w), o_y + row);
+        const uint32_t m = __ballot_sync(full, hit);
+        // this lane's pairs within the round are one run of ballot bits
+        const uint32_t lo = max(start, base), hi = min(start + total, base + 32u);
+        if (lo < hi) {
+          const uint32_t len = hi - lo;
+          const uint32_t bits = (m >> (lo - base)) & (len == 32u ? full : ((1u << len) - 1u));
+          local |= bits << (lo - start);
+        }
+      }
+      // rectangle order -> super-tile bits (row * 8 + column)
+      uint32_t mask = 0;
+      const uint32_t row_bits = w == 32u ? full : ((1u << w) - 1u);
+#pragma unroll
+      for (uint32_t r = 0; r < kSuperH; ++r)
+        if (r < h) mask |= ((local >> (r * w)) & row_bits) << ((y0 - ty0 + r) * kSuperW + (x0 - tx0));
+      if (valid) {
+        masks[e] = mask;
+        if (mask != 0u) atomicAdd(&n_touched[prim], static_cast<uint32_t>(__popc(mask)));
+      }
+      // per-tile counts: lane j collects tile j of the warp
+      uint32_t mine = 0;
+#pragma unroll
+      for (int j = 0; j < kSuperTiles; ++j) {
+        const uint32_t bj = __ballot_sync(full, (mask >> j) & 1u);
+        if (lane == static_cast<uint32_t>(j)) mine = __popc(bj);
+      }
+      if (mine) atomicAdd(&s_cnt[lane], mine);
+    }
+    __syncthreads();
+    if (threadIdx.x < kSuperTiles) chunk_counts[c * kSuperTiles + threadIdx.x] = s_cnt[threadIdx.x];
+    __syncthreads();
+  }
+}
+
+// 5b. per (super-tile, tile-in-super-tile): exclusive prefix of the chunk
+// counts in chunk (depth) order, in place, and the tile's total.
+__global__ void k_chunk_prefix(const uint2* __restrict__ super_ranges, const uint32_t* __restrict__ super_chunk,
+                               uint32_t n_super, uint32_t super_w, uint32_t grid_w, uint32_t grid_h,
+                               const DevCounts* __restrict__ counts, uint32_t* __restrict__ chunk_counts,
+                               uint32_t* __restrict__ tile_total) {
+  const uint32_t id = blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= n_super * kSuperTiles) return;
+  const uint32_t sp = id / kSuperTiles, j = id % kSuperTiles;
+  const uint32_t tx = (sp % super_w) * kSuperW + j % kSuperW, ty = (sp / super_w) * kSuperH + j / kSuperW;
+  if (tx >= grid_w || ty >= grid_h) return;
+  uint32_t run = 0;
+  if (counts->overflow == 0u) {
+    const uint2 r = super_ranges[sp];
+    const uint32_t first = super_chunk[sp], n_ch = (r.y - r.x + kChunk - 1u) / kChunk;
+    for (uint32_t c = first; c < first + n_ch; ++c) {
+      uint32_t* p = chunk_counts + c * kSuperTiles + j;
+      const uint32_t v = *p;
+      *p = run;
+      run += v;
+    }
+  }
+  tile_total[ty * grid_w + tx] = run;
+}
+
+// 5c. tile ranges (exclusive scan of the tile totals in tile order), the
+// instance count, and bucket offsets (inclusive scan of ceil(total / 32));
+// one block of 1024 threads, thread t owns a contiguous run of tiles.
+__global__ void __launch_bounds__(1024)
+    k_tile_offsets(const uint32_t* __restrict__ tile_total, uint32_t n_tiles, uint2* __restrict__ ranges,
+                   uint32_t* __restrict__ bucket_offsets, DevCounts* __restrict__ counts, uint32_t cap_inst,
+                   uint32_t cap_buckets) {
+  __shared__ uint32_t s_inst[32], s_buck[32];
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const uint32_t per = (n_tiles + 1023u) / 1024u;
+  const uint32_t begin = min(n_tiles, t * per), end = min(n_tiles, begin + per);
+  uint32_t li = 0, lb = 0;
+  for (uint32_t k = begin; k < end; ++k) {
+    const uint32_t v = tile_total[k];
+    li += v;
+    lb += (v + kBucket - 1u) / kBucket;
+  }
+  uint32_t xi = li, xb = lb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t yi = __shfl_up_sync(0xffffffffu, xi, o), yb = __shfl_up_sync(0xffffffffu, xb, o);
+    if (lane >= static_cast<uint32_t>(o)) {
+      xi += yi;
+      xb += yb;
+    }
+  }
+  if (lane == 31) {
+    s_inst[warp] = xi;
+    s_buck[warp] = xb;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t wi = s_inst[lane], wb = s_buck[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t yi = __shfl_up_sync(0xffffffffu, wi, o), yb = __shfl_up_sync(0xffffffffu, wb, o);
+      if (lane >= static_cast<uint32_t>(o)) {
+        wi += yi;
+        wb += yb;
+      }
+    }
+    s_inst[lane] = wi;
+    s_buck[lane] = wb;
+  }
+  __syncthreads();
+  uint32_t ri = (warp == 0 ? 0u : s_inst[warp - 1]) + xi - li;
+  uint32_t rb = (warp == 0 ? 0u : s_buck[warp - 1]) + xb - lb;
+  for (uint32_t k = begin; k < end; ++k) {
+    const uint32_t v = tile_total[k];
+    ranges[k] = make_uint2(ri, ri + v);
+    ri += v;
+    rb += (v + kBucket - 1u) / kBucket;
+    bucket_offsets[k] = rb;
   }
   if (t == 1023) {
-    const uint32_t total = warp_sums[31];
-    counts->n_buckets = total;
-    if (total > cap_buckets) atomicOr(&counts->overflow, kOverflowBuckets);
+    const uint32_t ni = s_inst[31], nb = s_buck[31];
+    counts->n_instances = ni;
+    counts->n_buckets = nb;
+    if (ni > cap_inst) atomicOr(&counts->overflow, kOverflowInstances);
+    if (nb > cap_buckets) atomicOr(&counts->overflow, kOverflowBuckets);
+  }
+}
+
+// 6. per chunk: every hit of every entry to its slot.  The chunk's hit
+// masks and Gaussian ids are staged in shared memory; each warp owns four of
+// the 32 tiles and walks the entries in order, so the hits of a tile are
+// compacted by ballot and stored as one contiguous run starting at the
+// tile's start + the chunk's prefix for it.
+__global__ void __launch_bounds__(kScanBlock)
+    k_emit_instances(const uint4* __restrict__ chunks, const uint32_t* __restrict__ ent_prim,
+                     const uint32_t* __restrict__ masks, const uint32_t* __restrict__ chunk_prefix,
+                     const uint2* __restrict__ ranges, const DevCounts* __restrict__ counts, uint32_t super_w,
+                     uint32_t grid_w, uint32_t grid_h, uint16_t* __restrict__ inst_key,
+                     uint32_t* __restrict__ inst_prim) {
+  constexpr int kWarps = kScanBlock / 32;
+  __shared__ uint32_t s_mask[kChunk];
+  __shared__ uint32_t s_prim[kChunk];
+  __shared__ uint32_t s_or;
+  const unsigned full = 0xffffffffu;
+  const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const uint32_t lt = lanemask_lt();
+  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const uint4 ch = chunks[c];
+    const uint32_t n_e = ch.z - ch.y;
+    const uint32_t tx0 = (ch.x % super_w) * kSuperW, ty0 = (ch.x / super_w) * kSuperH;
+    if (threadIdx.x == 0) s_or = 0;
+    __syncthreads();
+    uint32_t any = 0;
+    for (uint32_t i = threadIdx.x; i < n_e; i += kScanBlock) {
+      const uint32_t m = masks[ch.y + i];
+      s_mask[i] = m;
+      s_prim[i] = ent_prim[ch.y + i];
+      any |= m;
+    }
+    any = __reduce_or_sync(full, any);
+    if (lane == 0 && any) atomicOr(&s_or, any);
+    __syncthreads();
+    const uint32_t used = s_or;
+#pragma unroll
+    for (int q = 0; q < kSuperTiles / kWarps; ++q) {
+      const uint32_t j = warp * (kSuperTiles / kWarps) + q;
+      if (((used >> j) & 1u) == 0u) continue;  // warp-uniform
+      const uint32_t tx = tx0 + j % kSuperW, ty = ty0 + j / kSuperW;
+      const uint32_t tile = ty * grid_w + tx;  // inside the grid: it has hits
+      uint32_t pos = ranges[tile].x + chunk_prefix[c * kSuperTiles + j];
+      for (uint32_t b0 = 0; b0 < n_e; b0 += 32u) {
+        const uint32_t i = b0 + lane;
+        const bool hit = i < n_e && ((s_mask[i] >> j) & 1u);
+        const uint32_t bm = __ballot_sync(full, hit);
+        if (hit) {
+          const uint32_t at = pos + __popc(bm & lt);
+          inst_key[at] = static_cast<uint16_t>(tile);
+          inst_prim[at] = s_prim[i];
+        }
+        pos += __popc(bm);
+      }
+    }
+    (void)grid_h;
+    __syncthreads();
   }
 }
 
@@ -588,46 +719,55 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   const uint32_t n = static_cast<uint32_t>(n64);
   const uint32_t n_blocks = (n + kScanBlock - 1) / kScanBlock;
   const uint32_t n_tiles = cam.grid_w * cam.grid_h;
+  const uint32_t super_w = (cam.grid_w + kSuperW - 1) / kSuperW, super_h = (cam.grid_h + kSuperH - 1) / kSuperH;
+  const uint32_t n_super = super_w * super_h;
   DevCounts* counts = s.counts;
   // 1. compaction (block sums were written by the preprocess kernel)
   k_scan_sums<<<1, 1024, 0, stream>>>(s.block_sums, n_blocks, &counts->n_visible, nullptr, 0, 0);
   if (n_blocks > 0)
-    k_compact_visible<<<n_blocks, kScanBlock, 0, stream>>>(s.n_touched, s.depth_key, s.block_sums, n,
-                                                            s.vis_key[0], s.vis_idx[0]);
+    k_compact_visible<<<n_blocks, kScanBlock, 0, stream>>>(s.bounds, s.depth_key, s.block_sums, n, s.vis_key[0],
+                                                            s.vis_idx[0]);
   // 2. depth sort (32-bit keys)
   radix_sort<uint32_t>(s.vis_key, s.vis_idx, &counts->n_visible, nullptr, n64, 32, s.depth_result, s, stream);
   const uint32_t* sorted = s.vis_idx[s.depth_result];
-  // 3. instance offsets and emission
+  // 3. super-tile entries in depth order, sorted by super-tile
   if (n_blocks > 0) {
-    k_instance_block_sums<<<n_blocks, kScanBlock, 0, stream>>>(sorted, s.n_touched, counts, s.block_sums);
-    k_scan_sums<<<1, 1024, 0, stream>>>(s.block_sums, n_blocks, &counts->n_instances, counts,
-                                         static_cast<uint32_t>(s.cap_inst), kOverflowInstances);
-    if (fp16) {
-      k_create_instances<1><<<n_blocks, kScanBlock, 0, stream>>>(
-          sorted, s.n_touched, s.tile_mask, s.block_sums, s.bounds, s.mean2d, s.conic_opacity, s.prim_info, counts,
-          static_cast<uint32_t>(s.cap_inst), cam.grid_w, s.inst_key[0], s.inst_prim[0], s.big_list);
-      k_emit_big<1><<<s.num_sms * 8, kScanBlock, 0, stream>>>(s.big_list, s.bounds, s.mean2d, s.conic_opacity,
-                                                               s.prim_info, counts, cam.grid_w, s.inst_key[0],
-                                                               s.inst_prim[0]);
-    } else {
-      k_create_instances<0><<<n_blocks, kScanBlock, 0, stream>>>(
-          sorted, s.n_touched, s.tile_mask, s.block_sums, s.bounds, s.mean2d, s.conic_opacity, s.prim_info, counts,
-          static_cast<uint32_t>(s.cap_inst), cam.grid_w, s.inst_key[0], s.inst_prim[0], s.big_list);
-      k_emit_big<0><<<s.num_sms * 8, kScanBlock, 0, stream>>>(s.big_list, s.bounds, s.mean2d, s.conic_opacity,
-                                                               s.prim_info, counts, cam.grid_w, s.inst_key[0],
-                                                               s.inst_prim[0]);
-    }
+    k_entry_block_sums<<<n_blocks, kScanBlock, 0, stream>>>(sorted, s.bounds, counts, s.block_sums);
+    k_scan_sums<<<1, 1024, 0, stream>>>(s.block_sums, n_blocks, &counts->n_entries, counts,
+                                         static_cast<uint32_t>(s.cap_entries), kOverflowEntries);
+    k_create_entries<<<n_blocks, kScanBlock, 0, stream>>>(sorted, s.bounds, s.block_sums, counts, super_w,
+                                                           s.ent_key[0], s.ent_prim[0]);
   }
-  // 4. tile sort on the bits the tile ids need
-  int tile_bits = 1;
-  while ((1u << tile_bits) < n_tiles) ++tile_bits;
-  radix_sort<uint16_t>(s.inst_key, s.inst_prim, &counts->n_instances, counts, s.cap_inst, tile_bits,
-                       s.tile_result, s, stream);
-  // 5. ranges and buckets
-  cudaMemsetAsync(s.ranges, 0, sizeof(uint2) * n_tiles, stream);
-  k_tile_ranges<<<s.num_sms * 32, 256, 0, stream>>>(s.inst_key[s.tile_result], counts, n_tiles, s.ranges);
-  k_bucket_offsets<<<1, 1024, 0, stream>>>(s.ranges, n_tiles, s.bucket_offsets, counts,
-                                            static_cast<uint32_t>(s.cap_buckets));
+  int super_bits = 1;
+  while ((1u << super_bits) < n_super) ++super_bits;
+  radix_sort<uint16_t>(s.ent_key, s.ent_prim, &counts->n_entries, counts, s.cap_entries, super_bits, s.ent_result,
+                       s, stream);
+  const uint16_t* ent_key = s.ent_key[s.ent_result];
+  const uint32_t* ent_prim = s.ent_prim[s.ent_result];
+  // 4. chunks of each super-tile's entry list
+  cudaMemsetAsync(s.super_ranges, 0, sizeof(uint2) * n_super, stream);
+  k_super_ranges<<<s.num_sms * 8, 256, 0, stream>>>(ent_key, counts, s.super_ranges);
+  k_chunk_table<<<1, 1024, 0, stream>>>(s.super_ranges, n_super, s.chunks, s.super_chunk, counts);
+  // 5. hit masks and counts, then every (chunk, tile)'s first slot
+  const int persistent = s.num_sms * 8;
+  if (fp16)
+    k_chunk_hits<1><<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.bounds, s.mean2d, s.conic_opacity,
+                                                            s.prim_info, counts, super_w, s.masks, s.chunk_counts,
+                                                            s.n_touched);
+  else
+    k_chunk_hits<0><<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.bounds, s.mean2d, s.conic_opacity,
+                                                            s.prim_info, counts, super_w, s.masks, s.chunk_counts,
+                                                            s.n_touched);
+  k_chunk_prefix<<<(n_super * kSuperTiles + 255) / 256, 256, 0, stream>>>(
+      s.super_ranges, s.super_chunk, n_super, super_w, cam.grid_w, cam.grid_h, counts, s.chunk_counts,
+      s.tile_total);
+  k_tile_offsets<<<1, 1024, 0, stream>>>(s.tile_total, n_tiles, s.ranges, s.bucket_offsets, counts,
+                                          static_cast<uint32_t>(s.cap_inst), static_cast<uint32_t>(s.cap_buckets));
+  // 6. instances at their final slots
+  k_emit_instances<<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.masks, s.chunk_counts, s.ranges,
+                                                           counts, super_w, cam.grid_w, cam.grid_h,
+                                                           s.inst_key[0], s.inst_prim[0]);
+  s.tile_result = 0;
 }
 
 }  // namespace tgs

@@ -19,10 +19,12 @@ constexpr float kMaxAlphaF32 = 0.999f;
 constexpr float kMaxAlphaF16 = 0.99f;
 constexpr float kMinTransmittance = 1e-4f;
 constexpr int kSortTileItems = 2048;  // items per radix-sort block
-// the count pass records which of the first kMaskTiles tiles of a
-// rectangle (row-major) a Gaussian touches; instance emission expands those
-// bits and tests only the tiles past them
-constexpr uint32_t kMaskTiles = 64;
+// binning works on super-tiles of 8x4 tiles (one bit per tile in a 32-bit
+// mask) and cuts each super-tile's depth-ordered list into chunks
+constexpr uint32_t kSuperW = 8;
+constexpr uint32_t kSuperH = 4;
+constexpr int kSuperTiles = 32;
+constexpr uint32_t kChunk = 1024;
 
 // Device-side camera passed by value as a kernel parameter.
 struct DevCamera {
@@ -74,18 +76,18 @@ struct alignas(16) PrimInfo16 {
 // Error word written by device code when a capacity bound is exceeded.
 constexpr uint32_t kOverflowInstances = 1u;
 constexpr uint32_t kOverflowBuckets = 2u;
-// set if instance emission ever disagreed with the preprocess tile count
-constexpr uint32_t kInconsistentTiles = 4u;
+constexpr uint32_t kOverflowEntries = 4u;  // (Gaussian, super-tile) entries
 
-// Device counters of one forward, kept in one 16-byte record.
+// Device counters of one forward, kept in one 32-byte record.
 struct DevCounts {
   uint32_t n_visible;
   uint32_t n_instances;
   uint32_t n_buckets;
   uint32_t overflow;
   uint32_t n_live_buckets;  // buckets the backward runs (forward appends them)
-  uint32_t n_big;           // Gaussians whose rectangle extends past kMaskTiles tiles
-  uint32_t pad[2];
+  uint32_t n_entries;       // (Gaussian, super-tile) entries
+  uint32_t n_chunks;        // chunks of the super-tile entry lists
+  uint32_t pad;
 };
 
 }  // namespace tgs

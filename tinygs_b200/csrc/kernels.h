@@ -34,8 +34,6 @@ struct RasterState {
   // per Gaussian
   uint32_t* n_touched = nullptr;
   uint32_t* depth_key = nullptr;
-  uint64_t* tile_mask = nullptr;     // hit bits of the first kMaskTiles tiles
-  uint4* big_list = nullptr;         // (Gaussian, first slot, end) with tiles past kMaskTiles
   ushort4* bounds = nullptr;
   float2* mean2d = nullptr;
   float4* conic_opacity = nullptr;  // fp32 path; aliases prim_info storage
@@ -45,8 +43,21 @@ struct RasterState {
   uint32_t* vis_key[2] = {nullptr, nullptr};
   uint32_t* vis_idx[2] = {nullptr, nullptr};
   uint32_t* block_sums = nullptr;   // block partial sums for scans
-  // per instance
-  uint16_t* inst_key[2] = {nullptr, nullptr};
+  // per (Gaussian, super-tile) entry
+  int64_t cap_entries = 0;
+  uint16_t* ent_key[2] = {nullptr, nullptr};   // super-tile id (double-buffered for the sort)
+  uint32_t* ent_prim[2] = {nullptr, nullptr};
+  uint32_t* masks = nullptr;                   // hit mask over the 8x4 tiles of the super-tile
+  int ent_result = 0;
+  // per super-tile and per chunk of its entries
+  int64_t max_super = 0;
+  int64_t cap_chunks = 0;
+  uint2* super_ranges = nullptr;
+  uint32_t* super_chunk = nullptr;   // first chunk of each super-tile
+  uint4* chunks = nullptr;           // (super-tile, first entry, end entry)
+  uint32_t* chunk_counts = nullptr;  // [chunk][32] hits per tile, then first-slot offsets
+  // per instance, in final (tile, depth, index) order
+  uint16_t* inst_key[2] = {nullptr, nullptr};  // only [0] is allocated
   uint32_t* inst_prim[2] = {nullptr, nullptr};
   // radix sort scratch
   uint32_t* sort_hist = nullptr;    // [256][sort_max_blocks]
@@ -54,6 +65,7 @@ struct RasterState {
   int64_t sort_max_blocks = 0;
   // per tile
   uint2* ranges = nullptr;
+  uint32_t* tile_total = nullptr;
   uint32_t* bucket_offsets = nullptr;
   uint32_t* tile_max_contrib = nullptr;
   // per pixel

@@ -7,20 +7,21 @@
 // as fp16 in shared memory, which this implementation keeps because it
 // changes the result at the 1e-3 level).
 //
-// Layout of the work: one CTA per 16x16 output tile and channel
-// (grid.z = 3).  The forward loads the 26x26 halo tile once, runs the
-// horizontal then the vertical pass of the five moment images in shared
-// memory, writes the SSIM loss and the three per-pixel partial derivatives;
+// Layout of the work: one CTA per 32x32 output tile and channel (grid.z = 3).
+// The forward loads the 42x48 window once as aligned 8-pixel segments, runs
+// the horizontal then the vertical pass of the five moment images in shared
+// memory (four outputs per thread from a 14-value register window in each
+// pass), writes the SSIM loss and the three per-pixel partial derivatives;
 // the L1 term of the same pixels is fused into this pass.  The backward
-// convolves the partial-derivative maps the same way and finishes dL/dpred.
+// filters the partial-derivative maps the same way and finishes dL/dpred.
+#include <cstring>
+
 #include "kernels.h"
 
 namespace tgs {
 namespace {
 
-constexpr int kB = 16;          // output tile edge
 constexpr int kHalo = 5;
-constexpr int kS = kB + 2 * kHalo;  // 26
 
 __constant__ float c_gauss[11] = {0.001028380123898387f, 0.0075987582094967365f, 0.036000773310661316f,
                                   0.10936068743467331f,  0.21300552785396576f,   0.26601171493530273f,
@@ -73,88 +74,147 @@ __global__ void k_l1(uint32_t total, const void* __restrict__ pred, const void* 
   }
 }
 
-// SSIM forward (+ fused L1).  One CTA = 16x16 pixels of one channel.
+// Shared tile geometry of both SSIM passes: 32x32 output pixels of one
+// channel per CTA; the input window is 42 rows (5-pixel halo) by 48 columns
+// (six 8-pixel row segments of the tiled layout, x0 - 8 .. x0 + 40), so every
+// global load is one aligned 8-pixel segment.
+constexpr int kOut = 32;
+constexpr int kInH = kOut + 2 * kHalo;  // 42
+constexpr int kInW = kOut + 16;         // 48
+constexpr int kSegs = kInW / 8;         // 6
+
+__device__ __forceinline__ bool segment_of(const DevCamera& cam, int x0, int y0, int r, int sg, uint32_t& idx,
+                                           int& gx0) {
+  const int gy = y0 - kHalo + r;
+  gx0 = x0 - 8 + 8 * sg;
+  if (gy < 0 || gy >= static_cast<int>(cam.height) || gx0 < 0 || gx0 >= static_cast<int>(cam.width)) return false;
+  idx = tiled_index(static_cast<uint32_t>(gy), static_cast<uint32_t>(gx0), cam.tiled_w);
+  return true;
+}
+
+// Horizontal 11-tap sums of four consecutive outputs from 14 inputs.
+template <int kM>
+__device__ __forceinline__ void taps4(const float (&in)[kM][14], float (&out)[kM][4]) {
+#pragma unroll
+  for (int m = 0; m < kM; ++m)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float acc = 0.f;
+#pragma unroll
+      for (int d = 0; d < 11; ++d) acc += in[m][k + d] * c_gauss[d];
+      out[m][k] = acc;
+    }
+}
+
+// SSIM forward (+ fused L1).  Moments mu_p, E[p^2], mu_t, E[t^2], E[pt] by
+// separable 11x11 Gaussian filtering of the half-precision window.
 template <int kFp16>
 __global__ void __launch_bounds__(256)
     k_ssim_forward(DevCamera cam, const void* __restrict__ pred, const void* __restrict__ target,
                    void* __restrict__ loss_map, void* __restrict__ grad, float s_ssim, float s_l1,
                    float* __restrict__ partials, float* __restrict__ loss_sum) {
-  __shared__ __half2 tile[kS][kS];
-  __shared__ float hsum[kS][kB][5];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int x0 = blockIdx.x * kB, y0 = blockIdx.y * kB;
+  __shared__ __half2 tile[kInH][kInW];     // (pred, target)
+  __shared__ float hsum[5][kInH][kOut];
+  const int x0 = blockIdx.x * kOut, y0 = blockIdx.y * kOut;
   const uint32_t ch = blockIdx.z * cam.plane;
   const int W = static_cast<int>(cam.width), H = static_cast<int>(cam.height);
-  for (int k = threadIdx.x; k < kS * kS; k += 256) {
-    const int sy = k / kS, sx = k % kS;
-    const int gx = x0 + sx - kHalo, gy = y0 + sy - kHalo;
-    __half2 v = __float2half2_rn(0.f);
-    if (gx >= 0 && gy >= 0 && gx < W && gy < H) {
-      const uint32_t pi = ch + tiled_index(gy, gx, cam.tiled_w);
-      if constexpr (kFp16)
-        v = __halves2half2(reinterpret_cast<const __half*>(pred)[pi], reinterpret_cast<const __half*>(target)[pi]);
-      else
-        v = __floats2half2_rn(reinterpret_cast<const float*>(pred)[pi], reinterpret_cast<const float*>(target)[pi]);
+  // load: one 8-pixel segment per (row, segment)
+  for (int k = threadIdx.x; k < kInH * kSegs; k += 256) {
+    const int r = k / kSegs, sg = k % kSegs;
+    uint32_t idx;
+    int gx0;
+    __half2 v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = __float2half2_rn(0.f);
+    if (segment_of(cam, x0, y0, r, sg, idx, gx0)) {
+      __half p[8], t[8];
+      if constexpr (kFp16) {
+        const uint4 pv = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(pred) + ch + idx);
+        const uint4 tv = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(target) + ch + idx);
+        memcpy(p, &pv, 16);
+        memcpy(t, &tv, 16);
+      } else {
+        const float4* pf = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pred) + ch + idx);
+        const float4* tf = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(target) + ch + idx);
+        const float4 p0 = pf[0], p1 = pf[1], t0 = tf[0], t1 = tf[1];
+        const float pa[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const float ta[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          p[q] = __float2half_rn(pa[q]);
+          t[q] = __float2half_rn(ta[q]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (gx0 + q < W) v[q] = __halves2half2(p[q], t[q]);
     }
-    tile[sy][sx] = v;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) tile[r][8 * sg + q] = v[q];
   }
   __syncthreads();
-  for (int row = ty; row < kS; row += kB) {
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, s4 = 0.f;
+  // horizontal: four consecutive outputs per item (output x reads window
+  // columns x + 3 .. x + 13)
+  for (int it = threadIdx.x; it < kInH * (kOut / 4); it += 256) {
+    const int r = it / (kOut / 4), c0 = 4 * (it % (kOut / 4));
+    float in[5][14];
 #pragma unroll
-    for (int d = 0; d < 11; ++d) {
-      const float w = c_gauss[d];
-      const float2 xy = __half22float2(tile[row][tx + d]);
-      s0 += xy.x * w;
-      s1 += (xy.x * xy.x) * w;
-      s2 += xy.y * w;
-      s3 += (xy.y * xy.y) * w;
-      s4 += (xy.x * xy.y) * w;
+    for (int j = 0; j < 14; ++j) {
+      const float2 xy = __half22float2(tile[r][c0 + 3 + j]);
+      in[0][j] = xy.x;
+      in[1][j] = xy.x * xy.x;
+      in[2][j] = xy.y;
+      in[3][j] = xy.y * xy.y;
+      in[4][j] = xy.x * xy.y;
     }
-    hsum[row][tx][0] = s0;
-    hsum[row][tx][1] = s1;
-    hsum[row][tx][2] = s2;
-    hsum[row][tx][3] = s3;
-    hsum[row][tx][4] = s4;
+    float out[5][4];
+    taps4<5>(in, out);
+#pragma unroll
+    for (int m = 0; m < 5; ++m)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) hsum[m][r][c0 + k] = out[m][k];
   }
   __syncthreads();
-  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f, o4 = 0.f;
+  // vertical: lane = column, warp = group of four rows
+  const int c = threadIdx.x & 31, q0 = 4 * (threadIdx.x >> 5);
+  float in[5][14];
 #pragma unroll
-  for (int d = 0; d < 11; ++d) {
-    const float w = c_gauss[d];
-    o0 += hsum[ty + d][tx][0] * w;
-    o1 += hsum[ty + d][tx][1] * w;
-    o2 += hsum[ty + d][tx][2] * w;
-    o3 += hsum[ty + d][tx][3] * w;
-    o4 += hsum[ty + d][tx][4] * w;
-  }
-  const int px = x0 + tx, py = y0 + ty;
-  const uint32_t pi = ch + tiled_index(py, px, cam.tiled_w);
+  for (int m = 0; m < 5; ++m)
+#pragma unroll
+    for (int j = 0; j < 14; ++j) in[m][j] = hsum[m][q0 + j][c];
+  float o[5][4];
+  taps4<5>(in, o);
+  const int px = x0 + c;
   float contrib = 0.f;
-  // fused L1 term over the padded physical extent (l1.cu:117-129); applied
-  // first, as the reference evaluates the L1 loss before the SSIM loss
-  if (s_l1 != 0.f && static_cast<uint32_t>(px) < cam.tiled_w * 8u && static_cast<uint32_t>(py) < cam.tiled_h * 8u) {
-    const float d = sat(load_px<kFp16>(pred, pi)) - load_px<kFp16>(target, pi);
-    contrib += fabsf(d) * s_l1;
-    if (loss_map != nullptr) add_px<kFp16>(loss_map, pi, fabsf(d), s_l1);
-    if (grad != nullptr) add_px<kFp16>(grad, pi, copysignf(1.0f, d), s_l1);
-  }
-  if (px < W && py < H) {
-    const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
-    const float mu1 = o0, mu2 = o2;
-    const float m11 = mu1 * mu1, m22 = mu2 * mu2;
-    const float sg1 = o1 - m11, sg2 = o3 - m22, sg12 = o4 - mu1 * mu2;
-    const float A = m11 + m22 + C1, B = sg1 + sg2 + C2;
-    const float Cc = 2.f * mu1 * mu2 + C1, D = 2.f * sg12 + C2;
-    const float val = (Cc * D) / (A * B);
-    if (loss_map != nullptr) add_px<kFp16>(loss_map, pi, 1.0f - val, s_ssim);
-    contrib += (1.0f - val) * s_ssim;
-    if (partials != nullptr) {
-      const uint32_t plane3 = 3 * cam.plane;
-      partials[pi] = (mu2 * 2.f * D) / (A * B) - (mu2 * 2.f * Cc) / (A * B) - (mu1 * 2.f * Cc * D) / (A * A * B) +
-                     (mu1 * 2.f * Cc * D) / (A * B * B);
-      partials[pi + plane3] = (-Cc * D) / (A * B * B);
-      partials[pi + 2 * plane3] = (2.f * Cc) / (A * B);
+  const uint32_t plane3 = 3 * cam.plane;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int py = y0 + q0 + k;
+    const uint32_t pi = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
+    // fused L1 term over the padded physical extent (l1.cu:117-129); applied
+    // first, as the reference evaluates the L1 loss before the SSIM loss
+    if (s_l1 != 0.f && static_cast<uint32_t>(px) < cam.tiled_w * 8u && static_cast<uint32_t>(py) < cam.tiled_h * 8u) {
+      const float d = sat(load_px<kFp16>(pred, pi)) - load_px<kFp16>(target, pi);
+      contrib += fabsf(d) * s_l1;
+      if (loss_map != nullptr) add_px<kFp16>(loss_map, pi, fabsf(d), s_l1);
+      if (grad != nullptr) add_px<kFp16>(grad, pi, copysignf(1.0f, d), s_l1);
+    }
+    if (px < W && py < H) {
+      const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
+      const float mu1 = o[0][k], mu2 = o[2][k];
+      const float m11 = mu1 * mu1, m22 = mu2 * mu2;
+      const float sg1 = o[1][k] - m11, sg2 = o[3][k] - m22, sg12 = o[4][k] - mu1 * mu2;
+      const float A = m11 + m22 + C1, B = sg1 + sg2 + C2;
+      const float Cc = 2.f * mu1 * mu2 + C1, D = 2.f * sg12 + C2;
+      const float val = (Cc * D) / (A * B);
+      if (loss_map != nullptr) add_px<kFp16>(loss_map, pi, 1.0f - val, s_ssim);
+      contrib += (1.0f - val) * s_ssim;
+      if (partials != nullptr) {
+        partials[pi] = (mu2 * 2.f * D) / (A * B) - (mu2 * 2.f * Cc) / (A * B) - (mu1 * 2.f * Cc * D) / (A * A * B) +
+                       (mu1 * 2.f * Cc * D) / (A * B * B);
+        partials[pi + plane3] = (-Cc * D) / (A * B * B);
+        partials[pi + 2 * plane3] = (2.f * Cc) / (A * B);
+      }
     }
   }
   if (loss_sum != nullptr) {
@@ -163,61 +223,70 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// SSIM backward: dL/dpred = -s * (G*d_mu + 2 p G*d_s1 + t G*d_s12).
+// SSIM backward: dL/dpred = -s * (G*d_mu + 2 p G*d_s1 + t G*d_s12), the three
+// partial-derivative maps filtered with the same separable window.
 template <int kFp16>
 __global__ void __launch_bounds__(256)
     k_ssim_backward(DevCamera cam, const void* __restrict__ pred, const void* __restrict__ target,
                     void* __restrict__ grad, float s_ssim, const float* __restrict__ partials) {
-  __shared__ float tile[3][kS][kS + 1];
-  __shared__ float hsum[3][kS][kB + 1];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int x0 = blockIdx.x * kB, y0 = blockIdx.y * kB;
+  __shared__ float tile[3][kInH][kInW + 1];
+  __shared__ float hsum[3][kInH][kOut];
+  const int x0 = blockIdx.x * kOut, y0 = blockIdx.y * kOut;
   const uint32_t ch = blockIdx.z * cam.plane;
   const uint32_t plane3 = 3 * cam.plane;
   const int W = static_cast<int>(cam.width), H = static_cast<int>(cam.height);
-  for (int k = threadIdx.x; k < kS * kS; k += 256) {
-    const int sy = k / kS, sx = k % kS;
-    const int gx = x0 + sx - kHalo, gy = y0 + sy - kHalo;
-    float a = 0.f, b = 0.f, c = 0.f;
-    if (gx >= 0 && gy >= 0 && gx < W && gy < H) {
-      const uint32_t pi = ch + tiled_index(gy, gx, cam.tiled_w);
-      a = partials[pi];
-      b = partials[pi + plane3];
-      c = partials[pi + 2 * plane3];
+  for (int k = threadIdx.x; k < 3 * kInH * kSegs; k += 256) {
+    const int m = k / (kInH * kSegs), rs = k % (kInH * kSegs);
+    const int r = rs / kSegs, sg = rs % kSegs;
+    uint32_t idx;
+    int gx0;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (segment_of(cam, x0, y0, r, sg, idx, gx0)) {
+      const float4* src = reinterpret_cast<const float4*>(partials + ch + idx + m * plane3);
+      const float4 a = src[0], b = src[1];
+      const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (gx0 + q < W) v[q] = f[q];
     }
-    tile[0][sy][sx] = a;
-    tile[1][sy][sx] = b;
-    tile[2][sy][sx] = c;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) tile[m][r][8 * sg + q] = v[q];
   }
   __syncthreads();
-  for (int row = ty; row < kS; row += kB) {
-    float a = 0.f, b = 0.f, c = 0.f;
+  for (int it = threadIdx.x; it < kInH * (kOut / 4); it += 256) {
+    const int r = it / (kOut / 4), c0 = 4 * (it % (kOut / 4));
+    float in[3][14];
 #pragma unroll
-    for (int d = 0; d < 11; ++d) {
-      const float w = c_gauss[d];
-      a += tile[0][row][tx + d] * w;
-      b += tile[1][row][tx + d] * w;
-      c += tile[2][row][tx + d] * w;
-    }
-    hsum[0][row][tx] = a;
-    hsum[1][row][tx] = b;
-    hsum[2][row][tx] = c;
+    for (int m = 0; m < 3; ++m)
+#pragma unroll
+      for (int j = 0; j < 14; ++j) in[m][j] = tile[m][r][c0 + 3 + j];
+    float out[3][4];
+    taps4<3>(in, out);
+#pragma unroll
+    for (int m = 0; m < 3; ++m)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) hsum[m][r][c0 + k] = out[m][k];
   }
   __syncthreads();
-  const int px = x0 + tx, py = y0 + ty;
-  if (px >= W || py >= H) return;
-  float a = 0.f, b = 0.f, c = 0.f;
+  const int c = threadIdx.x & 31, q0 = 4 * (threadIdx.x >> 5);
+  float in[3][14];
 #pragma unroll
-  for (int d = 0; d < 11; ++d) {
-    const float w = c_gauss[d];
-    a += hsum[0][ty + d][tx] * w;
-    b += hsum[1][ty + d][tx] * w;
-    c += hsum[2][ty + d][tx] * w;
+  for (int m = 0; m < 3; ++m)
+#pragma unroll
+    for (int j = 0; j < 14; ++j) in[m][j] = hsum[m][q0 + j][c];
+  float o[3][4];
+  taps4<3>(in, o);
+  const int px = x0 + c;
+  if (px >= W) return;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int py = y0 + q0 + k;
+    if (py >= H) break;
+    const uint32_t pi = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
+    const float p1 = load_px<kFp16>(pred, pi), p2 = load_px<kFp16>(target, pi);
+    const float dL = o[0][k] + (2.f * p1) * o[1][k] + p2 * o[2][k];
+    add_px<kFp16>(grad, pi, dL, -s_ssim);
   }
-  const uint32_t pi = ch + tiled_index(py, px, cam.tiled_w);
-  const float p1 = load_px<kFp16>(pred, pi), p2 = load_px<kFp16>(target, pi);
-  const float dL = a + (2.f * p1) * b + p2 * c;
-  add_px<kFp16>(grad, pi, dL, -s_ssim);
 }
 
 }  // namespace
@@ -249,7 +318,7 @@ void launch_ssim(int fp16, int width, int height, const void* pred, const void* 
                  void* grad, float scale_ssim, float scale_l1, float* partials, float* loss_sum,
                  cudaStream_t stream) {
   const DevCamera g = image_geometry(width, height);
-  const dim3 grid((width + kB - 1) / kB, (height + kB - 1) / kB, 3);
+  const dim3 grid((width + kOut - 1) / kOut, (height + kOut - 1) / kOut, 3);
   const float s_ssim = scale_ssim / static_cast<float>(width * height);
   const float s_l1 = scale_l1 / static_cast<float>(width * height * 3);
   float* parts = grad != nullptr ? partials : nullptr;

@@ -2,15 +2,17 @@
 // (backward).
 //
 // Forward: cull, quaternion -> rotation, 3D covariance, EWA projection with
-// the 0.3 px dilation, conic, SH colour, screen-space tile rectangle and the
-// exact number of touched tiles.  Reference semantics:
+// the 0.3 px dilation, conic, SH colour and screen-space tile rectangle (the
+// exact tile tests and touched-tile counts are done during binning, per
+// super-tile).  Reference semantics:
 // tinygs/src/rasterizer/fastgs_ours/kernels_forward.cuh:157-412 (fp32) and
 // tinygs/src/rasterizer/fastgs_ours_fp16/kernels_forward.cuh:249-496 (fp16).
 //
-// Unlike the reference, visible Gaussians are not appended through an atomic
-// counter: each block publishes its number of visible Gaussians and a
-// separate compaction pass (binning.cu) writes the visible list in index
-// order, so the depth sort that follows is fully deterministic.
+// Unlike the reference, candidate Gaussians (culling passed, non-empty tile
+// rectangle) are not appended through an atomic counter: each block
+// publishes its number of candidates and a separate compaction pass
+// (binning.cu) writes the list in index order, so the depth sort that follows
+// is fully deterministic.
 #include "kernels.h"
 #include "tiles.cuh"
 
@@ -116,73 +118,6 @@ __device__ __forceinline__ uint32_t clamp_bound(int v, uint32_t hi) {
   return min(hi, static_cast<uint32_t>(max(0, v)));
 }
 
-// Exact tile count, the warp's (Gaussian, tile) pairs tested 32 at a time:
-// the rectangles of the 32 lanes are laid end to end (row-major inside each)
-// and lane j of a round tests pair base + j for whichever Gaussian owns it,
-// so lanes stay busy whatever the mix of rectangle sizes.  Every lane must
-// call this.  The hit pattern of the first kMaskTiles tiles of the lane's
-// rectangle is returned in `mask`, so that instance emission can expand it
-// instead of testing those tiles again.
-template <int kFp16>
-__device__ uint32_t count_tiles(const TileTest& p, uint4 b, bool active, uint64_t& mask) {
-  const unsigned full = 0xffffffffu;
-  const uint32_t lane = lane_id();
-  const uint32_t width = b.y - b.x;
-  const uint32_t total = active ? width * (b.w - b.z) : 0u;
-  const float inv_w = width > 0 ? 1.0f / static_cast<float>(width) : 0.f;
-  uint32_t incl = total;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(full, incl, o);
-    if (lane >= static_cast<uint32_t>(o)) incl += y;
-  }
-  const uint32_t start = incl - total;  // this lane's first pair
-  const uint32_t pairs = __shfl_sync(full, incl, 31);
-  uint32_t count = 0;
-  mask = 0;
-  for (uint32_t base = 0; base < pairs; base += 32u) {
-    const uint32_t slot = base + lane;
-    uint32_t owner = 0;
-#pragma unroll
-    for (uint32_t step = 16; step >= 1; step >>= 1) {
-      const uint32_t o = __shfl_sync(full, start, owner + step);
-      if (o <= slot) owner += step;
-    }
-    TileTest q;
-    q.mx = __shfl_sync(full, p.mx, owner);
-    q.my = __shfl_sync(full, p.my, owner);
-    if constexpr (kFp16) {
-      q.h_xy = __shfl_sync(full, p.h_xy, owner);
-      q.h_zw = __shfl_sync(full, p.h_zw, owner);
-    } else {
-      q.ca = __shfl_sync(full, p.ca, owner);
-      q.cb = __shfl_sync(full, p.cb, owner);
-      q.cc = __shfl_sync(full, p.cc, owner);
-    }
-    q.thr = __shfl_sync(full, p.thr, owner);
-    const uint32_t o_start = __shfl_sync(full, start, owner);
-    const uint32_t o_x = __shfl_sync(full, b.x, owner), o_y = __shfl_sync(full, b.z, owner);
-    const uint32_t o_w = __shfl_sync(full, width, owner);
-    const float o_inv = __shfl_sync(full, inv_w, owner);
-    const uint32_t t = slot - o_start;
-    // row = floor(t / w), exact for t < 2^21 with the half-step offset
-    const uint32_t row = __float2uint_rz((static_cast<float>(t) + 0.5f) * o_inv);
-    const uint32_t col = t - row * o_w;
-    const bool hit = slot < pairs && overlaps<kFp16>(q, o_x + col, o_y + row);
-    const uint32_t m = __ballot_sync(full, hit);
-    // this lane's pairs within the round
-    const uint32_t lo = max(start, base), hi = min(start + total, base + 32u);
-    if (lo < hi) {
-      const uint32_t len = hi - lo;
-      const uint32_t bits = (m >> (lo - base)) & (len == 32u ? full : ((1u << len) - 1u));
-      count += __popc(bits);
-      const uint32_t at = lo - start;  // first tile index of these bits
-      if (at < kMaskTiles) mask |= static_cast<uint64_t>(bits) << at;
-    }
-  }
-  return count;
-}
-
 template <int kFp16>
 __global__ void __launch_bounds__(kPreBlock)
     k_preprocess(const float* __restrict__ means, const float* __restrict__ opacities,
@@ -192,7 +127,7 @@ __global__ void __launch_bounds__(kPreBlock)
                  uint32_t* __restrict__ depth_key, ushort4* __restrict__ bounds,
                  float2* __restrict__ mean2d, float4* __restrict__ conic_opacity,
                  PrimInfo16* __restrict__ prim_info, float* __restrict__ color,
-                 uint64_t* __restrict__ tile_mask, float4* __restrict__ helpers,
+                 float4* __restrict__ helpers,
                  uint32_t* __restrict__ block_visible, int rest_vec) {
   // higher-order SH rows of the warp's 32 Gaussians, loaded coalesced (one
   // row per lane would touch 32 cache lines per load instruction)
@@ -224,12 +159,10 @@ __global__ void __launch_bounds__(kPreBlock)
   if (qn < 1e-8f) active = false;
   const bool warp_alive = __ballot_sync(0xffffffffu, active) != 0u;
 
-  uint32_t touched = 0;
-  uint64_t hits = 0;
   uint4 rect = make_uint4(0, 0, 0, 0);
   float2 m2 = make_float2(0.f, 0.f);
   float3 conic = make_float3(0.f, 0.f, 0.f);
-  TileTest tt{};
+  __half2 hxy = __float2half2_rn(0.f), hzw = __float2half2_rn(0.f);
   if (warp_alive) {
     const float e0 = __expf(s0), e1 = __expf(s1), e2 = __expf(s2);
     const float var[3] = {e0 * e0, e1 * e1, e2 * e2};
@@ -255,7 +188,6 @@ __global__ void __launch_bounds__(kPreBlock)
       dens[gi].w = fmaxf(dens[gi].w, rad);
     }
     m2 = make_float2(x * cam.fx + cam.cx, y * cam.fy + cam.cy);
-    __half2 hxy = __float2half2_rn(0.f), hzw = __float2half2_rn(0.f);
     float thr;
     if constexpr (kFp16) {
       hxy = __floats2half2_rn(conic.x, conic.y);
@@ -272,20 +204,11 @@ __global__ void __launch_bounds__(kPreBlock)
                       clamp_bound(__float2int_rd((m2.y - ey) / static_cast<float>(kTile)), cam.grid_h),
                       clamp_bound(__float2int_ru((m2.y + ey) / static_cast<float>(kTile)), cam.grid_h));
     if ((rect.y - rect.x) * (rect.w - rect.z) == 0u) active = false;
-    tt.mx = m2.x - 0.5f;
-    tt.my = m2.y - 0.5f;
-    tt.ca = conic.x;
-    tt.cb = conic.y;
-    tt.cc = conic.z;
-    tt.h_xy = hxy;
-    tt.h_zw = hzw;
-    tt.thr = thr;
-    if (__ballot_sync(0xffffffffu, active) != 0u) touched = count_tiles<kFp16>(tt, rect, active, hits);
-    if (!active) touched = 0;
   }
+  const bool candidate = in_range && warp_alive && active;
 
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  if (active_bases > 1 && __ballot_sync(0xffffffffu, in_range && touched > 0) != 0u) {
+  if (active_bases > 1 && __ballot_sync(0xffffffffu, candidate) != 0u) {
     const uint32_t first = i - lane;  // < n: some lane is in range
     const uint32_t cnt = min(32u, n - first);
     const float* src = sh_rest + 45 * static_cast<size_t>(first);
@@ -300,17 +223,17 @@ __global__ void __launch_bounds__(kPreBlock)
   }
 
   if (in_range) {
-    n_touched[i] = touched;
-    if (touched > 0) {
+    n_touched[i] = 0;  // binning adds the hits of each super-tile
+    bounds[i] = candidate ? make_ushort4(static_cast<unsigned short>(rect.x), static_cast<unsigned short>(rect.y),
+                                         static_cast<unsigned short>(rect.z), static_cast<unsigned short>(rect.w))
+                          : make_ushort4(0, 0, 0, 0);
+    if (candidate) {
       depth_key[i] = __float_as_uint(depth);
-      tile_mask[i] = hits;
       // the blend backward accumulates into these
       const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
       helpers[3 * i] = z;
       helpers[3 * i + 1] = z;
       helpers[3 * i + 2] = z;
-      bounds[i] = make_ushort4(static_cast<unsigned short>(rect.x), static_cast<unsigned short>(rect.y),
-                               static_cast<unsigned short>(rect.z), static_cast<unsigned short>(rect.w));
       mean2d[i] = m2;
       // view-dependent colour
       float3 col = make_float3(0.5f + 0.28209479177387814f * sh0[3 * i],
@@ -333,8 +256,8 @@ __global__ void __launch_bounds__(kPreBlock)
       }
       if constexpr (kFp16) {
         PrimInfo16 rec;
-        rec.conic_xy = tt.h_xy;
-        rec.conic_z_opacity = tt.h_zw;
+        rec.conic_xy = hxy;
+        rec.conic_z_opacity = hzw;
         rec.rgb_pad = make_uchar4(static_cast<unsigned char>(sat(col.x) * 255.0f),
                                   static_cast<unsigned char>(sat(col.y) * 255.0f),
                                   static_cast<unsigned char>(sat(col.z) * 255.0f), 0);
@@ -348,8 +271,8 @@ __global__ void __launch_bounds__(kPreBlock)
       }
     }
   }
-  // number of visible Gaussians of this block, for the compaction scan
-  const uint32_t vis = __syncthreads_count(in_range && touched > 0);
+  // number of candidates of this block, for the compaction scan
+  const uint32_t vis = __syncthreads_count(candidate);
   if (threadIdx.x == 0) block_visible[blockIdx.x] = vis;
 }
 
@@ -783,12 +706,12 @@ void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCam
     k_preprocess<1><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, s.tile_mask, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
+        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
   else
     k_preprocess<0><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, s.tile_mask, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
+        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
 }
 
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, const GaussianPtrs& grads,

@@ -245,6 +245,7 @@ def run_ours(args):
 
     from tinygs_b200 import runtime as rt
     from tinygs_b200 import scenes
+    from tinygs_b200.dp import DataParallel
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -255,6 +256,7 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dp = DataParallel.from_env()
     cfg = scene_config(args.config, args.n)
     W, H = cfg.width, cfg.height
     fp16 = cfg.dtype == "float16"
@@ -305,7 +307,7 @@ def run_ours(args):
     rast = make_raster(int(max_inst * 1.5) + 1024)
 
     def view_of(step):
-        return cams[(step * world + rank) % len(cams)]
+        return cams[dp.view_index(step, len(cams))]
 
     # one GPU: backward and Adam in one pass (tgs_raster_backward_adam); with
     # several GPUs the gradients must be all-reduced between the two
@@ -345,10 +347,10 @@ def run_ours(args):
             rast.backward(ctx)
             if ev is not None:
                 ev[2].record(stream)
-            dist.all_reduce(grads.storage)
+            dp.reduce_gradients(grads.storage)
             if ev is not None:
                 ev[3].record(stream)
-            opt.step(1.0 / (GRAD_SCALER * world), stream=stream)
+            opt.step(dp.gradient_scale(GRAD_SCALER), stream=stream)
             if ev is not None:
                 ev[4].record(stream)
         if e2e:
@@ -369,12 +371,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return dp.max_over_ranks(e0.elapsed_time(e1), "cuda")
 
     # clocks are sampled from the start of the warm-up to the end of both
     # timed regions (a 50 ms sampling period would miss a short timed region)

@@ -175,8 +175,8 @@ TGS_API int tgs_raster_counts(TgsRaster* r, TgsRasterCounts* out, tgs_stream_t s
 /* Debug / parity access to the intermediate state of the last forward
  * (device pointers owned by the handle, valid until the next forward):
  *   which = 0 n_touched_tiles   uint32[n]
- *         = 1 instance tile ids  uint32[n_instances]   (sorted)
- *         = 2 instance prim ids  uint32[n_instances]   (sorted)
+ *         = 1 (not kept: the tile of each instance follows from the ranges)
+ *         = 2 instance prim ids  uint32[n_instances]   (tile-major, depth order)
  *         = 3 tile ranges        uint32[2*n_tiles]      [start, end)
  *         = 4 per-pixel contribution counts  uint32[Hp*Wp] (fp32 path)
  *                                            uint16[Hp*Wp] (fp16 path)

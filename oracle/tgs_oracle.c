@@ -1496,3 +1496,223 @@ void orc_adam(int64_t count, float* theta, const float* grad, float* m,
         v[i] = vv;
     }
 }
+
+/* ------------------------------------------------------ densification */
+
+#define PCG32_MULT 0x5851f42d4c957f2dULL
+
+uint32_t orc_pcg32_next_uint(OrcPcg32* r) {
+    const uint64_t old = r->state;
+    r->state = old * PCG32_MULT + r->inc;
+    const uint32_t xorshifted = (uint32_t)(((old >> 18u) ^ old) >> 27u);
+    const uint32_t rot = (uint32_t)(old >> 59u);
+    return (xorshifted >> rot) | (xorshifted << ((~rot + 1u) & 31u));
+}
+
+void orc_pcg32_seed(OrcPcg32* r, uint64_t initstate, uint64_t initseq) {
+    r->state = 0u;
+    r->inc = (initseq << 1u) | 1u;
+    (void)orc_pcg32_next_uint(r);
+    r->state += initstate;
+    (void)orc_pcg32_next_uint(r);
+}
+
+/* [0, 1): 23 random mantissa bits under exponent 0, minus 1 */
+float orc_pcg32_next_float(OrcPcg32* r) {
+    union {
+        uint32_t u;
+        float f;
+    } x;
+    x.u = (orc_pcg32_next_uint(r) >> 9) | 0x3f800000u;
+    return x.f - 1.0f;
+}
+
+/* jump ahead by delta draws: the LCG's affine map composed by squaring
+ * (F. B. Brown, "Random number generation with arbitrary strides", 1994) */
+void orc_pcg32_advance(OrcPcg32* r, uint64_t delta) {
+    uint64_t cur_mult = PCG32_MULT, cur_plus = r->inc, acc_mult = 1u, acc_plus = 0u;
+    while (delta > 0) {
+        if (delta & 1u) {
+            acc_mult *= cur_mult;
+            acc_plus = acc_plus * cur_mult + cur_plus;
+        }
+        cur_plus = (cur_mult + 1u) * cur_plus;
+        cur_mult *= cur_mult;
+        delta >>= 1u;
+    }
+    r->state = acc_mult * r->state + acc_plus;
+}
+
+/* common.hpp:358-364 */
+static inline float logistic_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+static inline float logit_f(float x) { return -logf(1.0f / clampf(x, 1e-9f, 1.0f - 1e-9f) - 1.0f); }
+
+void orc_random_logistic(OrcPcg32* r, int64_t n, float* out) {
+    const int64_t per = 4, block = 128;
+    const int64_t work = (n + per - 1) / per;
+    const int64_t threads = ((work + block - 1) / block) * block;
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t idx = 0; idx < n; ++idx) {
+        OrcPcg32 g = *r;
+        orc_pcg32_advance(&g, (uint64_t)((idx % threads) * per + idx / threads));
+        out[idx] = logit_f(orc_pcg32_next_float(&g)) * 1.0f * 0.551328895f + 0.0f;
+    }
+    orc_pcg32_advance(r, (uint64_t)n);
+}
+
+static const int kSegW[6] = {3, 1, 4, 3, 3, 45};
+static float* seg_of(OrcSet s, int k) {
+    switch (k) {
+        case 0: return s.means;
+        case 1: return s.opacities;
+        case 2: return s.rotations;
+        case 3: return s.scales;
+        case 4: return s.sh0;
+        default: return s.sh_rest;
+    }
+}
+
+static void zero_rows(OrcSet s, int64_t from, int64_t to) {
+    for (int k = 0; k < 6; ++k) {
+        float* p = seg_of(s, k);
+        if (p != NULL && to > from) memset(p + from * kSegW[k], 0, sizeof(float) * (size_t)((to - from) * kSegW[k]));
+    }
+}
+
+/* stable compaction of the rows with keep[i] != 0 */
+static void compact_rows(OrcSet s, const uint8_t* keep, int64_t n) {
+    for (int k = 0; k < 6; ++k) {
+        float* p = seg_of(s, k);
+        if (p == NULL) continue;
+        const int w = kSegW[k];
+        int64_t o = 0;
+        for (int64_t i = 0; i < n; ++i)
+            if (keep[i]) {
+                if (o != i) memmove(p + o * w, p + i * w, sizeof(float) * (size_t)w);
+                ++o;
+            }
+    }
+}
+
+int64_t orc_densify_step(int64_t n, int64_t capacity, OrcSet params, OrcSet grads, OrcSet exp_avg,
+                         OrcSet exp_avg_sq, float* dens, const OrcDensifyConfig* cfg, int32_t step,
+                         OrcPcg32* rng) {
+    const int refine = step % cfg->refine_every == 0 && step >= cfg->start_refine && step <= cfg->end_refine;
+    if (refine) {
+        const int64_t n0 = n;
+        /* duplicate (default.cu:151-296) */
+        uint8_t* flag = (uint8_t*)calloc((size_t)(n0 > 0 ? n0 : 1), 1);
+        int64_t grows = 0;
+        if (n0 < cfg->max_num_gaussians) {
+            const float grow_scale = cfg->duplicate_scale_threshold * cfg->scene_scale;
+            const float grow_grad = cfg->duplicate_grad_threshold * cfg->grad_scaler;
+            for (int64_t i = 0; i < n0; ++i) {
+                const float* d = dens + 4 * i;
+                const float accum = cfg->absgrad ? d[2] : d[1];
+                const float grad = accum / fmaxf(d[0], 1.0f);
+                if (grad > grow_grad && d[0] > 0.0f) {
+                    const float* sc = params.scales + 3 * i;
+                    const float mx = fmaxf(fmaxf(expf(sc[0]), expf(sc[1])), expf(sc[2]));
+                    flag[i] = mx > grow_scale ? 2 : 1;
+                    ++grows;
+                }
+            }
+        }
+        if (n0 + grows > capacity) {
+            free(flag);
+            return -1;
+        }
+        if (grows > 0) {
+            float* rnd = (float*)malloc(sizeof(float) * (size_t)(6 * grows));
+            orc_random_logistic(rng, 6 * grows, rnd);
+            /* appended rows start as zeros (GPUGaussian3d::append, SimpleAdam::duplicate) */
+            zero_rows(grads, n0, n0 + grows);
+            zero_rows(exp_avg, n0, n0 + grows);
+            zero_rows(exp_avg_sq, n0, n0 + grows);
+            int64_t g = 0;
+            for (int64_t src = 0; src < n0; ++src) {
+                if (!flag[src]) continue;
+                const int64_t dst = n0 + g;
+                memcpy(params.rotations + 4 * dst, params.rotations + 4 * src, 4 * sizeof(float));
+                memcpy(params.sh0 + 3 * dst, params.sh0 + 3 * src, 3 * sizeof(float));
+                memcpy(params.sh_rest + 45 * dst, params.sh_rest + 45 * src, 45 * sizeof(float));
+                if (flag[src] == 1) {
+                    memcpy(params.means + 3 * dst, params.means + 3 * src, 3 * sizeof(float));
+                    memcpy(params.scales + 3 * dst, params.scales + 3 * src, 3 * sizeof(float));
+                    params.opacities[dst] = params.opacities[src];
+                } else {
+                    /* split: glm::mat3 built column by column from (w, x, y, z)
+                     * (default.cu:268-276), applied as a column-major matrix */
+                    const float* q = params.rotations + 4 * src;
+                    const float r = q[0], x = q[1], y = q[2], z = q[3];
+                    const float c0[3] = {1.f - 2.f * (y * y + z * z), 2.f * (x * y - r * z), 2.f * (x * z + r * y)};
+                    const float c1[3] = {2.f * (x * y + r * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z - r * x)};
+                    const float c2[3] = {2.f * (x * z - r * y), 2.f * (y * z + r * x), 1.f - 2.f * (x * x + y * y)};
+                    const float* sc = params.scales + 3 * src;
+                    const float act[3] = {expf(sc[0]), expf(sc[1]), expf(sc[2])};
+                    const float new_op = 1.0f - sqrtf(1.0f - logistic_f(params.opacities[src]));
+                    const float* r1 = rnd + 6 * g;
+                    const float* r2 = rnd + 6 * g + 3;
+                    float v1[3], v2[3];
+                    for (int k = 0; k < 3; ++k) {
+                        v1[k] = r1[k] * (act[k] + 1e-5f);
+                        v2[k] = r2[k] * (act[k] + 1e-5f);
+                    }
+                    float* ms = params.means + 3 * src;
+                    float* md = params.means + 3 * dst;
+                    for (int k = 0; k < 3; ++k) {
+                        const float off1 = c0[k] * v1[0] + c1[k] * v1[1] + c2[k] * v1[2];
+                        const float off2 = c0[k] * v2[0] + c1[k] * v2[1] + c2[k] * v2[2];
+                        md[k] = ms[k] + off1;
+                        ms[k] = ms[k] + off2;
+                    }
+                    for (int k = 0; k < 3; ++k) {
+                        const float ns = logf(act[k] / 1.6f);
+                        params.scales[3 * dst + k] = ns;
+                        params.scales[3 * src + k] = ns;
+                    }
+                    params.opacities[dst] = logit_f(new_op);
+                    params.opacities[src] = logit_f(new_op);
+                }
+                ++g;
+            }
+            free(rnd);
+        }
+        free(flag);
+        n = n0 + grows;
+        /* prune (default.cu:298-345) */
+        uint8_t* keep = (uint8_t*)malloc((size_t)(n > 0 ? n : 1));
+        const float ss_thr = (float)(cfg->image_width > cfg->image_height ? cfg->image_width : cfg->image_height) *
+                             cfg->max_screen_size;
+        const int prune_large = step > cfg->reset_every;
+        int64_t kept = 0;
+        for (int64_t i = 0; i < n; ++i) {
+            const float* sc = params.scales + 3 * i;
+            const float mx = fmaxf(fmaxf(expf(sc[0]), expf(sc[1])), expf(sc[2]));
+            const int not_large_ws = mx < cfg->pruning_scale_threshold * cfg->scene_scale;
+            const int not_large_ss = i >= n0 || dens[4 * i + 3] < ss_thr;
+            const int not_transparent = logistic_f(params.opacities[i]) > cfg->pruning_opacity_threshold;
+            const float* q = params.rotations + 4 * i;
+            const int not_degenerate = fabsf(q[0]) + fabsf(q[1]) + fabsf(q[2]) + fabsf(q[3]) > 1.1920929e-07f;
+            keep[i] = (uint8_t)(not_transparent && ((not_large_ws && not_large_ss) || !prune_large) && not_degenerate);
+            kept += keep[i];
+        }
+        if (kept > 0) {  /* StrategyBase::on_remove returns early on 0 (strategy.cpp:21) */
+            compact_rows(params, keep, n);
+            compact_rows(grads, keep, n);
+            compact_rows(exp_avg, keep, n);
+            compact_rows(exp_avg_sq, keep, n);
+            n = kept;
+        }
+        free(keep);
+        memset(dens, 0, sizeof(float) * 4 * (size_t)n);
+    }
+    if (cfg->reset_every > 0 && step % cfg->reset_every == 0 && step >= cfg->start_refine &&
+        step < cfg->end_refine) {
+        const float cap = 2.0f * cfg->pruning_opacity_threshold;
+        for (int64_t i = 0; i < n; ++i) params.opacities[i] = logit_f(fminf(logistic_f(params.opacities[i]), cap));
+        if (exp_avg.opacities) memset(exp_avg.opacities, 0, sizeof(float) * (size_t)n);
+        if (exp_avg_sq.opacities) memset(exp_avg_sq.opacities, 0, sizeof(float) * (size_t)n);
+    }
+    return n;
+}

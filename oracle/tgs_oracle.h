@@ -154,6 +154,68 @@ void orc_adam(int64_t count, float* theta, const float* grad, float* m,
               float bias_correction2_sqrt, float max_grad_1,
               int32_t decay_kind, float decay);
 
+/* ------------------------------------------------------ densification */
+
+/* PCG32 (M. E. O'Neill, "PCG: A Family of Simple Fast Space-Efficient
+ * Statistically Good Algorithms for Random Number Generation", 2014: 64-bit
+ * LCG state, XSH-RR 32-bit output), seeded and advanced as
+ * tinygs/include/tinygs/random/pcg32.hpp:40-150 does. */
+typedef struct OrcPcg32 {
+    uint64_t state;
+    uint64_t inc;
+} OrcPcg32;
+void orc_pcg32_seed(OrcPcg32* r, uint64_t initstate, uint64_t initseq);
+uint32_t orc_pcg32_next_uint(OrcPcg32* r);
+float orc_pcg32_next_float(OrcPcg32* r);
+void orc_pcg32_advance(OrcPcg32* r, uint64_t delta);
+/* generate_random_logistic(rng, n, out, 0, 1), random/device.cuh:38-79:
+ * element idx is draw (idx % T) * 4 + idx / T of the stream, T the number of
+ * threads its launch has; the generator then advances by n. */
+void orc_random_logistic(OrcPcg32* r, int64_t n, float* out);
+
+/* The six parameter arrays of one set (parameters, gradients or a moment),
+ * each holding `capacity` Gaussians. */
+typedef struct OrcSet {
+    float* means;      /* [cap][3] */
+    float* opacities;  /* [cap]    */
+    float* rotations;  /* [cap][4] (w, x, y, z) */
+    float* scales;     /* [cap][3] */
+    float* sh0;        /* [cap][3] */
+    float* sh_rest;    /* [cap][45] */
+} OrcSet;
+
+typedef struct OrcDensifyConfig {
+    float duplicate_grad_threshold;
+    float duplicate_scale_threshold;
+    float pruning_opacity_threshold;
+    float pruning_scale_threshold;
+    float max_screen_size;
+    float scene_scale;
+    float grad_scaler;
+    int32_t absgrad;
+    int32_t refine_every;
+    int32_t start_refine;
+    int32_t end_refine;
+    int32_t reset_every;
+    int32_t image_width;
+    int32_t image_height;
+    int32_t _pad;
+    int64_t max_num_gaussians;
+} OrcDensifyConfig;
+
+/* DefaultStrategy::step_impl at strategy step `step`
+ * (tinygs/src/strategy/default.cu:40-69): refine (duplicate, default.cu:75-296,
+ * then prune, :298-345, with the stable compaction of gpu_gaussian.cu:117-160
+ * and simple_adam.cu:841-906; appended Gaussians get zero gradients and
+ * moments, strategy.cpp:34-46, simple_adam.cu:908-924) and the opacity reset
+ * (default.cu:26-38, simple_adam.cu:981-985).  dens is [n][4] (counter,
+ * grad, absgrad, max radius) and is zeroed after a refine.  Sets whose
+ * pointers are NULL are skipped.  Returns the new Gaussian count, or -1 if
+ * the growth would pass `capacity` (nothing is modified then). */
+int64_t orc_densify_step(int64_t n, int64_t capacity, OrcSet params, OrcSet grads, OrcSet exp_avg,
+                         OrcSet exp_avg_sq, float* dens, const OrcDensifyConfig* cfg, int32_t step,
+                         OrcPcg32* rng);
+
 /* Timing samples only: blend stages process every `stride`-th tile. */
 void orc_set_tile_stride(int32_t stride);
 

@@ -70,9 +70,14 @@ class GpuRun:
         gw, gh = (self.W + 15) // 16, (self.H + 15) // 16
         r = self.rast
         ni = int(c.n_instances)
-        return {"inst_tile": to_np(r.debug_array(1, torch.int16, ni)).view(np.uint16).astype(np.uint32),
+        ranges = to_np(r.debug_array(3, torch.int32, 2 * gw * gh)).view(np.uint32).reshape(gw * gh, 2)
+        # tiles are not stored per instance: tile t owns [ranges[t,0], ranges[t,1])
+        tiles = np.zeros(ni, np.uint32)
+        for t in np.nonzero(ranges[:, 1] > ranges[:, 0])[0]:
+            tiles[ranges[t, 0]:ranges[t, 1]] = t
+        return {"inst_tile": tiles,
                 "inst_prim": to_np(r.debug_array(2, torch.int32, ni)).view(np.uint32),
-                "ranges": to_np(r.debug_array(3, torch.int32, 2 * gw * gh)).view(np.uint32).reshape(gw * gh, 2),
+                "ranges": ranges,
                 "bucket_offsets": to_np(r.debug_array(13, torch.int32, gw * gh)).view(np.uint32),
                 "n_instances": ni, "n_buckets": int(c.n_buckets), "n_visible": int(c.n_visible),
                 "sorted_visible": to_np(r.debug_array(10, torch.int32, int(c.n_visible))).view(np.uint32)}

@@ -149,7 +149,6 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   s.vis_idx[0] = c.take<uint32_t>(n);
   s.vis_idx[1] = c.take<uint32_t>(n);
   s.block_sums = c.take<uint32_t>((n + 255) / 256 + 1);
-  s.inst_key[0] = c.take<uint16_t>(ni);
   s.inst_prim[0] = c.take<uint32_t>(ni);
   const size_t ne = static_cast<size_t>(s.cap_entries > 0 ? s.cap_entries : 1);
   const size_t ns = static_cast<size_t>(s.max_super);
@@ -419,7 +418,6 @@ int tgs_raster_debug_buffer(TgsRaster* r, int32_t which, void** dev_ptr, size_t*
   const size_t n = static_cast<size_t>(s.cap_n);
   switch (which) {
     case 0: *dev_ptr = s.n_touched; *bytes = 4 * n; break;
-    case 1: *dev_ptr = s.inst_key[s.tile_result]; *bytes = 2 * static_cast<size_t>(s.cap_inst); break;
     case 2: *dev_ptr = s.inst_prim[s.tile_result]; *bytes = 4 * static_cast<size_t>(s.cap_inst); break;
     case 3: *dev_ptr = s.ranges; *bytes = 8 * static_cast<size_t>(s.max_tiles); break;
     case 4: *dev_ptr = s.n_contrib; *bytes = 4 * static_cast<size_t>(s.max_pixels); break;

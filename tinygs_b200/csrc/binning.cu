@@ -425,9 +425,7 @@ __device__ __forceinline__ TileTest tile_test_of(uint32_t p, const float2* __res
   q.my = m.y - 0.5f;
   if constexpr (kFp16) {
     const PrimInfo16 rec = prim_info[p];
-    q.h_xy = rec.conic_xy;
-    q.h_zw = rec.conic_z_opacity;
-    q.thr = __logf(__high2float(rec.conic_z_opacity) * 255.0f);
+    tile_test_f16(q, q.mx, q.my, rec.conic_xy, rec.conic_z_opacity);
   } else {
     const float4 co = conic_opacity[p];
     q.ca = co.x;
@@ -452,6 +450,7 @@ __global__ void __launch_bounds__(kScanBlock)
   const unsigned full = 0xffffffffu;
   const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
   const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t lt = lanemask_lt();
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const uint4 ch = chunks[c];
     const uint32_t tx0 = (ch.x % super_w) * kSuperW, ty0 = (ch.x / super_w) * kSuperH;
@@ -483,24 +482,28 @@ __global__ void __launch_bounds__(kScanBlock)
       const uint32_t start = incl - total;
       const uint32_t pairs = __shfl_sync(full, incl, 31);
       uint32_t local = 0;  // hits in rectangle order (bit t = row t / w, column t % w)
+      // owners are lanes 0 .. (valid entries - 1), every one with total >= 1,
+      // so the owner of a slot is the number of rectangle starts up to it - 1
+      uint32_t starts_before = 0;
       for (uint32_t base = 0; base < pairs; base += 32u) {
         const uint32_t slot = base + lane;
-        uint32_t owner = 0;
-#pragma unroll
-        for (uint32_t step = 16; step >= 1; step >>= 1) {
-          const uint32_t o = __shfl_sync(full, start, owner + step);
-          if (o <= slot) owner += step;
-        }
+        const uint32_t sbit = total > 0u && start >= base && start < base + 32u ? 1u << (start - base) : 0u;
+        const uint32_t starts = __reduce_or_sync(full, sbit);
+        const uint32_t owner = starts_before + __popc(starts & (lt | (1u << lane))) - 1u;
+        starts_before += __popc(starts);
         TileTest q;
-        q.mx = __shfl_sync(full, tt.mx, owner);
-        q.my = __shfl_sync(full, tt.my, owner);
+        q.ca = __shfl_sync(full, tt.ca, owner);
+        q.cb = __shfl_sync(full, tt.cb, owner);
+        q.cc = __shfl_sync(full, tt.cc, owner);
         if constexpr (kFp16) {
-          q.h_xy = __shfl_sync(full, tt.h_xy, owner);
-          q.h_zw = __shfl_sync(full, tt.h_zw, owner);
+          q.xs = __shfl_sync(full, tt.xs, owner);
+          q.ys = __shfl_sync(full, tt.ys, owner);
+          q.c_xy = __shfl_sync(full, tt.c_xy, owner);
+          q.c_yz = __shfl_sync(full, tt.c_yz, owner);
+          q.c_xz = __shfl_sync(full, tt.c_xz, owner);
         } else {
-          q.ca = __shfl_sync(full, tt.ca, owner);
-          q.cb = __shfl_sync(full, tt.cb, owner);
-          q.cc = __shfl_sync(full, tt.cc, owner);
+          q.mx = __shfl_sync(full, tt.mx, owner);
+          q.my = __shfl_sync(full, tt.my, owner);
         }
         q.thr = __shfl_sync(full, tt.thr, owner);
         const uint32_t o_start = __shfl_sync(full, start, owner);
@@ -631,63 +634,47 @@ __global__ void __launch_bounds__(1024)
   }
 }
 
-// 6. per chunk: every hit of every entry to its slot.  The chunk's hit
-// masks and Gaussian ids are staged in shared memory; each warp owns four of
-// the 32 tiles and walks the entries in order, so the hits of a tile are
-// compacted by ballot and stored as one contiguous run starting at the
-// tile's start + the chunk's prefix for it.
-__global__ void __launch_bounds__(kScanBlock)
+// 6. per chunk (one warp each): every hit of every entry to its slot.  The
+// warp walks the chunk's entries 32 at a time in order; lane j holds the
+// next slot of tile j of the super-tile (the tile's start + the chunk's
+// prefix for it).  For each tile hit in the window, the ballot of the
+// entries that hit it gives each of them its rank, and those entries store
+// their Gaussian ids as one contiguous run.  The tiles of the instances are
+// implied by the tile ranges and are not stored.
+constexpr int kEmitWarps = 4;
+
+__global__ void __launch_bounds__(32 * kEmitWarps)
     k_emit_instances(const uint4* __restrict__ chunks, const uint32_t* __restrict__ ent_prim,
                      const uint32_t* __restrict__ masks, const uint32_t* __restrict__ chunk_prefix,
                      const uint2* __restrict__ ranges, const DevCounts* __restrict__ counts, uint32_t super_w,
-                     uint32_t grid_w, uint32_t grid_h, uint16_t* __restrict__ inst_key,
-                     uint32_t* __restrict__ inst_prim) {
-  constexpr int kWarps = kScanBlock / 32;
-  __shared__ uint32_t s_mask[kChunk];
-  __shared__ uint32_t s_prim[kChunk];
-  __shared__ uint32_t s_or;
+                     uint32_t grid_w, uint32_t grid_h, uint32_t* __restrict__ inst_prim) {
   const unsigned full = 0xffffffffu;
   const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   const uint32_t lt = lanemask_lt();
-  for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+  for (uint32_t c = blockIdx.x * kEmitWarps + warp; c < n_chunks; c += gridDim.x * kEmitWarps) {
     const uint4 ch = chunks[c];
-    const uint32_t n_e = ch.z - ch.y;
-    const uint32_t tx0 = (ch.x % super_w) * kSuperW, ty0 = (ch.x / super_w) * kSuperH;
-    if (threadIdx.x == 0) s_or = 0;
-    __syncthreads();
-    uint32_t any = 0;
-    for (uint32_t i = threadIdx.x; i < n_e; i += kScanBlock) {
-      const uint32_t m = masks[ch.y + i];
-      s_mask[i] = m;
-      s_prim[i] = ent_prim[ch.y + i];
-      any |= m;
-    }
-    any = __reduce_or_sync(full, any);
-    if (lane == 0 && any) atomicOr(&s_or, any);
-    __syncthreads();
-    const uint32_t used = s_or;
+    const uint32_t tx = (ch.x % super_w) * kSuperW + lane % kSuperW;
+    const uint32_t ty = (ch.x / super_w) * kSuperH + lane / kSuperW;
+    uint32_t pos = 0;  // next slot of tile `lane`
+    if (tx < grid_w && ty < grid_h) pos = ranges[ty * grid_w + tx].x + chunk_prefix[c * kSuperTiles + lane];
+    for (uint32_t e0 = ch.y; e0 < ch.z; e0 += 32u) {
+      const uint32_t e = e0 + lane;
+      uint32_t mask = 0, prim = 0;
+      if (e < ch.z) {
+        mask = masks[e];
+        prim = ent_prim[e];
+      }
+      const uint32_t any = __reduce_or_sync(full, mask);
 #pragma unroll
-    for (int q = 0; q < kSuperTiles / kWarps; ++q) {
-      const uint32_t j = warp * (kSuperTiles / kWarps) + q;
-      if (((used >> j) & 1u) == 0u) continue;  // warp-uniform
-      const uint32_t tx = tx0 + j % kSuperW, ty = ty0 + j / kSuperW;
-      const uint32_t tile = ty * grid_w + tx;  // inside the grid: it has hits
-      uint32_t pos = ranges[tile].x + chunk_prefix[c * kSuperTiles + j];
-      for (uint32_t b0 = 0; b0 < n_e; b0 += 32u) {
-        const uint32_t i = b0 + lane;
-        const bool hit = i < n_e && ((s_mask[i] >> j) & 1u);
-        const uint32_t bm = __ballot_sync(full, hit);
-        if (hit) {
-          const uint32_t at = pos + __popc(bm & lt);
-          inst_key[at] = static_cast<uint16_t>(tile);
-          inst_prim[at] = s_prim[i];
-        }
-        pos += __popc(bm);
+      for (int j = 0; j < kSuperTiles; ++j) {
+        if (((any >> j) & 1u) == 0u) continue;  // warp-uniform
+        const uint32_t bj = __ballot_sync(full, (mask >> j) & 1u);
+        const uint32_t p = __shfl_sync(full, pos, j);
+        if ((bj >> lane) & 1u) inst_prim[p + __popc(bj & lt)] = prim;
+        if (lane == static_cast<uint32_t>(j)) pos += __popc(bj);
       }
     }
-    (void)grid_h;
-    __syncthreads();
   }
 }
 
@@ -764,9 +751,9 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   k_tile_offsets<<<1, 1024, 0, stream>>>(s.tile_total, n_tiles, s.ranges, s.bucket_offsets, counts,
                                           static_cast<uint32_t>(s.cap_inst), static_cast<uint32_t>(s.cap_buckets));
   // 6. instances at their final slots
-  k_emit_instances<<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.masks, s.chunk_counts, s.ranges,
-                                                           counts, super_w, cam.grid_w, cam.grid_h,
-                                                           s.inst_key[0], s.inst_prim[0]);
+  k_emit_instances<<<s.num_sms * 8, 32 * kEmitWarps, 0, stream>>>(s.chunks, ent_prim, s.masks, s.chunk_counts,
+                                                                   s.ranges, counts, super_w, cam.grid_w, cam.grid_h,
+                                                                   s.inst_prim[0]);
   s.tile_result = 0;
 }
 

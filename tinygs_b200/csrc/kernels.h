@@ -56,9 +56,9 @@ struct RasterState {
   uint32_t* super_chunk = nullptr;   // first chunk of each super-tile
   uint4* chunks = nullptr;           // (super-tile, first entry, end entry)
   uint32_t* chunk_counts = nullptr;  // [chunk][32] hits per tile, then first-slot offsets
-  // per instance, in final (tile, depth, index) order
-  uint16_t* inst_key[2] = {nullptr, nullptr};  // only [0] is allocated
-  uint32_t* inst_prim[2] = {nullptr, nullptr};
+  // per instance, in final (tile, depth, index) order (the tile of an
+  // instance follows from the tile ranges)
+  uint32_t* inst_prim[2] = {nullptr, nullptr};  // only [0] is allocated
   // radix sort scratch
   uint32_t* sort_hist = nullptr;    // [256][sort_max_blocks]
   uint32_t* sort_digit_total = nullptr;  // [256]

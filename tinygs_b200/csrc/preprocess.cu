@@ -21,6 +21,23 @@ namespace {
 
 constexpr int kPreBlock = 256;
 
+// 16-byte (or 4-byte) asynchronous global -> shared copies (cp.async), so
+// that the loads of a whole warp slice are in flight at once.
+__device__ __forceinline__ void cp_async16(float* smem_dst, const float* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gmem_src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kPending));
+}
+
+
 // Real spherical-harmonic basis up to degree 3 at the unit direction (x,y,z),
 // normalisation constants of the standard real SH
 // (fastgs_ours/kernels_forward.cuh:22-46).
@@ -133,6 +150,22 @@ __global__ void __launch_bounds__(kPreBlock)
   // row per lane would touch 32 cache lines per load instruction)
   __shared__ __align__(16) float s_rest[kPreBlock / 32][32 * 45];
   const uint32_t i = blockIdx.x * kPreBlock + threadIdx.x;
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  // start the copy of the warp's SH rows now; it lands while the projection
+  // below is computed (rows of culled Gaussians are copied too)
+  const uint32_t first = i - lane;
+  const bool stage_rest = active_bases > 1 && first < n;
+  if (stage_rest) {
+    const uint32_t cnt = min(32u, n - first);
+    const float* src = sh_rest + 45 * static_cast<size_t>(first);
+    float* dst = s_rest[warp];
+    if (rest_vec && cnt == 32u) {
+      for (uint32_t e = lane; e < 32u * 45u / 4u; e += 32u) cp_async16(dst + 4 * e, src + 4 * e);
+    } else {
+      for (uint32_t e = lane; e < cnt * 45u; e += 32u) cp_async4(dst + e, src + e);
+    }
+  }
+  cp_async_commit();
   const bool in_range = i < n;
   const uint32_t gi = in_range ? i : (n > 0 ? n - 1 : 0);
 
@@ -207,20 +240,8 @@ __global__ void __launch_bounds__(kPreBlock)
   }
   const bool candidate = in_range && warp_alive && active;
 
-  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  if (active_bases > 1 && __ballot_sync(0xffffffffu, candidate) != 0u) {
-    const uint32_t first = i - lane;  // < n: some lane is in range
-    const uint32_t cnt = min(32u, n - first);
-    const float* src = sh_rest + 45 * static_cast<size_t>(first);
-    float* dst = s_rest[warp];
-    if (rest_vec && cnt == 32u) {
-      for (uint32_t e = lane; e < 32u * 45u / 4u; e += 32u)
-        reinterpret_cast<float4*>(dst)[e] = reinterpret_cast<const float4*>(src)[e];
-    } else {
-      for (uint32_t e = lane; e < cnt * 45u; e += 32u) dst[e] = src[e];
-    }
-    __syncwarp();
-  }
+  cp_async_wait<0>();
+  __syncwarp();
 
   if (in_range) {
     n_touched[i] = 0;  // binning adds the hits of each super-tile
@@ -504,22 +525,6 @@ __device__ __forceinline__ void adam_element(float& th, float g_raw, float& m, f
   const float mh = m / a.bc1;
   const float den = sqrtf(v) / a.bc2_sqrt + a.eps;
   th -= mh * lr / den;
-}
-
-// 16-byte (or 4-byte) asynchronous global -> shared copies (cp.async), so
-// that the loads of a whole warp slice are in flight at once.
-__device__ __forceinline__ void cp_async16(float* smem_dst, const float* gmem_src) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem_src));
-}
-__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gmem_src) {
-  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gmem_src));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int kPending>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(kPending));
 }
 
 // Copy the warp's slice of six segments (rows of `cnt` Gaussians) into

@@ -42,21 +42,21 @@ __device__ __forceinline__ bool tile_overlaps_f32(float mx, float my, float ca, 
 // (fastgs_ours_fp16/kernels_forward.cuh:123-169): the tile-relative
 // distances and the edge parameter are evaluated in fp16 on the packed
 // conic, the final exponent in fp32.  Same operation sequence as the
-// reference so that instance lists coincide.
-__device__ __forceinline__ bool tile_overlaps_f16(float mx, float my, __half2 conic_xy, __half2 conic_zw,
-                                                  uint32_t tx, uint32_t ty, float thr) {
-  const __half2 one = __float2half2_rn(1.0f);
+// reference so that instance lists coincide.  The per-primitive terms
+// (mean / 16, conic component pairs, conic in fp32) come precomputed.
+__device__ __forceinline__ bool tile_overlaps_f16(float xs, float ys, __half2 c_xy, __half2 c_yz, __half2 c_xz,
+                                                  float fa, float fb, float fc, uint32_t tx, uint32_t ty,
+                                                  float thr) {
   const __half2 zero = __float2half2_rn(0.0f);
   const __half span_h = __float2half_rd(static_cast<float>(kTile - 1) / static_cast<float>(kTile));
   const __half2 span = __halves2half2(span_h, span_h);
-  const __half2 lo = __halves2half2(__float2half_rd(static_cast<float>(tx) - mx * (1.0f / kTile)),
-                                    __float2half_rd(static_cast<float>(ty) - my * (1.0f / kTile)));
+  const __half2 lo = __halves2half2(__float2half_rd(static_cast<float>(tx) - xs),
+                                    __float2half_rd(static_cast<float>(ty) - ys));
   const __half2 hi = __hadd2(lo, span);
   const __half2 before = __hgtu2(lo, zero);  // 1.0 where the mean lies before the tile
   const __half2 after = __hltu2(hi, zero);   // 1.0 where it lies after it
   const __half2 outside = __hadd2(before, after);
   if (__hbeq2(outside, zero)) return true;
-  (void)one;
   // step sign from the sign of lo
   const uint32_t lo_bits = *reinterpret_cast<const uint32_t*>(&lo);
   const uint32_t span_bits = *reinterpret_cast<const uint32_t*>(&span);
@@ -67,31 +67,44 @@ __device__ __forceinline__ bool tile_overlaps_f16(float mx, float my, __half2 co
   const __half2 dist = __hneg2(__hfma2(before, lo, __hfma2(nb, hi, hi)));
   const __half2 dist_xx = __lows2half2(dist, dist);
   const __half2 dist_yy = __highs2half2(dist, dist);
-  const __half2 c_xy = conic_xy;
-  const __half2 c_yz = __halves2half2(__high2half(conic_xy), __low2half(conic_zw));
-  const __half2 c_xz = __halves2half2(__low2half(conic_xy), __low2half(conic_zw));
   const __half2 num = __hadd2(__hmul2(__hmul2(step, c_xy), dist_xx), __hmul2(__hmul2(step, c_yz), dist_yy));
   const __half2 den = __hmul2(__hmul2(step, step), c_xz);
   const __half2 t = __hmul2_sat(__h2div(num, den), __lowhigh2highlow(outside));
   const float2 q = __half22float2(__hsub2(dist, __hmul2(t, step)));
   const float qx = q.x * static_cast<float>(kTile), qy = q.y * static_cast<float>(kTile);
-  const float fa = __low2float(conic_xy), fb = __high2float(conic_xy), fc = __low2float(conic_zw);
   const float power = 0.5f * (fa * qx * qx + fc * qy * qy) + fb * qx * qy;
   return power <= thr;
 }
 
 // Per-primitive tile-test inputs in one register bundle.
 struct TileTest {
-  float mx, my;   // mean2d - 0.5
-  float ca, cb, cc;
-  __half2 h_xy, h_zw;
-  float thr;
+  float mx, my;        // mean2d - 0.5 (fp32 test)
+  float ca, cb, cc;    // conic (fp16 test: the half conic widened)
+  float xs, ys;        // (mean2d - 0.5) / 16 (fp16 test)
+  __half2 c_xy, c_yz, c_xz;  // fp16 test: conic component pairs
+  float thr;           // ln(255 * opacity)
 };
+
+// Bundle of the fp16 test from the packed conic (x, y | z, opacity).
+__device__ __forceinline__ void tile_test_f16(TileTest& q, float mx, float my, __half2 conic_xy,
+                                              __half2 conic_z_opacity) {
+  q.mx = mx;
+  q.my = my;
+  q.xs = mx * (1.0f / kTile);
+  q.ys = my * (1.0f / kTile);
+  q.c_xy = conic_xy;
+  q.c_yz = __halves2half2(__high2half(conic_xy), __low2half(conic_z_opacity));
+  q.c_xz = __halves2half2(__low2half(conic_xy), __low2half(conic_z_opacity));
+  q.ca = __low2float(conic_xy);
+  q.cb = __high2float(conic_xy);
+  q.cc = __low2float(conic_z_opacity);
+  q.thr = __logf(__high2float(conic_z_opacity) * 255.0f);
+}
 
 template <int kFp16>
 __device__ __forceinline__ bool overlaps(const TileTest& p, uint32_t tx, uint32_t ty) {
   if constexpr (kFp16)
-    return tile_overlaps_f16(p.mx, p.my, p.h_xy, p.h_zw, tx, ty, p.thr);
+    return tile_overlaps_f16(p.xs, p.ys, p.c_xy, p.c_yz, p.c_xz, p.ca, p.cb, p.cc, tx, ty, p.thr);
   else
     return tile_overlaps_f32(p.mx, p.my, p.ca, p.cb, p.cc, tx, ty, p.thr);
 }

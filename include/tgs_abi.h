@@ -196,6 +196,65 @@ TGS_API int tgs_raster_counts(TgsRaster* r, TgsRasterCounts* out, tgs_stream_t s
 TGS_API int tgs_raster_debug_buffer(TgsRaster* r, int32_t which, void** dev_ptr,
                             size_t* bytes);
 
+/* ---------------------------------------------------------- densification
+ * DefaultStrategy (tinygs/src/strategy/default.cu:26-345): clone / split the
+ * Gaussians whose mean view-space gradient is large, prune transparent,
+ * oversized or degenerate ones, reset opacities periodically.  Arrays are
+ * updated in place within their capacity (the reference reallocates every
+ * array on each refine, gpu_gaussian.cu:117-171, simple_adam.cu:841-924). */
+typedef struct TgsDensifyConfig {     /* StrategyParams, strategy.hpp:9-29 */
+    float duplicate_grad_threshold;   /* 2e-4 */
+    float duplicate_scale_threshold;  /* 0.01 */
+    float pruning_opacity_threshold;  /* 0.005 */
+    float pruning_scale_threshold;    /* 0.1 */
+    float max_screen_size;            /* 10 */
+    float scene_scale;
+    float grad_scaler;                /* RasterizeContext::grad_scaler */
+    int32_t absgrad;
+    int32_t refine_every;             /* 100 */
+    int32_t start_refine;             /* 500 */
+    int32_t end_refine;               /* 15000 */
+    int32_t reset_every;              /* 3000 */
+    int32_t image_width;              /* camera of the step (prune by screen size) */
+    int32_t image_height;
+    int32_t _pad;
+    int64_t max_num_gaussians;        /* soft cap: refine grows only below it */
+} TgsDensifyConfig;
+
+/* PCG32 generator state (pcg32.hpp:40-150); seed with tgs_pcg32_seed. */
+typedef struct TgsPcg32 {
+    uint64_t state;
+    uint64_t inc;
+} TgsPcg32;
+
+typedef struct TgsDensifier TgsDensifier;
+
+/* pcg32::seed(initstate, initseq) (pcg32.hpp:50-56); DefaultStrategy seeds
+ * with StrategyParams::seed (42) and initseq 1. */
+TGS_API void tgs_pcg32_seed(TgsPcg32* rng, uint64_t initstate, uint64_t initseq);
+
+/* Scratch for densification of sets of up to `capacity` Gaussians (one
+ * cudaMalloc).  No counterpart in the reference, which allocates its flag and
+ * index vectors on every refine (default.cu:79-236). */
+TGS_API int tgs_densify_create(int64_t capacity, TgsDensifier** out);
+TGS_API int tgs_densify_destroy(TgsDensifier* d);
+
+/* One DefaultStrategy::step_impl at strategy step `step` (default.cu:40-69):
+ * at refine steps duplicate (default.cu:75-296: clones appended in ascending
+ * source order, split offsets from generate_random_logistic over `rng`) then
+ * prune (:298-345, stable compaction of params, grads and both moments;
+ * appended rows get zero gradients and moments); at reset steps the opacity
+ * reset (:26-38) with the opacity moments zeroed.  The six arrays of each set
+ * hold `capacity` Gaussians (their n fields are ignored); *n is the live count
+ * in and out; grads may be NULL.  dens ([*n] records) is zeroed after a
+ * refine.  A refine synchronises `stream` to read the growth and survivor
+ * counts (the reference synchronises every step, default.cu:42).  Growth past
+ * the capacity returns TGS_ERR_CAPACITY with nothing modified. */
+TGS_API int tgs_densify_step(TgsDensifier* d, TgsGaussians* params, TgsGaussians* grads,
+                             TgsGaussians* exp_avg, TgsGaussians* exp_avg_sq,
+                             TgsDensificationInfo* dens, const TgsDensifyConfig* cfg,
+                             int32_t step, TgsPcg32* rng, int64_t* n, tgs_stream_t stream);
+
 /* Stage timing for profiling.  When enabled, forward and backward record a
  * CUDA event between their stages on the caller's stream (no host sync).
  * tgs_raster_stage_times() waits for those events and returns the elapsed

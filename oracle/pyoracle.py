@@ -293,3 +293,102 @@ def train_step(params: dict, sh_degree: int, cam: dict, target: np.ndarray, fp16
         adam_step(params, grads, moments[0], moments[1], cfg, step, 1.0 / grad_scaler)
         out["moments"] = moments
     return out
+
+
+# ------------------------------------------------------------ densification
+
+class OrcPcg32(ctypes.Structure):
+    _fields_ = [("state", ctypes.c_uint64), ("inc", ctypes.c_uint64)]
+
+
+class OrcSet(ctypes.Structure):
+    _fields_ = [("means", c_void_p), ("opacities", c_void_p), ("rotations", c_void_p), ("scales", c_void_p),
+                ("sh0", c_void_p), ("sh_rest", c_void_p)]
+
+
+class OrcDensifyConfig(ctypes.Structure):
+    _fields_ = [("duplicate_grad_threshold", c_float), ("duplicate_scale_threshold", c_float),
+                ("pruning_opacity_threshold", c_float), ("pruning_scale_threshold", c_float),
+                ("max_screen_size", c_float), ("scene_scale", c_float), ("grad_scaler", c_float),
+                ("absgrad", c_int32), ("refine_every", c_int32), ("start_refine", c_int32),
+                ("end_refine", c_int32), ("reset_every", c_int32), ("image_width", c_int32),
+                ("image_height", c_int32), ("_pad", c_int32), ("max_num_gaussians", c_int64)]
+
+
+SEGMENT_WIDTHS = {"means": 3, "opacities": 1, "rotations": 4, "scales": 3, "sh0": 3, "sh_rest": 45}
+
+
+def _densify_protos(lib):
+    lib.orc_pcg32_seed.argtypes = [POINTER(OrcPcg32), ctypes.c_uint64, ctypes.c_uint64]
+    lib.orc_pcg32_next_uint.restype = c_uint32
+    lib.orc_pcg32_next_uint.argtypes = [POINTER(OrcPcg32)]
+    lib.orc_pcg32_next_float.restype = c_float
+    lib.orc_pcg32_next_float.argtypes = [POINTER(OrcPcg32)]
+    lib.orc_pcg32_advance.argtypes = [POINTER(OrcPcg32), ctypes.c_uint64]
+    lib.orc_random_logistic.argtypes = [POINTER(OrcPcg32), c_int64, c_void_p]
+    lib.orc_densify_step.restype = c_int64
+    lib.orc_densify_step.argtypes = [c_int64, c_int64, OrcSet, OrcSet, OrcSet, OrcSet, c_void_p,
+                                     POINTER(OrcDensifyConfig), c_int32, POINTER(OrcPcg32)]
+    return lib
+
+
+def pcg32(seed: int, seq: int = 1) -> OrcPcg32:
+    lib = _densify_protos(load())
+    r = OrcPcg32()
+    lib.orc_pcg32_seed(ctypes.byref(r), seed, seq)
+    return r
+
+
+def pcg32_next_uint(r: OrcPcg32, count: int) -> np.ndarray:
+    lib = _densify_protos(load())
+    return np.array([lib.orc_pcg32_next_uint(ctypes.byref(r)) for _ in range(count)], np.uint32)
+
+
+def pcg32_advance(r: OrcPcg32, delta: int) -> None:
+    _densify_protos(load()).orc_pcg32_advance(ctypes.byref(r), delta)
+
+
+def random_logistic(r: OrcPcg32, n: int) -> np.ndarray:
+    lib = _densify_protos(load())
+    out = np.zeros(max(n, 1), np.float32)
+    lib.orc_random_logistic(ctypes.byref(r), n, _p(out))
+    return out[:n]
+
+
+def densify_config(**kw) -> OrcDensifyConfig:
+    c = OrcDensifyConfig(duplicate_grad_threshold=2e-4, duplicate_scale_threshold=0.01,
+                         pruning_opacity_threshold=0.005, pruning_scale_threshold=0.1, max_screen_size=10.0,
+                         scene_scale=1.0, grad_scaler=10.0, absgrad=0, refine_every=100, start_refine=500,
+                         end_refine=15000, reset_every=3000, image_width=1280, image_height=720,
+                         max_num_gaussians=10_000_000)
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def _set_of(arrays: dict | None) -> OrcSet:
+    s = OrcSet()
+    if arrays is not None:
+        for k in SEGMENT_WIDTHS:
+            setattr(s, k, arrays[k].ctypes.data)
+    return s
+
+
+def alloc_set(capacity: int, init: dict | None = None) -> dict:
+    """Arrays of `capacity` Gaussians (the first rows copied from `init`)."""
+    out = {k: np.zeros((capacity, w), np.float32) for k, w in SEGMENT_WIDTHS.items()}
+    if init is not None:
+        for k, w in SEGMENT_WIDTHS.items():
+            a = np.asarray(init[k], np.float32).reshape(-1, w)
+            out[k][: a.shape[0]] = a
+    return out
+
+
+def densify_step(n: int, params: dict, grads: dict | None, m: dict, v: dict, dens: np.ndarray,
+                 cfg: OrcDensifyConfig, step: int, rng: OrcPcg32) -> int:
+    """DefaultStrategy::step_impl on capacity-sized arrays (in place); returns
+    the new count (-1 when the growth would pass the capacity)."""
+    lib = _densify_protos(load())
+    cap = params["means"].shape[0]
+    return int(lib.orc_densify_step(n, cap, _set_of(params), _set_of(grads), _set_of(m), _set_of(v),
+                                    _p(dens), ctypes.byref(cfg), step, ctypes.byref(rng)))

@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import re
-from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int32, c_int64, c_size_t, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -58,6 +58,19 @@ class TgsAdamConfig(ctypes.Structure):
                 ("scene_scale", c_float), ("global_lr", c_float), ("decay_reduction_mean", c_int32)]
 
 
+class TgsDensifyConfig(ctypes.Structure):
+    _fields_ = [("duplicate_grad_threshold", c_float), ("duplicate_scale_threshold", c_float),
+                ("pruning_opacity_threshold", c_float), ("pruning_scale_threshold", c_float),
+                ("max_screen_size", c_float), ("scene_scale", c_float), ("grad_scaler", c_float),
+                ("absgrad", c_int32), ("refine_every", c_int32), ("start_refine", c_int32),
+                ("end_refine", c_int32), ("reset_every", c_int32), ("image_width", c_int32),
+                ("image_height", c_int32), ("_pad", c_int32), ("max_num_gaussians", c_int64)]
+
+
+class TgsPcg32(ctypes.Structure):
+    _fields_ = [("state", c_uint64), ("inc", c_uint64)]
+
+
 _P = c_void_p
 PROTOTYPES = {
     "tgs_raster_create": (c_int32, [POINTER(TgsRasterCaps), POINTER(c_void_p)]),
@@ -82,6 +95,12 @@ PROTOTYPES = {
     "tgs_adam_step": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
                                 POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32, c_float, c_int32, _P]),
     "tgs_gaussians_zero": (c_int32, [POINTER(TgsGaussians), _P]),
+    "tgs_pcg32_seed": (None, [POINTER(TgsPcg32), c_uint64, c_uint64]),
+    "tgs_densify_create": (c_int32, [c_int64, POINTER(c_void_p)]),
+    "tgs_densify_destroy": (c_int32, [_P]),
+    "tgs_densify_step": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                   POINTER(TgsGaussians), _P, POINTER(TgsDensifyConfig), c_int32, POINTER(TgsPcg32),
+                                   POINTER(c_int64), _P]),
     "tgs_status_string": (c_char_p, [c_int32]),
     "tgs_version": (c_char_p, []),
 }

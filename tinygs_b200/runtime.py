@@ -21,7 +21,8 @@ import numpy as np
 import torch
 
 from . import _abi
-from ._abi import TgsAdamConfig, TgsCamera, TgsGaussians, TgsRasterCaps, TgsRasterCounts, check, load_library
+from ._abi import (TgsAdamConfig, TgsCamera, TgsDensifyConfig, TgsGaussians, TgsPcg32, TgsRasterCaps, TgsRasterCounts,
+                   check, load_library)
 
 SEGMENTS = ("means", "opacities", "rotations", "scales", "sh0", "sh_rest")
 WIDTHS = {"means": 3, "opacities": 1, "rotations": 4, "scales": 3, "sh0": 3, "sh_rest": 45}
@@ -45,19 +46,31 @@ class GaussianSet:
     single device allocation: 59 floats per Gaussian, segments padded to a
     multiple of four Gaussians so every segment starts 16-byte aligned."""
 
-    def __init__(self, n: int, sh_degree: int, device="cuda", storage: torch.Tensor | None = None):
+    def __init__(self, n: int, sh_degree: int, device="cuda", storage: torch.Tensor | None = None,
+                 capacity: int | None = None):
         self.n = int(n)
         self.sh_degree = int(sh_degree)
-        npad = (self.n + 3) // 4 * 4
+        self.capacity = max(self.n, int(capacity) if capacity is not None else self.n)
+        npad = (self.capacity + 3) // 4 * 4
         self.npad = npad
         total = FLOATS_PER_GAUSSIAN * npad
         self.storage = storage if storage is not None else torch.zeros(total, dtype=torch.float32, device=device)
+        self.full: dict[str, torch.Tensor] = {}
         off = 0
-        self.views: dict[str, torch.Tensor] = {}
         for name in SEGMENTS:
             w = WIDTHS[name]
-            self.views[name] = self.storage[off:off + w * npad].view(npad, w)[: self.n]
+            self.full[name] = self.storage[off:off + w * npad].view(npad, w)
             off += w * npad
+        self.views: dict[str, torch.Tensor] = {}
+        self.resize(self.n)
+
+    def resize(self, n: int) -> None:
+        """Live count within the capacity (densification moves it)."""
+        if not 0 <= n <= self.capacity:
+            raise ValueError(f"{n} Gaussians do not fit a capacity of {self.capacity}")
+        self.n = int(n)
+        for name in SEGMENTS:
+            self.views[name] = self.full[name][: self.n]
 
     def __getattr__(self, name):
         views = self.__dict__.get("views")
@@ -66,9 +79,10 @@ class GaussianSet:
         raise AttributeError(name)
 
     @classmethod
-    def from_numpy(cls, arrays: dict[str, np.ndarray], sh_degree: int, device="cuda") -> "GaussianSet":
+    def from_numpy(cls, arrays: dict[str, np.ndarray], sh_degree: int, device="cuda",
+                   capacity: int | None = None) -> "GaussianSet":
         n = arrays["means"].shape[0]
-        g = cls(n, sh_degree, device)
+        g = cls(n, sh_degree, device, capacity=capacity)
         g.copy_from_numpy(arrays)
         return g
 
@@ -85,12 +99,12 @@ class GaussianSet:
         return out
 
     def zeros_like(self) -> "GaussianSet":
-        return GaussianSet(self.n, self.sh_degree, self.storage.device)
+        return GaussianSet(self.n, self.sh_degree, self.storage.device, capacity=self.capacity)
 
     def abi(self) -> TgsGaussians:
         s = TgsGaussians()
         for name in SEGMENTS:
-            setattr(s, name, self.views[name].data_ptr() if self.n > 0 else None)
+            setattr(s, name, self.full[name].data_ptr() if self.capacity > 0 else None)
         s.n = self.n
         s.sh_degree = self.sh_degree
         return s
@@ -329,3 +343,91 @@ class SimpleAdam:
         check(self.lib.tgs_adam_step(ctypes.byref(p), ctypes.byref(g), ctypes.byref(m), ctypes.byref(v),
                                      ctypes.byref(cfg), self.global_steps, float(scale), 1 if zero_grads else 0,
                                      _stream_handle(stream)), "tgs_adam_step")
+
+
+@dataclass
+class DensifyParams:
+    """StrategyParams (tinygs/include/tinygs/strategy/strategy.hpp:9-29)."""
+    pruning_opacity_threshold: float = 0.005
+    pruning_scale_threshold: float = 0.1
+    max_screen_size: float = 10.0
+    duplicate_grad_threshold: float = 0.0002
+    duplicate_scale_threshold: float = 0.01
+    absgrad: bool = False
+    refine_every: int = 100
+    start_refine: int = 500
+    end_refine: int = 15_000
+    max_num_gaussians: int = 10_000_000
+    reset_every: int = 3_000
+    seed: int = 42
+
+    def abi(self, scene_scale: float, grad_scaler: float, width: int, height: int) -> TgsDensifyConfig:
+        c = TgsDensifyConfig()
+        c.duplicate_grad_threshold = self.duplicate_grad_threshold
+        c.duplicate_scale_threshold = self.duplicate_scale_threshold
+        c.pruning_opacity_threshold = self.pruning_opacity_threshold
+        c.pruning_scale_threshold = self.pruning_scale_threshold
+        c.max_screen_size = self.max_screen_size
+        c.scene_scale = scene_scale
+        c.grad_scaler = grad_scaler
+        c.absgrad = 1 if self.absgrad else 0
+        c.refine_every, c.start_refine, c.end_refine = self.refine_every, self.start_refine, self.end_refine
+        c.reset_every = self.reset_every
+        c.image_width, c.image_height = int(width), int(height)
+        c.max_num_gaussians = self.max_num_gaussians
+        return c
+
+
+class Densifier:
+    """DefaultStrategy (tinygs/src/strategy/default.cu:17-69) over GaussianSets
+    allocated with spare capacity: step() runs once per training step after
+    the optimizer, refines / resets when the step number asks, and moves the
+    live count of the parameters, gradients and both Adam moments."""
+
+    def __init__(self, params: GaussianSet, grads: GaussianSet | None, optimizer: SimpleAdam,
+                 cfg: DensifyParams | None = None, scene_scale: float = 1.0):
+        self.lib = load_library()
+        self.params, self.grads, self.optimizer = params, grads, optimizer
+        self.cfg = cfg or DensifyParams()
+        self.scene_scale = float(scene_scale)
+        self.capacity = params.capacity
+        h = ctypes.c_void_p()
+        check(self.lib.tgs_densify_create(self.capacity, ctypes.byref(h)), "tgs_densify_create")
+        self.handle = h
+        self.rng = TgsPcg32()
+        self.lib.tgs_pcg32_seed(ctypes.byref(self.rng), self.cfg.seed, 1)
+        # densification_info records (counter, grad, absgrad, max radius)
+        self.dens_storage = torch.zeros((self.capacity, 4), dtype=torch.float32, device=params.storage.device)
+        self.step_count = 0
+
+    @property
+    def densification_info(self) -> torch.Tensor:
+        return self.dens_storage[: self.params.n]
+
+    def step(self, ctx: RasterizeContext) -> int:
+        """One strategy step; returns the new number of Gaussians."""
+        cam = ctx.fwd_input
+        cfg = self.cfg.abi(self.scene_scale, ctx.grad_scaler, int(cam["width"]), int(cam["height"]))
+        n = ctypes.c_int64(self.params.n)
+        p, m, v = self.params.abi(), self.optimizer.exp_avg.abi(), self.optimizer.exp_avg_sq.abi()
+        g = self.grads.abi() if self.grads is not None else None
+        check(self.lib.tgs_densify_step(self.handle, ctypes.byref(p), ctypes.byref(g) if g else None,
+                                        ctypes.byref(m), ctypes.byref(v), self.dens_storage.data_ptr(),
+                                        ctypes.byref(cfg), self.step_count, ctypes.byref(self.rng),
+                                        ctypes.byref(n), _stream_handle(ctx.stream)), "tgs_densify_step")
+        self.step_count += 1
+        for s in (self.params, self.grads, self.optimizer.exp_avg, self.optimizer.exp_avg_sq):
+            if s is not None:
+                s.resize(n.value)
+        return n.value
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.tgs_densify_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--n", type=int, default=0, help="override the Gaussian count (profiling small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0, help="seconds of CPU work for the baseline sample")
+    ap.add_argument("--dp", choices=["peer", "nccl"], default="peer",
+                    help="several GPUs: accumulation + Adam over NVLink peer memory in one kernel (peer) or "
+                         "an NCCL all-reduce followed by Adam on every rank (nccl, the baseline)")
     return ap.parse_args()
 
 
@@ -193,6 +196,93 @@ def cpu_oracle_step_time(cfg_name: str, budget_s: float, fp32_math: bool = True,
             "threads": O.threads(), "fp16_emulated": fp16, "n_instances": bins["n_instances"]}
 
 
+def densify_sample(n: int, seed: int = 3):
+    """Seeded cfg3-sized state for one densification refine: parameters and
+    moments of `n` Gaussians and their accumulated view-space gradient
+    statistics, about a third of them above the growth threshold."""
+    import numpy as np
+
+    from tinygs_b200 import scenes
+
+    c = scenes.CONFIGS["cfg3"]
+    params = scenes.gaussian_params(n, c.sh_degree, c.means, seed)
+    rng = np.random.default_rng(seed + 1)
+    thr = 2e-4 * GRAD_SCALER
+    counter = rng.integers(1, 20, n).astype(np.float32)
+    dens = np.zeros((n, 4), np.float32)
+    dens[:, 0] = counter
+    dens[:, 1] = counter * thr * rng.choice([0.3, 3.0], size=n, p=[0.67, 0.33]).astype(np.float32)
+    dens[:, 2] = dens[:, 1]
+    dens[:, 3] = rng.uniform(1.0, 60.0, n).astype(np.float32)
+    return params, dens
+
+
+def densify_bench(n: int, capacity: int, cpu: bool) -> dict:
+    """One DefaultStrategy refine (grow + prune + compaction of parameters,
+    gradients and both moments) at strategy step 600, timed with CUDA events
+    around tgs_densify_step; the oracle's refine on the same state beside it."""
+    import ctypes
+    import time
+
+    import numpy as np
+    import torch
+
+    from tinygs_b200 import _abi
+    from tinygs_b200 import runtime as rt
+
+    params, dens = densify_sample(n)
+    lib = _abi.load_library()
+    cfgp = rt.DensifyParams(reset_every=3000)
+    sets = [rt.GaussianSet.from_numpy(params, 3, capacity=capacity) for _ in range(1)]
+    P = sets[0]
+    G, M, V = P.zeros_like(), P.zeros_like(), P.zeros_like()
+    d = torch.zeros((capacity, 4), dtype=torch.float32, device="cuda")
+    d[:n] = torch.from_numpy(dens).cuda()
+    h = ctypes.c_void_p()
+    _abi.check(lib.tgs_densify_create(capacity, ctypes.byref(h)), "tgs_densify_create")
+    rng = _abi.TgsPcg32()
+    lib.tgs_pcg32_seed(ctypes.byref(rng), 42, 1)
+    c = cfgp.abi(1.0, GRAD_SCALER, 1280, 720)
+    nn = ctypes.c_int64(n)
+    p, g, m, v = P.abi(), G.abi(), M.abi(), V.abi()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _abi.check(lib.tgs_densify_step(h, ctypes.byref(p), ctypes.byref(g), ctypes.byref(m), ctypes.byref(v),
+                                    d.data_ptr(), ctypes.byref(c), 600, ctypes.byref(rng), ctypes.byref(nn), None),
+               "tgs_densify_step")
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    lib.tgs_densify_destroy(h)
+    n_out = nn.value
+    grown = int(((dens[:, 1] / np.maximum(dens[:, 0], 1.0)) > 2e-4 * GRAD_SCALER).sum())
+    # bytes a refine has to move: statistics and scales read for the grow
+    # test, grown rows written (parameters; zeros for gradients and moments),
+    # the prune test's reads, and the kept rows of the four sets gathered and
+    # copied back
+    alg = n * (16 + 12) + grown * 236 * 5 + (n + grown) * (4 + 12 + 16 + 16) + n_out * 4 * 236 * 3
+    out = {"refine_ms": ms, "gaussians_in": n, "grown": grown, "gaussians_out": n_out,
+           "algorithmic_bytes": alg, "achieved_gbs": alg / (ms * 1e-3) / 1e9,
+           "note": "one refine at strategy step 600 (grow, split/clone, prune, stable compaction of params, "
+                   "grads and both moments), cfg3 start size, seeded statistics; host syncs included"}
+    if cpu:
+        from oracle import pyoracle as O
+
+        cap = capacity
+        Pa, Ga = O.alloc_set(cap, params), O.alloc_set(cap)
+        Ma, Va = O.alloc_set(cap), O.alloc_set(cap)
+        da = np.zeros((cap, 4), np.float32)
+        da[:n] = dens
+        oc = O.densify_config(reset_every=3000)
+        t0 = time.perf_counter()
+        on = O.densify_step(n, Pa, Ga, Ma, Va, da, oc, 600, O.pcg32(42, 1))
+        cpu_s = time.perf_counter() - t0
+        out["cpu_refine_ms"] = cpu_s * 1e3
+        out["cpu_gaussians_out"] = on
+    return out
+
+
 def run_reference(args):
     """--impl reference: the CPU restatement of the reference algorithm."""
     rank = int(os.environ.get("RANK", "0"))
@@ -245,6 +335,7 @@ def run_ours(args):
 
     from tinygs_b200 import runtime as rt
     from tinygs_b200 import scenes
+    from tinygs_b200 import dp as dpm
     from tinygs_b200.dp import DataParallel
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -262,10 +353,18 @@ def run_ours(args):
     fp16 = cfg.dtype == "float16"
     dt = torch.float16 if fp16 else torch.float32
     params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
-    g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+    peer = world > 1 and args.dp == "peer"
+    if peer:
+        # parameters and gradient arenas the other ranks map (CUDA IPC)
+        g = dpm.shared_gaussian_set(cfg.n, cfg.sh_degree)
+        g.copy_from_numpy(params)
+        grads = dpm.shared_gaussian_set(cfg.n, cfg.sh_degree)
+        opt = dpm.PeerAdam(dp, g, grads, rt.AdamParams(max_grad_1=0.3))
+    else:
+        g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+        grads = g.zeros_like()
+        opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
     del params
-    grads = g.zeros_like()
-    opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
     cams = scenes.cameras(cfg)
     n_targets = 4
     host_targets = [torch.from_numpy(scenes.target_image(W, H, cfg.seed + 100 + k).reshape(-1)).to(dt).pin_memory()
@@ -343,6 +442,14 @@ def run_ours(args):
             ev[1].record(stream)
         if fused:
             opt.fused_backward_step(rast, ctx, 1.0 / GRAD_SCALER)
+        elif peer:
+            rast.backward(ctx)
+            if ev is not None:
+                ev[2].record(stream)
+            opt.step(dp.gradient_scale(GRAD_SCALER), stream=stream)  # barrier, kernel, barrier
+            if ev is not None:
+                ev[3].record(stream)
+                ev[4].record(stream)
         else:
             rast.backward(ctx)
             if ev is not None:
@@ -405,6 +512,9 @@ def run_ours(args):
                "blend_backward": t[3]}
         if fused:
             row["gaussian_backward_adam"] = t[4]
+        elif peer:
+            row["gaussian_backward"] = t[4]
+            row["peer_reduce_adam"] = evs[2].elapsed_time(evs[3])
         else:
             row["gaussian_backward"] = t[4]
             row["allreduce"] = evs[2].elapsed_time(evs[3])
@@ -440,6 +550,12 @@ def run_ours(args):
         kernel = "k_preprocess_backward<true> (per-Gaussian backward fused with Adam)"
         kernel_bytes = cfg.n * (6 * 236 + 4) + touched_v * 48
         kernel_ms = stages["gaussian_backward_adam"]
+    elif peer:
+        # k_preprocess_backward<false>: parameters read, gradients written,
+        # the touched-tile counts and screen-space gradients read
+        kernel = "k_preprocess_backward<false> (per-Gaussian backward, gradients to the shared arena)"
+        kernel_bytes = cfg.n * (2 * 236 + 4) + touched_v * 48
+        kernel_ms = stages["gaussian_backward"]
     else:
         kernel = "k_adam (fused Adam over the 59-float arena)"
         kernel_bytes = ADAM_BYTES_PER_GAUSSIAN * cfg.n
@@ -452,6 +568,10 @@ def run_ours(args):
     except (OSError, KeyError, ValueError):
         hbm_peak, peak_src = 6650.0, "fallback"
     tile_count = ((W + 15) // 16) * ((H + 15) // 16)
+
+    dens_row = None
+    if rank == 0 and world == 1 and args.config == "cfg2" and args.n == 0:
+        dens_row = densify_bench(1_000_000, 3_000_000, cpu=not args.no_cpu_baseline)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -485,9 +605,28 @@ def run_ours(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if dens_row is not None:
+            line["densify"] = dens_row
+        if world > 1:
+            line["config"]["dp_impl"] = args.dp
+        if peer:
+            # per rank: its slice's gradients loaded from the other ranks and
+            # its new parameters stored into them, each way over NVLink
+            # (the two one-element all-reduces that order it are included)
+            slice_bytes = 236 * cfg.n / world
+            link_bytes = slice_bytes * (world - 1)
+            ms = stages["peer_reduce_adam"]
+            line["peer_reduce_adam"] = {
+                "kernel": "k_dp_adam (gradient sum over peer memory + Adam + parameter broadcast)",
+                "ms": ms, "nvlink_bytes_each_way_per_rank": link_bytes,
+                "achieved_gbs_each_way": link_bytes / (ms * 1e-3) / 1e9,
+                "peak_gbs_each_way": 770.0, "frac": link_bytes / (ms * 1e-3) / 1e9 / 770.0,
+                "peak_source": "measured peer copy on this pool (profiling recipe)"}
         print(json.dumps(line), flush=True)
     rast.close()
     loss.close()
+    if peer:
+        opt.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

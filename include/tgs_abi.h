@@ -391,6 +391,37 @@ TGS_API const char* tgs_status_string(int status);
 /* Library version string, e.g. "tinygs-b200 0.1 sm_100a". */
 TGS_API const char* tgs_version(void);
 
+/* ------------------------------------------------ multi-GPU (one process per GPU)
+ * The reference trains on one GPU; several views per optimizer step are its
+ * gradient accumulation (Orchestrator::train_step with accumulate_grad_steps,
+ * orchestrator.cu:343-403).  Here the views of one step are rendered on
+ * several GPUs and the accumulation + Adam is one kernel over NVLink peer
+ * memory.  No counterpart functions in the reference. */
+typedef struct TgsIpcHandle {
+    char bytes[64];
+} TgsIpcHandle;
+
+/* Zeroed device memory another process can map (CUDA IPC). */
+TGS_API int tgs_shared_alloc(size_t bytes, void** ptr, TgsIpcHandle* handle);
+TGS_API int tgs_shared_free(void* ptr);
+/* Maps another process's tgs_shared_alloc memory into this one. */
+TGS_API int tgs_shared_open(const TgsIpcHandle* handle, void** peer_ptr);
+TGS_API int tgs_shared_close(void* peer_ptr);
+
+/* Rank `rank` of `world` (<= 8) owns the Gaussians [rank*n/world,
+ * (rank+1)*n/world) (rounded to multiples of 4): it sums their gradients over
+ * the ranks' gradient arenas (grads_per_rank[r], summed in rank order as the
+ * reference's accumulation adds views), applies the Adam step of
+ * tgs_adam_step with its own exp_avg / exp_avg_sq rows, and stores the new
+ * parameters into every rank's parameter arena (params_per_rank[r]).  The
+ * per-rank pointers must be valid in this process (tgs_shared_open).  The
+ * caller orders the call after every rank's backward and before every
+ * rank's next forward (for example with a collective on `stream`). */
+TGS_API int tgs_dp_reduce_adam(const TgsGaussians* params_per_rank, const TgsGaussians* grads_per_rank,
+                               int32_t world, int32_t rank, TgsGaussians* exp_avg,
+                               TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg, uint32_t step,
+                               float gradient_scale, tgs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

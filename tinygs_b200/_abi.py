@@ -71,6 +71,19 @@ class TgsPcg32(ctypes.Structure):
     _fields_ = [("state", c_uint64), ("inc", c_uint64)]
 
 
+class TgsIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+    def raw(self) -> bytes:
+        return ctypes.string_at(ctypes.addressof(self), ctypes.sizeof(self))
+
+    @classmethod
+    def from_raw(cls, data: bytes) -> "TgsIpcHandle":
+        h = cls()
+        ctypes.memmove(ctypes.addressof(h), data, min(len(data), ctypes.sizeof(h)))
+        return h
+
+
 _P = c_void_p
 PROTOTYPES = {
     "tgs_raster_create": (c_int32, [POINTER(TgsRasterCaps), POINTER(c_void_p)]),
@@ -96,6 +109,13 @@ PROTOTYPES = {
                                 POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32, c_float, c_int32, _P]),
     "tgs_gaussians_zero": (c_int32, [POINTER(TgsGaussians), _P]),
     "tgs_pcg32_seed": (None, [POINTER(TgsPcg32), c_uint64, c_uint64]),
+    "tgs_shared_alloc": (c_int32, [c_size_t, POINTER(c_void_p), POINTER(TgsIpcHandle)]),
+    "tgs_shared_free": (c_int32, [_P]),
+    "tgs_shared_open": (c_int32, [POINTER(TgsIpcHandle), POINTER(c_void_p)]),
+    "tgs_shared_close": (c_int32, [_P]),
+    "tgs_dp_reduce_adam": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), c_int32, c_int32,
+                                     POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32,
+                                     c_float, _P]),
     "tgs_densify_create": (c_int32, [c_int64, POINTER(c_void_p)]),
     "tgs_densify_destroy": (c_int32, [_P]),
     "tgs_densify_step": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),

@@ -544,4 +544,65 @@ int tgs_gaussians_zero(const TgsGaussians* g, tgs_stream_t stream) {
   return cuda_status(cudaGetLastError());
 }
 
+
+int tgs_shared_alloc(size_t bytes, void** ptr, TgsIpcHandle* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0) return TGS_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return TGS_ERR_OUT_OF_MEMORY;
+  }
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) return TGS_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, *ptr) != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return TGS_ERR_CUDA;
+  }
+  static_assert(sizeof(h) <= sizeof(handle->bytes), "IPC handle size");
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  return TGS_OK;
+}
+
+int tgs_shared_free(void* ptr) { return ptr == nullptr ? TGS_ERR_INVALID_ARGUMENT : cuda_status(cudaFree(ptr)); }
+
+int tgs_shared_open(const TgsIpcHandle* handle, void** peer_ptr) {
+  if (handle == nullptr || peer_ptr == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  if (cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    *peer_ptr = nullptr;
+    return TGS_ERR_CUDA;
+  }
+  return TGS_OK;
+}
+
+int tgs_shared_close(void* peer_ptr) {
+  return peer_ptr == nullptr ? TGS_ERR_INVALID_ARGUMENT : cuda_status(cudaIpcCloseMemHandle(peer_ptr));
+}
+
+int tgs_dp_reduce_adam(const TgsGaussians* params_per_rank, const TgsGaussians* grads_per_rank, int32_t world,
+                       int32_t rank, TgsGaussians* exp_avg, TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg,
+                       uint32_t step, float gradient_scale, tgs_stream_t stream) {
+  if (params_per_rank == nullptr || grads_per_rank == nullptr || world < 1 || world > kMaxDpRanks || rank < 0 ||
+      rank >= world || cfg == nullptr || step == 0 || !gaussians_ok(exp_avg) || !gaussians_ok(exp_avg_sq))
+    return TGS_ERR_INVALID_ARGUMENT;
+  const int64_t n = params_per_rank[rank].n;
+  GaussianPtrs p[kMaxDpRanks], g[kMaxDpRanks];
+  for (int r = 0; r < world; ++r) {
+    if (!gaussians_ok(&params_per_rank[r]) || !gaussians_ok(&grads_per_rank[r]) || params_per_rank[r].n != n ||
+        grads_per_rank[r].n != n)
+      return TGS_ERR_INVALID_ARGUMENT;
+    p[r] = to_ptrs(&params_per_rank[r]);
+    g[r] = to_ptrs(&grads_per_rank[r]);
+  }
+  if (exp_avg->n != n || exp_avg_sq->n != n) return TGS_ERR_INVALID_ARGUMENT;
+  if (n == 0) return TGS_OK;
+  AdamStepArgs a{};
+  adam_segments(cfg, n, step, gradient_scale, &a);
+  launch_dp_adam(p, g, world, rank, to_ptrs(exp_avg), to_ptrs(exp_avg_sq), a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError());
+}
+
 }  // extern "C"

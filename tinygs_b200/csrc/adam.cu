@@ -95,7 +95,129 @@ __global__ void __launch_bounds__(256) k_adam(SegTable t, AdamScalars a, int64_t
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Data-parallel step over peer memory: this rank's slice of every segment
+// gets the sum of all ranks' gradients (peer loads, rank order, the same
+// order as the reference's accumulation into one arena), the Adam update on
+// this rank's moments, and the new parameters stored into every rank's
+// parameter arena (peer stores).
+struct PeerTable {
+  float* params[kMaxDpRanks][6];
+  const float* grads[kMaxDpRanks][6];
+  float* m[6];
+  float* v[6];
+  int64_t lo[6];
+  int64_t hi[6];
+  int64_t chunk_begin[7];
+  float lr[6];
+  float decay[6];
+  int kind[6];
+  int world, rank, vec;
+};
+
+__global__ void __launch_bounds__(256) k_dp_adam(PeerTable t, AdamScalars a, int64_t total_chunks) {
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total_chunks;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int s = 0;
+#pragma unroll
+    for (int k = 1; k < 6; ++k)
+      if (c >= t.chunk_begin[k]) s = k;
+    const int64_t e0 = t.lo[s] + (c - t.chunk_begin[s]) * 4;
+    const int64_t hi = t.hi[s];
+    const float lr = t.lr[s], decay = t.decay[s];
+    const int kind = t.kind[s];
+    float* own = t.params[t.rank][s];
+    if (t.vec && e0 + 4 <= hi) {
+      float4 g = *reinterpret_cast<const float4*>(t.grads[0][s] + e0);
+#pragma unroll
+      for (int r = 1; r < kMaxDpRanks; ++r) {
+        if (r >= t.world) break;
+        const float4 q = *reinterpret_cast<const float4*>(t.grads[r][s] + e0);
+        g.x += q.x;
+        g.y += q.y;
+        g.z += q.z;
+        g.w += q.w;
+      }
+      float4 th = *reinterpret_cast<const float4*>(own + e0);
+      float4 m = *reinterpret_cast<const float4*>(t.m[s] + e0);
+      float4 v = *reinterpret_cast<const float4*>(t.v[s] + e0);
+      adam_one(th.x, g.x, m.x, v.x, lr, kind, decay, a);
+      adam_one(th.y, g.y, m.y, v.y, lr, kind, decay, a);
+      adam_one(th.z, g.z, m.z, v.z, lr, kind, decay, a);
+      adam_one(th.w, g.w, m.w, v.w, lr, kind, decay, a);
+      *reinterpret_cast<float4*>(t.m[s] + e0) = m;
+      *reinterpret_cast<float4*>(t.v[s] + e0) = v;
+#pragma unroll
+      for (int r = 0; r < kMaxDpRanks; ++r) {
+        if (r >= t.world) break;
+        *reinterpret_cast<float4*>(t.params[r][s] + e0) = th;
+      }
+    } else {
+      for (int64_t e = e0; e < min(e0 + 4, hi); ++e) {
+        float g = t.grads[0][s][e];
+        for (int r = 1; r < t.world; ++r) g += t.grads[r][s][e];
+        float th = own[e], m = t.m[s][e], v = t.v[s][e];
+        adam_one(th, g, m, v, lr, kind, decay, a);
+        t.m[s][e] = m;
+        t.v[s][e] = v;
+        for (int r = 0; r < t.world; ++r) t.params[r][s][e] = th;
+      }
+    }
+  }
+  // the stores into the other ranks' memory are complete before this
+  // kernel is; the caller's collective orders them before the next forward
+  __threadfence_system();
+}
+
 }  // namespace
+
+void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int world, int rank,
+                    const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream) {
+  PeerTable t{};
+  t.world = world;
+  t.rank = rank;
+  const int64_t n = params[rank].n;
+  // slice boundaries on multiples of four Gaussians (16-byte aligned rows)
+  const int64_t lo_g = (n * rank / world) / 4 * 4;
+  const int64_t hi_g = rank == world - 1 ? n : (n * (rank + 1) / world) / 4 * 4;
+  const int widths[6] = {3, 1, 4, 3, 3, 45};
+  bool vec = true;
+  for (int r = 0; r < world; ++r) {
+    float* pp[6] = {params[r].means, params[r].opacities, params[r].rotations, params[r].scales, params[r].sh0,
+                    params[r].sh_rest};
+    float* gp[6] = {grads[r].means, grads[r].opacities, grads[r].rotations, grads[r].scales, grads[r].sh0,
+                    grads[r].sh_rest};
+    for (int k = 0; k < 6; ++k) {
+      t.params[r][k] = pp[k];
+      t.grads[r][k] = gp[k];
+      vec = vec && aligned16(pp[k]) && aligned16(gp[k]);
+    }
+  }
+  float* mp[6] = {m.means, m.opacities, m.rotations, m.scales, m.sh0, m.sh_rest};
+  float* vp[6] = {v.means, v.opacities, v.rotations, v.scales, v.sh0, v.sh_rest};
+  int64_t chunks = 0;
+  for (int k = 0; k < 6; ++k) {
+    t.m[k] = mp[k];
+    t.v[k] = vp[k];
+    vec = vec && aligned16(mp[k]) && aligned16(vp[k]);
+    t.lo[k] = lo_g * widths[k];
+    t.hi[k] = hi_g * widths[k];
+    t.lr[k] = adam.lr[k];
+    t.decay[k] = adam.decay[k];
+    t.kind[k] = adam.kind[k];
+    t.chunk_begin[k] = chunks;
+    chunks += (t.hi[k] - t.lo[k] + 3) / 4;
+  }
+  t.chunk_begin[6] = chunks;
+  t.vec = vec ? 1 : 0;
+  if (chunks <= 0) return;
+  AdamScalars a{adam.beta1, adam.beta2, adam.eps, adam.gradient_scale, adam.bc1, adam.bc2_sqrt, adam.max_grad_1, 0};
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (chunks + 255) / 256;
+  const int blocks = static_cast<int>(want < sms * 8 ? want : sms * 8);
+  k_dp_adam<<<blocks, 256, 0, stream>>>(t, a, chunks);
+}
 
 void launch_adam(const AdamSegment* segs, int n_segs, float beta1, float beta2, float eps, float gradient_scale,
                  float bc1, float bc2_sqrt, float max_grad_1, int zero_grads, cudaStream_t stream) {

@@ -123,6 +123,12 @@ void launch_ssim(int fp16, int width, int height, const void* pred, const void* 
                  void* loss_map, void* grad, float scale_ssim, float scale_l1, float* partials,
                  float* loss_sum, cudaStream_t stream);
 
+// data-parallel Adam over peer memory (adam.cu): params/grads hold one
+// entry per rank (pointers valid in this process)
+constexpr int kMaxDpRanks = 8;
+void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int world, int rank,
+                    const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream);
+
 // optimizer (adam.cu)
 struct AdamSegment {
   float* theta;

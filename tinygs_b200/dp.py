@@ -52,3 +52,122 @@ class DataParallel:
         t = torch.tensor([value], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
         return float(t.item())
+
+
+# ------------------------------------------------------------------------
+# Accumulation + Adam as one kernel over NVLink peer memory (the product path
+# for several GPUs; `reduce_gradients` + a local Adam is the NCCL baseline).
+
+import ctypes  # noqa: E402
+
+from . import runtime as rt  # noqa: E402
+from ._abi import TgsGaussians, TgsIpcHandle, check, load_library  # noqa: E402
+
+
+def shared_gaussian_set(n: int, sh_degree: int, capacity: int | None = None) -> "rt.GaussianSet":
+    """A GaussianSet whose storage other processes can map (CUDA IPC).  The
+    allocation is released when the set is garbage collected."""
+    lib = load_library()
+    cap = max(int(n), int(capacity) if capacity is not None else int(n))
+    npad = (cap + 3) // 4 * 4
+    nbytes = 4 * rt.FLOATS_PER_GAUSSIAN * npad
+    ptr, handle = ctypes.c_void_p(), TgsIpcHandle()
+    check(lib.tgs_shared_alloc(nbytes, ctypes.byref(ptr), ctypes.byref(handle)), "tgs_shared_alloc")
+    view = rt._DeviceView(ptr.value, rt.FLOATS_PER_GAUSSIAN * npad, "<f4")
+    storage = torch.as_tensor(view, device="cuda")
+    g = rt.GaussianSet(n, sh_degree, storage=storage, capacity=cap)
+    g.ipc_handle = handle.raw()
+    g._shared = _SharedBlock(lib, ptr.value)
+    return g
+
+
+class _SharedBlock:
+    def __init__(self, lib, ptr: int):
+        self.lib, self.ptr = lib, ptr
+
+    def __del__(self):
+        try:
+            self.lib.tgs_shared_free(ctypes.c_void_p(self.ptr))
+        except Exception:
+            pass
+
+
+class PeerAdam:
+    """Data-parallel optimizer step over peer memory (tgs_dp_reduce_adam).
+
+    Every rank holds the parameters and its gradient arena in shared memory;
+    the arenas of all ranks are mapped into every process once.  step()
+    orders itself after every rank's backward and before every rank's next
+    forward with a one-element all-reduce on the stream, then rank r sums
+    the gradients of its slice of the Gaussians over the ranks, applies
+    Adam with its moments, and writes the new parameters into every rank's
+    arena."""
+
+    def __init__(self, dp: DataParallel, params: "rt.GaussianSet", grads: "rt.GaussianSet",
+                 cfg: "rt.AdamParams | None" = None):
+        self.lib = load_library()
+        self.dp, self.params, self.grads = dp, params, grads
+        self.cfg = cfg or rt.AdamParams()
+        self.exp_avg = params.zeros_like()
+        self.exp_avg_sq = params.zeros_like()
+        self.global_steps = 0
+        self.flag = torch.zeros(1, dtype=torch.float32, device="cuda")
+        handles = [None] * dp.world
+        mine = (params.ipc_handle, grads.ipc_handle)
+        if dp.world > 1:
+            dist.all_gather_object(handles, mine, group=dp.group)
+        else:
+            handles = [mine]
+        self.opened: list[int] = []
+        base_p, base_g = [], []
+        for r, (hp, hg) in enumerate(handles):
+            if r == dp.rank:
+                base_p.append(params.storage.data_ptr())
+                base_g.append(grads.storage.data_ptr())
+                continue
+            ptrs = []
+            for h in (hp, hg):
+                ih = TgsIpcHandle.from_raw(h)
+                p = ctypes.c_void_p()
+                check(self.lib.tgs_shared_open(ctypes.byref(ih), ctypes.byref(p)), "tgs_shared_open")
+                self.opened.append(p.value)
+                ptrs.append(p.value)
+            base_p.append(ptrs[0])
+            base_g.append(ptrs[1])
+        self.base_p, self.base_g = base_p, base_g
+
+    def _sets(self, bases: list[int], like: "rt.GaussianSet"):
+        arr = (TgsGaussians * self.dp.world)()
+        offs, off = {}, 0
+        for name in rt.SEGMENTS:
+            offs[name] = off
+            off += rt.WIDTHS[name] * like.npad
+        for r, b in enumerate(bases):
+            for name in rt.SEGMENTS:
+                setattr(arr[r], name, b + 4 * offs[name])
+            arr[r].n = like.n
+            arr[r].sh_degree = like.sh_degree
+        return arr
+
+    def barrier(self) -> None:
+        if self.dp.world > 1:
+            dist.all_reduce(self.flag, group=self.dp.group)
+
+    def step(self, gradient_scale: float, stream=None) -> None:
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        self.global_steps += 1
+        P = self._sets(self.base_p, self.params)
+        G = self._sets(self.base_g, self.grads)
+        m, v = self.exp_avg.abi(), self.exp_avg_sq.abi()
+        cfg = self.cfg.abi()
+        self.barrier()  # every rank's gradients are written
+        check(self.lib.tgs_dp_reduce_adam(P, G, self.dp.world, self.dp.rank, ctypes.byref(m), ctypes.byref(v),
+                                          ctypes.byref(cfg), self.global_steps, float(gradient_scale),
+                                          rt._stream_handle(stream)), "tgs_dp_reduce_adam")
+        self.barrier()  # every rank's parameters are updated
+
+    def close(self) -> None:
+        for p in self.opened:
+            self.lib.tgs_shared_close(ctypes.c_void_p(p))
+        self.opened = []

@@ -207,6 +207,8 @@ def densify_sample(n: int, seed: int = 3):
     c = scenes.CONFIGS["cfg3"]
     params = scenes.gaussian_params(n, c.sh_degree, c.means, seed)
     rng = np.random.default_rng(seed + 1)
+    # a tenth of the Gaussians transparent enough to be pruned
+    params["opacities"][rng.random(n) < 0.1] = -7.0
     thr = 2e-4 * GRAD_SCALER
     counter = rng.integers(1, 20, n).astype(np.float32)
     dens = np.zeros((n, 4), np.float32)
@@ -261,7 +263,9 @@ def densify_bench(n: int, capacity: int, cpu: bool) -> dict:
     # test, grown rows written (parameters; zeros for gradients and moments),
     # the prune test's reads, and the kept rows of the four sets gathered and
     # copied back
-    alg = n * (16 + 12) + grown * 236 * 5 + (n + grown) * (4 + 12 + 16 + 16) + n_out * 4 * 236 * 3
+    alg = n * (16 + 12) + grown * 236 * 5 + (n + grown) * (4 + 12 + 16 + 16)
+    if n_out < n + grown:  # the compaction runs only when something is pruned
+        alg += n_out * 4 * 236 * 3
     out = {"refine_ms": ms, "gaussians_in": n, "grown": grown, "gaussians_out": n_out,
            "algorithmic_bytes": alg, "achieved_gbs": alg / (ms * 1e-3) / 1e9,
            "note": "one refine at strategy step 600 (grow, split/clone, prune, stable compaction of params, "
@@ -446,7 +450,8 @@ def run_ours(args):
             rast.backward(ctx)
             if ev is not None:
                 ev[2].record(stream)
-            opt.step(dp.gradient_scale(GRAD_SCALER), stream=stream)  # barrier, kernel, barrier
+            # barrier, kernel (between ev[5] and ev[6]), barrier
+            opt.step(dp.gradient_scale(GRAD_SCALER), stream=stream, events=None if ev is None else ev[5:7])
             if ev is not None:
                 ev[3].record(stream)
                 ev[4].record(stream)
@@ -504,7 +509,7 @@ def run_ours(args):
     rast.set_stage_timing(True)
     rows = []
     for k in range(n_stage):
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
         step(args.warmup + 2 * args.steps + k, False, evs)
         torch.cuda.synchronize()
         t = rast.stage_times()
@@ -515,6 +520,7 @@ def run_ours(args):
         elif peer:
             row["gaussian_backward"] = t[4]
             row["peer_reduce_adam"] = evs[2].elapsed_time(evs[3])
+            row["peer_kernel"] = evs[5].elapsed_time(evs[6])
         else:
             row["gaussian_backward"] = t[4]
             row["allreduce"] = evs[2].elapsed_time(evs[3])
@@ -610,15 +616,17 @@ def run_ours(args):
         if world > 1:
             line["config"]["dp_impl"] = args.dp
         if peer:
-            # per rank: its slice's gradients loaded from the other ranks and
-            # its new parameters stored into them, each way over NVLink
-            # (the two one-element all-reduces that order it are included)
+            # into each GPU over NVLink: its slice's gradients loaded from the
+            # other ranks plus the other ranks' new parameters stored into it,
+            # 2 * 236 B * n/N * (N-1) (the bytes of a ring all-reduce); the
+            # same out of it (kernel alone; with_barriers_ms adds the two
+            # one-element all-reduces that order it and absorb the ranks' skew)
             slice_bytes = 236 * cfg.n / world
-            link_bytes = slice_bytes * (world - 1)
-            ms = stages["peer_reduce_adam"]
+            link_bytes = 2 * slice_bytes * (world - 1)
+            ms = stages["peer_kernel"]
             line["peer_reduce_adam"] = {
                 "kernel": "k_dp_adam (gradient sum over peer memory + Adam + parameter broadcast)",
-                "ms": ms, "nvlink_bytes_each_way_per_rank": link_bytes,
+                "ms": ms, "with_barriers_ms": stages["peer_reduce_adam"], "nvlink_bytes_each_way_per_gpu": link_bytes,
                 "achieved_gbs_each_way": link_bytes / (ms * 1e-3) / 1e9,
                 "peak_gbs_each_way": 770.0, "frac": link_bytes / (ms * 1e-3) / 1e9 / 770.0,
                 "peak_source": "measured peer copy on this pool (profiling recipe)"}

@@ -114,54 +114,81 @@ struct PeerTable {
   int world, rank, vec;
 };
 
-__global__ void __launch_bounds__(256) k_dp_adam(PeerTable t, AdamScalars a, int64_t total_chunks) {
-  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total_chunks;
-       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    int s = 0;
+// One 16-byte chunk of the slice: segment, element offset and its data.
+struct DpChunk {
+  int s;
+  int64_t e0;
+  bool vec;
+  float4 g, th, m, v;
+};
+
+__device__ __forceinline__ DpChunk dp_load(const PeerTable& t, int64_t c) {
+  DpChunk k{};
+  k.s = 0;
 #pragma unroll
-    for (int k = 1; k < 6; ++k)
-      if (c >= t.chunk_begin[k]) s = k;
-    const int64_t e0 = t.lo[s] + (c - t.chunk_begin[s]) * 4;
-    const int64_t hi = t.hi[s];
-    const float lr = t.lr[s], decay = t.decay[s];
-    const int kind = t.kind[s];
-    float* own = t.params[t.rank][s];
-    if (t.vec && e0 + 4 <= hi) {
-      float4 g = *reinterpret_cast<const float4*>(t.grads[0][s] + e0);
+  for (int q = 1; q < 6; ++q)
+    if (c >= t.chunk_begin[q]) k.s = q;
+  k.e0 = t.lo[k.s] + (c - t.chunk_begin[k.s]) * 4;
+  k.vec = t.vec && k.e0 + 4 <= t.hi[k.s];
+  if (k.vec) {
+    k.g = *reinterpret_cast<const float4*>(t.grads[0][k.s] + k.e0);
 #pragma unroll
-      for (int r = 1; r < kMaxDpRanks; ++r) {
-        if (r >= t.world) break;
-        const float4 q = *reinterpret_cast<const float4*>(t.grads[r][s] + e0);
-        g.x += q.x;
-        g.y += q.y;
-        g.z += q.z;
-        g.w += q.w;
-      }
-      float4 th = *reinterpret_cast<const float4*>(own + e0);
-      float4 m = *reinterpret_cast<const float4*>(t.m[s] + e0);
-      float4 v = *reinterpret_cast<const float4*>(t.v[s] + e0);
-      adam_one(th.x, g.x, m.x, v.x, lr, kind, decay, a);
-      adam_one(th.y, g.y, m.y, v.y, lr, kind, decay, a);
-      adam_one(th.z, g.z, m.z, v.z, lr, kind, decay, a);
-      adam_one(th.w, g.w, m.w, v.w, lr, kind, decay, a);
-      *reinterpret_cast<float4*>(t.m[s] + e0) = m;
-      *reinterpret_cast<float4*>(t.v[s] + e0) = v;
-#pragma unroll
-      for (int r = 0; r < kMaxDpRanks; ++r) {
-        if (r >= t.world) break;
-        *reinterpret_cast<float4*>(t.params[r][s] + e0) = th;
-      }
-    } else {
-      for (int64_t e = e0; e < min(e0 + 4, hi); ++e) {
-        float g = t.grads[0][s][e];
-        for (int r = 1; r < t.world; ++r) g += t.grads[r][s][e];
-        float th = own[e], m = t.m[s][e], v = t.v[s][e];
-        adam_one(th, g, m, v, lr, kind, decay, a);
-        t.m[s][e] = m;
-        t.v[s][e] = v;
-        for (int r = 0; r < t.world; ++r) t.params[r][s][e] = th;
-      }
+    for (int r = 1; r < kMaxDpRanks; ++r) {
+      if (r >= t.world) break;
+      const float4 q = *reinterpret_cast<const float4*>(t.grads[r][k.s] + k.e0);
+      k.g.x += q.x;
+      k.g.y += q.y;
+      k.g.z += q.z;
+      k.g.w += q.w;
     }
+    k.th = *reinterpret_cast<const float4*>(t.params[t.rank][k.s] + k.e0);
+    k.m = *reinterpret_cast<const float4*>(t.m[k.s] + k.e0);
+    k.v = *reinterpret_cast<const float4*>(t.v[k.s] + k.e0);
+  }
+  return k;
+}
+
+__device__ __forceinline__ void dp_finish(const PeerTable& t, DpChunk& k, const AdamScalars& a) {
+  const float lr = t.lr[k.s], decay = t.decay[k.s];
+  const int kind = t.kind[k.s];
+  if (k.vec) {
+    adam_one(k.th.x, k.g.x, k.m.x, k.v.x, lr, kind, decay, a);
+    adam_one(k.th.y, k.g.y, k.m.y, k.v.y, lr, kind, decay, a);
+    adam_one(k.th.z, k.g.z, k.m.z, k.v.z, lr, kind, decay, a);
+    adam_one(k.th.w, k.g.w, k.m.w, k.v.w, lr, kind, decay, a);
+    *reinterpret_cast<float4*>(t.m[k.s] + k.e0) = k.m;
+    *reinterpret_cast<float4*>(t.v[k.s] + k.e0) = k.v;
+#pragma unroll
+    for (int r = 0; r < kMaxDpRanks; ++r) {
+      if (r >= t.world) break;
+      *reinterpret_cast<float4*>(t.params[r][k.s] + k.e0) = k.th;
+    }
+  } else {
+    // scalar tail (a slice end that is not a multiple of four floats)
+    for (int64_t e = k.e0; e < min(k.e0 + 4, t.hi[k.s]); ++e) {
+      float g = t.grads[0][k.s][e];
+      for (int r = 1; r < t.world; ++r) g += t.grads[r][k.s][e];
+      float th = t.params[t.rank][k.s][e], m = t.m[k.s][e], v = t.v[k.s][e];
+      adam_one(th, g, m, v, lr, kind, decay, a);
+      t.m[k.s][e] = m;
+      t.v[k.s][e] = v;
+      for (int r = 0; r < t.world; ++r) t.params[r][k.s][e] = th;
+    }
+  }
+}
+
+// Two chunks per thread and iteration, both loaded before either is
+// updated, so that more peer loads are in flight.
+__global__ void __launch_bounds__(256) k_dp_adam(PeerTable t, AdamScalars a, int64_t total_chunks) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < total_chunks;
+       c += 2 * stride) {
+    DpChunk k0 = dp_load(t, c);
+    const bool has1 = c + stride < total_chunks;
+    DpChunk k1{};
+    if (has1) k1 = dp_load(t, c + stride);
+    dp_finish(t, k0, a);
+    if (has1) dp_finish(t, k1, a);
   }
   // the stores into the other ranks' memory are complete before this
   // kernel is; the caller's collective orders them before the next forward

@@ -153,7 +153,9 @@ class PeerAdam:
         if self.dp.world > 1:
             dist.all_reduce(self.flag, group=self.dp.group)
 
-    def step(self, gradient_scale: float, stream=None) -> None:
+    def step(self, gradient_scale: float, stream=None, events=None) -> None:
+        """`events`: optional pair of CUDA events recorded around the kernel
+        (between the two barriers)."""
         if stream is None:
             stream = torch.cuda.current_stream()
         self.global_steps += 1
@@ -162,9 +164,13 @@ class PeerAdam:
         m, v = self.exp_avg.abi(), self.exp_avg_sq.abi()
         cfg = self.cfg.abi()
         self.barrier()  # every rank's gradients are written
+        if events is not None:
+            events[0].record(stream)
         check(self.lib.tgs_dp_reduce_adam(P, G, self.dp.world, self.dp.rank, ctypes.byref(m), ctypes.byref(v),
                                           ctypes.byref(cfg), self.global_steps, float(gradient_scale),
                                           rt._stream_handle(stream)), "tgs_dp_reduce_adam")
+        if events is not None:
+            events[1].record(stream)
         self.barrier()  # every rank's parameters are updated
 
     def close(self) -> None:

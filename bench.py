@@ -56,9 +56,10 @@ def parse():
     ap.add_argument("--n", type=int, default=0, help="override the Gaussian count (profiling small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0, help="seconds of CPU work for the baseline sample")
-    ap.add_argument("--dp", choices=["peer", "nccl"], default="peer",
-                    help="several GPUs: accumulation + Adam over NVLink peer memory in one kernel (peer) or "
-                         "an NCCL all-reduce followed by Adam on every rank (nccl, the baseline)")
+    ap.add_argument("--dp", choices=["auto", "multicast", "peer", "nccl"], default="auto",
+                    help="several GPUs: accumulation + Adam in one kernel through NVLink SHARP (multicast) or "
+                         "over peer memory (peer), or an NCCL all-reduce followed by Adam on every rank (nccl, "
+                         "the baseline); auto = multicast when the arenas get a multicast address, else peer")
     return ap.parse_args()
 
 
@@ -357,14 +358,29 @@ def run_ours(args):
     fp16 = cfg.dtype == "float16"
     dt = torch.float16 if fp16 else torch.float32
     params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
-    peer = world > 1 and args.dp == "peer"
-    if peer:
+    peer = world > 1 and args.dp != "nccl"
+    dp_impl = args.dp if world > 1 else "none"
+    opt = None
+    if peer and args.dp in ("auto", "multicast"):
+        # arenas bound to a multicast object (NVLink SHARP)
+        g = dpm.symmetric_gaussian_set(dp, cfg.n, cfg.sh_degree)
+        g.copy_from_numpy(params)
+        grads = dpm.symmetric_gaussian_set(dp, cfg.n, cfg.sh_degree)
+        try:
+            opt = dpm.MulticastAdam(dp, g, grads, rt.AdamParams(max_grad_1=0.3))
+            dp_impl = "multicast"
+        except RuntimeError:
+            if args.dp == "multicast":
+                raise
+            del g, grads
+    if peer and opt is None:
         # parameters and gradient arenas the other ranks map (CUDA IPC)
         g = dpm.shared_gaussian_set(cfg.n, cfg.sh_degree)
         g.copy_from_numpy(params)
         grads = dpm.shared_gaussian_set(cfg.n, cfg.sh_degree)
         opt = dpm.PeerAdam(dp, g, grads, rt.AdamParams(max_grad_1=0.3))
-    else:
+        dp_impl = "peer"
+    if not peer:
         g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
         grads = g.zeros_like()
         opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
@@ -614,18 +630,22 @@ def run_ours(args):
         if dens_row is not None:
             line["densify"] = dens_row
         if world > 1:
-            line["config"]["dp_impl"] = args.dp
+            line["config"]["dp_impl"] = dp_impl
         if peer:
             # into each GPU over NVLink: its slice's gradients loaded from the
             # other ranks plus the other ranks' new parameters stored into it,
             # 2 * 236 B * n/N * (N-1) (the bytes of a ring all-reduce); the
             # same out of it (kernel alone; with_barriers_ms adds the two
             # one-element all-reduces that order it and absorb the ranks' skew)
+            # (through the switch: 236 B * n, the slice's reduced gradients in
+            # plus the other slices' parameters in)
             slice_bytes = 236 * cfg.n / world
-            link_bytes = 2 * slice_bytes * (world - 1)
+            link_bytes = 236 * cfg.n if dp_impl == "multicast" else 2 * slice_bytes * (world - 1)
             ms = stages["peer_kernel"]
             line["peer_reduce_adam"] = {
-                "kernel": "k_dp_adam (gradient sum over peer memory + Adam + parameter broadcast)",
+                "kernel": ("k_dp_adam_mc (gradient sum by NVLink SHARP reducing loads + Adam + multicast "
+                           "parameter stores)" if dp_impl == "multicast" else
+                           "k_dp_adam (gradient sum over peer memory + Adam + parameter broadcast)"),
                 "ms": ms, "with_barriers_ms": stages["peer_reduce_adam"], "nvlink_bytes_each_way_per_gpu": link_bytes,
                 "achieved_gbs_each_way": link_bytes / (ms * 1e-3) / 1e9,
                 "peak_gbs_each_way": 770.0, "frac": link_bytes / (ms * 1e-3) / 1e9 / 770.0,

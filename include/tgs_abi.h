@@ -422,6 +422,20 @@ TGS_API int tgs_dp_reduce_adam(const TgsGaussians* params_per_rank, const TgsGau
                                TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg, uint32_t step,
                                float gradient_scale, tgs_stream_t stream);
 
+/* tgs_dp_reduce_adam through NVLink SHARP: params_mc / grads_mc are the
+ * multicast addresses of the parameter and gradient arenas (segment pointers
+ * in the layout of `params`, e.g. from a multicast object bound to every
+ * rank's arena); the slice's gradient sum is read with one reducing load
+ * through the switch and the new parameters are stored to every rank with
+ * one multicast store.  `params` are this rank's parameters (read).  For more
+ * than two ranks the switch's summation order can change the last bit of the
+ * summed gradient. */
+TGS_API int tgs_dp_reduce_adam_multicast(const TgsGaussians* params_mc, const TgsGaussians* grads_mc,
+                                         TgsGaussians* params, int32_t world, int32_t rank,
+                                         TgsGaussians* exp_avg, TgsGaussians* exp_avg_sq,
+                                         const TgsAdamConfig* cfg, uint32_t step, float gradient_scale,
+                                         tgs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,7 +28,7 @@ def _arrays(seed: int, n: int, scale: float):
     return {k: (rng.normal(0, scale, (n, c))).astype(np.float32) for k, c in w.items()}
 
 
-def _worker(rank: int, port: int, out_dir: str) -> None:
+def _worker(rank: int, port: int, out_dir: str, mode: str = "peer") -> None:
     import torch.distributed as dist
 
     from tinygs_b200 import dp as dpm
@@ -41,11 +41,16 @@ def _worker(rank: int, port: int, out_dir: str) -> None:
                             device_id=torch.device("cuda", rank))
     try:
         dp = dpm.DataParallel.from_env()
-        params = dpm.shared_gaussian_set(N, 3)
+        if mode == "multicast":
+            params = dpm.symmetric_gaussian_set(dp, N, 3)
+            grads = dpm.symmetric_gaussian_set(dp, N, 3)
+        else:
+            params = dpm.shared_gaussian_set(N, 3)
+            grads = dpm.shared_gaussian_set(N, 3)
         params.copy_from_numpy(_arrays(1, N, 1.0))
-        grads = dpm.shared_gaussian_set(N, 3)
         grads.copy_from_numpy(_arrays(100 + rank, N, 1e-2))
-        opt = dpm.PeerAdam(dp, params, grads, rt.AdamParams(max_grad_1=0.3))
+        cls = dpm.MulticastAdam if mode == "multicast" else dpm.PeerAdam
+        opt = cls(dp, params, grads, rt.AdamParams(max_grad_1=0.3))
         for _ in range(2):
             opt.step(dp.gradient_scale(10.0))
         torch.cuda.synchronize()
@@ -57,14 +62,17 @@ def _worker(rank: int, port: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
-def test_peer_adam_two_gpus(tmp_path):
+@pytest.mark.parametrize("mode", ["peer", "multicast"])
+def test_peer_adam_two_gpus(tmp_path, mode):
+    """With two ranks the switch's sum a + b equals the rank-order sum, so
+    both exchange paths must match one GPU bit for bit."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
 
     from tinygs_b200 import runtime as rt
 
-    mp.start_processes(_worker, args=(_free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker, args=(_free_port(), str(tmp_path), mode), nprocs=2, start_method="spawn")
     r0, r1 = (np.load(tmp_path / f"rank{k}.npz") for k in range(2))
     # one GPU: Adam twice over g0 + g1 (summed in rank order)
     g0, g1 = _arrays(100, N, 1e-2), _arrays(101, N, 1e-2)

@@ -113,6 +113,9 @@ PROTOTYPES = {
     "tgs_shared_free": (c_int32, [_P]),
     "tgs_shared_open": (c_int32, [POINTER(TgsIpcHandle), POINTER(c_void_p)]),
     "tgs_shared_close": (c_int32, [_P]),
+    "tgs_dp_reduce_adam_multicast": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                               c_int32, c_int32, POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                               POINTER(TgsAdamConfig), c_uint32, c_float, _P]),
     "tgs_dp_reduce_adam": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), c_int32, c_int32,
                                      POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32,
                                      c_float, _P]),

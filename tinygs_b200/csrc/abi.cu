@@ -605,4 +605,22 @@ int tgs_dp_reduce_adam(const TgsGaussians* params_per_rank, const TgsGaussians* 
   return cuda_status(cudaGetLastError());
 }
 
+int tgs_dp_reduce_adam_multicast(const TgsGaussians* params_mc, const TgsGaussians* grads_mc,
+                                 TgsGaussians* params, int32_t world, int32_t rank, TgsGaussians* exp_avg,
+                                 TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg, uint32_t step,
+                                 float gradient_scale, tgs_stream_t stream) {
+  if (!gaussians_ok(params_mc) || !gaussians_ok(grads_mc) || !gaussians_ok(params) || world < 1 ||
+      world > kMaxDpRanks || rank < 0 || rank >= world || cfg == nullptr || step == 0 || !gaussians_ok(exp_avg) ||
+      !gaussians_ok(exp_avg_sq))
+    return TGS_ERR_INVALID_ARGUMENT;
+  const int64_t n = params->n;
+  if (params_mc->n != n || grads_mc->n != n || exp_avg->n != n || exp_avg_sq->n != n) return TGS_ERR_INVALID_ARGUMENT;
+  if (n == 0) return TGS_OK;
+  AdamStepArgs a{};
+  adam_segments(cfg, n, step, gradient_scale, &a);
+  launch_dp_adam_mc(to_ptrs(params_mc), to_ptrs(grads_mc), to_ptrs(params), world, rank, to_ptrs(exp_avg),
+                    to_ptrs(exp_avg_sq), a, static_cast<cudaStream_t>(stream));
+  return cuda_status(cudaGetLastError());
+}
+
 }  // extern "C"

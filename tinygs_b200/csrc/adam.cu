@@ -195,7 +195,151 @@ __global__ void __launch_bounds__(256) k_dp_adam(PeerTable t, AdamScalars a, int
   __threadfence_system();
 }
 
+// Same step through NVLink SHARP: the slice's gradients are read already
+// summed over the ranks by the switch (multimem.ld_reduce on the gradient
+// arenas' multicast address) and the new parameters are written to every
+// rank at once (multimem.st on the parameter arenas' multicast address).
+// The sum's order is the switch's, so for more than two ranks it can differ
+// from the rank-order sum in the last bit.
+struct McTable {
+  float* mc_params[6];
+  const float* mc_grads[6];
+  const float* own[6];
+  float* m[6];
+  float* v[6];
+  int64_t lo[6];
+  int64_t hi[6];
+  int64_t chunk_begin[7];
+  float lr[6];
+  float decay[6];
+  int kind[6];
+};
+
+__device__ __forceinline__ float4 mc_ld_reduce4(const float* p) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ float mc_ld_reduce1(const float* p) {
+  float r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];\n" : "=f"(r) : "l"(p) : "memory");
+  return r;
+}
+__device__ __forceinline__ void mc_st4(float* p, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(p), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st1(float* p, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;\n" ::"l"(p), "f"(v) : "memory");
+}
+
+// Four chunks per thread and iteration: the reducing loads of all four are
+// issued before any update, to keep more of them in flight through the
+// switch.
+constexpr int kMcUnroll = 4;
+
+__global__ void __launch_bounds__(256) k_dp_adam_mc(McTable t, AdamScalars a, int64_t total_chunks) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t c0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c0 < total_chunks;
+       c0 += kMcUnroll * stride) {
+    int seg[kMcUnroll];
+    int64_t e0[kMcUnroll];
+    bool full[kMcUnroll];
+    float4 g[kMcUnroll];
+#pragma unroll
+    for (int u = 0; u < kMcUnroll; ++u) {
+      const int64_t c = c0 + u * stride;
+      seg[u] = 0;
+      e0[u] = 0;
+      full[u] = false;
+      if (c < total_chunks) {
+#pragma unroll
+        for (int k = 1; k < 6; ++k)
+          if (c >= t.chunk_begin[k]) seg[u] = k;
+        e0[u] = t.lo[seg[u]] + (c - t.chunk_begin[seg[u]]) * 4;
+        full[u] = e0[u] + 4 <= t.hi[seg[u]];
+        if (full[u]) g[u] = mc_ld_reduce4(t.mc_grads[seg[u]] + e0[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kMcUnroll; ++u) {
+      const int64_t c = c0 + u * stride;
+      if (c >= total_chunks) continue;
+      const int s = seg[u];
+      const float lr = t.lr[s], decay = t.decay[s];
+      const int kind = t.kind[s];
+      if (full[u]) {
+        float4 th = *reinterpret_cast<const float4*>(t.own[s] + e0[u]);
+        float4 m = *reinterpret_cast<const float4*>(t.m[s] + e0[u]);
+        float4 v = *reinterpret_cast<const float4*>(t.v[s] + e0[u]);
+        adam_one(th.x, g[u].x, m.x, v.x, lr, kind, decay, a);
+        adam_one(th.y, g[u].y, m.y, v.y, lr, kind, decay, a);
+        adam_one(th.z, g[u].z, m.z, v.z, lr, kind, decay, a);
+        adam_one(th.w, g[u].w, m.w, v.w, lr, kind, decay, a);
+        *reinterpret_cast<float4*>(t.m[s] + e0[u]) = m;
+        *reinterpret_cast<float4*>(t.v[s] + e0[u]) = v;
+        mc_st4(t.mc_params[s] + e0[u], th);
+      } else {
+        for (int64_t e = e0[u]; e < min(e0[u] + 4, t.hi[s]); ++e) {
+          const float gs = mc_ld_reduce1(t.mc_grads[s] + e);
+          float th = t.own[s][e], m = t.m[s][e], v = t.v[s][e];
+          adam_one(th, gs, m, v, lr, kind, decay, a);
+          t.m[s][e] = m;
+          t.v[s][e] = v;
+          mc_st1(t.mc_params[s] + e, th);
+        }
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 }  // namespace
+
+void launch_dp_adam_mc(const GaussianPtrs& params_mc, const GaussianPtrs& grads_mc, const GaussianPtrs& own,
+                       int world, int rank, const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam,
+                       cudaStream_t stream) {
+  McTable t{};
+  const int64_t n = own.n;
+  const int64_t lo_g = (n * rank / world) / 4 * 4;
+  const int64_t hi_g = rank == world - 1 ? n : (n * (rank + 1) / world) / 4 * 4;
+  const int widths[6] = {3, 1, 4, 3, 3, 45};
+  float* pm[6] = {params_mc.means, params_mc.opacities, params_mc.rotations, params_mc.scales, params_mc.sh0,
+                  params_mc.sh_rest};
+  float* gm[6] = {grads_mc.means, grads_mc.opacities, grads_mc.rotations, grads_mc.scales, grads_mc.sh0,
+                  grads_mc.sh_rest};
+  float* ow[6] = {own.means, own.opacities, own.rotations, own.scales, own.sh0, own.sh_rest};
+  float* mp[6] = {m.means, m.opacities, m.rotations, m.scales, m.sh0, m.sh_rest};
+  float* vp[6] = {v.means, v.opacities, v.rotations, v.scales, v.sh0, v.sh_rest};
+  int64_t chunks = 0;
+  for (int k = 0; k < 6; ++k) {
+    t.mc_params[k] = pm[k];
+    t.mc_grads[k] = gm[k];
+    t.own[k] = ow[k];
+    t.m[k] = mp[k];
+    t.v[k] = vp[k];
+    t.lo[k] = lo_g * widths[k];
+    t.hi[k] = hi_g * widths[k];
+    t.lr[k] = adam.lr[k];
+    t.decay[k] = adam.decay[k];
+    t.kind[k] = adam.kind[k];
+    t.chunk_begin[k] = chunks;
+    chunks += (t.hi[k] - t.lo[k] + 3) / 4;
+  }
+  t.chunk_begin[6] = chunks;
+  if (chunks <= 0) return;
+  AdamScalars a{adam.beta1, adam.beta2, adam.eps, adam.gradient_scale, adam.bc1, adam.bc2_sqrt, adam.max_grad_1, 0};
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (chunks + 255) / 256;
+  const int blocks = static_cast<int>(want < sms * 8 ? want : sms * 8);
+  k_dp_adam_mc<<<blocks, 256, 0, stream>>>(t, a, chunks);
+}
 
 void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int world, int rank,
                     const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream) {

@@ -129,6 +129,12 @@ constexpr int kMaxDpRanks = 8;
 void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int world, int rank,
                     const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream);
 
+// the same over the multicast addresses of the gradient and parameter
+// arenas (NVLink SHARP); `own` are this rank's parameters
+void launch_dp_adam_mc(const GaussianPtrs& params_mc, const GaussianPtrs& grads_mc, const GaussianPtrs& own,
+                       int world, int rank, const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam,
+                       cudaStream_t stream);
+
 // optimizer (adam.cu)
 struct AdamSegment {
   float* theta;

@@ -177,3 +177,79 @@ class PeerAdam:
         for p in self.opened:
             self.lib.tgs_shared_close(ctypes.c_void_p(p))
         self.opened = []
+
+
+# ------------------------------------------------------------------------
+# The same exchange through NVLink SHARP (multimem loads that reduce in the
+# switch and multimem stores that reach every GPU), over arenas allocated in
+# torch's symmetric memory, which binds them to a multicast object.
+
+def symmetric_gaussian_set(dp: DataParallel, n: int, sh_degree: int) -> "rt.GaussianSet":
+    """A GaussianSet in symmetric memory (collective: every rank calls it
+    with the same n); `.symm` is the rendezvous handle."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    npad = (int(n) + 3) // 4 * 4
+    t = symm_mem.empty(rt.FLOATS_PER_GAUSSIAN * npad, dtype=torch.float32, device="cuda")
+    t.zero_()
+    h = symm_mem.rendezvous(t, dp.group if dp.group is not None else dist.group.WORLD)
+    g = rt.GaussianSet(n, sh_degree, storage=t)
+    g.symm = h
+    return g
+
+
+class MulticastAdam:
+    """PeerAdam through the switch: rank r reads its slice's gradient sum with
+    one reducing load per 16 bytes and writes the new parameters to every
+    rank with one multicast store (tgs_dp_reduce_adam_multicast).  Raises
+    RuntimeError when the arenas have no multicast address."""
+
+    def __init__(self, dp: DataParallel, params: "rt.GaussianSet", grads: "rt.GaussianSet",
+                 cfg: "rt.AdamParams | None" = None):
+        self.lib = load_library()
+        self.dp, self.params, self.grads = dp, params, grads
+        self.cfg = cfg or rt.AdamParams()
+        self.exp_avg = params.zeros_like()
+        self.exp_avg_sq = params.zeros_like()
+        self.global_steps = 0
+        self.flag = torch.zeros(1, dtype=torch.float32, device="cuda")
+        self.mc = []
+        for s in (params, grads):
+            mc = int(s.symm.multicast_ptr)
+            if mc == 0:
+                raise RuntimeError("no multicast address for the symmetric arenas (NVLink SHARP unavailable)")
+            self.mc.append(mc)
+
+    def _mc_set(self, mc_base: int, like: "rt.GaussianSet") -> TgsGaussians:
+        local = like.abi()
+        base = like.storage.data_ptr()
+        out = TgsGaussians()
+        for name in rt.SEGMENTS:
+            setattr(out, name, mc_base + (getattr(local, name) - base))
+        out.n, out.sh_degree = like.n, like.sh_degree
+        return out
+
+    def barrier(self) -> None:
+        if self.dp.world > 1:
+            dist.all_reduce(self.flag, group=self.dp.group)
+
+    def step(self, gradient_scale: float, stream=None, events=None) -> None:
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        self.global_steps += 1
+        pm, gm = self._mc_set(self.mc[0], self.params), self._mc_set(self.mc[1], self.grads)
+        p, m, v = self.params.abi(), self.exp_avg.abi(), self.exp_avg_sq.abi()
+        cfg = self.cfg.abi()
+        self.barrier()
+        if events is not None:
+            events[0].record(stream)
+        check(self.lib.tgs_dp_reduce_adam_multicast(ctypes.byref(pm), ctypes.byref(gm), ctypes.byref(p),
+                                                    self.dp.world, self.dp.rank, ctypes.byref(m), ctypes.byref(v),
+                                                    ctypes.byref(cfg), self.global_steps, float(gradient_scale),
+                                                    rt._stream_handle(stream)), "tgs_dp_reduce_adam_multicast")
+        if events is not None:
+            events[1].record(stream)
+        self.barrier()
+
+    def close(self) -> None:
+        pass

@@ -56,10 +56,11 @@ def parse():
     ap.add_argument("--n", type=int, default=0, help="override the Gaussian count (profiling small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0, help="seconds of CPU work for the baseline sample")
-    ap.add_argument("--dp", choices=["auto", "multicast", "peer", "nccl"], default="auto",
-                    help="several GPUs: accumulation + Adam in one kernel through NVLink SHARP (multicast) or "
-                         "over peer memory (peer), or an NCCL all-reduce followed by Adam on every rank (nccl, "
-                         "the baseline); auto = multicast when the arenas get a multicast address, else peer")
+    ap.add_argument("--dp", choices=["auto", "inbox", "multicast", "peer", "nccl"], default="auto",
+                    help="several GPUs: gradients stored into their owners' inboxes by the backward, then "
+                         "accumulation + Adam + parameter broadcast in one kernel (inbox); accumulation + Adam in "
+                         "one kernel through NVLink SHARP (multicast) or over peer memory (peer); or an NCCL "
+                         "all-reduce followed by Adam on every rank (nccl, the baseline); auto = inbox")
     return ap.parse_args()
 
 
@@ -361,18 +362,22 @@ def run_ours(args):
     peer = world > 1 and args.dp != "nccl"
     dp_impl = args.dp if world > 1 else "none"
     opt = None
-    if peer and args.dp in ("auto", "multicast"):
+    if peer and args.dp in ("auto", "inbox"):
+        # parameters the other ranks map (CUDA IPC) and a gradient inbox per
+        # rank: the backward stores each Gaussian's gradients into the inbox
+        # of the rank that owns its slice (no local gradient arena)
+        g = dpm.shared_gaussian_set(cfg.n, cfg.sh_degree)
+        g.copy_from_numpy(params)
+        grads = None
+        opt = dpm.InboxAdam(dp, g, rt.AdamParams(max_grad_1=0.3))
+        dp_impl = "inbox"
+    if peer and opt is None and args.dp == "multicast":
         # arenas bound to a multicast object (NVLink SHARP)
         g = dpm.symmetric_gaussian_set(dp, cfg.n, cfg.sh_degree)
         g.copy_from_numpy(params)
         grads = dpm.symmetric_gaussian_set(dp, cfg.n, cfg.sh_degree)
-        try:
-            opt = dpm.MulticastAdam(dp, g, grads, rt.AdamParams(max_grad_1=0.3))
-            dp_impl = "multicast"
-        except RuntimeError:
-            if args.dp == "multicast":
-                raise
-            del g, grads
+        opt = dpm.MulticastAdam(dp, g, grads, rt.AdamParams(max_grad_1=0.3))
+        dp_impl = "multicast"
     if peer and opt is None:
         # parameters and gradient arenas the other ranks map (CUDA IPC)
         g = dpm.shared_gaussian_set(cfg.n, cfg.sh_degree)
@@ -462,6 +467,15 @@ def run_ours(args):
             ev[1].record(stream)
         if fused:
             opt.fused_backward_step(rast, ctx, 1.0 / GRAD_SCALER)
+        elif dp_impl == "inbox":
+            rast.backward_routed(ctx, *opt.route())
+            if ev is not None:
+                ev[2].record(stream)
+            # barrier, kernel (between ev[5] and ev[6]), barrier
+            opt.step(dp.gradient_scale(GRAD_SCALER), stream=stream, events=None if ev is None else ev[5:7])
+            if ev is not None:
+                ev[3].record(stream)
+                ev[4].record(stream)
         elif peer:
             rast.backward(ctx)
             if ev is not None:
@@ -572,6 +586,12 @@ def run_ours(args):
         kernel = "k_preprocess_backward<true> (per-Gaussian backward fused with Adam)"
         kernel_bytes = cfg.n * (6 * 236 + 4) + touched_v * 48
         kernel_ms = stages["gaussian_backward_adam"]
+    elif dp_impl == "inbox":
+        # k_preprocess_backward<false, true>: as below, but (N-1)/N of the
+        # gradient stores cross NVLink into the owners' inboxes
+        kernel = "k_preprocess_backward<false,true> (per-Gaussian backward, gradients routed to the owners' inboxes)"
+        kernel_bytes = cfg.n * (2 * 236 + 4) + touched_v * 48
+        kernel_ms = stages["gaussian_backward"]
     elif peer:
         # k_preprocess_backward<false>: parameters read, gradients written,
         # the touched-tile counts and screen-space gradients read
@@ -632,24 +652,32 @@ def run_ours(args):
         if world > 1:
             line["config"]["dp_impl"] = dp_impl
         if peer:
-            # into each GPU over NVLink: its slice's gradients loaded from the
-            # other ranks plus the other ranks' new parameters stored into it,
-            # 2 * 236 B * n/N * (N-1) (the bytes of a ring all-reduce); the
-            # same out of it (kernel alone; with_barriers_ms adds the two
-            # one-element all-reduces that order it and absorb the ranks' skew)
-            # (through the switch: 236 B * n, the slice's reduced gradients in
-            # plus the other slices' parameters in)
+            # NVLink bytes into each GPU (and the same out of it) per step.
+            # peer: its slice's gradients loaded from the other ranks plus the
+            # other ranks' new parameters stored into it, 2 * 236 B * n/N *
+            # (N-1) (the bytes of a ring all-reduce).  multicast: 236 B * n
+            # through the switch (reduced gradients of its slice in, the other
+            # slices' parameters in).  inbox: the kernel moves only the
+            # parameters, 236 B * n/N * (N-1); the gradients crossed during the
+            # backward.  "ms" is the kernel alone; with_barriers_ms adds the two
+            # one-element all-reduces that order it and absorb the ranks' skew
             slice_bytes = 236 * cfg.n / world
-            link_bytes = 236 * cfg.n if dp_impl == "multicast" else 2 * slice_bytes * (world - 1)
+            link_bytes = {"multicast": 236 * cfg.n, "inbox": slice_bytes * (world - 1)}.get(
+                dp_impl, 2 * slice_bytes * (world - 1))
             ms = stages["peer_kernel"]
+            kname = {"multicast": "k_dp_adam_mc (gradient sum by NVLink SHARP reducing loads + Adam + multicast "
+                                  "parameter stores)",
+                     "inbox": "k_dp_adam over the local inbox (gradient sum of the N slots + Adam + parameter "
+                              "broadcast to the peers)"}.get(
+                dp_impl, "k_dp_adam (gradient sum over peer memory + Adam + parameter broadcast)")
             line["peer_reduce_adam"] = {
-                "kernel": ("k_dp_adam_mc (gradient sum by NVLink SHARP reducing loads + Adam + multicast "
-                           "parameter stores)" if dp_impl == "multicast" else
-                           "k_dp_adam (gradient sum over peer memory + Adam + parameter broadcast)"),
-                "ms": ms, "with_barriers_ms": stages["peer_reduce_adam"], "nvlink_bytes_each_way_per_gpu": link_bytes,
+                "kernel": kname, "ms": ms, "with_barriers_ms": stages["peer_reduce_adam"],
+                "nvlink_bytes_each_way_per_gpu": link_bytes,
                 "achieved_gbs_each_way": link_bytes / (ms * 1e-3) / 1e9,
                 "peak_gbs_each_way": 770.0, "frac": link_bytes / (ms * 1e-3) / 1e9 / 770.0,
                 "peak_source": "measured peer copy on this pool (profiling recipe)"}
+            if dp_impl == "inbox":
+                line["peer_reduce_adam"]["routed_gradient_bytes_each_way_per_gpu"] = slice_bytes * (world - 1)
         print(json.dumps(line), flush=True)
     rast.close()
     loss.close()

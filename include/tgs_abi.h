@@ -436,6 +436,27 @@ TGS_API int tgs_dp_reduce_adam_multicast(const TgsGaussians* params_mc, const Tg
                                          const TgsAdamConfig* cfg, uint32_t step, float gradient_scale,
                                          tgs_stream_t stream);
 
+/* Gradient routing for several GPUs: the backward of tgs_raster_backward
+ * (overwrite mode) with each Gaussian's gradients stored into the gradient
+ * inbox of the rank whose slice holds it (inbox_per_rank[s], mapped into this
+ * process), into slot `rank`, while the kernel computes them -- the transfer
+ * the exchange would do afterwards overlaps the backward.  An inbox holds
+ * `world` slots, each laid out like a parameter arena of `slice_pad`
+ * Gaussians (segments back to back, slice_pad rows each); slices as in
+ * tgs_dp_reduce_adam. */
+TGS_API int tgs_raster_backward_routed(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cam,
+                                       int32_t dtype, const void* image, const void* grad_image,
+                                       float* const* inbox_per_rank, int64_t slice_pad, int32_t world,
+                                       int32_t rank, TgsDensificationInfo* dens, tgs_stream_t stream);
+
+/* The owner's half of the routed exchange: the slice's gradients are the sum
+ * of this rank's inbox slots (local memory, rank order), then the Adam step
+ * and the parameter stores into every rank as in tgs_dp_reduce_adam. */
+TGS_API int tgs_dp_inbox_adam(const TgsGaussians* params_per_rank, const float* inbox, int64_t slice_pad,
+                              int32_t world, int32_t rank, TgsGaussians* exp_avg, TgsGaussians* exp_avg_sq,
+                              const TgsAdamConfig* cfg, uint32_t step, float gradient_scale,
+                              tgs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

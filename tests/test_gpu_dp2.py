@@ -85,3 +85,93 @@ def test_peer_adam_two_gpus(tmp_path, mode):
     for k in ref:
         np.testing.assert_array_equal(r0[k], ref[k])
         np.testing.assert_array_equal(r1[k], ref[k])
+
+
+def _train_worker(rank: int, port: int, out_dir: str) -> None:
+    """One routed training step per rank (rank r renders view r)."""
+    import torch.distributed as dist
+
+    from tinygs_b200 import dp as dpm
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dp = dpm.DataParallel.from_env()
+        cfg = scenes.CONFIGS["cfg1"]
+        n = 20_001
+        params = scenes.gaussian_params(n, cfg.sh_degree, cfg.means, 9)
+        cam = scenes.cameras(cfg)[dp.view_index(0, len(scenes.cameras(cfg)))]
+        W, H = cam["width"], cam["height"]
+        g = dpm.shared_gaussian_set(n, cfg.sh_degree)
+        g.copy_from_numpy(params)
+        opt = dpm.InboxAdam(dp, g, rt.AdamParams(max_grad_1=0.3))
+        rast = rt.FastGSB200Rasterizer(n, W, H)
+        rast.set_gaussians(g)
+        img = torch.zeros(rt.image_numel(W, H), device="cuda")
+        gimg, lmap = torch.zeros_like(img), torch.zeros_like(img)
+        tgt = torch.from_numpy(scenes.target_image(W, H, 3).reshape(-1)).cuda()
+        loss = rt.FusedLoss(W, H)
+        ctx = rt.RasterizeContext(fwd_input=cam, fwd_output_image=img, grad_output_image=gimg, grad_scaler=10.0)
+        rast.forward(ctx)
+        loss.evaluate(img, tgt, lmap, gimg, W, H, grad_scaler=10.0)
+        rast.backward_routed(ctx, *opt.route())
+        opt.step(dp.gradient_scale(10.0))
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"train{rank}.npz"), **g.to_numpy())
+        opt.barrier()
+        opt.close()
+        rast.close()
+        loss.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_routed_training_step_two_gpus(tmp_path):
+    """Both ranks end with identical parameters (every slice broadcast by its
+    owner), equal to one GPU accumulating the two views' gradients and
+    stepping once, up to float-atomic order noise of the blend backward."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    mp.start_processes(_train_worker, args=(_free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    r0, r1 = (np.load(tmp_path / f"train{k}.npz") for k in range(2))
+    for k in r0.files:
+        np.testing.assert_array_equal(r0[k], r1[k])
+    # one GPU: views 0 and 1 accumulated, one Adam step at scale 1/(10*2)
+    cfg = scenes.CONFIGS["cfg1"]
+    n = 20_001
+    params = scenes.gaussian_params(n, cfg.sh_degree, cfg.means, 9)
+    cams = scenes.cameras(cfg)
+    g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+    grads = g.zeros_like()
+    opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
+    for v in range(2):
+        cam = cams[v]
+        W, H = cam["width"], cam["height"]
+        rast = rt.FastGSB200Rasterizer(n, W, H)
+        rast.set_gaussians(g)
+        img = torch.zeros(rt.image_numel(W, H), device="cuda")
+        gimg, lmap = torch.zeros_like(img), torch.zeros_like(img)
+        tgt = torch.from_numpy(scenes.target_image(W, H, 3).reshape(-1)).cuda()
+        loss = rt.FusedLoss(W, H)
+        ctx = rt.RasterizeContext(fwd_input=cam, fwd_output_image=img, grad_output_image=gimg,
+                                  gaussians_grad=grads, grad_scaler=10.0, accumulate=True)
+        rast.forward(ctx)
+        loss.evaluate(img, tgt, lmap, gimg, W, H, grad_scaler=10.0)
+        rast.backward(ctx)
+        rast.close()
+        loss.close()
+    opt.step(1.0 / (10.0 * 2))
+    ref = g.to_numpy()
+    for k in ref:
+        close = np.abs(r0[k] - ref[k]) <= 1e-6 + 1e-5 * np.abs(ref[k])
+        assert close.mean() > 0.999, (k, close.mean())

@@ -113,6 +113,10 @@ PROTOTYPES = {
     "tgs_shared_free": (c_int32, [_P]),
     "tgs_shared_open": (c_int32, [POINTER(TgsIpcHandle), POINTER(c_void_p)]),
     "tgs_shared_close": (c_int32, [_P]),
+    "tgs_raster_backward_routed": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, _P, _P,
+                                             POINTER(c_void_p), c_int64, c_int32, c_int32, _P, _P]),
+    "tgs_dp_inbox_adam": (c_int32, [POINTER(TgsGaussians), _P, c_int64, c_int32, c_int32, POINTER(TgsGaussians),
+                                    POINTER(TgsGaussians), POINTER(TgsAdamConfig), c_uint32, c_float, _P]),
     "tgs_dp_reduce_adam_multicast": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
                                                c_int32, c_int32, POINTER(TgsGaussians), POINTER(TgsGaussians),
                                                POINTER(TgsAdamConfig), c_uint32, c_float, _P]),

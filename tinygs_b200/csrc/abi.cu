@@ -623,4 +623,73 @@ int tgs_dp_reduce_adam_multicast(const TgsGaussians* params_mc, const TgsGaussia
   return cuda_status(cudaGetLastError());
 }
 
+int tgs_raster_backward_routed(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cam, int32_t dtype,
+                               const void* image, const void* grad_image, float* const* inbox_per_rank,
+                               int64_t slice_pad, int32_t world, int32_t rank, TgsDensificationInfo* dens,
+                               tgs_stream_t stream) {
+  if (r == nullptr || !gaussians_ok(params) || !camera_ok(cam) || image == nullptr || grad_image == nullptr ||
+      inbox_per_rank == nullptr || world < 1 || world > kMaxDpRanks || rank < 0 || rank >= world)
+    return TGS_ERR_INVALID_ARGUMENT;
+  RasterState& s = r->s;
+  if (!s.have_forward || s.last_dtype != dtype || s.last_n != params->n) return TGS_ERR_NO_FORWARD;
+  GradRoute route{};
+  for (int k = 0; k < world; ++k) {
+    if (inbox_per_rank[k] == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+    route.inbox[k] = inbox_per_rank[k];
+  }
+  for (int k = 0; k <= world; ++k) route.lo[k] = dp_slice_begin(params->n, world, k);
+  for (int k = 0; k < world; ++k)
+    if (route.lo[k + 1] - route.lo[k] > slice_pad) return TGS_ERR_CAPACITY;
+  route.slice_pad = slice_pad;
+  route.world = world;
+  route.rank = rank;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const DevCamera dc = make_camera(cam->width, cam->height, cam->fx, cam->fy, cam->cx, cam->cy, cam->near_plane,
+                                   cam->far_plane, cam->w2c);
+  mark(r, 4, st);
+  launch_blend_backward(s, dc, dtype == TGS_FLOAT16, image, grad_image, dens != nullptr, st);
+  mark(r, 5, st);
+  if (params->n > 0) {
+    GaussianPtrs none{};
+    none.n = params->n;
+    launch_preprocess_backward(s, to_ptrs(params), none, dc, 0, reinterpret_cast<float4*>(dens), st, nullptr,
+                               nullptr, nullptr, &route);
+  }
+  mark(r, 6, st);
+  r->bwd_timed = r->timing;
+  return cuda_status(cudaGetLastError());
+}
+
+int tgs_dp_inbox_adam(const TgsGaussians* params_per_rank, const float* inbox, int64_t slice_pad, int32_t world,
+                      int32_t rank, TgsGaussians* exp_avg, TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg,
+                      uint32_t step, float gradient_scale, tgs_stream_t stream) {
+  if (params_per_rank == nullptr || inbox == nullptr || world < 1 || world > kMaxDpRanks || rank < 0 ||
+      rank >= world || cfg == nullptr || step == 0 || !gaussians_ok(exp_avg) || !gaussians_ok(exp_avg_sq))
+    return TGS_ERR_INVALID_ARGUMENT;
+  const int64_t n = params_per_rank[rank].n;
+  if (dp_slice_begin(n, world, rank + 1) - dp_slice_begin(n, world, rank) > slice_pad) return TGS_ERR_CAPACITY;
+  GaussianPtrs p[kMaxDpRanks], g[kMaxDpRanks];
+  const int widths[6] = {3, 1, 4, 3, 3, 45};
+  for (int r = 0; r < world; ++r) {
+    if (!gaussians_ok(&params_per_rank[r]) || params_per_rank[r].n != n) return TGS_ERR_INVALID_ARGUMENT;
+    p[r] = to_ptrs(&params_per_rank[r]);
+    // slot r of the inbox: an arena of slice_pad Gaussians
+    float* slot = const_cast<float*>(inbox) + static_cast<int64_t>(r) * 59 * slice_pad;
+    float* seg[6];
+    int64_t off = 0;
+    for (int k = 0; k < 6; ++k) {
+      seg[k] = slot + off;
+      off += widths[k] * slice_pad;
+    }
+    g[r] = GaussianPtrs{seg[0], seg[1], seg[2], seg[3], seg[4], seg[5], n, 0};
+  }
+  if (exp_avg->n != n || exp_avg_sq->n != n) return TGS_ERR_INVALID_ARGUMENT;
+  if (n == 0) return TGS_OK;
+  AdamStepArgs a{};
+  adam_segments(cfg, n, step, gradient_scale, &a);
+  launch_dp_adam(p, g, world, rank, to_ptrs(exp_avg), to_ptrs(exp_avg_sq), a, static_cast<cudaStream_t>(stream),
+                 true);
+  return cuda_status(cudaGetLastError());
+}
+
 }  // extern "C"

@@ -103,6 +103,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 struct PeerTable {
   float* params[kMaxDpRanks][6];
   const float* grads[kMaxDpRanks][6];
+  int64_t goff[6];  // gradient arrays indexed by (element - goff)
   float* m[6];
   float* v[6];
   int64_t lo[6];
@@ -131,11 +132,12 @@ __device__ __forceinline__ DpChunk dp_load(const PeerTable& t, int64_t c) {
   k.e0 = t.lo[k.s] + (c - t.chunk_begin[k.s]) * 4;
   k.vec = t.vec && k.e0 + 4 <= t.hi[k.s];
   if (k.vec) {
-    k.g = *reinterpret_cast<const float4*>(t.grads[0][k.s] + k.e0);
+    const int64_t ge = k.e0 - t.goff[k.s];
+    k.g = *reinterpret_cast<const float4*>(t.grads[0][k.s] + ge);
 #pragma unroll
     for (int r = 1; r < kMaxDpRanks; ++r) {
       if (r >= t.world) break;
-      const float4 q = *reinterpret_cast<const float4*>(t.grads[r][k.s] + k.e0);
+      const float4 q = *reinterpret_cast<const float4*>(t.grads[r][k.s] + ge);
       k.g.x += q.x;
       k.g.y += q.y;
       k.g.z += q.z;
@@ -166,8 +168,8 @@ __device__ __forceinline__ void dp_finish(const PeerTable& t, DpChunk& k, const 
   } else {
     // scalar tail (a slice end that is not a multiple of four floats)
     for (int64_t e = k.e0; e < min(k.e0 + 4, t.hi[k.s]); ++e) {
-      float g = t.grads[0][k.s][e];
-      for (int r = 1; r < t.world; ++r) g += t.grads[r][k.s][e];
+      float g = t.grads[0][k.s][e - t.goff[k.s]];
+      for (int r = 1; r < t.world; ++r) g += t.grads[r][k.s][e - t.goff[k.s]];
       float th = t.params[t.rank][k.s][e], m = t.m[k.s][e], v = t.v[k.s][e];
       adam_one(th, g, m, v, lr, kind, decay, a);
       t.m[k.s][e] = m;
@@ -305,8 +307,7 @@ void launch_dp_adam_mc(const GaussianPtrs& params_mc, const GaussianPtrs& grads_
                        cudaStream_t stream) {
   McTable t{};
   const int64_t n = own.n;
-  const int64_t lo_g = (n * rank / world) / 4 * 4;
-  const int64_t hi_g = rank == world - 1 ? n : (n * (rank + 1) / world) / 4 * 4;
+  const int64_t lo_g = dp_slice_begin(n, world, rank), hi_g = dp_slice_begin(n, world, rank + 1);
   const int widths[6] = {3, 1, 4, 3, 3, 45};
   float* pm[6] = {params_mc.means, params_mc.opacities, params_mc.rotations, params_mc.scales, params_mc.sh0,
                   params_mc.sh_rest};
@@ -342,14 +343,13 @@ void launch_dp_adam_mc(const GaussianPtrs& params_mc, const GaussianPtrs& grads_
 }
 
 void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int world, int rank,
-                    const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream) {
+                    const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream,
+                    bool grads_are_slices) {
   PeerTable t{};
   t.world = world;
   t.rank = rank;
   const int64_t n = params[rank].n;
-  // slice boundaries on multiples of four Gaussians (16-byte aligned rows)
-  const int64_t lo_g = (n * rank / world) / 4 * 4;
-  const int64_t hi_g = rank == world - 1 ? n : (n * (rank + 1) / world) / 4 * 4;
+  const int64_t lo_g = dp_slice_begin(n, world, rank), hi_g = dp_slice_begin(n, world, rank + 1);
   const int widths[6] = {3, 1, 4, 3, 3, 45};
   bool vec = true;
   for (int r = 0; r < world; ++r) {
@@ -372,6 +372,7 @@ void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int w
     vec = vec && aligned16(mp[k]) && aligned16(vp[k]);
     t.lo[k] = lo_g * widths[k];
     t.hi[k] = hi_g * widths[k];
+    t.goff[k] = grads_are_slices ? t.lo[k] : 0;
     t.lr[k] = adam.lr[k];
     t.decay[k] = adam.decay[k];
     t.kind[k] = adam.kind[k];

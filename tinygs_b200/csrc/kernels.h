@@ -102,6 +102,7 @@ void launch_blend_backward(const RasterState& s, const DevCamera& cam, int fp16,
                            const void* grad_image, int abs_grad, cudaStream_t stream);
 // Optimizer step fused into the preprocess backward (per-segment learning
 // rate, decay kind and weight in the reference's segment order).
+struct GradRoute;  // below: multi-GPU gradient routing
 struct AdamStepArgs {
   float lr[6];
   float decay[6];
@@ -114,7 +115,8 @@ struct AdamStepArgs {
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g,
                                 const GaussianPtrs& grads, const DevCamera& cam, int accumulate,
                                 float4* dens, cudaStream_t stream, const GaussianPtrs* exp_avg = nullptr,
-                                const GaussianPtrs* exp_avg_sq = nullptr, const AdamStepArgs* adam = nullptr);
+                                const GaussianPtrs* exp_avg_sq = nullptr, const AdamStepArgs* adam = nullptr,
+                                const GradRoute* route = nullptr);
 
 // losses (loss.cu)
 void launch_l1(int fp16, int width, int height, const void* pred, const void* target,
@@ -126,8 +128,26 @@ void launch_ssim(int fp16, int width, int height, const void* pred, const void* 
 // data-parallel Adam over peer memory (adam.cu): params/grads hold one
 // entry per rank (pointers valid in this process)
 constexpr int kMaxDpRanks = 8;
+// First Gaussian of rank r's slice (multiples of four, so every slice's rows
+// start 16-byte aligned); dp_slice_begin(n, world, world) == n.
+inline int64_t dp_slice_begin(int64_t n, int world, int r) {
+  return r >= world ? n : (n * r / world) / 4 * 4;
+}
+// grads_are_slices: grads[r] hold only this rank's slice (row 0 = the
+// slice's first Gaussian), as in the gradient inbox
 void launch_dp_adam(const GaussianPtrs* params, const GaussianPtrs* grads, int world, int rank,
-                    const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream);
+                    const GaussianPtrs& m, const GaussianPtrs& v, const AdamStepArgs& adam, cudaStream_t stream,
+                    bool grads_are_slices = false);
+// Gradient routing of the per-Gaussian backward: Gaussian i's gradients go
+// to the inbox of the rank whose slice holds it, into slot `rank`.  An inbox
+// holds `world` slots, each laid out like a parameter arena of `slice_pad`
+// Gaussians.
+struct GradRoute {
+  float* inbox[kMaxDpRanks];
+  int64_t lo[kMaxDpRanks + 1];
+  int64_t slice_pad;
+  int world, rank;
+};
 
 // the same over the multicast addresses of the gradient and parameter
 // arenas (NVLink SHARP); `own` are this rank's parameters

@@ -333,6 +333,17 @@ struct AdamArgs {
   float beta1, beta2, eps, gscale, bc1, bc2_sqrt, max_g;
 };
 
+struct RouteArgs {
+  float* inbox[kMaxDpRanks];
+  int64_t lo[kMaxDpRanks + 1];
+  int64_t slice_pad;
+  int world, rank;
+  // warps start at the next rank's slice and end with this rank's own, so the
+  // stores crossing NVLink go out first (overlapping the local slice's work)
+  // and the ranks begin with different owners
+  uint32_t warp_shift;
+};
+
 // SH colour backward (fastgs_ours/kernels_backward.cuh:22-86): writes the 45
 // higher-band gradients and returns dL/dposition through the view direction.
 __device__ __forceinline__ float3 sh_backward_slice(const float* __restrict__ rest, float* __restrict__ sb,
@@ -560,15 +571,45 @@ __device__ __forceinline__ float slice_grad(const float* __restrict__ g, const f
 // Write-out of segment k: gradients (=, or += when accumulate) or, when
 // kAdam, the Adam step on (params, exp_avg, exp_avg_sq) plus the optional
 // gradient store.
-template <bool kAdam, int k>
+// Destination of gradient element `elem` (index within segment k, i.e.
+// Gaussian * width + component) under gradient routing: slot `rank` of the
+// inbox of the rank whose slice holds the Gaussian.
+template <int k>
+__device__ __forceinline__ float* routed_dst(const RouteArgs& r, int64_t elem) {
+  constexpr int w = seg_width(k);
+  const int64_t gi = elem / w;
+  int s = r.world - 1;
+  while (s > 0 && r.lo[s] > gi) --s;
+  int64_t seg_base = 0;
+#pragma unroll
+  for (int j = 0; j < k; ++j) seg_base += seg_width(j) * r.slice_pad;
+  return r.inbox[s] + r.rank * 59 * r.slice_pad + seg_base + (elem - r.lo[s] * w);
+}
+
+template <bool kAdam, int k, bool kRoute = false>
 __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, int accumulate,
                                               const float* __restrict__ th, const float* __restrict__ g,
                                               const float* __restrict__ sb, uint32_t first, uint32_t cnt,
-                                              uint32_t lane, bool v16) {
+                                              uint32_t lane, bool v16, const RouteArgs& route) {
   constexpr int w = seg_width(k);
   const size_t base = static_cast<size_t>(first) * w;
   const uint32_t count = cnt * w;
+  if constexpr (kRoute) {
+    // overwrite into the owners' inboxes; a slice boundary is a multiple of
+    // four Gaussians, so no 16-byte chunk straddles two owners
+    if (v16) {
+      for (uint32_t e4 = lane; e4 < count / 4; e4 += 32) {
+        const float4 gv = make_float4(slice_grad<k>(g, sb, 4 * e4), slice_grad<k>(g, sb, 4 * e4 + 1),
+                                      slice_grad<k>(g, sb, 4 * e4 + 2), slice_grad<k>(g, sb, 4 * e4 + 3));
+        *reinterpret_cast<float4*>(routed_dst<k>(route, static_cast<int64_t>(base) + 4 * e4)) = gv;
+      }
+    } else {
+      for (uint32_t e = lane; e < count; e += 32)
+        *routed_dst<k>(route, static_cast<int64_t>(base) + e) = slice_grad<k>(g, sb, e);
+    }
+    return;
+  }
   float* G = grads.p[k] != nullptr ? grads.p[k] + base : nullptr;
   if constexpr (kAdam) {
     const float* ts = th + seg_off(k);
@@ -633,16 +674,22 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
 // followed by tgs_adam_step without the gradient round trip through HBM.
 // The moments of the warp's Gaussians are prefetched into L2 (bulk
 // prefetch) at the start, so their reads in the write-out hit L2.
-template <bool kAdam>
+template <bool kAdam, bool kRoute = false>
 __global__ void __launch_bounds__(32 * kBwdWarps)
     k_preprocess_backward(SegPtrs params, SegPtrs grads, SegPtrs exp_avg, SegPtrs exp_avg_sq, AdamArgs adam,
                           int accumulate, int vec, int active_bases, uint32_t n, DevCamera cam,
                           const uint32_t* __restrict__ n_touched, const float4* __restrict__ helpers,
-                          float4* __restrict__ dens, const DevCounts* __restrict__ counts) {
+                          float4* __restrict__ dens, const DevCounts* __restrict__ counts, RouteArgs route) {
   __shared__ __align__(16) float smem[kBwdWarps * kWarpFloats];
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  const uint32_t first = (blockIdx.x * kBwdWarps + warp) * kWarpGaussians;
-  if (first >= n) return;
+  uint32_t wi = blockIdx.x * kBwdWarps + warp;
+  const uint32_t n_warps = (n + kWarpGaussians - 1) / kWarpGaussians;
+  if (wi >= n_warps) return;
+  if constexpr (kRoute) {
+    wi += route.warp_shift;
+    if (wi >= n_warps) wi -= n_warps;
+  }
+  const uint32_t first = wi * kWarpGaussians;
   const uint32_t cnt = min(static_cast<uint32_t>(kWarpGaussians), n - first);
   const bool v16 = vec != 0 && cnt == kWarpGaussians;
   float* th = smem + warp * kWarpFloats;
@@ -690,12 +737,20 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
     for (int c = 0; c < 18; ++c) my_sb[c] = 0.f;
   }
   __syncwarp();
-  write_segment<kAdam, 0>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
-  write_segment<kAdam, 1>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
-  write_segment<kAdam, 2>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
-  write_segment<kAdam, 3>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
-  write_segment<kAdam, 4>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
-  write_segment<kAdam, 5>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane, v16);
+  write_segment<kAdam, 0, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
+                                    v16, route);
+  write_segment<kAdam, 1, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
+                                    v16, route);
+  write_segment<kAdam, 2, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
+                                    v16, route);
+  write_segment<kAdam, 3, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
+                                    v16, route);
+  write_segment<kAdam, 4, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
+                                    v16, route);
+  write_segment<kAdam, 5, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
+                                    v16, route);
+  // routed stores reach the other ranks' memory before this kernel completes
+  if constexpr (kRoute) __threadfence_system();
 }
 
 }  // namespace
@@ -722,7 +777,7 @@ void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCam
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, const GaussianPtrs& grads,
                                 const DevCamera& cam, int accumulate, float4* dens, cudaStream_t stream,
                                 const GaussianPtrs* exp_avg, const GaussianPtrs* exp_avg_sq,
-                                const AdamStepArgs* adam) {
+                                const AdamStepArgs* adam, const GradRoute* route) {
   const uint32_t n = static_cast<uint32_t>(g.n);
   if (n == 0) return;
   const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
@@ -757,12 +812,30 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, con
     const int vec = aligned(segs(g)) && aligned(m) && aligned(v) && aligned(segs(grads));
     k_preprocess_backward<true><<<blocks, 32 * kBwdWarps, 0, stream>>>(
         segs(g), segs(grads), m, v, a, 0, vec, active_bases, n, cam, s.n_touched,
-        reinterpret_cast<const float4*>(s.helpers), dens, s.counts);
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{});
+  } else if (route != nullptr) {
+    RouteArgs r{};
+    bool vec = aligned(segs(g));
+    for (int k = 0; k < route->world; ++k) {
+      r.inbox[k] = route->inbox[k];
+      vec = vec && (reinterpret_cast<uintptr_t>(route->inbox[k]) & 15u) == 0;
+    }
+    for (int k = 0; k <= route->world; ++k) r.lo[k] = route->lo[k];
+    r.slice_pad = route->slice_pad;
+    r.world = route->world;
+    r.rank = route->rank;
+    const uint32_t n_warps = (n + kWarpGaussians - 1) / kWarpGaussians;
+    const int64_t next_lo = route->lo[(route->rank + 1) % route->world];
+    r.warp_shift = static_cast<uint32_t>(next_lo / kWarpGaussians) % n_warps;
+    vec = vec && route->slice_pad % 4 == 0;
+    k_preprocess_backward<false, true><<<blocks, 32 * kBwdWarps, 0, stream>>>(
+        segs(g), segs(grads), m, v, a, 0, vec ? 1 : 0, active_bases, n, cam, s.n_touched,
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, r);
   } else {
     const int vec = aligned(segs(g)) && aligned(segs(grads));
     k_preprocess_backward<false><<<blocks, 32 * kBwdWarps, 0, stream>>>(
         segs(g), segs(grads), m, v, a, accumulate, vec, active_bases, n, cam, s.n_touched,
-        reinterpret_cast<const float4*>(s.helpers), dens, s.counts);
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{});
   }
 }
 

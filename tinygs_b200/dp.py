@@ -253,3 +253,99 @@ class MulticastAdam:
 
     def close(self) -> None:
         pass
+
+
+# ------------------------------------------------------------------------
+# Gradient routing: the backward stores each Gaussian's gradients straight
+# into the gradient inbox of the rank that owns it, so the gradient transfer
+# overlaps the backward; the exchange kernel then sums the local inbox slots
+# and only broadcasts the new parameters.
+
+def dp_slice_begin(n: int, world: int, r: int) -> int:
+    """First Gaussian of rank r's slice (as the C library cuts them)."""
+    return n if r >= world else (n * r // world) // 4 * 4
+
+
+class InboxAdam:
+    """Routed data-parallel step.  Usage per training step:
+    `rast.backward_routed(ctx, *opt.route())` after the forward and loss, then
+    `opt.step(scale)` (barrier, tgs_dp_inbox_adam, barrier)."""
+
+    def __init__(self, dp: DataParallel, params: "rt.GaussianSet", cfg: "rt.AdamParams | None" = None):
+        self.lib = load_library()
+        self.dp, self.params = dp, params
+        self.cfg = cfg or rt.AdamParams()
+        self.exp_avg = params.zeros_like()
+        self.exp_avg_sq = params.zeros_like()
+        self.global_steps = 0
+        self.flag = torch.zeros(1, dtype=torch.float32, device="cuda")
+        n, w = params.n, dp.world
+        widest = max(dp_slice_begin(n, w, r + 1) - dp_slice_begin(n, w, r) for r in range(w))
+        self.slice_pad = (widest + 3) // 4 * 4
+        nbytes = 4 * rt.FLOATS_PER_GAUSSIAN * self.slice_pad * w
+        ptr, handle = ctypes.c_void_p(), TgsIpcHandle()
+        check(self.lib.tgs_shared_alloc(max(nbytes, 256), ctypes.byref(ptr), ctypes.byref(handle)),
+              "tgs_shared_alloc")
+        self.inbox = ptr.value
+        self._inbox_block = _SharedBlock(self.lib, ptr.value)
+        handles = [None] * w
+        mine = (params.ipc_handle, handle.raw())
+        if w > 1:
+            dist.all_gather_object(handles, mine, group=dp.group)
+        else:
+            handles = [mine]
+        self.opened: list[int] = []
+        self.base_p, self.inboxes = [], []
+        for r, (hp, hi) in enumerate(handles):
+            if r == dp.rank:
+                self.base_p.append(params.storage.data_ptr())
+                self.inboxes.append(self.inbox)
+                continue
+            ptrs = []
+            for h in (hp, hi):
+                p = ctypes.c_void_p()
+                check(self.lib.tgs_shared_open(ctypes.byref(TgsIpcHandle.from_raw(h)), ctypes.byref(p)),
+                      "tgs_shared_open")
+                self.opened.append(p.value)
+                ptrs.append(p.value)
+            self.base_p.append(ptrs[0])
+            self.inboxes.append(ptrs[1])
+
+    def route(self):
+        """Arguments of FastGSB200Rasterizer.backward_routed after ctx."""
+        return self.inboxes, self.slice_pad, self.dp.world, self.dp.rank
+
+    def barrier(self) -> None:
+        if self.dp.world > 1:
+            dist.all_reduce(self.flag, group=self.dp.group)
+
+    def step(self, gradient_scale: float, stream=None, events=None) -> None:
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        self.global_steps += 1
+        arr = (TgsGaussians * self.dp.world)()
+        offs, off = {}, 0
+        for name in rt.SEGMENTS:
+            offs[name] = off
+            off += rt.WIDTHS[name] * self.params.npad
+        for r, b in enumerate(self.base_p):
+            for name in rt.SEGMENTS:
+                setattr(arr[r], name, b + 4 * offs[name])
+            arr[r].n, arr[r].sh_degree = self.params.n, self.params.sh_degree
+        m, v = self.exp_avg.abi(), self.exp_avg_sq.abi()
+        cfg = self.cfg.abi()
+        self.barrier()  # every rank's routed gradients have landed
+        if events is not None:
+            events[0].record(stream)
+        check(self.lib.tgs_dp_inbox_adam(arr, ctypes.c_void_p(self.inbox), self.slice_pad, self.dp.world,
+                                         self.dp.rank, ctypes.byref(m), ctypes.byref(v), ctypes.byref(cfg),
+                                         self.global_steps, float(gradient_scale), rt._stream_handle(stream)),
+              "tgs_dp_inbox_adam")
+        if events is not None:
+            events[1].record(stream)
+        self.barrier()  # every rank's parameters are updated
+
+    def close(self) -> None:
+        for p in self.opened:
+            self.lib.tgs_shared_close(ctypes.c_void_p(p))
+        self.opened = []

@@ -196,6 +196,19 @@ class FastGSB200Rasterizer:
                                            1 if ctx.accumulate else 0, _ptr(ctx.densification_info),
                                            _stream_handle(ctx.stream)), "tgs_raster_backward")
 
+    def backward_routed(self, ctx: RasterizeContext, inbox_ptrs: list[int], slice_pad: int, world: int,
+                        rank: int) -> None:
+        """Backward (overwrite mode) storing each Gaussian's gradients into its
+        owner's gradient inbox, slot `rank` (tgs_raster_backward_routed)."""
+        g = self.gaussians.abi()
+        cam = make_camera(ctx.fwd_input)
+        arr = (ctypes.c_void_p * world)(*inbox_ptrs)
+        check(self.lib.tgs_raster_backward_routed(self.handle, ctypes.byref(g), ctypes.byref(cam),
+                                                  self._dtype(ctx.fwd_output_image), _ptr(ctx.fwd_output_image),
+                                                  _ptr(ctx.grad_output_image), arr, int(slice_pad), world, rank,
+                                                  _ptr(ctx.densification_info), _stream_handle(ctx.stream)),
+              "tgs_raster_backward_routed")
+
     def set_stage_timing(self, enable: bool) -> None:
         check(self.lib.tgs_raster_set_stage_timing(self.handle, 1 if enable else 0), "tgs_raster_set_stage_timing")
 

@@ -1,8 +1,11 @@
-"""The data-parallel optimizer step over peer memory on two GPUs
-(tgs_dp_reduce_adam through tinygs_b200.dp.PeerAdam): after one step every
-rank holds exactly the parameters that one GPU gets from Adam over the sum
-of both ranks' gradients (the reference's accumulation of two views).
-Needs two GPUs; skipped otherwise."""
+"""The data-parallel optimizer steps on two GPUs: over peer memory
+(tgs_dp_reduce_adam, tinygs_b200.dp.PeerAdam) and through NVLink SHARP
+(tgs_dp_reduce_adam_multicast, MulticastAdam) every rank ends with exactly
+the parameters that one GPU gets from Adam over the sum of both ranks'
+gradients (the reference's accumulation of two views); a whole routed
+training step (tgs_raster_backward_routed + tgs_dp_inbox_adam, InboxAdam)
+against one GPU accumulating the same two views.  Needs two GPUs; skipped
+otherwise."""
 import os
 import socket
 from datetime import timedelta

@@ -571,19 +571,67 @@ __device__ __forceinline__ float slice_grad(const float* __restrict__ g, const f
 // Write-out of segment k: gradients (=, or += when accumulate) or, when
 // kAdam, the Adam step on (params, exp_avg, exp_avg_sq) plus the optional
 // gradient store.
+// Owner of Gaussian gi under gradient routing: the last rank whose slice
+// starts at or before it (empty slices are skipped that way).
+__device__ __forceinline__ int route_owner(const RouteArgs& r, int64_t gi) {
+  int s = r.world - 1;
+  while (s > 0 && r.lo[s] > gi) --s;
+  return s;
+}
+
 // Destination of gradient element `elem` (index within segment k, i.e.
 // Gaussian * width + component) under gradient routing: slot `rank` of the
 // inbox of the rank whose slice holds the Gaussian.
 template <int k>
 __device__ __forceinline__ float* routed_dst(const RouteArgs& r, int64_t elem) {
   constexpr int w = seg_width(k);
-  const int64_t gi = elem / w;
-  int s = r.world - 1;
-  while (s > 0 && r.lo[s] > gi) --s;
+  const int s = route_owner(r, elem / w);
   int64_t seg_base = 0;
 #pragma unroll
   for (int j = 0; j < k; ++j) seg_base += seg_width(j) * r.slice_pad;
   return r.inbox[s] + r.rank * 59 * r.slice_pad + seg_base + (elem - r.lo[s] * w);
+}
+
+// Routed write-out of a full, 16-byte aligned warp slice through the bulk
+// copy engine: segments 0..4 of the gradients already sit in shared memory
+// in the arenas' layout (g), segment 5 (the rank-1 SH gradient) is written
+// out into the no longer needed parameter staging area, then one lane hands
+// every (segment, owner) piece to cp.async.bulk, so the warp does not wait on
+// the stores crossing NVLink.  Pieces start and end on multiples of four
+// Gaussians (warp slices start on multiples of 32, owner slices on multiples
+// of four), so every address and size is a multiple of 16 bytes.
+__device__ __forceinline__ void route_warp_bulk(const RouteArgs& r, float* th, const float* g, const float* sb,
+                                                uint32_t first, uint32_t lane) {
+  for (uint32_t e = lane; e < 45u * kWarpGaussians; e += 32) th[seg_off(5) + e] = slice_grad<5>(g, sb, e);
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+    int64_t g0 = first;
+    const int64_t end = static_cast<int64_t>(first) + kWarpGaussians;
+    while (g0 < end) {
+      const int s = route_owner(r, g0);
+      const int64_t g1 = min(end, r.lo[s + 1]);
+      float* slot = r.inbox[s] + static_cast<int64_t>(r.rank) * 59 * r.slice_pad;
+      int64_t seg_base = 0;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        const int w = seg_width(k);
+        const float* src = (k < 5 ? g : th) + seg_off(k) + (g0 - first) * w;
+        float* dst = slot + seg_base + (g0 - r.lo[s]) * w;
+        const uint32_t bytes = static_cast<uint32_t>((g1 - g0) * w * 4);
+        const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(src));
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(dst), "r"(saddr),
+                     "r"(bytes)
+                     : "memory");
+        seg_base += w * r.slice_pad;
+      }
+      g0 = g1;
+    }
+    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+    // the shared-memory sources are read before the warp's slot is freed
+    asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+  }
+  __syncwarp();
 }
 
 template <bool kAdam, int k, bool kRoute = false>
@@ -737,20 +785,25 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
     for (int c = 0; c < 18; ++c) my_sb[c] = 0.f;
   }
   __syncwarp();
-  write_segment<kAdam, 0, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
-                                    v16, route);
-  write_segment<kAdam, 1, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
-                                    v16, route);
-  write_segment<kAdam, 2, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
-                                    v16, route);
-  write_segment<kAdam, 3, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
-                                    v16, route);
-  write_segment<kAdam, 4, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
-                                    v16, route);
-  write_segment<kAdam, 5, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt, lane,
-                                    v16, route);
-  // routed stores reach the other ranks' memory before this kernel completes
-  if constexpr (kRoute) __threadfence_system();
+  if (kRoute && v16) {
+    route_warp_bulk(route, th, g, sb, first, lane);
+  } else {
+    write_segment<kAdam, 0, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
+                                      lane, v16, route);
+    write_segment<kAdam, 1, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
+                                      lane, v16, route);
+    write_segment<kAdam, 2, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
+                                      lane, v16, route);
+    write_segment<kAdam, 3, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
+                                      lane, v16, route);
+    write_segment<kAdam, 4, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
+                                      lane, v16, route);
+    write_segment<kAdam, 5, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
+                                      lane, v16, route);
+  }
+  // (routed stores: the kernel's completion orders them before the
+  // collective that the owners wait on; no per-warp system fence, which
+  // would hold every warp until its stores crossed NVLink)
 }
 
 }  // namespace

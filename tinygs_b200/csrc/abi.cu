@@ -162,6 +162,7 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   s.cap_chunks = static_cast<int64_t>(ne / kChunk + ns + 1);
   s.chunks = c.take<uint4>(static_cast<size_t>(s.cap_chunks));
   s.chunk_counts = c.take<uint32_t>(static_cast<size_t>(s.cap_chunks) * kSuperTiles);
+  s.sub_offsets = c.take<uint32_t>(static_cast<size_t>(s.cap_chunks) * kSubChunks * kSuperTiles);
   s.tile_total = c.take<uint32_t>(nt);
   s.sort_max_blocks = static_cast<int64_t>((std::max(n, ne) + kSortTileItems - 1) / kSortTileItems);
   s.sort_hist = c.take<uint32_t>(256 * static_cast<size_t>(s.sort_max_blocks));

@@ -445,8 +445,10 @@ __global__ void __launch_bounds__(kScanBlock)
                  const ushort4* __restrict__ bounds, const float2* __restrict__ mean2d,
                  const float4* __restrict__ conic_opacity, const PrimInfo16* __restrict__ prim_info,
                  const DevCounts* __restrict__ counts, uint32_t super_w, uint32_t* __restrict__ masks,
-                 uint32_t* __restrict__ chunk_counts, uint32_t* __restrict__ n_touched) {
-  __shared__ uint32_t s_cnt[kSuperTiles];
+                 uint32_t* __restrict__ chunk_counts, uint32_t* __restrict__ sub_offsets,
+                 uint32_t* __restrict__ n_touched) {
+  static_assert(kSubChunk == kScanBlock, "one block pass per emission sub-chunk");
+  __shared__ uint32_t s_cnt[kSubChunks * kSuperTiles];
   const unsigned full = 0xffffffffu;
   const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
   const uint32_t lane = threadIdx.x & 31u;
@@ -454,9 +456,10 @@ __global__ void __launch_bounds__(kScanBlock)
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const uint4 ch = chunks[c];
     const uint32_t tx0 = (ch.x % super_w) * kSuperW, ty0 = (ch.x / super_w) * kSuperH;
-    if (threadIdx.x < kSuperTiles) s_cnt[threadIdx.x] = 0;
+    if (threadIdx.x < kSubChunks * kSuperTiles) s_cnt[threadIdx.x] = 0;
     __syncthreads();
     for (uint32_t e0 = ch.y; e0 < ch.z; e0 += kScanBlock) {
+      uint32_t* sub_cnt = s_cnt + (e0 - ch.y) / kScanBlock * kSuperTiles;
       const uint32_t e = e0 + threadIdx.x;
       const bool valid = e < ch.z;
       uint32_t prim = 0, x0 = 0, y0 = 0, w = 0, h = 0, magic = 0;
@@ -538,10 +541,19 @@ __global__ void __launch_bounds__(kScanBlock)
         const uint32_t bj = __ballot_sync(full, (mask >> j) & 1u);
         if (lane == static_cast<uint32_t>(j)) mine = __popc(bj);
       }
-      if (mine) atomicAdd(&s_cnt[lane], mine);
+      if (mine) atomicAdd(&sub_cnt[lane], mine);
     }
     __syncthreads();
-    if (threadIdx.x < kSuperTiles) chunk_counts[c * kSuperTiles + threadIdx.x] = s_cnt[threadIdx.x];
+    if (threadIdx.x < kSuperTiles) {
+      // each sub-chunk's first slot within the chunk's run of every tile
+      uint32_t run = 0;
+#pragma unroll
+      for (uint32_t q = 0; q < kSubChunks; ++q) {
+        sub_offsets[(c * kSubChunks + q) * kSuperTiles + threadIdx.x] = run;
+        run += s_cnt[q * kSuperTiles + threadIdx.x];
+      }
+      chunk_counts[c * kSuperTiles + threadIdx.x] = run;
+    }
     __syncthreads();
   }
 }
@@ -646,24 +658,38 @@ constexpr int kEmitWarps = 4;
 __global__ void __launch_bounds__(32 * kEmitWarps)
     k_emit_instances(const uint4* __restrict__ chunks, const uint32_t* __restrict__ ent_prim,
                      const uint32_t* __restrict__ masks, const uint32_t* __restrict__ chunk_prefix,
-                     const uint2* __restrict__ ranges, const DevCounts* __restrict__ counts, uint32_t super_w,
-                     uint32_t grid_w, uint32_t grid_h, uint32_t* __restrict__ inst_prim) {
+                     const uint32_t* __restrict__ sub_offsets, const uint2* __restrict__ ranges,
+                     const DevCounts* __restrict__ counts, uint32_t super_w, uint32_t grid_w, uint32_t grid_h,
+                     uint32_t* __restrict__ inst_prim) {
   const unsigned full = 0xffffffffu;
-  const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
+  const uint32_t n_units = counts->overflow ? 0u : counts->n_chunks * kSubChunks;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   const uint32_t lt = lanemask_lt();
-  for (uint32_t c = blockIdx.x * kEmitWarps + warp; c < n_chunks; c += gridDim.x * kEmitWarps) {
+  for (uint32_t u = blockIdx.x * kEmitWarps + warp; u < n_units; u += gridDim.x * kEmitWarps) {
+    const uint32_t c = u / kSubChunks;
     const uint4 ch = chunks[c];
+    const uint32_t b = ch.y + (u % kSubChunks) * kSubChunk;
+    if (b >= ch.z) continue;  // warp-uniform: the chunk is shorter
+    const uint32_t end = min(ch.z, b + kSubChunk);
     const uint32_t tx = (ch.x % super_w) * kSuperW + lane % kSuperW;
     const uint32_t ty = (ch.x / super_w) * kSuperH + lane / kSuperW;
     uint32_t pos = 0;  // next slot of tile `lane`
-    if (tx < grid_w && ty < grid_h) pos = ranges[ty * grid_w + tx].x + chunk_prefix[c * kSuperTiles + lane];
-    for (uint32_t e0 = ch.y; e0 < ch.z; e0 += 32u) {
-      const uint32_t e = e0 + lane;
-      uint32_t mask = 0, prim = 0;
-      if (e < ch.z) {
-        mask = masks[e];
-        prim = ent_prim[e];
+    if (tx < grid_w && ty < grid_h)
+      pos = ranges[ty * grid_w + tx].x + chunk_prefix[c * kSuperTiles + lane] + sub_offsets[u * kSuperTiles + lane];
+    // masks and primitives of the next 32 entries are loaded one round ahead
+    uint32_t mask_n = 0, prim_n = 0;
+    if (b + lane < end) {
+      mask_n = masks[b + lane];
+      prim_n = ent_prim[b + lane];
+    }
+    for (uint32_t e0 = b; e0 < end; e0 += 32u) {
+      const uint32_t mask = mask_n, prim = prim_n;
+      const uint32_t en = e0 + 32u + lane;
+      mask_n = 0;
+      prim_n = 0;
+      if (en < end) {
+        mask_n = masks[en];
+        prim_n = ent_prim[en];
       }
       const uint32_t any = __reduce_or_sync(full, mask);
 #pragma unroll
@@ -740,20 +766,20 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   if (fp16)
     k_chunk_hits<1><<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.bounds, s.mean2d, s.conic_opacity,
                                                             s.prim_info, counts, super_w, s.masks, s.chunk_counts,
-                                                            s.n_touched);
+                                                            s.sub_offsets, s.n_touched);
   else
     k_chunk_hits<0><<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.bounds, s.mean2d, s.conic_opacity,
                                                             s.prim_info, counts, super_w, s.masks, s.chunk_counts,
-                                                            s.n_touched);
+                                                            s.sub_offsets, s.n_touched);
   k_chunk_prefix<<<(n_super * kSuperTiles + 255) / 256, 256, 0, stream>>>(
       s.super_ranges, s.super_chunk, n_super, super_w, cam.grid_w, cam.grid_h, counts, s.chunk_counts,
       s.tile_total);
   k_tile_offsets<<<1, 1024, 0, stream>>>(s.tile_total, n_tiles, s.ranges, s.bucket_offsets, counts,
                                           static_cast<uint32_t>(s.cap_inst), static_cast<uint32_t>(s.cap_buckets));
   // 6. instances at their final slots
-  k_emit_instances<<<s.num_sms * 8, 32 * kEmitWarps, 0, stream>>>(s.chunks, ent_prim, s.masks, s.chunk_counts,
-                                                                   s.ranges, counts, super_w, cam.grid_w, cam.grid_h,
-                                                                   s.inst_prim[0]);
+  k_emit_instances<<<s.num_sms * 16, 32 * kEmitWarps, 0, stream>>>(s.chunks, ent_prim, s.masks, s.chunk_counts,
+                                                                    s.sub_offsets, s.ranges, counts, super_w,
+                                                                    cam.grid_w, cam.grid_h, s.inst_prim[0]);
   s.tile_result = 0;
 }
 

@@ -25,6 +25,8 @@ constexpr uint32_t kSuperW = 8;
 constexpr uint32_t kSuperH = 4;
 constexpr int kSuperTiles = 32;
 constexpr uint32_t kChunk = 1024;
+constexpr uint32_t kSubChunk = 256;  // emission work unit (one warp)
+constexpr uint32_t kSubChunks = kChunk / kSubChunk;
 
 // Device-side camera passed by value as a kernel parameter.
 struct DevCamera {

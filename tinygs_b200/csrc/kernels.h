@@ -56,6 +56,7 @@ struct RasterState {
   uint32_t* super_chunk = nullptr;   // first chunk of each super-tile
   uint4* chunks = nullptr;           // (super-tile, first entry, end entry)
   uint32_t* chunk_counts = nullptr;  // [chunk][32] hits per tile, then first-slot offsets
+  uint32_t* sub_offsets = nullptr;   // [chunk][kSubChunks][32] slots of a sub-chunk's tile runs within its chunk
   // per instance, in final (tile, depth, index) order (the tile of an
   // instance follows from the tile ranges)
   uint32_t* inst_prim[2] = {nullptr, nullptr};  // only [0] is allocated

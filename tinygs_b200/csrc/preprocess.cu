@@ -667,7 +667,7 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
     const float lr = adam.lr[k], decay = adam.decay[k];
     const int kind = adam.kind[k];
     if (v16) {
-#pragma unroll 2
+#pragma unroll 4
       for (uint32_t e4 = lane; e4 < count / 4; e4 += 32) {
         float4 t = reinterpret_cast<const float4*>(ts)[e4];
         float4 m = reinterpret_cast<const float4*>(M)[e4];
@@ -757,17 +757,26 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
   }
   stage_slice(params, th, first, cnt, lane, v16);
   cp_async_commit();
+  // the per-Gaussian loads go out together with the staging copies (the
+  // screen-space gradients of an untouched Gaussian are loaded and unused)
+  const uint32_t i = first + lane;
+  const bool ok = counts->overflow == 0u;
+  uint32_t nt = 0;
+  float4 h0{}, h1{}, h2{}, d{};
+  if (lane < cnt) {
+    nt = n_touched[i];
+    h0 = helpers[3 * i];
+    h1 = helpers[3 * i + 1];
+    h2 = helpers[3 * i + 2];
+    if (dens != nullptr) d = dens[i];
+  }
   cp_async_wait<0>();
   __syncwarp();
-  const bool ok = counts->overflow == 0u;
-  const uint32_t i = first + lane;
-  const bool touched = ok && lane < cnt && n_touched[i] > 0;
+  const bool touched = ok && lane < cnt && nt > 0;
   float* my_sb = sb + kShStride * lane;
   if (touched) {
-    const float4 h0 = helpers[3 * i], h1 = helpers[3 * i + 1], h2 = helpers[3 * i + 2];
     gaussian_backward(th, g, my_sb, lane, h0, h1, h2, active_bases, cam);
     if (dens != nullptr) {
-      float4 d = dens[i];
       d.x += 1.0f;
       const float ux = h0.x * (0.5f * cam.w), uy = h0.y * (0.5f * cam.h);
       d.y += sqrtf(ux * ux + uy * uy);

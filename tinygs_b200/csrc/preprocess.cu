@@ -634,6 +634,144 @@ __device__ __forceinline__ void route_warp_bulk(const RouteArgs& r, float* th, c
   __syncwarp();
 }
 
+// Adam write-out of a full, 16-byte aligned warp slice with the moment
+// loads grouped, so that a warp waits on L2 about three times per slice
+// instead of once per segment and batch.  Segments 0..4 are 112 16-byte
+// chunks whose staged values (theta, gradients) sit back to back in shared
+// memory (chunk c at float 4c), taken in four rounds of 32 chunks; each round
+// spans at most two segments (kLo, kHi).  Segment 5 (sh_rest) is 360 chunks,
+// taken in batches of four per lane with the next batch's moments loaded
+// before the current batch is computed.
+__host__ __device__ constexpr uint32_t seg_chunk0(int k) { return static_cast<uint32_t>(seg_off(k)) / 4u; }
+
+struct ChunkRef {
+  float* p;
+  float* m;
+  float* v;
+  float* g;
+  float lr, decay;
+  int kind;
+};
+
+template <int kLo, int kHi>
+__device__ __forceinline__ ChunkRef chunk_ref(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
+                                              const SegPtrs& exp_avg_sq, const AdamArgs& adam, uint32_t first,
+                                              uint32_t c) {
+  const bool hi = kLo != kHi && c >= seg_chunk0(kHi);
+  const size_t lo_off = static_cast<size_t>(first) * seg_width(kLo) + 4u * (c - seg_chunk0(kLo));
+  const size_t hi_off = static_cast<size_t>(first) * seg_width(kHi) + 4u * (c - seg_chunk0(kHi));
+  ChunkRef r;
+  r.p = hi ? params.p[kHi] + hi_off : params.p[kLo] + lo_off;
+  r.m = hi ? exp_avg.p[kHi] + hi_off : exp_avg.p[kLo] + lo_off;
+  r.v = hi ? exp_avg_sq.p[kHi] + hi_off : exp_avg_sq.p[kLo] + lo_off;
+  float* glo = grads.p[kLo];
+  float* ghi = grads.p[kHi];
+  r.g = hi ? (ghi != nullptr ? ghi + hi_off : nullptr) : (glo != nullptr ? glo + lo_off : nullptr);
+  r.lr = hi ? adam.lr[kHi] : adam.lr[kLo];
+  r.decay = hi ? adam.decay[kHi] : adam.decay[kLo];
+  r.kind = hi ? adam.kind[kHi] : adam.kind[kLo];
+  return r;
+}
+
+__device__ __forceinline__ void adam_chunk(const ChunkRef& r, float4 t, float4 m, float4 v, float4 gv,
+                                           const AdamArgs& adam) {
+  adam_element(t.x, gv.x, m.x, v.x, r.lr, r.kind, r.decay, adam);
+  adam_element(t.y, gv.y, m.y, v.y, r.lr, r.kind, r.decay, adam);
+  adam_element(t.z, gv.z, m.z, v.z, r.lr, r.kind, r.decay, adam);
+  adam_element(t.w, gv.w, m.w, v.w, r.lr, r.kind, r.decay, adam);
+  *reinterpret_cast<float4*>(r.p) = t;
+  *reinterpret_cast<float4*>(r.m) = m;
+  *reinterpret_cast<float4*>(r.v) = v;
+  if (r.g != nullptr) *reinterpret_cast<float4*>(r.g) = gv;
+}
+
+template <int kLo, int kHi>
+__device__ __forceinline__ void geom_round(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
+                                           const SegPtrs& exp_avg_sq, const AdamArgs& adam, const float* th,
+                                           const float* g, uint32_t first, uint32_t c, float4 m, float4 v) {
+  if (c >= seg_chunk0(5)) return;
+  const ChunkRef r = chunk_ref<kLo, kHi>(params, grads, exp_avg, exp_avg_sq, adam, first, c);
+  adam_chunk(r, reinterpret_cast<const float4*>(th)[c], m, v, reinterpret_cast<const float4*>(g)[c], adam);
+}
+
+__device__ __forceinline__ float4 rest_grad4(const float* sb, uint32_t e4) {
+  return make_float4(slice_grad<5>(nullptr, sb, 4 * e4), slice_grad<5>(nullptr, sb, 4 * e4 + 1),
+                     slice_grad<5>(nullptr, sb, 4 * e4 + 2), slice_grad<5>(nullptr, sb, 4 * e4 + 3));
+}
+
+__device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
+                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, const float* th,
+                                               const float* g, const float* sb, uint32_t first, uint32_t lane) {
+  constexpr uint32_t kRestChunks = 45u * kWarpGaussians / 4u;  // 360
+  constexpr int kBatch = 4;
+  constexpr uint32_t kRestRounds = (kRestChunks + 31u) / 32u;  // 12 (the last one: lanes < 8)
+  const size_t rest_base = static_cast<size_t>(first) * 45u;
+  const float* RM = exp_avg.p[5] + rest_base;
+  const float* RV = exp_avg_sq.p[5] + rest_base;
+  // moments of segments 0..4 and of the first sh_rest batch
+  float4 gm[4], gvv[4], rm[kBatch], rv[kBatch];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t c = 32u * j + lane;
+    if (c < seg_chunk0(5)) {
+      const ChunkRef r = j == 0   ? chunk_ref<0, 1>(params, grads, exp_avg, exp_avg_sq, adam, first, c)
+                         : j == 1 ? chunk_ref<2, 2>(params, grads, exp_avg, exp_avg_sq, adam, first, c)
+                         : j == 2 ? chunk_ref<3, 4>(params, grads, exp_avg, exp_avg_sq, adam, first, c)
+                                  : chunk_ref<4, 4>(params, grads, exp_avg, exp_avg_sq, adam, first, c);
+      gm[j] = *reinterpret_cast<const float4*>(r.m);
+      gvv[j] = *reinterpret_cast<const float4*>(r.v);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < kBatch; ++q) {
+    const uint32_t e4 = 32u * q + lane;
+    rm[q] = reinterpret_cast<const float4*>(RM)[e4];
+    rv[q] = reinterpret_cast<const float4*>(RV)[e4];
+  }
+  geom_round<0, 1>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, lane, gm[0], gvv[0]);
+  geom_round<2, 2>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 32u + lane, gm[1], gvv[1]);
+  geom_round<3, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 64u + lane, gm[2], gvv[2]);
+  geom_round<4, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 96u + lane, gm[3], gvv[3]);
+  // sh_rest
+  ChunkRef rr;
+  rr.lr = adam.lr[5];
+  rr.decay = adam.decay[5];
+  rr.kind = adam.kind[5];
+  const float* ts = th + seg_off(5);
+#pragma unroll
+  for (uint32_t b0 = 0; b0 < kRestRounds; b0 += kBatch) {
+    float4 nm[kBatch], nv[kBatch];
+    if (b0 + kBatch < kRestRounds) {
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) {
+        const uint32_t e4 = 32u * (b0 + kBatch + q) + lane;
+        if (e4 < kRestChunks) {
+          nm[q] = reinterpret_cast<const float4*>(RM)[e4];
+          nv[q] = reinterpret_cast<const float4*>(RV)[e4];
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kBatch; ++q) {
+      const uint32_t e4 = 32u * (b0 + q) + lane;
+      if (e4 < kRestChunks) {
+        rr.p = params.p[5] + rest_base + 4u * e4;
+        rr.m = exp_avg.p[5] + rest_base + 4u * e4;
+        rr.v = exp_avg_sq.p[5] + rest_base + 4u * e4;
+        rr.g = grads.p[5] != nullptr ? grads.p[5] + rest_base + 4u * e4 : nullptr;
+        adam_chunk(rr, reinterpret_cast<const float4*>(ts)[e4], rm[q], rv[q], rest_grad4(sb, e4), adam);
+      }
+    }
+    if (b0 + kBatch < kRestRounds) {
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) {
+        rm[q] = nm[q];
+        rv[q] = nv[q];
+      }
+    }
+  }
+}
+
 template <bool kAdam, int k, bool kRoute = false>
 __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, int accumulate,
@@ -723,7 +861,7 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
 // The moments of the warp's Gaussians are prefetched into L2 (bulk
 // prefetch) at the start, so their reads in the write-out hit L2.
 template <bool kAdam, bool kRoute = false>
-__global__ void __launch_bounds__(32 * kBwdWarps)
+__global__ void __launch_bounds__(32 * kBwdWarps, 4)
     k_preprocess_backward(SegPtrs params, SegPtrs grads, SegPtrs exp_avg, SegPtrs exp_avg_sq, AdamArgs adam,
                           int accumulate, int vec, int active_bases, uint32_t n, DevCamera cam,
                           const uint32_t* __restrict__ n_touched, const float4* __restrict__ helpers,
@@ -796,6 +934,8 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
   __syncwarp();
   if (kRoute && v16) {
     route_warp_bulk(route, th, g, sb, first, lane);
+  } else if (kAdam && v16) {
+    adam_slice_v16(params, grads, exp_avg, exp_avg_sq, adam, th, g, sb, first, lane);
   } else {
     write_segment<kAdam, 0, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
                                       lane, v16, route);

@@ -381,14 +381,27 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
                      const void* __restrict__ image_v, const void* __restrict__ grad_v,
                      const void* __restrict__ n_contrib_v, const void* __restrict__ ckpt_v,
                      const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ helpers) {
-  __shared__ float4 s_a[kBwdWarps][32];  // (T, adg, px, py)
-  __shared__ float4 s_b[kBwdWarps][32];  // (G.r, G.g, G.b, last as bits)
+  // Per warp, the pixels of the current and the previous 32-pixel chunk in
+  // a ring of 64 records: the constant part of a pixel (centre, dL/dpixel,
+  // contributor count) is read by each lane from the ring at index
+  // (step - lane); only the evolving state (T, adg) travels from lane to
+  // lane, and lane 0 takes a new pixel's (T, adg) from s_ta.
+  __shared__ float4 s_rec[kBwdWarps][64];  // (px, py, G.r, G.g)
+  __shared__ float s_g2[kBwdWarps][64];    // G.b
+  __shared__ uint32_t s_last[kBwdWarps][kFp16 ? 1 : 64];
+  __shared__ float2 s_ta[kBwdWarps][32];   // (T, adg) entering the bucket
   if (counts->overflow != 0u) return;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   const uint32_t n_live = counts->n_live_buckets;
   const uint32_t stride = gridDim.x * kBwdWarps;
   const float max_alpha = kFp16 ? __half2float(__float2half_rn(kMaxAlphaF16)) : kMaxAlphaF32;
   constexpr uint32_t kChunks = kTilePixels / 32;
+  // lanes see the "previous chunk" half of the ring before the first chunk:
+  // finite values there (their T = adg = 0 makes every term zero)
+  s_rec[warp][lane] = s_rec[warp][32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+  s_g2[warp][lane] = s_g2[warp][32 + lane] = 0.f;
+  if constexpr (!kFp16) s_last[warp][lane] = s_last[warp][32 + lane] = 0u;
+  __syncwarp();
 
   for (uint32_t item = blockIdx.x * kBwdWarps + warp; item < n_live; item += stride) {
     const uint2 lb = live_buckets[item];
@@ -399,7 +412,6 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
     const uint32_t tp = tb * kBucket + lane;
     const bool valid_prim = tp < count && (!kFp16 || tp <= 0xffffu);
     const uint32_t gx = tile % cam.grid_w, gy = tile / cam.grid_w;
-
 
     uint32_t p = 0;
     float mx = 0.f, my = 0.f, op = 0.f, ka = 0.f, kb = 0.f, kc = 0.f;
@@ -430,9 +442,8 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
     float g_op = 0.f, g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_c0 = 0.f, g_c1 = 0.f, g_c2 = 0.f;
     float s_x = 0.f, s_y = 0.f;  // sums of dop * (mean - pixel)
     float g_mx = 0.f, g_my = 0.f, a_mx = 0.f, a_my = 0.f;
-    // pixel state travelling along the lanes (zero: no contribution)
-    float T = 0.f, adg = 0.f, G0 = 0.f, G1 = 0.f, G2 = 0.f, px = 0.f, py = 0.f;
-    uint32_t last = 0;
+    // evolving pixel state travelling along the lanes (zero: no pixel)
+    float T = 0.f, adg = 0.f;
 
     for (uint32_t chunk = 0; chunk <= kChunks; ++chunk) {
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -441,35 +452,31 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
         const PixelRaw<kFp16> raw = fetch_pixel<kFp16>(i, bucket, gx, gy, cam, image_v, grad_v, n_contrib_v, ckpt_v);
         pixel_state<kFp16>(raw, i, gx, gy, a4, b4);
       }
-      s_a[warp][lane] = a4;
-      s_b[warp][lane] = b4;
+      const uint32_t slot = (chunk & 1u) * 32u + lane;
+      s_rec[warp][slot] = make_float4(a4.z, a4.w, b4.x, b4.y);
+      s_g2[warp][slot] = b4.z;
+      if constexpr (!kFp16) s_last[warp][slot] = __float_as_uint(b4.w);
+      s_ta[warp][lane] = make_float2(a4.x, a4.y);
       __syncwarp();
+      const uint32_t base = (chunk & 1u) * 32u + 64u;  // slot of step 0, lane 0, plus 64
 #pragma unroll 8
       for (uint32_t st = 0; st < 32; ++st) {
         T = __shfl_up_sync(0xffffffffu, T, 1);
         adg = __shfl_up_sync(0xffffffffu, adg, 1);
-        G0 = __shfl_up_sync(0xffffffffu, G0, 1);
-        G1 = __shfl_up_sync(0xffffffffu, G1, 1);
-        G2 = __shfl_up_sync(0xffffffffu, G2, 1);
-        px = __shfl_up_sync(0xffffffffu, px, 1);
-        py = __shfl_up_sync(0xffffffffu, py, 1);
-        if constexpr (!kFp16) last = __shfl_up_sync(0xffffffffu, last, 1);
         if (lane == 0) {
-          const float4 na = s_a[warp][st], nb = s_b[warp][st];
-          T = na.x;
-          adg = na.y;
-          px = na.z;
-          py = na.w;
-          G0 = nb.x;
-          G1 = nb.y;
-          G2 = nb.z;
-          if constexpr (!kFp16) last = __float_as_uint(nb.w);
+          const float2 ta = s_ta[warp][st];
+          T = ta.x;
+          adg = ta.y;
         }
+        const uint32_t ring = (base + st - lane) & 63u;
+        const float4 rec = s_rec[warp][ring];
+        const float px = rec.x, py = rec.y, G0 = rec.z, G1 = rec.w;
+        const float G2 = s_g2[warp][ring];
         const float ddx = mx - px, ddy = my - py;
         const float dxx = ddx * ddx, dxy = ddx * ddy, dyy = ddy * ddy;
         const float q2 = fmaxf(ka * dxx + kc * dyy + kb * dxy, 0.f);
         float a = fminf(op * exp2f(-q2), max_alpha);
-        if constexpr (!kFp16) a = tp < last ? a : 0.f;
+        if constexpr (!kFp16) a = tp < s_last[warp][ring] ? a : 0.f;
         const float w = T * a;
         const float om = 1.0f - a;
         const float cdg = col0 * G0 + col1 * G1 + col2 * G2;

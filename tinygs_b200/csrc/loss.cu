@@ -82,6 +82,11 @@ constexpr int kOut = 32;
 constexpr int kInH = kOut + 2 * kHalo;  // 42
 constexpr int kInW = kOut + 16;         // 48
 constexpr int kSegs = kInW / 8;         // 6
+// shared-memory row strides padded by one word: the horizontal pass has
+// lanes on four rows (and eight column groups) at once, which an unpadded
+// 32- or 48-word stride maps onto the same eight banks
+constexpr int kInStride = kInW + 1;
+constexpr int kSumStride = kOut + 1;
 
 __device__ __forceinline__ bool segment_of(const DevCamera& cam, int x0, int y0, int r, int sg, uint32_t& idx,
                                            int& gx0) {
@@ -113,8 +118,8 @@ __global__ void __launch_bounds__(256)
     k_ssim_forward(DevCamera cam, const void* __restrict__ pred, const void* __restrict__ target,
                    void* __restrict__ loss_map, void* __restrict__ grad, float s_ssim, float s_l1,
                    float* __restrict__ partials, float* __restrict__ loss_sum) {
-  __shared__ __half2 tile[kInH][kInW];     // (pred, target)
-  __shared__ float hsum[5][kInH][kOut];
+  __shared__ __half2 tile[kInH][kInStride];  // (pred, target)
+  __shared__ float hsum[5][kInH][kSumStride];
   const int x0 = blockIdx.x * kOut, y0 = blockIdx.y * kOut;
   const uint32_t ch = blockIdx.z * cam.plane;
   const int W = static_cast<int>(cam.width), H = static_cast<int>(cam.height);
@@ -229,8 +234,8 @@ template <int kFp16>
 __global__ void __launch_bounds__(256)
     k_ssim_backward(DevCamera cam, const void* __restrict__ pred, const void* __restrict__ target,
                     void* __restrict__ grad, float s_ssim, const float* __restrict__ partials) {
-  __shared__ float tile[3][kInH][kInW + 1];
-  __shared__ float hsum[3][kInH][kOut];
+  __shared__ float tile[3][kInH][kInStride];
+  __shared__ float hsum[3][kInH][kSumStride];
   const int x0 = blockIdx.x * kOut, y0 = blockIdx.y * kOut;
   const uint32_t ch = blockIdx.z * cam.plane;
   const uint32_t plane3 = 3 * cam.plane;

@@ -44,6 +44,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "train iters/s (fwd+bwd+SSIM+Adam) @3M Gaussians 1080p; render Mpix/s"
 GRAD_SCALER = 10.0
 ADAM_BYTES_PER_GAUSSIAN = 7 * 59 * 4  # read theta, g, m, v; write theta, m, v
+# measured DRAM bytes per Gaussian of the fused backward + Adam (ncu, 1M)
+TRAFFIC_BWD_ADAM_PER_GAUSSIAN = 1476.7
 
 
 def parse():
@@ -586,6 +588,10 @@ def run_ours(args):
         kernel = "k_preprocess_backward<true> (per-Gaussian backward fused with Adam)"
         kernel_bytes = cfg.n * (6 * 236 + 4) + touched_v * 48
         kernel_ms = stages["gaussian_backward_adam"]
+        # DRAM read + write per Gaussian of this kernel from one ncu capture
+        # at 1M Gaussians (profiles/k_preprocess_backward_adam_cfg2_1M.md:
+        # 823.5 + 653.2 MB); traffic grows with the Gaussians processed
+        kernel_traffic = TRAFFIC_BWD_ADAM_PER_GAUSSIAN * cfg.n
     elif dp_impl == "inbox":
         # k_preprocess_backward<false, true>: as below, but (N-1)/N of the
         # gradient stores cross NVLink into the owners' inboxes
@@ -602,6 +608,8 @@ def run_ours(args):
         kernel = "k_adam (fused Adam over the 59-float arena)"
         kernel_bytes = ADAM_BYTES_PER_GAUSSIAN * cfg.n
         kernel_ms = stages["adam"]
+    if not fused:
+        kernel_traffic = None  # no capture of the multi-GPU kernels
     kernel_gbs = kernel_bytes / (kernel_ms * 1e-3) / 1e9
     peaks = {}
     try:
@@ -640,7 +648,7 @@ def run_ours(args):
             "render_mpix_s": W * H / (render_ms * 1e-3) / 1e6,
             "stages_ms": {k: round(v, 4) for k, v in stages.items()},
             "roofline": {"bound": "hbm", "kernel": kernel, "achieved": kernel_gbs, "peak": hbm_peak,
-                         "unit": "GB/s", "frac": kernel_gbs / hbm_peak, "peak_source": peak_src, "traffic": None,
+                         "unit": "GB/s", "frac": kernel_gbs / hbm_peak, "peak_source": peak_src, "traffic": kernel_traffic,
                          "algorithmic_bytes_per_launch": kernel_bytes, "avg_launch_ms": kernel_ms},
             "counts": {"visible": counts.n_visible, "instances": counts.n_instances, "buckets": counts.n_buckets},
             "gpu_launches": kernels_per_step(tile_count, world) * args.steps,

@@ -450,3 +450,4 @@ def test_stage_times_are_reported(cuda_lib):
     t = run.rast.stage_times()
     assert len(t) == 5 and all(x > 0 for x in t), t
     run.rast.set_stage_timing(False)
+

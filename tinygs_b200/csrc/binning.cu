@@ -449,6 +449,9 @@ __global__ void __launch_bounds__(kScanBlock)
                  uint32_t* __restrict__ n_touched) {
   static_assert(kSubChunk == kScanBlock, "one block pass per emission sub-chunk");
   __shared__ uint32_t s_cnt[kSubChunks * kSuperTiles];
+  // each entry's test inputs and rectangle, read by the lanes that test its
+  // tiles (48 bytes used of 64-byte records)
+  __shared__ float4 s_rec[kScanBlock / 32][32][4];
   const unsigned full = 0xffffffffu;
   const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
   const uint32_t lane = threadIdx.x & 31u;
@@ -484,6 +487,17 @@ __global__ void __launch_bounds__(kScanBlock)
       }
       const uint32_t start = incl - total;
       const uint32_t pairs = __shfl_sync(full, incl, 31);
+      {
+        float4* rec = s_rec[threadIdx.x >> 5][lane];
+        rec[0] = make_float4(tt.ca, tt.cb, tt.cc, tt.thr);
+        rec[1] = make_float4(kFp16 ? tt.xs : tt.mx, kFp16 ? tt.ys : tt.my,
+                             __uint_as_float(*reinterpret_cast<const uint32_t*>(&tt.c_xy)),
+                             __uint_as_float(*reinterpret_cast<const uint32_t*>(&tt.c_yz)));
+        rec[2] = make_float4(__uint_as_float(*reinterpret_cast<const uint32_t*>(&tt.den)),
+                             __uint_as_float(start), __uint_as_float(x0 | (y0 << 16)),
+                             __uint_as_float(w | (magic << 8)));
+      }
+      __syncwarp();
       uint32_t local = 0;  // hits in rectangle order (bit t = row t / w, column t % w)
       // owners are lanes 0 .. (valid entries - 1), every one with total >= 1,
       // so the owner of a slot is the number of rectangle starts up to it - 1
@@ -492,26 +506,28 @@ __global__ void __launch_bounds__(kScanBlock)
         const uint32_t slot = base + lane;
         const uint32_t sbit = total > 0u && start >= base && start < base + 32u ? 1u << (start - base) : 0u;
         const uint32_t starts = __reduce_or_sync(full, sbit);
-        const uint32_t owner = starts_before + __popc(starts & (lt | (1u << lane))) - 1u;
+        const uint32_t owner = (starts_before + __popc(starts & (lt | (1u << lane))) - 1u) & 31u;
         starts_before += __popc(starts);
+        const float4* orec = s_rec[threadIdx.x >> 5][owner];
+        const float4 r0 = orec[0], r1 = orec[1], r2 = orec[2];
         TileTest q;
-        q.ca = __shfl_sync(full, tt.ca, owner);
-        q.cb = __shfl_sync(full, tt.cb, owner);
-        q.cc = __shfl_sync(full, tt.cc, owner);
+        q.ca = r0.x;
+        q.cb = r0.y;
+        q.cc = r0.z;
+        q.thr = r0.w;
         if constexpr (kFp16) {
-          q.xs = __shfl_sync(full, tt.xs, owner);
-          q.ys = __shfl_sync(full, tt.ys, owner);
-          q.c_xy = __shfl_sync(full, tt.c_xy, owner);
-          q.c_yz = __shfl_sync(full, tt.c_yz, owner);
-          q.c_xz = __shfl_sync(full, tt.c_xz, owner);
+          q.xs = r1.x;
+          q.ys = r1.y;
+          const uint32_t cxy = __float_as_uint(r1.z), cyz = __float_as_uint(r1.w), den = __float_as_uint(r2.x);
+          q.c_xy = *reinterpret_cast<const __half2*>(&cxy);
+          q.c_yz = *reinterpret_cast<const __half2*>(&cyz);
+          q.den = *reinterpret_cast<const __half2*>(&den);
         } else {
-          q.mx = __shfl_sync(full, tt.mx, owner);
-          q.my = __shfl_sync(full, tt.my, owner);
+          q.mx = r1.x;
+          q.my = r1.y;
         }
-        q.thr = __shfl_sync(full, tt.thr, owner);
-        const uint32_t o_start = __shfl_sync(full, start, owner);
-        const uint32_t o_x = __shfl_sync(full, x0, owner), o_y = __shfl_sync(full, y0, owner);
-        const uint32_t o_w = __shfl_sync(full, w, owner), o_magic = __shfl_sync(full, magic, owner);
+        const uint32_t o_start = __float_as_uint(r2.y), o_xy = __float_as_uint(r2.z), o_wm = __float_as_uint(r2.w);
+        const uint32_t o_x = o_xy & 0xffffu, o_y = o_xy >> 16, o_w = o_wm & 0xffu, o_magic = o_wm >> 8;
         const uint32_t t = slot - o_start;
         const uint32_t row = (t * o_magic) >> 8;
         const bool hit = slot < pairs && overlaps<kFp16>(q, o_x + (t - row * o_w), o_y + row);
@@ -524,6 +540,7 @@ __global__ void __launch_bounds__(kScanBlock)
           local |= bits << (lo - start);
         }
       }
+      __syncwarp();  // the records are rewritten by the next pass
       // rectangle order -> super-tile bits (row * 8 + column)
       uint32_t mask = 0;
       const uint32_t row_bits = w == 32u ? full : ((1u << w) - 1u);

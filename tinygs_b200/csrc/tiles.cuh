@@ -38,20 +38,29 @@ __device__ __forceinline__ bool tile_overlaps_f32(float mx, float my, float ca, 
   return power <= thr;
 }
 
+// Per-primitive tile-test inputs in one register bundle.
+struct TileTest {
+  float mx, my;        // mean2d - 0.5 (fp32 test)
+  float ca, cb, cc;    // conic (fp16 test: the half conic widened)
+  float xs, ys;        // (mean2d - 0.5) / 16 (fp16 test)
+  __half2 c_xy, c_yz;  // fp16 test: conic component pairs of the edge numerator
+  __half2 den;         // fp16 test: the edge denominator span^2 * (a, c)
+  float thr;           // ln(255 * opacity)
+};
+
 // Half-precision variant of the same test used by the fp16 rasterizer
 // (fastgs_ours_fp16/kernels_forward.cuh:123-169): the tile-relative
 // distances and the edge parameter are evaluated in fp16 on the packed
-// conic, the final exponent in fp32.  Same operation sequence as the
-// reference so that instance lists coincide.  The per-primitive terms
-// (mean / 16, conic component pairs, conic in fp32) come precomputed.
-__device__ __forceinline__ bool tile_overlaps_f16(float xs, float ys, __half2 c_xy, __half2 c_yz, __half2 c_xz,
-                                                  float fa, float fb, float fc, uint32_t tx, uint32_t ty,
-                                                  float thr) {
+// conic, the final exponent in fp32.  Same operation sequence and roundings
+// as the reference so that instance lists coincide; the denominator
+// step * step * (a, c) equals span^2 * (a, c) bit for bit (step = +-span, and
+// rounding to nearest is symmetric in sign), so it is a per-primitive term.
+__device__ __forceinline__ bool tile_overlaps_f16(const TileTest& p, uint32_t tx, uint32_t ty) {
   const __half2 zero = __float2half2_rn(0.0f);
   const __half span_h = __float2half_rd(static_cast<float>(kTile - 1) / static_cast<float>(kTile));
   const __half2 span = __halves2half2(span_h, span_h);
-  const __half2 lo = __halves2half2(__float2half_rd(static_cast<float>(tx) - xs),
-                                    __float2half_rd(static_cast<float>(ty) - ys));
+  const __half2 lo = __halves2half2(__float2half_rd(static_cast<float>(tx) - p.xs),
+                                    __float2half_rd(static_cast<float>(ty) - p.ys));
   const __half2 hi = __hadd2(lo, span);
   const __half2 before = __hgtu2(lo, zero);  // 1.0 where the mean lies before the tile
   const __half2 after = __hltu2(hi, zero);   // 1.0 where it lies after it
@@ -67,23 +76,13 @@ __device__ __forceinline__ bool tile_overlaps_f16(float xs, float ys, __half2 c_
   const __half2 dist = __hneg2(__hfma2(before, lo, __hfma2(nb, hi, hi)));
   const __half2 dist_xx = __lows2half2(dist, dist);
   const __half2 dist_yy = __highs2half2(dist, dist);
-  const __half2 num = __hadd2(__hmul2(__hmul2(step, c_xy), dist_xx), __hmul2(__hmul2(step, c_yz), dist_yy));
-  const __half2 den = __hmul2(__hmul2(step, step), c_xz);
-  const __half2 t = __hmul2_sat(__h2div(num, den), __lowhigh2highlow(outside));
+  const __half2 num = __hadd2(__hmul2(__hmul2(step, p.c_xy), dist_xx), __hmul2(__hmul2(step, p.c_yz), dist_yy));
+  const __half2 t = __hmul2_sat(__h2div(num, p.den), __lowhigh2highlow(outside));
   const float2 q = __half22float2(__hsub2(dist, __hmul2(t, step)));
   const float qx = q.x * static_cast<float>(kTile), qy = q.y * static_cast<float>(kTile);
-  const float power = 0.5f * (fa * qx * qx + fc * qy * qy) + fb * qx * qy;
-  return power <= thr;
+  const float power = 0.5f * (p.ca * qx * qx + p.cc * qy * qy) + p.cb * qx * qy;
+  return power <= p.thr;
 }
-
-// Per-primitive tile-test inputs in one register bundle.
-struct TileTest {
-  float mx, my;        // mean2d - 0.5 (fp32 test)
-  float ca, cb, cc;    // conic (fp16 test: the half conic widened)
-  float xs, ys;        // (mean2d - 0.5) / 16 (fp16 test)
-  __half2 c_xy, c_yz, c_xz;  // fp16 test: conic component pairs
-  float thr;           // ln(255 * opacity)
-};
 
 // Bundle of the fp16 test from the packed conic (x, y | z, opacity).
 __device__ __forceinline__ void tile_test_f16(TileTest& q, float mx, float my, __half2 conic_xy,
@@ -94,7 +93,10 @@ __device__ __forceinline__ void tile_test_f16(TileTest& q, float mx, float my, _
   q.ys = my * (1.0f / kTile);
   q.c_xy = conic_xy;
   q.c_yz = __halves2half2(__high2half(conic_xy), __low2half(conic_z_opacity));
-  q.c_xz = __halves2half2(__low2half(conic_xy), __low2half(conic_z_opacity));
+  const __half2 c_xz = __halves2half2(__low2half(conic_xy), __low2half(conic_z_opacity));
+  const __half span_h = __float2half_rd(static_cast<float>(kTile - 1) / static_cast<float>(kTile));
+  const __half2 span = __halves2half2(span_h, span_h);
+  q.den = __hmul2(__hmul2(span, span), c_xz);
   q.ca = __low2float(conic_xy);
   q.cb = __high2float(conic_xy);
   q.cc = __low2float(conic_z_opacity);
@@ -104,7 +106,7 @@ __device__ __forceinline__ void tile_test_f16(TileTest& q, float mx, float my, _
 template <int kFp16>
 __device__ __forceinline__ bool overlaps(const TileTest& p, uint32_t tx, uint32_t ty) {
   if constexpr (kFp16)
-    return tile_overlaps_f16(p.xs, p.ys, p.c_xy, p.c_yz, p.c_xz, p.ca, p.cb, p.cc, tx, ty, p.thr);
+    return tile_overlaps_f16(p, tx, ty);
   else
     return tile_overlaps_f32(p.mx, p.my, p.ca, p.cb, p.cc, tx, ty, p.thr);
 }

@@ -708,15 +708,18 @@ __global__ void __launch_bounds__(32 * kEmitWarps)
         mask_n = masks[en];
         prim_n = ent_prim[en];
       }
-      const uint32_t any = __reduce_or_sync(full, mask);
+      // all 32 tiles unconditionally: the ballots and shuffles of different
+      // tiles are independent, so the unrolled steps overlap (lane j's slot
+      // is read at step j before lane j moves it on)
+      uint32_t grow = 0;
 #pragma unroll
       for (int j = 0; j < kSuperTiles; ++j) {
-        if (((any >> j) & 1u) == 0u) continue;  // warp-uniform
         const uint32_t bj = __ballot_sync(full, (mask >> j) & 1u);
         const uint32_t p = __shfl_sync(full, pos, j);
         if ((bj >> lane) & 1u) inst_prim[p + __popc(bj & lt)] = prim;
-        if (lane == static_cast<uint32_t>(j)) pos += __popc(bj);
+        if (lane == static_cast<uint32_t>(j)) grow = __popc(bj);
       }
+      pos += grow;
     }
   }
 }

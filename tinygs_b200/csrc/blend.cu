@@ -359,6 +359,41 @@ __device__ __forceinline__ void pixel_state(const PixelRaw<kFp16>& r, uint32_t i
   b4 = make_float4(r.grad[0], r.grad[1], r.grad[2], __uint_as_float(kFp16 ? 0xffffffffu : r.last));
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions): two pixels per lane, each
+// element rounded exactly like the scalar operation (ftz, as the rest of the
+// fast-math build).
+__device__ __forceinline__ uint64_t pk(float2 v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 upk(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)));
+  return upk(d);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  uint64_t d;
+  asm("sub.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)));
+  return upk(d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)));
+  return upk(d);
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.ftz.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk(a)), "l"(pk(b)), "l"(pk(c)));
+  return upk(d);
+}
+__device__ __forceinline__ float2 dup2(float v) { return make_float2(v, v); }
+
 template <int kFp16>
 __device__ __forceinline__ void load_conic(uint32_t p, const float4* __restrict__ conic_opacity,
                                            const PrimInfo16* __restrict__ prim_info, float4& co) {
@@ -381,26 +416,31 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
                      const void* __restrict__ image_v, const void* __restrict__ grad_v,
                      const void* __restrict__ n_contrib_v, const void* __restrict__ ckpt_v,
                      const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ helpers) {
-  // Per warp, the pixels of the current and the previous 32-pixel chunk in
-  // a ring of 64 records: the constant part of a pixel (centre, dL/dpixel,
-  // contributor count) is read by each lane from the ring at index
-  // (step - lane); only the evolving state (T, adg) travels from lane to
-  // lane, and lane 0 takes a new pixel's (T, adg) from s_ta.
-  __shared__ float4 s_rec[kBwdWarps][64];  // (px, py, G.r, G.g)
-  __shared__ float s_g2[kBwdWarps][64];    // G.b
-  __shared__ uint32_t s_last[kBwdWarps][kFp16 ? 1 : 64];
-  __shared__ float2 s_ta[kBwdWarps][32];   // (T, adg) entering the bucket
+  // Two pixel streams per lane (pixels 0..127 and 128..255 of the tile),
+  // evaluated together with packed fp32 pairs.  Per warp, the pixel pairs of
+  // the current and the previous 32-step chunk sit in a ring of 64 records:
+  // the constant part of a pixel (centre, dL/dpixel, contributor count) is
+  // read by each lane from the ring at index (step - lane); only the
+  // evolving state (T, -adg) travels from lane to lane, and lane 0 takes a
+  // new pair's state from s_ta.
+  __shared__ float4 s_pxy[kBwdWarps][64];  // (px A, px B, py A, py B)
+  __shared__ float4 s_g01[kBwdWarps][64];  // (G.r A, G.r B, G.g A, G.g B)
+  __shared__ float2 s_g2[kBwdWarps][64];   // (G.b A, G.b B)
+  __shared__ uint2 s_last[kBwdWarps][kFp16 ? 1 : 64];
+  __shared__ float4 s_ta[kBwdWarps][32];   // (T A, T B, -adg A, -adg B) entering the bucket
   if (counts->overflow != 0u) return;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   const uint32_t n_live = counts->n_live_buckets;
   const uint32_t stride = gridDim.x * kBwdWarps;
   const float max_alpha = kFp16 ? __half2float(__float2half_rn(kMaxAlphaF16)) : kMaxAlphaF32;
-  constexpr uint32_t kChunks = kTilePixels / 32;
+  constexpr uint32_t kHalf = kTilePixels / 2;  // pixels per stream
+  constexpr uint32_t kChunks = kHalf / 32;
   // lanes see the "previous chunk" half of the ring before the first chunk:
   // finite values there (their T = adg = 0 makes every term zero)
-  s_rec[warp][lane] = s_rec[warp][32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
-  s_g2[warp][lane] = s_g2[warp][32 + lane] = 0.f;
-  if constexpr (!kFp16) s_last[warp][lane] = s_last[warp][32 + lane] = 0u;
+  s_pxy[warp][lane] = s_pxy[warp][32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+  s_g01[warp][lane] = s_g01[warp][32 + lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+  s_g2[warp][lane] = s_g2[warp][32 + lane] = make_float2(0.f, 0.f);
+  if constexpr (!kFp16) s_last[warp][lane] = s_last[warp][32 + lane] = make_uint2(0u, 0u);
   __syncwarp();
 
   for (uint32_t item = blockIdx.x * kBwdWarps + warp; item < n_live; item += stride) {
@@ -439,103 +479,129 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
         col2 = fmaxf(color[3 * p + 2], 0.f);
       }
     }
-    float g_op = 0.f, g_ca = 0.f, g_cb = 0.f, g_cc = 0.f, g_c0 = 0.f, g_c1 = 0.f, g_c2 = 0.f;
-    float s_x = 0.f, s_y = 0.f;  // sums of dop * (mean - pixel)
-    float g_mx = 0.f, g_my = 0.f, a_mx = 0.f, a_my = 0.f;
-    // evolving pixel state travelling along the lanes (zero: no pixel)
-    float T = 0.f, adg = 0.f;
+    const float2 MX = dup2(mx), MY = dup2(my), OP = dup2(op), KA = dup2(ka), KB = dup2(kb), KC = dup2(kc);
+    const float2 C0 = dup2(col0), C1 = dup2(col1), C2 = dup2(col2);
+    // per-primitive sums, one partial per stream (added at the end)
+    float2 g_op = dup2(0.f), g_ca = dup2(0.f), g_cb = dup2(0.f), g_cc = dup2(0.f);
+    float2 g_c0 = dup2(0.f), g_c1 = dup2(0.f), g_c2 = dup2(0.f);
+    float2 s_x = dup2(0.f), s_y = dup2(0.f);  // sums of dop * (mean - pixel)
+    float2 g_mx = dup2(0.f), g_my = dup2(0.f), a_mx = dup2(0.f), a_my = dup2(0.f);
+    // evolving state of the lane's two pixels (zero: no pixel)
+    float2 T = dup2(0.f), nadg = dup2(0.f);
 
     for (uint32_t chunk = 0; chunk <= kChunks; ++chunk) {
-      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = a4, c4 = a4, d4 = a4;
       if (chunk < kChunks) {
-        const uint32_t i = chunk * 32 + lane;
-        const PixelRaw<kFp16> raw = fetch_pixel<kFp16>(i, bucket, gx, gy, cam, image_v, grad_v, n_contrib_v, ckpt_v);
-        pixel_state<kFp16>(raw, i, gx, gy, a4, b4);
+        const uint32_t ia = chunk * 32 + lane, ib = kHalf + ia;
+        const PixelRaw<kFp16> ra = fetch_pixel<kFp16>(ia, bucket, gx, gy, cam, image_v, grad_v, n_contrib_v, ckpt_v);
+        const PixelRaw<kFp16> rb = fetch_pixel<kFp16>(ib, bucket, gx, gy, cam, image_v, grad_v, n_contrib_v, ckpt_v);
+        pixel_state<kFp16>(ra, ia, gx, gy, a4, b4);
+        pixel_state<kFp16>(rb, ib, gx, gy, c4, d4);
       }
       const uint32_t slot = (chunk & 1u) * 32u + lane;
-      s_rec[warp][slot] = make_float4(a4.z, a4.w, b4.x, b4.y);
-      s_g2[warp][slot] = b4.z;
-      if constexpr (!kFp16) s_last[warp][slot] = __float_as_uint(b4.w);
-      s_ta[warp][lane] = make_float2(a4.x, a4.y);
+      s_pxy[warp][slot] = make_float4(a4.z, c4.z, a4.w, c4.w);
+      s_g01[warp][slot] = make_float4(b4.x, d4.x, b4.y, d4.y);
+      s_g2[warp][slot] = make_float2(b4.z, d4.z);
+      if constexpr (!kFp16) s_last[warp][slot] = make_uint2(__float_as_uint(b4.w), __float_as_uint(d4.w));
+      s_ta[warp][lane] = make_float4(a4.x, c4.x, -a4.y, -c4.y);
       __syncwarp();
       const uint32_t base = (chunk & 1u) * 32u + 64u;  // slot of step 0, lane 0, plus 64
-#pragma unroll 8
+#pragma unroll 4
       for (uint32_t st = 0; st < 32; ++st) {
-        T = __shfl_up_sync(0xffffffffu, T, 1);
-        adg = __shfl_up_sync(0xffffffffu, adg, 1);
+        T.x = __shfl_up_sync(0xffffffffu, T.x, 1);
+        T.y = __shfl_up_sync(0xffffffffu, T.y, 1);
+        nadg.x = __shfl_up_sync(0xffffffffu, nadg.x, 1);
+        nadg.y = __shfl_up_sync(0xffffffffu, nadg.y, 1);
         if (lane == 0) {
-          const float2 ta = s_ta[warp][st];
-          T = ta.x;
-          adg = ta.y;
+          const float4 ta = s_ta[warp][st];
+          T = make_float2(ta.x, ta.y);
+          nadg = make_float2(ta.z, ta.w);
         }
         const uint32_t ring = (base + st - lane) & 63u;
-        const float4 rec = s_rec[warp][ring];
-        const float px = rec.x, py = rec.y, G0 = rec.z, G1 = rec.w;
-        const float G2 = s_g2[warp][ring];
-        const float ddx = mx - px, ddy = my - py;
-        const float dxx = ddx * ddx, dxy = ddx * ddy, dyy = ddy * ddy;
-        const float q2 = fmaxf(ka * dxx + kc * dyy + kb * dxy, 0.f);
-        float a = fminf(op * exp2f(-q2), max_alpha);
-        if constexpr (!kFp16) a = tp < s_last[warp][ring] ? a : 0.f;
-        const float w = T * a;
-        const float om = 1.0f - a;
-        const float cdg = col0 * G0 + col1 * G1 + col2 * G2;
-        g_c0 += w * G0;
-        g_c1 += w * G1;
-        g_c2 += w * G2;
-        adg -= w * cdg;  // what lies behind this primitive
-        const float dop = a * (T * cdg - adg / om);
-        g_op += dop;
-        g_ca += dop * dxx;
-        g_cb += dop * dxy;
-        g_cc += dop * dyy;
+        const float4 pxy = s_pxy[warp][ring], g01 = s_g01[warp][ring];
+        const float2 G2 = s_g2[warp][ring];
+        const float2 G0 = make_float2(g01.x, g01.y), G1 = make_float2(g01.z, g01.w);
+        const float2 ddx = sub2(MX, make_float2(pxy.x, pxy.y)), ddy = sub2(MY, make_float2(pxy.z, pxy.w));
+        const float2 dxx = mul2(ddx, ddx), dxy = mul2(ddx, ddy), dyy = mul2(ddy, ddy);
+        const float2 q = fma2(KB, dxy, fma2(KC, dyy, mul2(KA, dxx)));
+        float2 a = mul2(OP, make_float2(exp2f(-fmaxf(q.x, 0.f)), exp2f(-fmaxf(q.y, 0.f))));
+        a.x = fminf(a.x, max_alpha);
+        a.y = fminf(a.y, max_alpha);
+        if constexpr (!kFp16) {
+          const uint2 last = s_last[warp][ring];
+          a.x = tp < last.x ? a.x : 0.f;
+          a.y = tp < last.y ? a.y : 0.f;
+        }
+        const float2 w = mul2(T, a);
+        const float2 om = fma2(a, dup2(-1.0f), dup2(1.0f));
+        const float2 cdg = fma2(C2, G2, fma2(C1, G1, mul2(C0, G0)));
+        g_c0 = fma2(w, G0, g_c0);
+        g_c1 = fma2(w, G1, g_c1);
+        g_c2 = fma2(w, G2, g_c2);
+        nadg = fma2(w, cdg, nadg);  // what lies behind this primitive (negated)
+        const float2 ro = make_float2(1.0f / om.x, 1.0f / om.y);
+        const float2 dop = mul2(a, fma2(T, cdg, mul2(nadg, ro)));
+        g_op = add2(g_op, dop);
+        g_ca = fma2(dop, dxx, g_ca);
+        g_cb = fma2(dop, dxy, g_cb);
+        g_cc = fma2(dop, dyy, g_cc);
         if constexpr (kAbs) {
           // (ca, cb, cc) = (2 ka, kb, 2 kc) / log2 e
-          const float gmx = dop * (2.0f * ka * ddx + kb * ddy) * (1.0f / kLog2e);
-          const float gmy = dop * (kb * ddx + 2.0f * kc * ddy) * (1.0f / kLog2e);
-          g_mx += gmx;
-          g_my += gmy;
-          a_mx += fabsf(gmx);
-          a_my += fabsf(gmy);
+          const float2 gmx = mul2(dop, fma2(dup2(2.0f * ka), ddx, mul2(KB, ddy)));
+          const float2 gmy = mul2(dop, fma2(KB, ddx, mul2(dup2(2.0f * kc), ddy)));
+          g_mx = add2(g_mx, gmx);
+          g_my = add2(g_my, gmy);
+          a_mx = add2(a_mx, make_float2(fabsf(gmx.x), fabsf(gmx.y)));
+          a_my = add2(a_my, make_float2(fabsf(gmy.x), fabsf(gmy.y)));
         } else {
-          s_x += dop * ddx;
-          s_y += dop * ddy;
+          s_x = fma2(dop, ddx, s_x);
+          s_y = fma2(dop, ddy, s_y);
         }
-        T *= om;
+        T = mul2(T, om);
       }
       __syncwarp();
     }
+    float go = g_op.x + g_op.y, gca = g_ca.x + g_ca.y, gcb = g_cb.x + g_cb.y, gcc = g_cc.x + g_cc.y;
+    float gc0 = g_c0.x + g_c0.y, gc1 = g_c1.x + g_c1.y, gc2 = g_c2.x + g_c2.y;
+    float gmx_s = 0.f, gmy_s = 0.f, amx_s = 0.f, amy_s = 0.f;
+    if constexpr (kAbs) {
+      gmx_s = (g_mx.x + g_mx.y) * (1.0f / kLog2e);
+      gmy_s = (g_my.x + g_my.y) * (1.0f / kLog2e);
+      amx_s = (a_mx.x + a_mx.y) * (1.0f / kLog2e);
+      amy_s = (a_my.x + a_my.y) * (1.0f / kLog2e);
+    }
+    const float sxs = s_x.x + s_x.y, sys = s_y.x + s_y.y;
     if (valid_prim) {
       if constexpr (!kAbs) {
         float4 co;
         load_conic<kFp16>(p, conic_opacity, prim_info, co);
-        g_mx = co.x * s_x + co.y * s_y;
-        g_my = co.y * s_x + co.z * s_y;
+        gmx_s = co.x * sxs + co.y * sys;
+        gmy_s = co.y * sxs + co.z * sys;
       }
       if constexpr (!kFp16) {
         // colour clamped at zero passes no gradient
-        if (color[3 * p] < 0.f) g_c0 = 0.f;
-        if (color[3 * p + 1] < 0.f) g_c1 = 0.f;
-        if (color[3 * p + 2] < 0.f) g_c2 = 0.f;
+        if (color[3 * p] < 0.f) gc0 = 0.f;
+        if (color[3 * p + 1] < 0.f) gc1 = 0.f;
+        if (color[3 * p + 2] < 0.f) gc2 = 0.f;
       }
       // scale conventions: fp32 accumulates in [0,1] colour units; the fp16
       // path carries colour and the colour-behind scaled by 255 (reference
       // lines 1359-1369 divide by 255 at the end)
       const float sc = kFp16 ? (1.0f / 255.0f) : 1.0f;
       float* h = helpers + static_cast<size_t>(p) * kHelperFloats;
-      atomicAdd(h + 0, -g_mx * sc);
-      atomicAdd(h + 1, -g_my * sc);
+      atomicAdd(h + 0, -gmx_s * sc);
+      atomicAdd(h + 1, -gmy_s * sc);
       if constexpr (kAbs) {
-        atomicAdd(h + 2, a_mx * sc);
-        atomicAdd(h + 3, a_my * sc);
+        atomicAdd(h + 2, amx_s * sc);
+        atomicAdd(h + 3, amy_s * sc);
       }
-      atomicAdd(h + 4, -0.5f * g_ca * sc);
-      atomicAdd(h + 5, -0.5f * g_cb * sc);
-      atomicAdd(h + 6, -0.5f * g_cc * sc);
-      atomicAdd(h + 7, g_op * sc * (1.0f - op));
-      atomicAdd(h + 8, g_c0);
-      atomicAdd(h + 9, g_c1);
-      atomicAdd(h + 10, g_c2);
+      atomicAdd(h + 4, -0.5f * gca * sc);
+      atomicAdd(h + 5, -0.5f * gcb * sc);
+      atomicAdd(h + 6, -0.5f * gcc * sc);
+      atomicAdd(h + 7, go * sc * (1.0f - op));
+      atomicAdd(h + 8, gc0);
+      atomicAdd(h + 9, gc1);
+      atomicAdd(h + 10, gc2);
     }
   }
 }

@@ -551,13 +551,16 @@ __global__ void __launch_bounds__(kScanBlock)
         masks[e] = mask;
         if (mask != 0u) atomicAdd(&n_touched[prim], static_cast<uint32_t>(__popc(mask)));
       }
-      // per-tile counts: lane j collects tile j of the warp
-      uint32_t mine = 0;
+      // per-tile counts: transpose the warp's 32 x 32 bit matrix of masks
+      // (rows = entries, columns = tiles) across the lanes, so that lane j
+      // holds column j, and count its bits
+      uint32_t col = mask;
 #pragma unroll
-      for (int j = 0; j < kSuperTiles; ++j) {
-        const uint32_t bj = __ballot_sync(full, (mask >> j) & 1u);
-        if (lane == static_cast<uint32_t>(j)) mine = __popc(bj);
+      for (uint32_t sh = 16, m0 = 0x0000ffffu; sh > 0; sh >>= 1, m0 ^= m0 << sh) {
+        const uint32_t other = __shfl_xor_sync(full, col, sh);
+        col = (lane & sh) == 0u ? (col & m0) | ((other & m0) << sh) : (col & ~m0) | ((other & ~m0) >> sh);
       }
+      const uint32_t mine = __popc(col);
       if (mine) atomicAdd(&sub_cnt[lane], mine);
     }
     __syncthreads();

@@ -436,6 +436,18 @@ __device__ __forceinline__ TileTest tile_test_of(uint32_t p, const float2* __res
   return q;
 }
 
+// 32 x 32 bit-matrix transpose across a warp: lane i holds row i on entry
+// (bit j = column j); on exit lane j holds column j (bit i = row i).
+__device__ __forceinline__ uint32_t warp_transpose_bits(uint32_t row, uint32_t lane) {
+  uint32_t col = row;
+#pragma unroll
+  for (uint32_t sh = 16, m0 = 0x0000ffffu; sh > 0; sh >>= 1, m0 ^= m0 << sh) {
+    const uint32_t other = __shfl_xor_sync(0xffffffffu, col, sh);
+    col = (lane & sh) == 0u ? (col & m0) | ((other & m0) << sh) : (col & ~m0) | ((other & ~m0) >> sh);
+  }
+  return col;
+}
+
 // 5a. per chunk: hit mask of every entry (exact tile tests of its rectangle
 // inside the super-tile, the warp's (entry, tile) pairs tested 32 at a time),
 // per-tile hit counts of the chunk, and each Gaussian's touched-tile total.
@@ -554,13 +566,7 @@ __global__ void __launch_bounds__(kScanBlock)
       // per-tile counts: transpose the warp's 32 x 32 bit matrix of masks
       // (rows = entries, columns = tiles) across the lanes, so that lane j
       // holds column j, and count its bits
-      uint32_t col = mask;
-#pragma unroll
-      for (uint32_t sh = 16, m0 = 0x0000ffffu; sh > 0; sh >>= 1, m0 ^= m0 << sh) {
-        const uint32_t other = __shfl_xor_sync(full, col, sh);
-        col = (lane & sh) == 0u ? (col & m0) | ((other & m0) << sh) : (col & ~m0) | ((other & ~m0) >> sh);
-      }
-      const uint32_t mine = __popc(col);
+      const uint32_t mine = __popc(warp_transpose_bits(mask, lane));
       if (mine) atomicAdd(&sub_cnt[lane], mine);
     }
     __syncthreads();
@@ -712,17 +718,16 @@ __global__ void __launch_bounds__(32 * kEmitWarps)
         prim_n = ent_prim[en];
       }
       // all 32 tiles unconditionally: the ballots and shuffles of different
-      // tiles are independent, so the unrolled steps overlap (lane j's slot
-      // is read at step j before lane j moves it on)
-      uint32_t grow = 0;
+      // tiles are independent, so the unrolled steps overlap; the slots of
+      // tile `lane` advance by its hit count in these 32 entries, one
+      // popcount of the transposed masks
 #pragma unroll
       for (int j = 0; j < kSuperTiles; ++j) {
         const uint32_t bj = __ballot_sync(full, (mask >> j) & 1u);
         const uint32_t p = __shfl_sync(full, pos, j);
         if ((bj >> lane) & 1u) inst_prim[p + __popc(bj & lt)] = prim;
-        if (lane == static_cast<uint32_t>(j)) grow = __popc(bj);
       }
-      pos += grow;
+      pos += __popc(warp_transpose_bits(mask, lane));
     }
   }
 }

@@ -76,6 +76,21 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t& t
   return before + x - v;
 }
 
+// Loads of a thread's contiguous run [begin, end) in batches of 8 whose
+// loads are in flight together (a plain loop waits on every load in turn):
+// f(k, value) is called for every k in order.
+template <typename F>
+__device__ __forceinline__ void for_run(const uint32_t* src, uint32_t begin, uint32_t end, F&& f) {
+  for (uint32_t k0 = begin; k0 < end; k0 += 8u) {
+    uint32_t v[8];
+#pragma unroll
+    for (uint32_t j = 0; j < 8u; ++j) v[j] = k0 + j < end ? src[k0 + j] : 0u;
+#pragma unroll
+    for (uint32_t j = 0; j < 8u; ++j)
+      if (k0 + j < end) f(k0 + j, v[j]);
+  }
+}
+
 // Exclusive scan of `count` block sums in place (one block of 1024 threads);
 // the grand total goes to *total_out.  Optional capacity check raises
 // `overflow_bit` in counts->overflow.
@@ -87,7 +102,7 @@ __global__ void __launch_bounds__(1024)
   const uint32_t per = (count + 1023u) / 1024u;
   const uint32_t begin = min(count, t * per), end = min(count, begin + per);
   uint32_t local = 0;
-  for (uint32_t k = begin; k < end; ++k) local += sums[k];
+  for_run(sums, begin, end, [&](uint32_t, uint32_t v) { local += v; });
   // block scan of `local`
   const uint32_t lane = t & 31u, warp = t >> 5;
   uint32_t x = local;
@@ -109,11 +124,10 @@ __global__ void __launch_bounds__(1024)
   }
   __syncthreads();
   uint32_t run = (warp == 0 ? 0u : warp_sums[warp - 1]) + x - local;
-  for (uint32_t k = begin; k < end; ++k) {
-    const uint32_t v = sums[k];
+  for_run(sums, begin, end, [&](uint32_t k, uint32_t v) {
     sums[k] = run;
     run += v;
-  }
+  });
   if (t == 1023) {
     const uint32_t total = warp_sums[31];
     *total_out = total;
@@ -195,14 +209,13 @@ __global__ void __launch_bounds__(kSortThreads)
   const uint32_t per = (nb + kSortThreads - 1) / kSortThreads;
   const uint32_t begin = min(nb, threadIdx.x * per), end = min(nb, begin + per);
   uint32_t local = 0;
-  for (uint32_t b = begin; b < end; ++b) local += row[b];
+  for_run(row, begin, end, [&](uint32_t, uint32_t v) { local += v; });
   uint32_t total;
   uint32_t run = block_exclusive_scan(local, total);
-  for (uint32_t b = begin; b < end; ++b) {
-    const uint32_t v = row[b];
+  for_run(row, begin, end, [&](uint32_t b, uint32_t v) {
     row[b] = run;
     run += v;
-  }
+  });
   if (threadIdx.x == 0) digit_total[d] = total;
 }
 
@@ -373,14 +386,28 @@ __global__ void k_super_ranges(const uint16_t* __restrict__ keys, const DevCount
 }
 
 // 4b. chunk table: each super-tile's entries cut into chunks of kChunk
-// (one block of 1024 threads; thread t owns a contiguous run of super-tiles)
+// (one block of 1024 threads; thread t owns a contiguous run of super-tiles).
+// With `totals` (the per-digit counts of a single-pass entry sort, i.e. the
+// entries of each super-tile), the super-tile ranges are first derived from
+// them by an exclusive scan and written to `super_ranges`.
 __global__ void __launch_bounds__(1024)
-    k_chunk_table(const uint2* __restrict__ super_ranges, uint32_t n_super, uint4* __restrict__ chunks,
-                  uint32_t* __restrict__ super_chunk, DevCounts* __restrict__ counts) {
+    k_chunk_table(uint2* __restrict__ super_ranges, const uint32_t* __restrict__ totals, uint32_t n_super,
+                  uint4* __restrict__ chunks, uint32_t* __restrict__ super_chunk, DevCounts* __restrict__ counts) {
   __shared__ uint32_t warp_sums[32];
   const uint32_t t = threadIdx.x;
   const uint32_t per = (n_super + 1023u) / 1024u;
   const uint32_t begin = min(n_super, t * per), end = min(n_super, begin + per);
+  if (totals != nullptr) {
+    uint32_t mine = 0;
+    for (uint32_t k = begin; k < end; ++k) mine += totals[k];
+    uint32_t all;
+    uint32_t start = block_exclusive_scan(mine, all);
+    for (uint32_t k = begin; k < end; ++k) {
+      super_ranges[k] = make_uint2(start, start + totals[k]);
+      start += totals[k];
+    }
+    __syncthreads();
+  }
   uint32_t local = 0;
   for (uint32_t k = begin; k < end; ++k) {
     const uint2 r = super_ranges[k];
@@ -621,11 +648,10 @@ __global__ void __launch_bounds__(1024)
   const uint32_t per = (n_tiles + 1023u) / 1024u;
   const uint32_t begin = min(n_tiles, t * per), end = min(n_tiles, begin + per);
   uint32_t li = 0, lb = 0;
-  for (uint32_t k = begin; k < end; ++k) {
-    const uint32_t v = tile_total[k];
+  for_run(tile_total, begin, end, [&](uint32_t, uint32_t v) {
     li += v;
     lb += (v + kBucket - 1u) / kBucket;
-  }
+  });
   uint32_t xi = li, xb = lb;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -656,13 +682,12 @@ __global__ void __launch_bounds__(1024)
   __syncthreads();
   uint32_t ri = (warp == 0 ? 0u : s_inst[warp - 1]) + xi - li;
   uint32_t rb = (warp == 0 ? 0u : s_buck[warp - 1]) + xb - lb;
-  for (uint32_t k = begin; k < end; ++k) {
-    const uint32_t v = tile_total[k];
+  for_run(tile_total, begin, end, [&](uint32_t k, uint32_t v) {
     ranges[k] = make_uint2(ri, ri + v);
     ri += v;
     rb += (v + kBucket - 1u) / kBucket;
     bucket_offsets[k] = rb;
-  }
+  });
   if (t == 1023) {
     const uint32_t ni = s_inst[31], nb = s_buck[31];
     counts->n_instances = ni;
@@ -786,9 +811,15 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   const uint16_t* ent_key = s.ent_key[s.ent_result];
   const uint32_t* ent_prim = s.ent_prim[s.ent_result];
   // 4. chunks of each super-tile's entry list
-  cudaMemsetAsync(s.super_ranges, 0, sizeof(uint2) * n_super, stream);
-  k_super_ranges<<<s.num_sms * 8, 256, 0, stream>>>(ent_key, counts, s.super_ranges);
-  k_chunk_table<<<1, 1024, 0, stream>>>(s.super_ranges, n_super, s.chunks, s.super_chunk, counts);
+  if (super_bits <= kRadixBits) {
+    // one pass: its digit totals are the super-tiles' entry counts
+    k_chunk_table<<<1, 1024, 0, stream>>>(s.super_ranges, s.sort_digit_total, n_super, s.chunks, s.super_chunk,
+                                          counts);
+  } else {
+    cudaMemsetAsync(s.super_ranges, 0, sizeof(uint2) * n_super, stream);
+    k_super_ranges<<<s.num_sms * 8, 256, 0, stream>>>(ent_key, counts, s.super_ranges);
+    k_chunk_table<<<1, 1024, 0, stream>>>(s.super_ranges, nullptr, n_super, s.chunks, s.super_chunk, counts);
+  }
   // 5. hit masks and counts, then every (chunk, tile)'s first slot
   const int persistent = s.num_sms * 8;
   if (fp16)

@@ -151,9 +151,10 @@ __global__ void __launch_bounds__(kF16Threads)
                         uint16_t* __restrict__ n_contrib, uint32_t* __restrict__ tile_max,
                         uint2* __restrict__ live_buckets, DevCounts* __restrict__ live_count,
                         uint4* __restrict__ ckpt) {
-  __shared__ __half2 s_mx[kF16Threads], s_my[kF16Threads];
-  __shared__ __half2 s_cx[kF16Threads], s_cy[kF16Threads], s_cz[kF16Threads], s_op[kF16Threads];
-  __shared__ __half2 s_r[kF16Threads], s_g[kF16Threads], s_b[kF16Threads];
+  // per primitive of the batch, as broadcast vector loads: (mx, my, cx, cy),
+  // (cz, opacity, r, g) and b, every value duplicated into both halves
+  __shared__ uint4 s_q0[kF16Threads], s_q1[kF16Threads];
+  __shared__ __half2 s_b[kF16Threads];
   __shared__ uint32_t s_max[kF16Threads / 32];
   __shared__ uint32_t s_live[2];
   const uint32_t tid = threadIdx.x;
@@ -206,17 +207,14 @@ __global__ void __launch_bounds__(kF16Threads)
       const uint32_t p = inst_prim[r.x + k];
       const float2 m = mean2d[p];
       const float mx = m.x / 16.0f - anchor.x, my = m.y / 16.0f - anchor.y;
-      s_mx[tid] = __float2half2_rn(mx);
-      s_my[tid] = __float2half2_rn(my);
       const PrimInfo16 rec = prim_info[p];
       const __half2 cxy = __hmul2(rec.conic_xy, h16);
       const __half2 czo = __hmul2(rec.conic_z_opacity, s16_1);
-      s_cx[tid] = __lows2half2(cxy, cxy);
-      s_cy[tid] = __highs2half2(cxy, cxy);
-      s_cz[tid] = __lows2half2(czo, czo);
-      s_op[tid] = __highs2half2(czo, czo);
-      s_r[tid] = __float2half2_rn(static_cast<float>(rec.rgb_pad.x));
-      s_g[tid] = __float2half2_rn(static_cast<float>(rec.rgb_pad.y));
+      s_q0[tid] = make_uint4(h2u(__float2half2_rn(mx)), h2u(__float2half2_rn(my)), h2u(__lows2half2(cxy, cxy)),
+                             h2u(__highs2half2(cxy, cxy)));
+      s_q1[tid] = make_uint4(h2u(__lows2half2(czo, czo)), h2u(__highs2half2(czo, czo)),
+                             h2u(__float2half2_rn(static_cast<float>(rec.rgb_pad.x))),
+                             h2u(__float2half2_rn(static_cast<float>(rec.rgb_pad.y))));
       s_b[tid] = __float2half2_rn(static_cast<float>(rec.rgb_pad.z));
     }
     __syncthreads();
@@ -226,22 +224,23 @@ __global__ void __launch_bounds__(kF16Threads)
       store_ckpt((start + i) >> 5);
       const uint32_t j_end = min(i + 32u, batch);
       for (uint32_t j = i; j < j_end && live; ++j) {
-        const __half2 dx = __hsub2(s_mx[j], off_x);
-        const __half2 dy = __hsub2(s_my[j], off_y);
-        const __half2 qx = __hmul2(dx, __hmul2(s_cx[j], dx));
-        const __half2 qz = __hmul2(dy, __hmul2(s_cz[j], dy));
-        const __half2 qy = __hmul2(dx, __hmul2(s_cy[j], dy));
+        const uint4 q0 = s_q0[j], q1 = s_q1[j];
+        const __half2 dx = __hsub2(u2h(q0.x), off_x);
+        const __half2 dy = __hsub2(u2h(q0.y), off_y);
+        const __half2 qx = __hmul2(dx, __hmul2(u2h(q0.z), dx));
+        const __half2 qz = __hmul2(dy, __hmul2(u2h(q1.x), dy));
+        const __half2 qy = __hmul2(dx, __hmul2(u2h(q0.w), dy));
         const __half2 power = __hmul2(__hfma2(half_2, __hadd2(qx, qz), qy), h16);
         const __half2 g = h2exp2_approx(__hmul2(__hneg2(power), log2e));
-        const __half2 a = __hmin2(__hmul2(s_op[j], g), max_a2);
+        const __half2 a = __hmin2(__hmul2(u2h(q1.y), g), max_a2);
         const __half2 Tn = __hfma2(__hneg2(a), T, T);
         // positive halves compare like their bit patterns
         const uint32_t accept = __vsetgeu2(h2u(Tn), h2u(min_t2));
         const uint32_t on = live & accept;
         const uint32_t mask = (on << 16) - on;  // 0xffff per enabled pixel
         const __half2 w = u2h(h2u(__hmul2(__hmul2(T, a), unscale2)) & mask);
-        cr = __hfma2(s_r[j], w, cr);
-        cg = __hfma2(s_g[j], w, cg);
+        cr = __hfma2(u2h(q1.z), w, cr);
+        cg = __hfma2(u2h(q1.w), w, cg);
         cb = __hfma2(s_b[j], w, cb);
         T = u2h(h2u(T) ^ (mask & (h2u(Tn) ^ h2u(T))));
         n_seen = __vaddus2(n_seen, live);

@@ -48,6 +48,23 @@ __device__ __forceinline__ void add_px(void* p, uint32_t i, float v, float s) {
   }
 }
 
+// the image type's rounding of v (fp16: round to nearest half)
+template <int kFp16>
+__device__ __forceinline__ float round_px(float v) {
+  if constexpr (kFp16)
+    return __half2float(__float2half_rn(v));
+  else
+    return v;
+}
+
+template <int kFp16>
+__device__ __forceinline__ void store_px(void* p, uint32_t i, float v) {
+  if constexpr (kFp16)
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else
+    reinterpret_cast<float*>(p)[i] = v;
+}
+
 __device__ __forceinline__ float block_sum_256(float v) {
   __shared__ float ws[8];
   v += __shfl_xor_sync(0xffffffffu, v, 16);
@@ -192,19 +209,47 @@ __global__ void __launch_bounds__(256)
   const int px = x0 + c;
   float contrib = 0.f;
   const uint32_t plane3 = 3 * cam.plane;
+  // every global load of the four pixels first, then the arithmetic, then
+  // the stores; fp16 images inside the picture come from the staged window
+  // (exact), the L1 term's padding pixels from memory
+  uint32_t pis[4];
+  bool l1_on[4], in_img[4];
+  float pv[4], tv[4], lm[4], gr[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int py = y0 + q0 + k;
-    const uint32_t pi = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
-    // fused L1 term over the padded physical extent (l1.cu:117-129); applied
-    // first, as the reference evaluates the L1 loss before the SSIM loss
-    if (s_l1 != 0.f && static_cast<uint32_t>(px) < cam.tiled_w * 8u && static_cast<uint32_t>(py) < cam.tiled_h * 8u) {
-      const float d = sat(load_px<kFp16>(pred, pi)) - load_px<kFp16>(target, pi);
-      contrib += fabsf(d) * s_l1;
-      if (loss_map != nullptr) add_px<kFp16>(loss_map, pi, fabsf(d), s_l1);
-      if (grad != nullptr) add_px<kFp16>(grad, pi, copysignf(1.0f, d), s_l1);
+    pis[k] = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
+    l1_on[k] = s_l1 != 0.f && static_cast<uint32_t>(px) < cam.tiled_w * 8u && static_cast<uint32_t>(py) < cam.tiled_h * 8u;
+    in_img[k] = px < W && py < H;
+    pv[k] = tv[k] = lm[k] = gr[k] = 0.f;
+    if (l1_on[k]) {
+      if (kFp16 && in_img[k]) {
+        const float2 v = __half22float2(tile[q0 + k + kHalo][c + 8]);
+        pv[k] = v.x;
+        tv[k] = v.y;
+      } else {
+        pv[k] = load_px<kFp16>(pred, pis[k]);
+        tv[k] = load_px<kFp16>(target, pis[k]);
+      }
+      if (grad != nullptr) gr[k] = load_px<kFp16>(grad, pis[k]);
     }
-    if (px < W && py < H) {
+    if (loss_map != nullptr && (l1_on[k] || in_img[k])) lm[k] = load_px<kFp16>(loss_map, pis[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t pi = pis[k];
+    float lmv = lm[k];
+    // fused L1 term over the padded physical extent (l1.cu:117-129); applied
+    // first, as the reference evaluates the L1 loss before the SSIM loss;
+    // each update of the loss map and the gradient rounds once to the image
+    // type, like two separate read-modify-writes
+    if (l1_on[k]) {
+      const float d = sat(pv[k]) - tv[k];
+      contrib += fabsf(d) * s_l1;
+      lmv = round_px<kFp16>(fmaf(fabsf(d), s_l1, lmv));
+      if (grad != nullptr) store_px<kFp16>(grad, pi, round_px<kFp16>(fmaf(copysignf(1.0f, d), s_l1, gr[k])));
+    }
+    if (in_img[k]) {
       const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
       const float mu1 = o[0][k], mu2 = o[2][k];
       const float m11 = mu1 * mu1, m22 = mu2 * mu2;
@@ -212,7 +257,7 @@ __global__ void __launch_bounds__(256)
       const float A = m11 + m22 + C1, B = sg1 + sg2 + C2;
       const float Cc = 2.f * mu1 * mu2 + C1, D = 2.f * sg12 + C2;
       const float val = (Cc * D) / (A * B);
-      if (loss_map != nullptr) add_px<kFp16>(loss_map, pi, 1.0f - val, s_ssim);
+      lmv = round_px<kFp16>(fmaf(1.0f - val, s_ssim, lmv));
       contrib += (1.0f - val) * s_ssim;
       if (partials != nullptr) {
         partials[pi] = (mu2 * 2.f * D) / (A * B) - (mu2 * 2.f * Cc) / (A * B) - (mu1 * 2.f * Cc * D) / (A * A * B) +
@@ -221,6 +266,7 @@ __global__ void __launch_bounds__(256)
         partials[pi + 2 * plane3] = (2.f * Cc) / (A * B);
       }
     }
+    if (loss_map != nullptr && (l1_on[k] || in_img[k])) store_px<kFp16>(loss_map, pi, lmv);
   }
   if (loss_sum != nullptr) {
     const float t = block_sum_256(contrib);
@@ -283,14 +329,24 @@ __global__ void __launch_bounds__(256)
   taps4<3>(in, o);
   const int px = x0 + c;
   if (px >= W) return;
+  uint32_t pis[4];
+  float p1[4], p2[4], g0[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int py = y0 + q0 + k;
-    if (py >= H) break;
-    const uint32_t pi = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
-    const float p1 = load_px<kFp16>(pred, pi), p2 = load_px<kFp16>(target, pi);
-    const float dL = o[0][k] + (2.f * p1) * o[1][k] + p2 * o[2][k];
-    add_px<kFp16>(grad, pi, dL, -s_ssim);
+    pis[k] = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
+    p1[k] = p2[k] = g0[k] = 0.f;
+    if (py < H) {
+      p1[k] = load_px<kFp16>(pred, pis[k]);
+      p2[k] = load_px<kFp16>(target, pis[k]);
+      g0[k] = load_px<kFp16>(grad, pis[k]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (y0 + q0 + k >= H) break;
+    const float dL = o[0][k] + (2.f * p1[k]) * o[1][k] + p2[k] * o[2][k];
+    store_px<kFp16>(grad, pis[k], round_px<kFp16>(fmaf(dL, -s_ssim, g0[k])));
   }
 }
 

@@ -166,34 +166,38 @@ __global__ void __launch_bounds__(kSortThreads)
   __shared__ uint32_t h[kWarps][kRadix];
   const uint32_t mask = (1u << bits) - 1u;
   const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
-  const uint32_t base = blockIdx.x * kSortTile;
-  if (base >= n) return;
   const uint32_t t = threadIdx.x, warp = t >> 5;
+  // grid-stride over the 2048-item tiles (the grid is sized by the resident
+  // blocks, not by the capacity)
+  for (uint32_t tb = blockIdx.x; tb * kSortTile < n; tb += gridDim.x) {
+    const uint32_t base = tb * kSortTile;
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) h[w][t] = 0;
-  __syncthreads();
-  const uint32_t first = base + t * kSortItems;
-  K k[kSortItems];
-  if (base + kSortTile <= n) {
-    constexpr int kVec = kSortItems * sizeof(K) / 16;
-    const uint4* src = reinterpret_cast<const uint4*>(keys + first);
+    for (int w = 0; w < kWarps; ++w) h[w][t] = 0;
+    __syncthreads();
+    const uint32_t first = base + t * kSortItems;
+    K k[kSortItems];
+    if (base + kSortTile <= n) {
+      constexpr int kVec = kSortItems * sizeof(K) / 16;
+      const uint4* src = reinterpret_cast<const uint4*>(keys + first);
 #pragma unroll
-    for (int v = 0; v < kVec; ++v) {
-      const uint4 q = src[v];
-      memcpy(&k[v * (16 / sizeof(K))], &q, 16);
+      for (int v = 0; v < kVec; ++v) {
+        const uint4 q = src[v];
+        memcpy(&k[v * (16 / sizeof(K))], &q, 16);
+      }
+#pragma unroll
+      for (int j = 0; j < kSortItems; ++j) atomicAdd(&h[warp][(static_cast<uint32_t>(k[j]) >> shift) & mask], 1u);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kSortItems; ++j)
+        if (first + j < n) atomicAdd(&h[warp][(static_cast<uint32_t>(keys[first + j]) >> shift) & mask], 1u);
     }
+    __syncthreads();
+    uint32_t c = 0;
 #pragma unroll
-    for (int j = 0; j < kSortItems; ++j) atomicAdd(&h[warp][(static_cast<uint32_t>(k[j]) >> shift) & mask], 1u);
-  } else {
-#pragma unroll
-    for (int j = 0; j < kSortItems; ++j)
-      if (first + j < n) atomicAdd(&h[warp][(static_cast<uint32_t>(keys[first + j]) >> shift) & mask], 1u);
+    for (int w = 0; w < kWarps; ++w) c += h[w][t];
+    hist[t * max_blocks + tb] = c;
+    __syncthreads();  // h is cleared again for the next tile
   }
-  __syncthreads();
-  uint32_t c = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) c += h[w][t];
-  hist[t * max_blocks + blockIdx.x] = c;
 }
 
 // One block per digit: exclusive scan of the digit's per-block counts in
@@ -239,77 +243,82 @@ __global__ void __launch_bounds__(kSortThreads)
   __shared__ K s_keys[kSortTile];
   __shared__ uint32_t s_vals[kSortTile];
   const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
-  const uint32_t base = blockIdx.x * kSortTile;
-  if (base >= n) return;
+  if (blockIdx.x * kSortTile >= n) return;
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   const uint32_t mask_bits = (1u << bits) - 1u;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) s_cnt[w][t] = 0;
   uint32_t all_digits;
   const uint32_t smaller = block_exclusive_scan(digit_total[t], all_digits);
-  s_global[t] = smaller + hist[t * max_blocks + blockIdx.x];
-  __syncthreads();
-  const uint32_t lt = lanemask_lt();
-  K key[kSortItems];
-  uint32_t val[kSortItems];
-  uint32_t rank[kSortItems];
-  const uint32_t wbase = base + warp * kPerWarp;
+  // grid-stride over the 2048-item tiles (the grid is sized by the resident
+  // blocks, not by the capacity)
+  for (uint32_t tb = blockIdx.x; tb * kSortTile < n; tb += gridDim.x) {
+    const uint32_t base = tb * kSortTile;
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    const uint32_t idx = wbase + r * 32 + lane;
-    const bool valid = idx < n;
-    key[r] = valid ? keys_in[idx] : K(0);
-    val[r] = valid ? vals_in[idx] : 0u;
-    const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
-    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+    for (int w = 0; w < kWarps; ++w) s_cnt[w][t] = 0;
+    s_global[t] = smaller + hist[t * max_blocks + tb];
+    __syncthreads();
+    const uint32_t lt = lanemask_lt();
+    K key[kSortItems];
+    uint32_t val[kSortItems];
+    uint32_t rank[kSortItems];
+    const uint32_t wbase = base + warp * kPerWarp;
 #pragma unroll
-    for (int bt = 0; bt < kRadixBits; ++bt) {
-      if (bt < bits) {
-        const uint32_t m = __ballot_sync(0xffffffffu, (digit >> bt) & 1u);
-        peers &= ((digit >> bt) & 1u) ? m : ~m;
+    for (int r = 0; r < kSortItems; ++r) {
+      const uint32_t idx = wbase + r * 32 + lane;
+      const bool valid = idx < n;
+      key[r] = valid ? keys_in[idx] : K(0);
+      val[r] = valid ? vals_in[idx] : 0u;
+      const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
+      uint32_t peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+      for (int bt = 0; bt < kRadixBits; ++bt) {
+        if (bt < bits) {
+          const uint32_t m = __ballot_sync(0xffffffffu, (digit >> bt) & 1u);
+          peers &= ((digit >> bt) & 1u) ? m : ~m;
+        }
+      }
+      // the lowest lane of each digit group advances the warp's counter
+      const int leader = __ffs(peers) - 1;
+      uint32_t before = 0;
+      if (valid && static_cast<int>(lane) == leader) {
+        before = s_cnt[warp][digit];
+        s_cnt[warp][digit] = before + __popc(peers);
+      }
+      before = __shfl_sync(0xffffffffu, before, leader < 0 ? 0 : leader);
+      rank[r] = valid ? before + __popc(peers & lt) : 0xffffffffu;
+      __syncwarp();
+    }
+    __syncthreads();
+    // per-digit offsets of each warp and block-local digit starts
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t c = s_cnt[w][t];
+      s_cnt[w][t] = run;
+      run += c;
+    }
+    uint32_t block_total;
+    const uint32_t start = block_exclusive_scan(run, block_total);
+    s_start[t] = start;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      if (rank[r] != 0xffffffffu) {
+        const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
+        const uint32_t pos = s_start[digit] + s_cnt[warp][digit] + rank[r];
+        s_keys[pos] = key[r];
+        s_vals[pos] = val[r];
       }
     }
-    // the lowest lane of each digit group advances the warp's counter
-    const int leader = __ffs(peers) - 1;
-    uint32_t before = 0;
-    if (valid && static_cast<int>(lane) == leader) {
-      before = s_cnt[warp][digit];
-      s_cnt[warp][digit] = before + __popc(peers);
+    __syncthreads();
+    // consecutive items of the same digit go to consecutive global addresses
+    for (uint32_t i = t; i < block_total; i += kSortThreads) {
+      const K k = s_keys[i];
+      const uint32_t digit = (static_cast<uint32_t>(k) >> shift) & mask_bits;
+      const uint32_t g = s_global[digit] + (i - s_start[digit]);
+      keys_out[g] = k;
+      vals_out[g] = s_vals[i];
     }
-    before = __shfl_sync(0xffffffffu, before, leader < 0 ? 0 : leader);
-    rank[r] = valid ? before + __popc(peers & lt) : 0xffffffffu;
-    __syncwarp();
-  }
-  __syncthreads();
-  // per-digit offsets of each warp and block-local digit starts
-  uint32_t run = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const uint32_t c = s_cnt[w][t];
-    s_cnt[w][t] = run;
-    run += c;
-  }
-  uint32_t block_total;
-  const uint32_t start = block_exclusive_scan(run, block_total);
-  s_start[t] = start;
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    if (rank[r] != 0xffffffffu) {
-      const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
-      const uint32_t pos = s_start[digit] + s_cnt[warp][digit] + rank[r];
-      s_keys[pos] = key[r];
-      s_vals[pos] = val[r];
-    }
-  }
-  __syncthreads();
-  // consecutive items of the same digit go to consecutive global addresses
-  for (uint32_t i = t; i < block_total; i += kSortThreads) {
-    const K k = s_keys[i];
-    const uint32_t digit = (static_cast<uint32_t>(k) >> shift) & mask_bits;
-    const uint32_t g = s_global[digit] + (i - s_start[digit]);
-    keys_out[g] = k;
-    vals_out[g] = s_vals[i];
+    __syncthreads();  // shared state is rebuilt for the next tile
   }
 }
 
@@ -760,7 +769,9 @@ __global__ void __launch_bounds__(32 * kEmitWarps)
 template <typename K>
 void radix_sort(K* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, const DevCounts* counts,
                 int64_t capacity, int total_bits, int& result, const RasterState& s, cudaStream_t stream) {
-  const uint32_t blocks = static_cast<uint32_t>((capacity + kSortTile - 1) / kSortTile);
+  const uint32_t tiles = static_cast<uint32_t>((capacity + kSortTile - 1) / kSortTile);
+  const uint32_t resident = static_cast<uint32_t>(s.num_sms) * 8u;
+  const uint32_t blocks = tiles < resident ? tiles : resident;
   const uint32_t max_blocks = static_cast<uint32_t>(s.sort_max_blocks);
   int cur = 0;
   for (int shift = 0; shift < total_bits; shift += kRadixBits) {

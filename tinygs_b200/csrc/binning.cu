@@ -635,11 +635,19 @@ __global__ void k_chunk_prefix(const uint2* __restrict__ super_ranges, const uin
   if (counts->overflow == 0u) {
     const uint2 r = super_ranges[sp];
     const uint32_t first = super_chunk[sp], n_ch = (r.y - r.x + kChunk - 1u) / kChunk;
-    for (uint32_t c = first; c < first + n_ch; ++c) {
-      uint32_t* p = chunk_counts + c * kSuperTiles + j;
-      const uint32_t v = *p;
-      *p = run;
-      run += v;
+    // the counts of eight chunks are loaded together, then replaced by
+    // their prefixes (one thread per tile: a plain loop would wait on every
+    // load in turn)
+    for (uint32_t c0 = first; c0 < first + n_ch; c0 += 8u) {
+      uint32_t v[8];
+#pragma unroll
+      for (uint32_t q = 0; q < 8u; ++q) v[q] = c0 + q < first + n_ch ? chunk_counts[(c0 + q) * kSuperTiles + j] : 0u;
+#pragma unroll
+      for (uint32_t q = 0; q < 8u; ++q)
+        if (c0 + q < first + n_ch) {
+          chunk_counts[(c0 + q) * kSuperTiles + j] = run;
+          run += v[q];
+        }
     }
   }
   tile_total[ty * grid_w + tx] = run;

@@ -327,12 +327,23 @@ def run_reference(args):
 
 # ------------------------------------------------------------------- ours
 
-def kernels_per_step(n_tiles: int, world: int) -> int:
-    tile_bits = max(1, (n_tiles - 1).bit_length())
-    tile_passes = (tile_bits + 7) // 8
-    forward = 1 + 2 + 4 * 3 + 3 + 3 * tile_passes + 2 + 1  # preprocess, compaction, sorts, instances, ranges, blend
-    # loss fwd/bwd; blend bwd; per-Gaussian backward fused with Adam (one GPU)
-    # or per-Gaussian backward + Adam (several GPUs; NCCL's kernel not counted)
+def kernels_per_step(width: int, height: int, world: int) -> int:
+    """Launches of this library's kernels in one training step (what
+    launch_preprocess / launch_binning / launch_blend_* / the loss and the
+    backward enqueue)."""
+    grid_w, grid_h = (width + 15) // 16, (height + 15) // 16
+    n_super = ((grid_w + 7) // 8) * ((grid_h + 3) // 4)
+    entry_passes = max(1, ((max(1, n_super - 1)).bit_length() + 7) // 8)
+    forward = (1  # preprocess
+               + 2  # candidate compaction: block-sum scan, compaction
+               + 4 * 3  # depth sort: 4 passes of histogram, scan, scatter
+               + 3  # per-block entry counts, their scan, entry creation
+               + 3 * entry_passes  # entry sort by super-tile
+               + (1 if entry_passes > 1 else 0) + 1  # super-tile ranges (multi-pass sort only), chunk table
+               + 4  # tile tests, chunk prefix, tile offsets, emission
+               + 1)  # blend forward
+    # loss forward + backward; blend backward; per-Gaussian backward fused
+    # with Adam (one GPU) or routed backward + accumulation/Adam kernel
     return forward + 2 + 1 + (1 if world == 1 else 2)
 
 
@@ -617,7 +628,6 @@ def run_ours(args):
         hbm_peak, peak_src = float(peaks["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         hbm_peak, peak_src = 6650.0, "fallback"
-    tile_count = ((W + 15) // 16) * ((H + 15) // 16)
 
     dens_row = None
     if rank == 0 and world == 1 and args.config == "cfg2" and args.n == 0:
@@ -651,7 +661,7 @@ def run_ours(args):
                          "unit": "GB/s", "frac": kernel_gbs / hbm_peak, "peak_source": peak_src, "traffic": kernel_traffic,
                          "algorithmic_bytes_per_launch": kernel_bytes, "avg_launch_ms": kernel_ms},
             "counts": {"visible": counts.n_visible, "instances": counts.n_instances, "buckets": counts.n_buckets},
-            "gpu_launches": kernels_per_step(tile_count, world) * args.steps,
+            "gpu_launches": kernels_per_step(W, H, world) * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }

@@ -152,10 +152,12 @@ __global__ void k_logistic(Pcg rng, uint32_t count, uint32_t threads, float* __r
   out[idx] = logit(g.next_float()) * 1.0f * 0.551328895f + 0.0f;
 }
 
-// default.cu:239-295; the appended rows of gradients and moments are zero
+// default.cu:239-295: the means, scales and opacities of the appended rows
+// (clone: copies; split: both halves moved and shrunk); the appended rows of
+// gradients and moments are zeroed by the caller
 __global__ void __launch_bounds__(kBlock)
     k_duplicate(const uint32_t* __restrict__ grow_src, const uint8_t* __restrict__ flags, uint32_t n_grow,
-                uint32_t n0, Set params, Set grads, Set m, Set v, const float* __restrict__ rnd) {
+                uint32_t n0, Set params, const float* __restrict__ rnd) {
   const uint32_t k = blockIdx.x * kBlock + threadIdx.x;
   if (k >= n_grow) return;
   const uint32_t src = grow_src[k], dst = n0 + k;
@@ -163,9 +165,8 @@ __global__ void __launch_bounds__(kBlock)
   float* opac = params.p[1];
   float* rot = params.p[2];
   float* scales = params.p[3];
-  for (int c = 0; c < 4; ++c) rot[4 * dst + c] = rot[4 * src + c];
-  for (int c = 0; c < 3; ++c) params.p[4][3 * dst + c] = params.p[4][3 * src + c];
-  for (int c = 0; c < 45; ++c) params.p[5][45 * static_cast<size_t>(dst) + c] = params.p[5][45 * static_cast<size_t>(src) + c];
+  // (rotations and SH rows: k_duplicate_rows; gradient and moment rows:
+  // zeroed by the caller)
   if (flags[src] == 1) {
     for (int c = 0; c < 3; ++c) {
       means[3 * dst + c] = means[3 * src + c];
@@ -201,16 +202,37 @@ __global__ void __launch_bounds__(kBlock)
     opac[dst] = lo;
     opac[src] = lo;
   }
-  const Set zero_sets[3] = {grads, m, v};
-  for (const Set& s : zero_sets) {
-#pragma unroll
-    for (int seg = 0; seg < 6; ++seg) {
-      float* p = s.p[seg];
-      if (p == nullptr) continue;
-      const int w = seg_width(seg);
-      for (int c = 0; c < w; ++c) p[static_cast<size_t>(dst) * w + c] = 0.f;
-    }
+}
+
+// Rows of width W: destination rows [0, cnt) of `dst` (a contiguous block)
+// taken from rows s_rows[0..cnt) of `src`; the lanes of a warp run over the
+// block's elements, so stores are coalesced and reads coalesced within a row.
+template <int W>
+__device__ __forceinline__ void copy_rows(const float* __restrict__ src, float* __restrict__ dst,
+                                          const uint32_t* s_rows, uint32_t cnt, uint32_t lane) {
+  for (uint32_t e = lane; e < cnt * W; e += 32u) {
+    const uint32_t r = e / W, c = e - r * W;
+    dst[e] = src[static_cast<size_t>(s_rows[r]) * W + c];
   }
+}
+
+constexpr int kRowWarps = 8;
+
+// The appended rows' rotations and SH coefficients (copies of their source
+// rows), one warp per 32 appended rows.
+__global__ void __launch_bounds__(32 * kRowWarps)
+    k_duplicate_rows(const uint32_t* __restrict__ grow_src, uint32_t n_grow, uint32_t n0, Set params) {
+  __shared__ uint32_t s_rows[kRowWarps][32];
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const uint32_t wb = (blockIdx.x * kRowWarps + warp) * 32u;
+  if (wb >= n_grow) return;
+  const uint32_t cnt = min(32u, n_grow - wb);
+  if (lane < cnt) s_rows[warp][lane] = grow_src[wb + lane];
+  __syncwarp();
+  const size_t d = static_cast<size_t>(n0) + wb;
+  copy_rows<4>(params.p[2], params.p[2] + 4 * d, s_rows[warp], cnt, lane);
+  copy_rows<3>(params.p[4], params.p[4] + 3 * d, s_rows[warp], cnt, lane);
+  copy_rows<45>(params.p[5], params.p[5] + 45 * d, s_rows[warp], cnt, lane);
 }
 
 // default.cu:309-332
@@ -234,14 +256,30 @@ __global__ void __launch_bounds__(kBlock)
   if (threadIdx.x == 0) block_counts[blockIdx.x] = c;
 }
 
-// rows of the kept list gathered into scratch (copied back by the host)
-__global__ void k_gather_rows(const float* __restrict__ src, float* __restrict__ dst, const uint32_t* __restrict__ list,
-                              uint32_t n_rows, int width) {
-  const size_t total = static_cast<size_t>(n_rows) * width;
-  for (size_t e = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; e < total;
-       e += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t row = e / width, c = e - row * width;
-    dst[e] = src[static_cast<size_t>(list[row]) * width + c];
+// rows of the kept list gathered into scratch (copied back by the host), one
+// warp per 32 kept rows of width W
+template <int W>
+__global__ void __launch_bounds__(32 * kRowWarps)
+    k_gather_rows(const float* __restrict__ src, float* __restrict__ dst, const uint32_t* __restrict__ list,
+                  uint32_t n_rows) {
+  __shared__ uint32_t s_rows[kRowWarps][32];
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  for (uint32_t wb = (blockIdx.x * kRowWarps + warp) * 32u; wb < n_rows; wb += gridDim.x * kRowWarps * 32u) {
+    const uint32_t cnt = min(32u, n_rows - wb);
+    if (lane < cnt) s_rows[warp][lane] = list[wb + lane];
+    __syncwarp();
+    copy_rows<W>(src, dst + static_cast<size_t>(wb) * W, s_rows[warp], cnt, lane);
+    __syncwarp();  // s_rows is refilled for the next 32 rows
+  }
+}
+
+void gather_rows(const float* src, float* dst, const uint32_t* list, uint32_t n_rows, int width, int blocks,
+                 cudaStream_t st) {
+  switch (width) {
+    case 1: k_gather_rows<1><<<blocks, 32 * kRowWarps, 0, st>>>(src, dst, list, n_rows); break;
+    case 3: k_gather_rows<3><<<blocks, 32 * kRowWarps, 0, st>>>(src, dst, list, n_rows); break;
+    case 4: k_gather_rows<4><<<blocks, 32 * kRowWarps, 0, st>>>(src, dst, list, n_rows); break;
+    default: k_gather_rows<45><<<blocks, 32 * kRowWarps, 0, st>>>(src, dst, list, n_rows); break;
   }
 }
 
@@ -391,8 +429,16 @@ int tgs_densify_step(TgsDensifier* d, TgsGaussians* params, TgsGaussians* grads,
       g.advance(count);
       rng->state = g.state;
       rng->inc = g.inc;
-      k_duplicate<<<(grows + kBlock - 1) / kBlock, kBlock, 0, st>>>(d->list, d->flags, grows, n0, P, G, M, V,
-                                                                     d->rnd);
+      k_duplicate<<<(grows + kBlock - 1) / kBlock, kBlock, 0, st>>>(d->list, d->flags, grows, n0, P, d->rnd);
+      const uint32_t row_warps = (grows + 31u) / 32u;
+      k_duplicate_rows<<<(row_warps + kRowWarps - 1) / kRowWarps, 32 * kRowWarps, 0, st>>>(d->list, grows, n0, P);
+      // gradients and moments of the appended rows are zero
+      const Set zero_sets[3] = {G, M, V};
+      for (const Set& zs : zero_sets)
+        for (int seg = 0; seg < 6; ++seg)
+          if (zs.p[seg] != nullptr)
+            cudaMemsetAsync(zs.p[seg] + static_cast<size_t>(n0) * seg_width(seg), 0,
+                            sizeof(float) * seg_width(seg) * static_cast<size_t>(grows), st);
     }
     n = n0 + grows;
     // prune
@@ -417,7 +463,7 @@ int tgs_densify_step(TgsDensifier* d, TgsGaussians* params, TgsGaussians* grads,
           float* p = s.p[seg];
           if (p == nullptr) continue;
           const int w = seg_width(seg);
-          k_gather_rows<<<d->num_sms * 8, 256, 0, st>>>(p, d->scratch, d->list, kept, w);
+          gather_rows(p, d->scratch, d->list, kept, w, d->num_sms * 8, st);
           cudaMemcpyAsync(p, d->scratch, sizeof(float) * w * static_cast<size_t>(kept), cudaMemcpyDeviceToDevice,
                           st);
         }

@@ -138,6 +138,27 @@ def test_binning_large_footprints_use_warp_path(oracle, cuda_lib):
     _check_instance_lists(gb, gp, ob, op["fragile"])
 
 
+def test_binning_many_super_tiles_multi_pass(oracle, cuda_lib, fp16):
+    """3840x2160 has 30 x 34 = 1020 super-tiles: the entry sort takes two
+    passes and the super-tile ranges come from the boundary search instead of
+    the single pass's digit totals."""
+    cfg, params, sh, cam = scene("cfg0", n=4000)
+    f = 3840 / 256
+    cam = dict(cam, width=3840, height=2160, fx=cam["fx"] * f, fy=cam["fy"] * f, cx=1920.0, cy=1080.0)
+    run = GpuRun(params, sh, cam, fp16).forward()
+    assert run.counts.overflow == 0
+    gp, gb = run.prims(), run.bins()
+    op = oracle.preprocess(params, sh, cam, fp16)
+    ob = oracle.binning(op, cam, fp16)
+    _check_instance_lists(gb, gp, ob, op["fragile"])
+    gp2 = dict(gp)
+    gp2["fragile"] = np.zeros(params["means"].shape[0], np.uint8)
+    ob2 = oracle.binning(gp2, cam, fp16)
+    if (op["fragile"] == 0).all():
+        np.testing.assert_array_equal(ob2["inst_prim"], gb["inst_prim"])
+        np.testing.assert_array_equal(ob2["inst_tile"], gb["inst_tile"])
+
+
 # ---------------------------------------------------------- blend forward
 
 def test_blend_forward_matches_oracle(oracle, cuda_lib, fp16):

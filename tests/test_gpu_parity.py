@@ -145,7 +145,7 @@ def test_binning_many_super_tiles_multi_pass(oracle, cuda_lib, fp16):
     cfg, params, sh, cam = scene("cfg0", n=4000)
     f = 3840 / 256
     cam = dict(cam, width=3840, height=2160, fx=cam["fx"] * f, fy=cam["fy"] * f, cx=1920.0, cy=1080.0)
-    run = GpuRun(params, sh, cam, fp16).forward()
+    run = GpuRun(params, sh, cam, fp16, max_instances=2_000_000).forward()  # ~0.43M instances
     assert run.counts.overflow == 0
     gp, gb = run.prims(), run.bins()
     op = oracle.preprocess(params, sh, cam, fp16)

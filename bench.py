@@ -421,6 +421,7 @@ def run_ours(args):
     loss_sum = torch.zeros(1, device="cuda")
     loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
     loss = rt.FusedLoss(W, H)
+    loss.set_accumulate(False)  # writes the whole loss map and gradient image: no per-step zeroing
     stream = torch.cuda.current_stream()
 
     def make_raster(cap_inst):
@@ -462,8 +463,6 @@ def run_ours(args):
         ctx.fwd_input = view_of(k)
         if e2e and k + 1 < last:
             upload(k + 1)  # overlaps this step's forward
-        loss_map.zero_()
-        grad_image.zero_()
         rast.forward(ctx)
         if ev is not None:
             ev[0].record(stream)

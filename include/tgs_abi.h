@@ -300,6 +300,15 @@ TGS_API int tgs_loss_l1_ssim(TgsLoss* l, int32_t dtype, int32_t width, int32_t h
                      void* grad, float scale_l1, float scale_ssim,
                      float* loss_sum, tgs_stream_t stream);
 
+/* Accumulation mode of tgs_loss_l1_ssim on this handle (no counterpart in
+ * the reference, whose loss adds into buffers its trainer zeroes every step).
+ * accumulate != 0 (the default): loss_map and grad are added into, as in the
+ * reference.  accumulate == 0: tgs_loss_l1_ssim writes every element of the
+ * padded loss_map and grad (the values the accumulate mode would leave in
+ * zeroed buffers), so the caller needs no per-step zeroing; it requires
+ * scale_l1 != 0 or the padding pixels' values (zero) still being written. */
+TGS_API int tgs_loss_set_accumulate(TgsLoss* l, int32_t accumulate);
+
 /* Largest padded image (Wp * Hp pixels, e.g. 512 x 512) that
  * tgs_loss_l1_ssim_noalloc accepts. */
 #define TGS_NOALLOC_MAX_PIXELS 262144

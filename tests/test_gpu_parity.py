@@ -472,3 +472,30 @@ def test_stage_times_are_reported(cuda_lib):
     assert len(t) == 5 and all(x > 0 for x in t), t
     run.rast.set_stage_timing(False)
 
+
+
+def test_loss_overwrite_mode_equals_accumulate_into_zero(cuda_lib, fp16):
+    """tgs_loss_set_accumulate(0): the loss map and gradient come out as the
+    accumulating call leaves zeroed buffers, whatever they held before."""
+    from tinygs_b200 import scenes
+
+    W, H = 203, 117  # ragged: padding pixels in the last 8x8 tiles
+    dt = torch.float16 if fp16 else torch.float32
+    n = rt.image_numel(W, H)
+    rng = np.random.default_rng(3)
+    pred = torch.from_numpy(rng.random(n, dtype=np.float32)).to(dt).cuda()
+    tgt = torch.from_numpy(scenes.target_image(W, H, 4).reshape(-1)).to(dt).cuda()
+    loss = rt.FusedLoss(W, H)
+    lm0, g0 = torch.zeros(n, dtype=dt, device="cuda"), torch.zeros(n, dtype=dt, device="cuda")
+    s0 = torch.zeros(1, device="cuda")
+    loss.evaluate(pred, tgt, lm0, g0, W, H, grad_scaler=10.0, loss_sum=s0)
+    loss.set_accumulate(False)
+    lm1 = torch.full((n,), 7.0, dtype=dt, device="cuda")
+    g1 = torch.full((n,), -3.0, dtype=dt, device="cuda")
+    s1 = torch.zeros(1, device="cuda")
+    loss.evaluate(pred, tgt, lm1, g1, W, H, grad_scaler=10.0, loss_sum=s1)
+    torch.cuda.synchronize()
+    assert torch.equal(lm0, lm1) and torch.equal(g0, g1)
+    # the loss scalar is a float atomic sum over blocks: equal up to its order
+    assert abs(float(s0) - float(s1)) <= 1e-6 * abs(float(s0))
+    loss.close()

@@ -129,6 +129,7 @@ PROTOTYPES = {
                                    POINTER(TgsGaussians), _P, POINTER(TgsDensifyConfig), c_int32, POINTER(TgsPcg32),
                                    POINTER(c_int64), _P]),
     "tgs_status_string": (c_char_p, [c_int32]),
+    "tgs_loss_set_accumulate": (c_int32, [c_void_p, c_int32]),
     "tgs_version": (c_char_p, []),
 }
 

@@ -85,6 +85,7 @@ void mark(TgsRaster* r, int k, cudaStream_t st) {
 struct TgsLoss {
   float* partials = nullptr;
   int32_t max_w = 0, max_h = 0;
+  int32_t accumulate = 1;  // tgs_loss_l1_ssim adds into loss_map / grad
 };
 
 namespace {
@@ -492,10 +493,16 @@ int tgs_loss_l1_ssim(TgsLoss* l, int32_t dtype, int32_t width, int32_t height, c
   if (width > l->max_w || height > l->max_h) return TGS_ERR_CAPACITY;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (loss_sum != nullptr) cudaMemsetAsync(loss_sum, 0, sizeof(float), st);
-  if (scale_l1 == 0.0f && scale_ssim == 0.0f) return cuda_status(cudaGetLastError());
+  if (scale_l1 == 0.0f && scale_ssim == 0.0f && l->accumulate) return cuda_status(cudaGetLastError());
   launch_ssim(dtype == TGS_FLOAT16, width, height, pred, target, loss_map, grad, scale_ssim, scale_l1, l->partials,
-              loss_sum, st);
+              loss_sum, st, l->accumulate);
   return cuda_status(cudaGetLastError());
+}
+
+int tgs_loss_set_accumulate(TgsLoss* l, int32_t accumulate) {
+  if (l == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  l->accumulate = accumulate != 0 ? 1 : 0;
+  return TGS_OK;
 }
 
 int tgs_adam_step(const TgsGaussians* params, const TgsGaussians* grads, const TgsGaussians* exp_avg,

@@ -124,7 +124,7 @@ void launch_l1(int fp16, int width, int height, const void* pred, const void* ta
                void* loss_map, void* grad, float scale, cudaStream_t stream);
 void launch_ssim(int fp16, int width, int height, const void* pred, const void* target,
                  void* loss_map, void* grad, float scale_ssim, float scale_l1, float* partials,
-                 float* loss_sum, cudaStream_t stream);
+                 float* loss_sum, cudaStream_t stream, int accumulate = 1);
 
 // data-parallel Adam over peer memory (adam.cu): params/grads hold one
 // entry per rank (pointers valid in this process)

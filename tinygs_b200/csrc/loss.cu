@@ -134,7 +134,7 @@ template <int kFp16>
 __global__ void __launch_bounds__(256)
     k_ssim_forward(DevCamera cam, const void* __restrict__ pred, const void* __restrict__ target,
                    void* __restrict__ loss_map, void* __restrict__ grad, float s_ssim, float s_l1,
-                   float* __restrict__ partials, float* __restrict__ loss_sum) {
+                   float* __restrict__ partials, float* __restrict__ loss_sum, int accumulate) {
   __shared__ __half2 tile[kInH][kInStride];  // (pred, target)
   __shared__ float hsum[5][kInH][kSumStride];
   const int x0 = blockIdx.x * kOut, y0 = blockIdx.y * kOut;
@@ -212,14 +212,16 @@ __global__ void __launch_bounds__(256)
   // every global load of the four pixels first, then the arithmetic, then
   // the stores; fp16 images inside the picture come from the staged window
   // (exact), the L1 term's padding pixels from memory
+  // accumulate == 0: every pixel of the padded extent is written (from zero)
   uint32_t pis[4];
-  bool l1_on[4], in_img[4];
+  bool l1_on[4], in_img[4], in_pad[4];
   float pv[4], tv[4], lm[4], gr[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int py = y0 + q0 + k;
     pis[k] = ch + tiled_index(static_cast<uint32_t>(py), static_cast<uint32_t>(px), cam.tiled_w);
-    l1_on[k] = s_l1 != 0.f && static_cast<uint32_t>(px) < cam.tiled_w * 8u && static_cast<uint32_t>(py) < cam.tiled_h * 8u;
+    in_pad[k] = static_cast<uint32_t>(px) < cam.tiled_w * 8u && static_cast<uint32_t>(py) < cam.tiled_h * 8u;
+    l1_on[k] = s_l1 != 0.f && in_pad[k];
     in_img[k] = px < W && py < H;
     pv[k] = tv[k] = lm[k] = gr[k] = 0.f;
     if (l1_on[k]) {
@@ -231,9 +233,9 @@ __global__ void __launch_bounds__(256)
         pv[k] = load_px<kFp16>(pred, pis[k]);
         tv[k] = load_px<kFp16>(target, pis[k]);
       }
-      if (grad != nullptr) gr[k] = load_px<kFp16>(grad, pis[k]);
+      if (grad != nullptr && accumulate) gr[k] = load_px<kFp16>(grad, pis[k]);
     }
-    if (loss_map != nullptr && (l1_on[k] || in_img[k])) lm[k] = load_px<kFp16>(loss_map, pis[k]);
+    if (loss_map != nullptr && accumulate && (l1_on[k] || in_img[k])) lm[k] = load_px<kFp16>(loss_map, pis[k]);
   }
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -248,6 +250,8 @@ __global__ void __launch_bounds__(256)
       contrib += fabsf(d) * s_l1;
       lmv = round_px<kFp16>(fmaf(fabsf(d), s_l1, lmv));
       if (grad != nullptr) store_px<kFp16>(grad, pi, round_px<kFp16>(fmaf(copysignf(1.0f, d), s_l1, gr[k])));
+    } else if (!accumulate && grad != nullptr && in_pad[k]) {
+      store_px<kFp16>(grad, pi, 0.0f);
     }
     if (in_img[k]) {
       const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(256)
         partials[pi + 2 * plane3] = (2.f * Cc) / (A * B);
       }
     }
-    if (loss_map != nullptr && (l1_on[k] || in_img[k])) store_px<kFp16>(loss_map, pi, lmv);
+    if (loss_map != nullptr && (l1_on[k] || in_img[k] || (!accumulate && in_pad[k]))) store_px<kFp16>(loss_map, pi, lmv);
   }
   if (loss_sum != nullptr) {
     const float t = block_sum_256(contrib);
@@ -377,17 +381,19 @@ void launch_l1(int fp16, int width, int height, const void* pred, const void* ta
 // scale_l1 == 0 disables the fused L1 term; grad == nullptr skips the backward.
 void launch_ssim(int fp16, int width, int height, const void* pred, const void* target, void* loss_map,
                  void* grad, float scale_ssim, float scale_l1, float* partials, float* loss_sum,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, int accumulate) {
   const DevCamera g = image_geometry(width, height);
   const dim3 grid((width + kOut - 1) / kOut, (height + kOut - 1) / kOut, 3);
   const float s_ssim = scale_ssim / static_cast<float>(width * height);
   const float s_l1 = scale_l1 / static_cast<float>(width * height * 3);
   float* parts = grad != nullptr ? partials : nullptr;
   if (fp16) {
-    k_ssim_forward<1><<<grid, 256, 0, stream>>>(g, pred, target, loss_map, grad, s_ssim, s_l1, parts, loss_sum);
+    k_ssim_forward<1><<<grid, 256, 0, stream>>>(g, pred, target, loss_map, grad, s_ssim, s_l1, parts, loss_sum,
+                                                accumulate);
     if (grad != nullptr) k_ssim_backward<1><<<grid, 256, 0, stream>>>(g, pred, target, grad, s_ssim, partials);
   } else {
-    k_ssim_forward<0><<<grid, 256, 0, stream>>>(g, pred, target, loss_map, grad, s_ssim, s_l1, parts, loss_sum);
+    k_ssim_forward<0><<<grid, 256, 0, stream>>>(g, pred, target, loss_map, grad, s_ssim, s_l1, parts, loss_sum,
+                                                accumulate);
     if (grad != nullptr) k_ssim_backward<0><<<grid, 256, 0, stream>>>(g, pred, target, grad, s_ssim, partials);
   }
 }

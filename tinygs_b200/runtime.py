@@ -266,6 +266,12 @@ class FusedLoss:
         self.handle = h
         self.w_l1, self.w_ssim = w_l1, w_ssim
 
+    def set_accumulate(self, accumulate: bool) -> None:
+        """False: evaluate() writes every element of the padded loss map and
+        gradient (what the accumulating mode leaves in zeroed buffers), so no
+        per-step zeroing is needed (tgs_loss_set_accumulate)."""
+        check(self.lib.tgs_loss_set_accumulate(self.handle, 1 if accumulate else 0), "tgs_loss_set_accumulate")
+
     def close(self):
         if getattr(self, "handle", None) is not None and self.handle.value:
             self.lib.tgs_loss_destroy(self.handle)

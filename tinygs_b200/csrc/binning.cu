@@ -373,14 +373,34 @@ __global__ void __launch_bounds__(kScanBlock)
     r = super_rect(bounds[prim]);
   }
   uint32_t total;
-  const uint32_t off = block_exclusive_scan(r.nsx * r.nsy, total) + block_offsets[blockIdx.x];
-  if (!active) return;
-  uint32_t o = off;
-  for (uint32_t y = 0; y < r.nsy; ++y)
-    for (uint32_t x = 0; x < r.nsx; ++x, ++o) {
-      ent_key[o] = static_cast<uint16_t>((r.sy0 + y) * super_w + r.sx0 + x);
-      ent_prim[o] = prim;
+  const uint32_t cnt = r.nsx * r.nsy;
+  const uint32_t off = block_exclusive_scan(cnt, total) + block_offsets[blockIdx.x];
+  // the warp's entries laid end to end (they are contiguous in the output):
+  // lane j writes entry base + j of each round of 32, so every store is
+  // coalesced; the owner of an entry is the number of Gaussian starts up to
+  // it minus one (Gaussians with no entry start nowhere)
+  const unsigned full = 0xffffffffu;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t w_off = __shfl_sync(full, off, 0);
+  const uint32_t start = off - w_off;
+  const uint32_t w_total = __shfl_sync(full, start + cnt, 31);
+  const uint32_t lt = lanemask_lt();
+  uint32_t starts_before = 0;
+  for (uint32_t base = 0; base < w_total; base += 32u) {
+    const uint32_t sbit = cnt > 0u && start >= base && start < base + 32u ? 1u << (start - base) : 0u;
+    const uint32_t starts = __reduce_or_sync(full, sbit);
+    const uint32_t owner = (starts_before + __popc(starts & (lt | (1u << lane))) - 1u) & 31u;
+    starts_before += __popc(starts);
+    const uint32_t o_prim = __shfl_sync(full, prim, owner), o_start = __shfl_sync(full, start, owner);
+    const uint32_t o_x0 = __shfl_sync(full, r.sx0, owner), o_y0 = __shfl_sync(full, r.sy0, owner);
+    const uint32_t o_w = __shfl_sync(full, r.nsx, owner);
+    const uint32_t e = base + lane;
+    if (e < w_total) {
+      const uint32_t t = e - o_start, ty = t / o_w, tx = t - ty * o_w;
+      ent_key[w_off + e] = static_cast<uint16_t>((o_y0 + ty) * super_w + o_x0 + tx);
+      ent_prim[w_off + e] = o_prim;
     }
+  }
 }
 
 // 4a. [start, end) of each super-tile in the sorted entry list

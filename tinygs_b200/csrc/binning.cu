@@ -97,6 +97,7 @@ __device__ __forceinline__ void for_run(const uint32_t* src, uint32_t begin, uin
 __global__ void __launch_bounds__(1024)
     k_scan_sums(uint32_t* __restrict__ sums, uint32_t count, uint32_t* __restrict__ total_out,
                 DevCounts* __restrict__ counts, uint32_t cap, uint32_t overflow_bit) {
+  pdl_entry();
   __shared__ uint32_t warp_sums[32];
   const uint32_t t = threadIdx.x;
   const uint32_t per = (count + 1023u) / 1024u;
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(kScanBlock)
     k_compact_visible(const ushort4* __restrict__ bounds, const uint32_t* __restrict__ depth_key,
                       const uint32_t* __restrict__ block_offsets, uint32_t n, uint32_t* __restrict__ out_key,
                       uint32_t* __restrict__ out_idx) {
+  pdl_entry();
   const uint32_t i = blockIdx.x * kScanBlock + threadIdx.x;
   bool vis = false;
   if (i < n) {
@@ -162,6 +164,7 @@ __global__ void __launch_bounds__(kSortThreads)
     k_radix_hist(const K* __restrict__ keys, const uint32_t* __restrict__ count_ptr,
                  const DevCounts* __restrict__ counts, int shift, int bits, uint32_t* __restrict__ hist,
                  uint32_t max_blocks) {
+  pdl_entry();
   constexpr int kWarps = kSortThreads / 32;
   __shared__ uint32_t h[kWarps][kRadix];
   const uint32_t mask = (1u << bits) - 1u;
@@ -206,6 +209,7 @@ __global__ void __launch_bounds__(kSortThreads)
 __global__ void __launch_bounds__(kSortThreads)
     k_radix_scan(uint32_t* __restrict__ hist, const uint32_t* __restrict__ count_ptr,
                  const DevCounts* __restrict__ counts, uint32_t max_blocks, uint32_t* __restrict__ digit_total) {
+  pdl_entry();
   const uint32_t d = blockIdx.x;
   const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
   const uint32_t nb = (n + kSortTile - 1) / kSortTile;
@@ -235,6 +239,7 @@ __global__ void __launch_bounds__(kSortThreads)
                     const uint32_t* __restrict__ count_ptr, const DevCounts* __restrict__ counts, int shift,
                     int bits, const uint32_t* __restrict__ hist, uint32_t max_blocks,
                     const uint32_t* __restrict__ digit_total) {
+  pdl_entry();
   constexpr int kWarps = kSortThreads / 32;
   constexpr int kPerWarp = kSortTile / kWarps;  // 256
   __shared__ uint32_t s_cnt[kWarps][kRadix];    // running counts, then per-warp offsets
@@ -342,6 +347,7 @@ __device__ __forceinline__ SuperRect super_rect(ushort4 b) {
 __global__ void __launch_bounds__(kScanBlock)
     k_entry_block_sums(const uint32_t* __restrict__ sorted_idx, const ushort4* __restrict__ bounds,
                        const DevCounts* __restrict__ counts, uint32_t* __restrict__ sums) {
+  pdl_entry();
   const uint32_t k = blockIdx.x * kScanBlock + threadIdx.x;
   uint32_t v = 0;
   if (k < counts->n_visible) {
@@ -364,6 +370,7 @@ __global__ void __launch_bounds__(kScanBlock)
     k_create_entries(const uint32_t* __restrict__ sorted_idx, const ushort4* __restrict__ bounds,
                      const uint32_t* __restrict__ block_offsets, const DevCounts* __restrict__ counts,
                      uint32_t super_w, uint16_t* __restrict__ ent_key, uint32_t* __restrict__ ent_prim) {
+  pdl_entry();
   const uint32_t k = blockIdx.x * kScanBlock + threadIdx.x;
   const bool active = k < counts->n_visible && counts->overflow == 0u;
   uint32_t prim = 0;
@@ -406,6 +413,7 @@ __global__ void __launch_bounds__(kScanBlock)
 // 4a. [start, end) of each super-tile in the sorted entry list
 __global__ void k_super_ranges(const uint16_t* __restrict__ keys, const DevCounts* __restrict__ counts,
                                uint2* __restrict__ ranges) {
+  pdl_entry();
   const uint32_t n = counts->overflow ? 0u : counts->n_entries;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const uint16_t k = keys[i];
@@ -422,6 +430,7 @@ __global__ void k_super_ranges(const uint16_t* __restrict__ keys, const DevCount
 __global__ void __launch_bounds__(1024)
     k_chunk_table(uint2* __restrict__ super_ranges, const uint32_t* __restrict__ totals, uint32_t n_super,
                   uint4* __restrict__ chunks, uint32_t* __restrict__ super_chunk, DevCounts* __restrict__ counts) {
+  pdl_entry();
   __shared__ uint32_t warp_sums[32];
   const uint32_t t = threadIdx.x;
   const uint32_t per = (n_super + 1023u) / 1024u;
@@ -515,6 +524,7 @@ __global__ void __launch_bounds__(kScanBlock)
                  const DevCounts* __restrict__ counts, uint32_t super_w, uint32_t* __restrict__ masks,
                  uint32_t* __restrict__ chunk_counts, uint32_t* __restrict__ sub_offsets,
                  uint32_t* __restrict__ n_touched) {
+  pdl_entry();
   static_assert(kSubChunk == kScanBlock, "one block pass per emission sub-chunk");
   __shared__ uint32_t s_cnt[kSubChunks * kSuperTiles];
   // each entry's test inputs and rectangle, read by the lanes that test its
@@ -646,6 +656,7 @@ __global__ void k_chunk_prefix(const uint2* __restrict__ super_ranges, const uin
                                uint32_t n_super, uint32_t super_w, uint32_t grid_w, uint32_t grid_h,
                                const DevCounts* __restrict__ counts, uint32_t* __restrict__ chunk_counts,
                                uint32_t* __restrict__ tile_total) {
+  pdl_entry();
   const uint32_t id = blockIdx.x * blockDim.x + threadIdx.x;
   if (id >= n_super * kSuperTiles) return;
   const uint32_t sp = id / kSuperTiles, j = id % kSuperTiles;
@@ -680,6 +691,7 @@ __global__ void __launch_bounds__(1024)
     k_tile_offsets(const uint32_t* __restrict__ tile_total, uint32_t n_tiles, uint2* __restrict__ ranges,
                    uint32_t* __restrict__ bucket_offsets, DevCounts* __restrict__ counts, uint32_t cap_inst,
                    uint32_t cap_buckets) {
+  pdl_entry();
   __shared__ uint32_t s_inst[32], s_buck[32];
   const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
   const uint32_t per = (n_tiles + 1023u) / 1024u;
@@ -749,6 +761,7 @@ __global__ void __launch_bounds__(32 * kEmitWarps)
                      const uint32_t* __restrict__ sub_offsets, const uint2* __restrict__ ranges,
                      const DevCounts* __restrict__ counts, uint32_t super_w, uint32_t grid_w, uint32_t grid_h,
                      uint32_t* __restrict__ inst_prim) {
+  pdl_entry();
   const unsigned full = 0xffffffffu;
   const uint32_t n_units = counts->overflow ? 0u : counts->n_chunks * kSubChunks;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
@@ -805,13 +818,12 @@ void radix_sort(K* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, const 
   for (int shift = 0; shift < total_bits; shift += kRadixBits) {
     const int bits = min(kRadixBits, total_bits - shift);
     if (blocks > 0) {
-      k_radix_hist<K><<<blocks, kSortThreads, 0, stream>>>(keys[cur], count_ptr, counts, shift, bits, s.sort_hist,
-                                                             max_blocks);
-      k_radix_scan<<<kRadix, kSortThreads, 0, stream>>>(s.sort_hist, count_ptr, counts, max_blocks,
-                                                         s.sort_digit_total);
-      k_radix_scatter<K><<<blocks, kSortThreads, 0, stream>>>(keys[cur], vals[cur], keys[1 - cur], vals[1 - cur],
-                                                                count_ptr, counts, shift, bits, s.sort_hist,
-                                                                max_blocks, s.sort_digit_total);
+      pdl_launch(k_radix_hist<K>, blocks, kSortThreads, 0, stream, keys[cur], count_ptr, counts, shift, bits,
+                 s.sort_hist, max_blocks);
+      pdl_launch(k_radix_scan, kRadix, kSortThreads, 0, stream, s.sort_hist, count_ptr, counts, max_blocks,
+                 s.sort_digit_total);
+      pdl_launch(k_radix_scatter<K>, blocks, kSortThreads, 0, stream, keys[cur], vals[cur], keys[1 - cur],
+                 vals[1 - cur], count_ptr, counts, shift, bits, s.sort_hist, max_blocks, s.sort_digit_total);
     }
     cur = 1 - cur;
   }
@@ -828,20 +840,20 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   const uint32_t n_super = super_w * super_h;
   DevCounts* counts = s.counts;
   // 1. compaction (block sums were written by the preprocess kernel)
-  k_scan_sums<<<1, 1024, 0, stream>>>(s.block_sums, n_blocks, &counts->n_visible, nullptr, 0, 0);
+  pdl_launch(k_scan_sums, 1, 1024, 0, stream, s.block_sums, n_blocks, &counts->n_visible, nullptr, 0, 0);
   if (n_blocks > 0)
-    k_compact_visible<<<n_blocks, kScanBlock, 0, stream>>>(s.bounds, s.depth_key, s.block_sums, n, s.vis_key[0],
-                                                            s.vis_idx[0]);
+    pdl_launch(k_compact_visible, n_blocks, kScanBlock, 0, stream, s.bounds, s.depth_key, s.block_sums, n,
+               s.vis_key[0], s.vis_idx[0]);
   // 2. depth sort (32-bit keys)
   radix_sort<uint32_t>(s.vis_key, s.vis_idx, &counts->n_visible, nullptr, n64, 32, s.depth_result, s, stream);
   const uint32_t* sorted = s.vis_idx[s.depth_result];
   // 3. super-tile entries in depth order, sorted by super-tile
   if (n_blocks > 0) {
-    k_entry_block_sums<<<n_blocks, kScanBlock, 0, stream>>>(sorted, s.bounds, counts, s.block_sums);
-    k_scan_sums<<<1, 1024, 0, stream>>>(s.block_sums, n_blocks, &counts->n_entries, counts,
-                                         static_cast<uint32_t>(s.cap_entries), kOverflowEntries);
-    k_create_entries<<<n_blocks, kScanBlock, 0, stream>>>(sorted, s.bounds, s.block_sums, counts, super_w,
-                                                           s.ent_key[0], s.ent_prim[0]);
+    pdl_launch(k_entry_block_sums, n_blocks, kScanBlock, 0, stream, sorted, s.bounds, counts, s.block_sums);
+    pdl_launch(k_scan_sums, 1, 1024, 0, stream, s.block_sums, n_blocks, &counts->n_entries, counts,
+               static_cast<uint32_t>(s.cap_entries), kOverflowEntries);
+    pdl_launch(k_create_entries, n_blocks, kScanBlock, 0, stream, sorted, s.bounds, s.block_sums, counts, super_w,
+               s.ent_key[0], s.ent_prim[0]);
   }
   int super_bits = 1;
   while ((1u << super_bits) < n_super) ++super_bits;
@@ -852,32 +864,28 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   // 4. chunks of each super-tile's entry list
   if (super_bits <= kRadixBits) {
     // one pass: its digit totals are the super-tiles' entry counts
-    k_chunk_table<<<1, 1024, 0, stream>>>(s.super_ranges, s.sort_digit_total, n_super, s.chunks, s.super_chunk,
-                                          counts);
+    pdl_launch(k_chunk_table, 1, 1024, 0, stream, s.super_ranges, s.sort_digit_total, n_super, s.chunks,
+               s.super_chunk, counts);
   } else {
     cudaMemsetAsync(s.super_ranges, 0, sizeof(uint2) * n_super, stream);
-    k_super_ranges<<<s.num_sms * 8, 256, 0, stream>>>(ent_key, counts, s.super_ranges);
-    k_chunk_table<<<1, 1024, 0, stream>>>(s.super_ranges, nullptr, n_super, s.chunks, s.super_chunk, counts);
+    pdl_launch(k_super_ranges, s.num_sms * 8, 256, 0, stream, ent_key, counts, s.super_ranges);
+    pdl_launch(k_chunk_table, 1, 1024, 0, stream, s.super_ranges, nullptr, n_super, s.chunks, s.super_chunk, counts);
   }
   // 5. hit masks and counts, then every (chunk, tile)'s first slot
   const int persistent = s.num_sms * 8;
   if (fp16)
-    k_chunk_hits<1><<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.bounds, s.mean2d, s.conic_opacity,
-                                                            s.prim_info, counts, super_w, s.masks, s.chunk_counts,
-                                                            s.sub_offsets, s.n_touched);
+    pdl_launch(k_chunk_hits<1>, persistent, kScanBlock, 0, stream, s.chunks, ent_prim, s.bounds, s.mean2d,
+               s.conic_opacity, s.prim_info, counts, super_w, s.masks, s.chunk_counts, s.sub_offsets, s.n_touched);
   else
-    k_chunk_hits<0><<<persistent, kScanBlock, 0, stream>>>(s.chunks, ent_prim, s.bounds, s.mean2d, s.conic_opacity,
-                                                            s.prim_info, counts, super_w, s.masks, s.chunk_counts,
-                                                            s.sub_offsets, s.n_touched);
-  k_chunk_prefix<<<(n_super * kSuperTiles + 255) / 256, 256, 0, stream>>>(
-      s.super_ranges, s.super_chunk, n_super, super_w, cam.grid_w, cam.grid_h, counts, s.chunk_counts,
-      s.tile_total);
-  k_tile_offsets<<<1, 1024, 0, stream>>>(s.tile_total, n_tiles, s.ranges, s.bucket_offsets, counts,
-                                          static_cast<uint32_t>(s.cap_inst), static_cast<uint32_t>(s.cap_buckets));
+    pdl_launch(k_chunk_hits<0>, persistent, kScanBlock, 0, stream, s.chunks, ent_prim, s.bounds, s.mean2d,
+               s.conic_opacity, s.prim_info, counts, super_w, s.masks, s.chunk_counts, s.sub_offsets, s.n_touched);
+  pdl_launch(k_chunk_prefix, (n_super * kSuperTiles + 255) / 256, 256, 0, stream, s.super_ranges, s.super_chunk,
+             n_super, super_w, cam.grid_w, cam.grid_h, counts, s.chunk_counts, s.tile_total);
+  pdl_launch(k_tile_offsets, 1, 1024, 0, stream, s.tile_total, n_tiles, s.ranges, s.bucket_offsets, counts,
+             static_cast<uint32_t>(s.cap_inst), static_cast<uint32_t>(s.cap_buckets));
   // 6. instances at their final slots
-  k_emit_instances<<<s.num_sms * 16, 32 * kEmitWarps, 0, stream>>>(s.chunks, ent_prim, s.masks, s.chunk_counts,
-                                                                    s.sub_offsets, s.ranges, counts, super_w,
-                                                                    cam.grid_w, cam.grid_h, s.inst_prim[0]);
+  pdl_launch(k_emit_instances, s.num_sms * 16, 32 * kEmitWarps, 0, stream, s.chunks, ent_prim, s.masks,
+             s.chunk_counts, s.sub_offsets, s.ranges, counts, super_w, cam.grid_w, cam.grid_h, s.inst_prim[0]);
   s.tile_result = 0;
 }
 

@@ -7,6 +7,35 @@
 
 namespace tgs {
 
+// Programmatic dependent launch.  A kernel launched with pdl_launch may be
+// scheduled while the kernel before it on the stream is finishing; its
+// pdl_entry() (first statement of the kernel) waits until that kernel has
+// completed and its memory is visible, then allows the next kernel to be
+// scheduled once every block of this one has got that far.  Results are the
+// same as with plain launches; the launch latency and the ramp of the next
+// grid overlap the tail of the current one.  A kernel without the launch
+// attribute passes the wait at once.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline void pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Rendering constants of the reference rasterizer
 // (tinygs/src/rasterizer/fastgs_ours/rasterization_config.h:18-40 and
 //  tinygs/src/rasterizer/fastgs_ours_fp16/rasterization_config.h:21-45).

@@ -15,16 +15,20 @@
 //      super-tile (one 8-bit pass for up to 256 super-tiles),
 //   4. the entry list of each super-tile is cut into chunks of 1024 entries;
 //      per chunk, the exact tile tests of each entry give a 32-bit hit mask
-//      and per-tile counts (and each Gaussian's touched-tile total),
+//      and per-tile counts of each 256-entry sub-chunk (and each Gaussian's
+//      touched-tile total),
 //   5. scans give every (chunk, tile) its first slot: tiles in index order,
 //      chunks in depth order inside a tile; the per-tile [start, end) ranges
 //      and bucket offsets fall out of the same scan,
-//   6. per chunk, stable ranks of the entries in each tile (ballots over the
-//      hit masks) place every instance at its final slot.
+//   6. per 256-entry sub-chunk (one warp), stable ranks of the entries in
+//      each tile (ballots over the hit masks) place every instance at its
+//      final slot.
 // Ties among equal depths follow the index order, a deterministic member of
 // the reference's order set (its ties follow atomic arrival order).  All
-// counts stay on the device: the launches are sized from capacities and each
-// kernel reads the live count.
+// counts stay on the device: the launches are sized from capacities (or the
+// resident blocks, for grid-stride kernels) and each kernel reads the live
+// count.  The kernels are chained with programmatic dependent launch
+// (pdl_launch / pdl_entry).
 #include <cstring>
 
 #include "kernels.h"

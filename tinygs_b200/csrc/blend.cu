@@ -1,7 +1,8 @@
 // blend.cu -- per-tile front-to-back alpha blending, forward and backward.
 //
 // Forward (one CTA per 16x16 tile): primitives are staged through shared
-// memory in batches, each pixel composites front to back until its
+// memory in batches (fp16: one 36-byte record per primitive, read with
+// broadcast vector loads), each pixel composites front to back until its
 // transmittance would drop below 1e-4, and every 32 primitives the running
 // (colour, transmittance) of every pixel is checkpointed so that the
 // backward can restart any 32-primitive bucket independently.
@@ -10,11 +11,14 @@
 //   arithmetic, two horizontally adjacent pixels per thread, colour and
 //   transmittance carried scaled by 255)
 // Backward (one warp per bucket, one lane per primitive): the 256 pixels of
-// the tile stream through the warp as a diagonal wavefront (lane l sees
-// pixel i - l at step i), so each pixel's state passes from primitive to
-// primitive in depth order by a one-lane shuffle.  Per-primitive sums are
-// reduced in registers and added to the per-Gaussian scratch with one set of
-// atomics per bucket.
+// the tile stream through the warp as two diagonal wavefronts (pixels 0-127
+// and 128-255, evaluated together with packed fp32x2 instructions; lane l
+// sees pixel i - l of each stream at step i), so each pixel's evolving state
+// (transmittance, colour still to come) passes from primitive to primitive in
+// depth order by a one-lane shuffle while its constant part (centre,
+// dL/dpixel) is read from a per-warp ring in shared memory.  Per-primitive
+// sums are reduced in registers and added to the per-Gaussian scratch with one
+// set of atomics per bucket.
 //   fp32 reference: fastgs_ours/kernels_backward.cuh:675-927
 //   fp16 reference: fastgs_ours_fp16/kernels_backward.cuh:861-1389; its
 //   semantics (no per-pixel contributor mask, alpha capped at fp16(0.99),

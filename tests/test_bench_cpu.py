@@ -24,3 +24,14 @@ def test_reference_arm_prints_contract_line():
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "iters/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_without_output():
+    import os
+
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", "cfg0",
+                          "--gpus", "2", "--steps", "1", "--warmup", "1", "--cpu-budget", "1"],
+                         capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.strip() == ""

@@ -148,8 +148,6 @@ def cpu_oracle_step_time(cfg_name: str, budget_s: float, fp32_math: bool = True,
     target = scenes.target_image(W, H, cfg.seed + 100).reshape(-1)
     fp16 = False if fp32_math else cfg.dtype == "float16"
     lib = O.load()
-    gw, gh = O.grid(cam)
-    n_tiles = gw * gh
     t = {}
     t0 = time.perf_counter()
     prims = O.preprocess(params, cfg.sh_degree, cam, fp16)
@@ -585,7 +583,6 @@ def run_ours(args):
     render_ms = r0.elapsed_time(r1) / args.steps
 
     counts = rast.counts()
-    counts_v = int(counts.n_visible)
     # Gaussians that touch a tile (the backward reads their screen gradients)
     touched_v = int((rast.debug_array(0, torch.int32, cfg.n) > 0).sum())
     ms_step = ms_dev / args.steps

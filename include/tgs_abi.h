@@ -320,11 +320,14 @@ TGS_API int tgs_loss_set_accumulate(TgsLoss* l, int32_t accumulate);
  * library (9 MiB held by every GPU that loads it, until exit) instead of
  * memory the caller allocates; the caller still passes inputs and outputs.
  * Same arguments and results as tgs_loss_l1_ssim without its first argument.
- * Returns TGS_ERR_CAPACITY if Wp * Hp exceeds TGS_NOALLOC_MAX_PIXELS.  The
- * first call on a device looks up the array's device address (make it
- * before any stream capture).  Every call on a device shares the array:
- * calls whose GPU work may overlap race on it and must be serialised.
- * Calls no cudaMalloc or cudaFree. */
+ * Returns TGS_ERR_CAPACITY if Wp * Hp exceeds TGS_NOALLOC_MAX_PIXELS.  Every
+ * call looks up the array's device address on the current device (make the
+ * first call before any stream capture).  The array is placed in device
+ * memory when the library's device code loads on a device, which with lazy
+ * module loading is the library's first call there: make that call before
+ * the host's pool reserves all free device memory.  Every call on a device
+ * shares the array: calls whose GPU work may overlap race on it and must be
+ * serialised.  Calls no cudaMalloc or cudaFree. */
 TGS_API int tgs_loss_l1_ssim_noalloc(int32_t dtype, int32_t width,
                                      int32_t height, const void* pred,
                                      const void* target, void* loss_map,

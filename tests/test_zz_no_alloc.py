@@ -31,8 +31,12 @@ def test_noalloc_loss_equals_allocating_loss_two_calls(dt):
     lib = _abi.load_library()
     dtype = _abi.TGS_FLOAT16 if dt == np.float16 else _abi.TGS_FLOAT32
     stream = torch.cuda.current_stream().cuda_stream
-    # a full-size call, then a smaller one that reuses the same fixed array
-    for call, (w, h, seed) in enumerate([(512, 512, 30), (200, 136, 40)]):
+    # a full-size call, then smaller ones that reuse the same fixed array:
+    # 509 x 507 pads to exactly TGS_NOALLOC_MAX_PIXELS, 203 x 131 has ragged
+    # edge tiles in both directions
+    shapes = [(512, 512, 30), (200, 136, 40), (509, 507, 50), (203, 131, 60)]
+    assert ((509 + 7) // 8 * 8) * ((507 + 7) // 8 * 8) == _abi.TGS_NOALLOC_MAX_PIXELS
+    for call, (w, h, seed) in enumerate(shapes):
         pred, tgt = _inputs(w, h, seed, dt)
         ref_loss, ref_grad = torch.zeros_like(pred), torch.zeros_like(pred)
         ref_sum = torch.zeros(1, device="cuda")

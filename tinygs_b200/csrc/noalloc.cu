@@ -15,38 +15,33 @@
 // between calls: the forward pass writes each map entry it later reads.
 // Calls whose work overlaps on the GPU (different streams, no ordering) race
 // on the array and must be serialised by the caller.
-#include <mutex>
-
+//
+// The array is placed in device memory when the library's device code is
+// loaded on a device.  With lazy module loading (the CUDA default) that is
+// the first call of this library on that device; a host that lets its own
+// pool reserve all free device memory must make that first call (for
+// example one warm-up call of this entry point) before the pool reserves
+// it, or the load fails and the call returns TGS_ERR_CUDA.
 #include "../../include/tgs_abi.h"
 #include "kernels.h"
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-
 // Three partial-derivative maps for each of the three channels.
 static __device__ __align__(256) float g_ssim_scratch[9 * static_cast<size_t>(TGS_NOALLOC_MAX_PIXELS)];
 
-std::mutex g_setup_mutex;
-float* g_scratch_ptr[kMaxDevices] = {};
-
-// The host-side name of a __device__ array is not a device address; the
-// device address is looked up once per device, with that device current,
-// on the first call made on it.
+// The host-side name of a __device__ array is not a device address.  The
+// device address is looked up on every call, with the caller's device
+// current: the lookup allocates nothing and costs about a microsecond, and a
+// cached address would go stale when the module is loaded again at another
+// address (after cudaDeviceReset, or in another driver-API context).
 int scratch_for_current_device(float** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return TGS_ERR_CUDA;
-  if (dev < 0 || dev >= kMaxDevices) return TGS_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_ssim_scratch) != cudaSuccess) {
-      cudaGetLastError();
-      return TGS_ERR_CUDA;
-    }
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_ssim_scratch) != cudaSuccess) {
+    cudaGetLastError();
+    return TGS_ERR_CUDA;
   }
-  *out = g_scratch_ptr[dev];
+  *out = static_cast<float*>(p);
   return TGS_OK;
 }
 

@@ -17,6 +17,16 @@ import torch
 import torch.distributed as dist
 
 
+def _as_torch_stream(stream) -> torch.cuda.Stream:
+    """`stream` as a torch stream object (None: the current stream; a raw
+    cudaStream_t handle is wrapped as an external stream)."""
+    if stream is None:
+        return torch.cuda.current_stream()
+    if isinstance(stream, torch.cuda.Stream):
+        return stream
+    return torch.cuda.ExternalStream(int(stream))
+
+
 @dataclass
 class DataParallel:
     world: int = 1
@@ -149,9 +159,13 @@ class PeerAdam:
             arr[r].sh_degree = like.sh_degree
         return arr
 
-    def barrier(self) -> None:
+    def barrier(self, stream=None) -> None:
+        """A one-element all-reduce ordered on `stream` (torch's current
+        stream if None): the exchange kernel launched on that stream runs
+        after every rank's earlier work on its own stream."""
         if self.dp.world > 1:
-            dist.all_reduce(self.flag, group=self.dp.group)
+            with torch.cuda.stream(_as_torch_stream(stream)):
+                dist.all_reduce(self.flag, group=self.dp.group)
 
     def step(self, gradient_scale: float, stream=None, events=None) -> None:
         """`events`: optional pair of CUDA events recorded around the kernel
@@ -163,7 +177,7 @@ class PeerAdam:
         G = self._sets(self.base_g, self.grads)
         m, v = self.exp_avg.abi(), self.exp_avg_sq.abi()
         cfg = self.cfg.abi()
-        self.barrier()  # every rank's gradients are written
+        self.barrier(stream)  # every rank's gradients are written
         if events is not None:
             events[0].record(stream)
         check(self.lib.tgs_dp_reduce_adam(P, G, self.dp.world, self.dp.rank, ctypes.byref(m), ctypes.byref(v),
@@ -171,7 +185,7 @@ class PeerAdam:
                                           rt._stream_handle(stream)), "tgs_dp_reduce_adam")
         if events is not None:
             events[1].record(stream)
-        self.barrier()  # every rank's parameters are updated
+        self.barrier(stream)  # every rank's parameters are updated
 
     def close(self) -> None:
         for p in self.opened:
@@ -229,9 +243,13 @@ class MulticastAdam:
         out.n, out.sh_degree = like.n, like.sh_degree
         return out
 
-    def barrier(self) -> None:
+    def barrier(self, stream=None) -> None:
+        """A one-element all-reduce ordered on `stream` (torch's current
+        stream if None): the exchange kernel launched on that stream runs
+        after every rank's earlier work on its own stream."""
         if self.dp.world > 1:
-            dist.all_reduce(self.flag, group=self.dp.group)
+            with torch.cuda.stream(_as_torch_stream(stream)):
+                dist.all_reduce(self.flag, group=self.dp.group)
 
     def step(self, gradient_scale: float, stream=None, events=None) -> None:
         if stream is None:
@@ -240,7 +258,7 @@ class MulticastAdam:
         pm, gm = self._mc_set(self.mc[0], self.params), self._mc_set(self.mc[1], self.grads)
         p, m, v = self.params.abi(), self.exp_avg.abi(), self.exp_avg_sq.abi()
         cfg = self.cfg.abi()
-        self.barrier()
+        self.barrier(stream)
         if events is not None:
             events[0].record(stream)
         check(self.lib.tgs_dp_reduce_adam_multicast(ctypes.byref(pm), ctypes.byref(gm), ctypes.byref(p),
@@ -249,7 +267,7 @@ class MulticastAdam:
                                                     rt._stream_handle(stream)), "tgs_dp_reduce_adam_multicast")
         if events is not None:
             events[1].record(stream)
-        self.barrier()
+        self.barrier(stream)
 
     def close(self) -> None:
         pass
@@ -315,9 +333,13 @@ class InboxAdam:
         """Arguments of FastGSB200Rasterizer.backward_routed after ctx."""
         return self.inboxes, self.slice_pad, self.dp.world, self.dp.rank
 
-    def barrier(self) -> None:
+    def barrier(self, stream=None) -> None:
+        """A one-element all-reduce ordered on `stream` (torch's current
+        stream if None): the exchange kernel launched on that stream runs
+        after every rank's earlier work on its own stream."""
         if self.dp.world > 1:
-            dist.all_reduce(self.flag, group=self.dp.group)
+            with torch.cuda.stream(_as_torch_stream(stream)):
+                dist.all_reduce(self.flag, group=self.dp.group)
 
     def step(self, gradient_scale: float, stream=None, events=None) -> None:
         if stream is None:
@@ -334,7 +356,7 @@ class InboxAdam:
             arr[r].n, arr[r].sh_degree = self.params.n, self.params.sh_degree
         m, v = self.exp_avg.abi(), self.exp_avg_sq.abi()
         cfg = self.cfg.abi()
-        self.barrier()  # every rank's routed gradients have landed
+        self.barrier(stream)  # every rank's routed gradients have landed
         if events is not None:
             events[0].record(stream)
         check(self.lib.tgs_dp_inbox_adam(arr, ctypes.c_void_p(self.inbox), self.slice_pad, self.dp.world,
@@ -343,7 +365,7 @@ class InboxAdam:
               "tgs_dp_inbox_adam")
         if events is not None:
             events[1].record(stream)
-        self.barrier()  # every rank's parameters are updated
+        self.barrier(stream)  # every rank's parameters are updated
 
     def close(self) -> None:
         for p in self.opened:

@@ -1,8 +1,12 @@
 """numpy/ctypes front end of the CPU oracle (oracle/tgs_oracle.c).
 
 TEST INFRASTRUCTURE ONLY -- imported by tests/, __graft_entry__.smoke() and
-bench.py's cpu_baseline leg as the checker.  Parity status: UNPINNED (the
-reference has no golden vectors for this path and cannot be built here).
+bench.py's cpu_baseline leg as the checker.  Parity status: pinned to the
+reference's own kernels for the rasterizer and the losses through the golden
+vectors in tests/golden/ (made by tests/golden/make_reference_golden.py from
+oracle/_ref, the reference's CUDA sources built unchanged); the optimizer
+and densification restatements are pinned by formula and published-vector
+tests only (the reference ships no golden vectors for this path).
 """
 from __future__ import annotations
 
@@ -46,6 +50,14 @@ def _p(a: np.ndarray | None):
         return None
     assert a.flags["C_CONTIGUOUS"], "oracle buffers must be C-contiguous"
     return a.ctypes.data_as(c_void_p)
+
+
+def set_fragile_f16(rel: float) -> None:
+    """Width of the fp16 path's fragile band around the tile-test threshold
+    (relative to max(|threshold|, 1)); rel <= 0 restores the default."""
+    lib = load()
+    lib.orc_set_fragile_f16.argtypes = [c_float]
+    lib.orc_set_fragile_f16(float(rel))
 
 
 def threads() -> int:
@@ -103,6 +115,35 @@ def prim_struct(prims: dict):
         a = prims.get(k)
         arrs.append(None if a is None else np.ascontiguousarray(a, dtype=dtypes[k]))
     return OrcPrimitives(*[_p(a) for a in arrs]), arrs
+
+
+def count_tiles(prims: dict, cam: dict, fp16: bool, band: float = 0.0):
+    """Per-Gaussian touched-tile counts recomputed from the screen-space
+    records in `prims` (the decision create_instances repeats).  With
+    band > 0, returns (counts, fragile) where fragile flags a tile test
+    within `band` of its threshold (relative to max(|threshold|, 1))."""
+    lib = load()
+    st, keep = prim_struct(prims)
+    n = prims["n_touched"].shape[0]
+    out = np.zeros(n, np.uint32)
+    fr = np.zeros(n, np.uint8)
+    c = camera(cam)
+    lib.orc_count_tiles(c_int64(n), ctypes.byref(st), ctypes.byref(c), c_int32(int(fp16)), _p(out), _p(fr),
+                        c_float(band), c_int32(threads()))
+    return (out, fr) if band > 0 else out
+
+
+def pixel_fragile(cam: dict, band: float):
+    """Starts recording blend decisions within `band` (relative) of their
+    thresholds; returns the per-pixel flag array the next blend forwards
+    fill.  pixel_fragile_off() stops it."""
+    buf = np.zeros(plane(cam), np.uint8)
+    load().orc_set_pixel_fragile(_p(buf), c_float(band))
+    return buf
+
+
+def pixel_fragile_off() -> None:
+    load().orc_set_pixel_fragile(None, c_float(0.0))
 
 
 def binning(prims: dict, cam: dict, fp16: bool, cap: int | None = None) -> dict:

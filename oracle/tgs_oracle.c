@@ -30,6 +30,26 @@ void orc_set_tile_stride(int32_t stride) { g_tile_stride = stride > 0 ? stride :
  * tile of the grid is touched, no alpha < 1/255 cut, no early termination),
  * of which the restated backward is the exact derivative. */
 static int g_smooth = 0;
+/* Width of the fp16 path's fragile band around the tile test's threshold,
+ * relative to max(|threshold|, 1).  The oracle's half-precision inputs come
+ * from IEEE fp32 arithmetic and the GPU's from fast-math fp32, which round
+ * to different half values for a small fraction of Gaussians (one half ulp,
+ * 2^-11 relative); tile decisions within a few half ulps of the threshold
+ * can then differ. */
+static float g_fragile_f16 = 2e-2f;
+void orc_set_fragile_f16(float rel) { g_fragile_f16 = rel > 0.0f ? rel : 2e-2f; }
+/* Optional per-pixel record of blend decisions near their thresholds (alpha
+ * against 1/255 and against its cap, the transmittance stop at 1e-4), within
+ * `g_pix_band` relative: the pixels whose value an end-to-end comparison
+ * from the parameters cannot pin, since upstream last-bit differences of a
+ * conic move such a decision.  One byte per pixel of the tiled plane. */
+static uint8_t* g_pix_fragile = NULL;
+static float g_pix_band = 0.0f;
+void orc_set_pixel_fragile(uint8_t* buf, float band) {
+    g_pix_fragile = buf;
+    g_pix_band = band;
+}
+static inline int near_rel(float v, float thr, float band) { return fabsf(v - thr) <= band * fabsf(thr); }
 void orc_set_smooth_forward(int32_t on) { g_smooth = on != 0; }
 
 /* ---------------------------------------------------------------- helpers */
@@ -450,7 +470,7 @@ void orc_preprocess(int64_t n, const float* means, const float* opacities,
             int c = fp16 ? tile_test_f16(smx, smy, hcx, hcy, hcz, tx_, ty_, thr, &margin)
                          : tile_test_f32(smx, smy, conic, tx_, ty_, thr, &margin);
             if (c || g_smooth) touched++;
-            float tol = fp16 ? 2e-2f * fmaxf(fabsf(thr), 1.f) : FRAGILE_REL * fmaxf(fabsf(thr), 1.f);
+            float tol = fp16 ? g_fragile_f16 * fmaxf(fabsf(thr), 1.f) : FRAGILE_REL * fmaxf(fabsf(thr), 1.f);
             if (isfinite(margin) && fabsf(margin) <= tol) fragile = 1;
         }
         out->fragile[i] = fragile;
@@ -509,6 +529,51 @@ static int cmp_keyidx(const void* a, const void* b) {
     const KeyIdx* y = (const KeyIdx*)b;
     if (x->key != y->key) return x->key < y->key ? -1 : 1;
     return x->idx < y->idx ? -1 : (x->idx > y->idx ? 1 : 0);
+}
+
+/* Exact touched-tile count of every Gaussian recomputed from its stored
+ * screen-space record (bounds, mean2d, conic + opacity or the fp16 record):
+ * the decision the reference's create_instances_cu repeats
+ * (fastgs_ours/kernels_forward.cuh:427-530, fp16 :517-631).  Gaussians with
+ * n_touched == 0 in `prim` get 0. */
+void orc_count_tiles(int64_t n, const OrcPrimitives* prim, const OrcCamera* cam, int32_t fp16,
+                     uint32_t* out, uint8_t* fragile, float band, int32_t n_threads) {
+    (void)cam;
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+#pragma omp parallel for schedule(dynamic, 4096)
+    for (int64_t i = 0; i < n; ++i) {
+        out[i] = 0;
+        if (fragile) fragile[i] = 0;
+        if (prim->n_touched[i] == 0) continue;
+        const uint16_t* b = prim->bounds + 4 * (size_t)i;
+        uint32_t bw = (uint32_t)(b[1] - b[0]);
+        uint32_t cnt = bw * (uint32_t)(b[3] - b[2]);
+        float smx = prim->mean2d[2 * i] - 0.5f, smy = prim->mean2d[2 * i + 1] - 0.5f;
+        float thr, conic[3] = {0.f, 0.f, 0.f};
+        uint16_t hc[4] = {0, 0, 0, 0};
+        if (fp16) {
+            memcpy(hc, prim->prim_info + 16 * (size_t)i, 8);
+            thr = logf(orc_h2f(hc[3]) * 255.0f);
+        } else {
+            const float* co = prim->conic_opacity + 4 * (size_t)i;
+            conic[0] = co[0];
+            conic[1] = co[1];
+            conic[2] = co[2];
+            thr = logf(co[3] * 255.0f);
+        }
+        uint32_t touched = 0;
+        uint8_t fr = 0;
+        for (uint32_t q = 0; q < cnt; ++q) {
+            uint32_t ty = b[2] + q / bw, tx = b[0] + q % bw;
+            float margin;
+            int c = fp16 ? tile_test_f16(smx, smy, hc[0], hc[1], hc[2], tx, ty, thr, &margin)
+                         : tile_test_f32(smx, smy, conic, tx, ty, thr, &margin);
+            touched += c ? 1u : 0u;
+            if (isfinite(margin) && fabsf(margin) <= band * fmaxf(fabsf(thr), 1.f)) fr = 1;
+        }
+        out[i] = touched;
+        if (fragile) fragile[i] = fr;
+    }
 }
 
 int64_t orc_binning(int64_t n, const OrcPrimitives* prim, const OrcCamera* cam,
@@ -679,6 +744,10 @@ void orc_blend_forward_f32(const OrcCamera* cam, const uint32_t* ranges,
                     if (s < 0.f) continue;
                     float g = expf(-s);
                     float a = fminf(co[3] * g, 0.999f);
+                    if (g_pix_fragile && inside &&
+                        (near_rel(co[3] * g, 1.0f / 255.0f, g_pix_band) || near_rel(co[3] * g, 0.999f, g_pix_band) ||
+                         near_rel(T * (1.0f - a), 1e-4f, g_pix_band)))
+                        g_pix_fragile[tiled_index(py, px, tw)] = 1;
                     if (a < 1.0f / 255.0f && !g_smooth) continue;
                     float Tn = T * (1.0f - a);
                     if (Tn < 1e-4f && !g_smooth) {
@@ -921,6 +990,10 @@ void orc_blend_forward_f16(const OrcCamera* cam, const uint32_t* ranges,
                     uint16_t gauss = hex2(hmul(hneg(sig), h_log2e));
                     uint16_t a = hmin(hmul(op, gauss), h_max_a);
                     uint16_t Tn = hfma(hneg(a), T, T);
+                    if (g_pix_fragile && inside && unfinished &&
+                        (near_rel(orc_h2f(Tn), orc_h2f(h_min_T), g_pix_band) ||
+                         near_rel(orc_h2f(hmul(op, gauss)), orc_h2f(h_max_a), g_pix_band)))
+                        g_pix_fragile[tiled_index(py, px, tw)] = 1;
                     int ok = Tn >= h_min_T; /* bit compare of positive halves */
                     int en = unfinished && ok;
                     uint16_t tah = hmul(hmul(T, a), h_unscale);

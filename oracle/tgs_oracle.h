@@ -55,6 +55,17 @@ void orc_preprocess(int64_t n, const float* means, const float* opacities,
  * (fastgs_ours/forward.cu:146-250, kernels_forward.cuh:414-567).
  * Visible Gaussians are ordered by (depth, index).  Returns the number of
  * instances, or -1 if `cap` was too small.  ranges: [n_tiles][2]. */
+/* Touched-tile count of every Gaussian recomputed from its stored record
+ * (the test create_instances repeats); 0 where prim->n_touched is 0.
+ * fragile[i] (if given) flags a tile test within `band` (relative to
+ * max(|threshold|, 1)) of its threshold. */
+void orc_count_tiles(int64_t n, const OrcPrimitives* prim, const OrcCamera* cam, int32_t fp16,
+                     uint32_t* out, uint8_t* fragile /* or NULL */, float band, int32_t n_threads);
+
+/* Optional per-pixel flags set by the blend forwards for decisions within
+ * `band` (relative) of their thresholds; NULL turns the recording off. */
+void orc_set_pixel_fragile(uint8_t* buf, float band);
+
 int64_t orc_binning(int64_t n, const OrcPrimitives* prim, const OrcCamera* cam,
                     int32_t fp16, uint32_t* inst_tile, uint32_t* inst_prim,
                     int64_t cap, uint32_t* ranges, uint32_t* sorted_visible,
@@ -221,6 +232,10 @@ void orc_set_tile_stride(int32_t stride);
 
 /* Finite-difference checks only: smooth fp32 forward (see tgs_oracle.c). */
 void orc_set_smooth_forward(int32_t on);
+/* fp16 path: width of the band around the tile-test threshold inside which
+ * a decision is marked fragile, relative to max(|threshold|, 1); <= 0
+ * restores the default 2e-2. */
+void orc_set_fragile_f16(float rel);
 
 /* IEEE binary16 helpers used by the fp16 emulation. */
 uint16_t orc_f2h(float f);

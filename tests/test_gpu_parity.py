@@ -35,9 +35,20 @@ def test_preprocess_matches_oracle(oracle, cuda_lib, fp16):
     cfg, params, sh, cam = scene("cfg0")
     run = GpuRun(params, sh, cam, fp16).forward()
     gp = run.prims()
-    op = oracle.preprocess(params, sh, cam, fp16)
+    # every tile decision, recomputed by the oracle from the GPU's records
+    # (outside tests that sit on their threshold, see test_gpu_fullsize)
+    cnt, fr = oracle.count_tiles(gp, cam, fp16, band=1e-3 if fp16 else 2e-5)
+    assert fr.mean() < 1e-2
+    np.testing.assert_array_equal(gp["n_touched"][fr == 0], cnt[fr == 0])
+    # from the parameters: fragile decisions (within 2e-5 of a threshold in
+    # fp32; for the fp16 tile test within 4e-3 relative, about eight half
+    # ulps, since the half-rounded conics can land one ulp apart) excluded
+    oracle.set_fragile_f16(4e-3)
+    try:
+        op = oracle.preprocess(params, sh, cam, fp16)
+    finally:
+        oracle.set_fragile_f16(0)
     stable = op["fragile"] == 0
-    # the fp16 tile test runs in half precision, so its margin is wider
     assert (~stable).sum() < (0.05 if fp16 else 0.005) * cfg.n
     np.testing.assert_array_equal(gp["n_touched"][stable], op["n_touched"][stable])
     vis = stable & (op["n_touched"] > 0)
@@ -345,12 +356,39 @@ def test_adam_zero_grads_fused(cuda_lib):
 
 # -------------------------------------------------------------- end to end
 
+def _tiles_of(prims_idx, bins, n_tiles):
+    mask = np.zeros(n_tiles, bool)
+    if prims_idx.size:
+        sel = np.isin(bins["inst_prim"], prims_idx)
+        mask[bins["inst_tile"][sel].astype(np.int64)] = True
+    return mask
+
+
 def test_train_step_end_to_end(oracle, cuda_lib, fp16):
+    """A whole step from the parameters on both sides.  Both compute the
+    screen-space records from the parameters (IEEE on the CPU, fast-math on
+    the GPU, which differ in the last bits), so decisions that sit on a
+    threshold can go either way; the stage-by-stage tests above feed each
+    stage the GPU's own inputs and are exact.  Here:
+      * image, fp32: every pixel within 1e-5 except pixels whose own blend
+        decision sits within 1e-2 of its threshold and the tiles of
+        Gaussians whose tile decision is fragile or differs; fp16: at least
+        99.5% of the values within 2e-3;
+      * gradients (sh_rest included): relative L2 error within 2e-3 (fp32)
+        / 2e-2 (fp16) per array, and (fp32) at least 99% of the entries
+        within 1e-3 relative (+1e-4 of the array's maximum)."""
     cfg, params, sh, cam = scene("cfg0")
     W, H = cfg.width, cfg.height
+    gw, gh = (W + 15) // 16, (H + 15) // 16
     target = scenes.target_image(W, H, 77).reshape(-1)
     dt = np.float16 if fp16 else np.float32
-    ref = oracle.train_step({k: v.copy() for k, v in params.items()}, sh, cam, target, fp16, do_adam=False)
+    oracle.set_fragile_f16(4e-3)
+    pix = oracle.pixel_fragile(cam, 1e-2)
+    try:
+        ref = oracle.train_step({k: v.copy() for k, v in params.items()}, sh, cam, target, fp16, do_adam=False)
+    finally:
+        oracle.pixel_fragile_off()
+        oracle.set_fragile_f16(0)
     run = GpuRun(params, sh, cam, fp16).forward()
     loss = rt.FusedLoss(W, H)
     tgt = torch.from_numpy(target.astype(dt)).cuda()
@@ -358,20 +396,37 @@ def test_train_step_end_to_end(oracle, cuda_lib, fp16):
     loss.evaluate(run.image, tgt, lmap, run.grad_image, W, H, grad_scaler=10.0)
     run.rast.backward(run.ctx)
     torch.cuda.synchronize()
+    op, gp, gb = ref["render"]["prims"], run.prims(), run.bins()
+    flip = np.nonzero((op["fragile"] != 0) | (gp["n_touched"] != op["n_touched"]))[0]
+    bad_tiles = _tiles_of(flip, gb, gw * gh) | _tiles_of(flip, ref["render"]["bins"], gw * gh)
+    pl = rt.image_numel(W, H) // 3
+    idx = np.arange(pl)
+    tw = (W + 7) // 8
+    y = (idx >> 6) // tw * 8 + ((idx >> 3) & 7)
+    x = (idx >> 6) % tw * 8 + (idx & 7)
+    tile_of_px = (np.minimum(y, H - 1) // 16) * gw + np.minimum(x, W - 1) // 16
+    keep_px = (pix == 0) & ~bad_tiles[tile_of_px]
     img_o = ref["render"]["fwd"]["image"].astype(np.float32)
-    err = np.abs(run.image.cpu().numpy().astype(np.float32) - img_o)
+    err = np.abs(run.image.cpu().numpy().astype(np.float32) - img_o).reshape(3, pl)
     tol = 2e-3 if fp16 else 1e-5
-    assert np.mean(err <= tol) >= 0.999, (err.max(), np.mean(err <= tol))
-    gg = run.grads_np()
-    og = ref["grads"]
-    for k in ("means", "opacities", "rotations", "scales", "sh0"):
-        a, b = gg[k].astype(np.float64).ravel(), og[k].astype(np.float64).ravel()
-        cos = float(a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-30))
-        # end to end, rare threshold flips (fragile tile tests, L1 signs
-        # where pred == target) move a few entries; the direction must agree
-        assert cos > (0.99 if fp16 else 0.999), (k, cos)
-        rel = np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
-        assert rel < (0.1 if fp16 else 0.02), (k, rel)
+    print(f"end to end fp16={fp16}: {flip.size} fragile/flipped Gaussians, {int((~keep_px).sum())} of {pl} "
+          f"pixels excluded")
+    if fp16:
+        # half-precision decisions are far denser near their thresholds;
+        # the image is checked pixel by pixel over the whole frame
+        assert (err > tol).mean() <= 5e-3, float((err > tol).mean())
+    else:
+        assert keep_px.mean() > 0.5
+        assert err[:, keep_px].max() <= tol, err[:, keep_px].max()
+    gg, og = run.grads_np(), ref["grads"]
+    for k in gg:
+        a, b = gg[k], og[k].reshape(gg[k].shape)
+        rel = float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+        ok, worst, nbad = close_rel(a, b, 1e-3, 1e-4)
+        print(f"  {k}: rel L2 {rel:.2e}, {nbad} of {a.size} entries beyond 1e-3")
+        assert rel <= (2e-2 if fp16 else 2e-3), (k, rel)
+        if not fp16:
+            assert nbad <= 0.01 * a.size, (k, nbad)
 
 
 def test_empty_and_degenerate_scenes(cuda_lib, fp16):

@@ -23,9 +23,11 @@ fused Adam kernel (the HBM-bound kernel whose time is measured live), clocks
 sampled during the timed region, and a CPU baseline (the oracle restatement,
 timed on a bounded sample on the host cores).
 
-`--impl reference` times the CPU restatement of the reference's algorithm
-(the reference itself has no CPU implementation and its CUDA build cannot be
-reproduced here) on the same workload and prints it in the same format.
+`--impl reference` times the reference's own training step on the same
+workload and GPU -- its CUDA kernels built unchanged from its sources into
+oracle/_ref (rasterizer forward/backward, L1, fused SSIM, SimpleAdam) -- and
+prints it in the same format (the CPU restatement where that library is not
+built).
 """
 from __future__ import annotations
 
@@ -289,11 +291,149 @@ def densify_bench(n: int, capacity: int, cpu: bool) -> dict:
     return out
 
 
+def workload(cfg, n_views: int, world: int) -> dict:
+    """The `config` object of both arms' lines."""
+    return {"workload": f"{cfg.name}: {cfg.n} Gaussians SH{cfg.sh_degree}, {cfg.dtype} rasterizer, "
+                        f"{cfg.width}x{cfg.height}, {n_views}-view orbit r={cfg.cam_distance}",
+            "gaussians": cfg.n, "width": cfg.width, "height": cfg.height, "sh_degree": cfg.sh_degree,
+            "views_per_gpu_step": 1, "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (parameters+gradients+moments 2.8 GB per step)"}
+
+
 def run_reference(args):
-    """--impl reference: the CPU restatement of the reference algorithm."""
+    """--impl reference: the reference's own training step on the GPU.
+
+    oracle/_ref/libtgs_ref.so holds the reference's CUDA kernels built
+    unchanged from its sources (fastgs_ours_fp16 / fastgs_ours rasterizers,
+    L1Loss, FusedSSIMLoss, SimpleAdam).  One step is what
+    Orchestrator::train_step (orchestrator.cu:335-439) runs for this
+    workload: zero the gradient container, the loss map and the gradient
+    image; rasterizer forward; L1 (weight 0.8) and fused SSIM (0.2) scaled
+    by grad_scaler 10; rasterizer backward; SimpleAdam::step(1/10) with
+    max_grad_1 0.3 -- with the reference's own host synchronisations inside
+    its forward and backward.  The reference has no multi-GPU code: under
+    torchrun rank 0 alone runs it on its GPU and the other ranks exit.
+    Where the library is absent (or no GPU is present), the CPU restatement
+    (the oracle) is timed instead."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    import torch
+
+    from oracle import refpy
+
+    if not refpy.available() or not torch.cuda.is_available():
+        return run_reference_cpu(args)
+    import numpy as np
+
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    cfg = scene_config(args.config, args.n)
+    W, H = cfg.width, cfg.height
+    fp16 = cfg.dtype == "float16"
+    dt = torch.float16 if fp16 else torch.float32
+    params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
+    adam = refpy.RefAdam(cfg.n, cfg.sh_degree, {"max_grad_1": 0.3})
+    for name in refpy.RefAdam.SEGMENTS:
+        adam.param(name).copy_(torch.from_numpy(np.ascontiguousarray(params[name], np.float32).reshape(-1)))
+    del params
+
+    class Arrays:  # the containers as the harness's pointer struct source
+        def __init__(self, s):
+            self.full = {k: _Ptr(getattr(s, k)) for k in refpy.RefAdam.SEGMENTS}
+            self.n, self.sh_degree = cfg.n, cfg.sh_degree
+
+    class _Ptr:
+        def __init__(self, p):
+            self.p = p
+
+        def data_ptr(self):
+            return self.p
+
+    g, gr = Arrays(adam.params), Arrays(adam.grads)
+    grad_views = [adam.grad(k) for k in refpy.RefAdam.SEGMENTS]
+    cams = scenes.cameras(cfg)
+    n_targets = 4
+    targets = [torch.from_numpy(scenes.target_image(W, H, cfg.seed + 100 + k).reshape(-1)).to(dt).cuda()
+               for k in range(n_targets)]
+    numel = rt.image_numel(W, H)
+    image = torch.zeros(numel, dtype=dt, device="cuda")
+    grad_image = torch.zeros_like(image)
+    loss_map = torch.zeros_like(image)
+    ref = refpy.RefRasterizer()
+    stream = torch.cuda.current_stream()
+    counts = [0, 0, 0]
+
+    def step(k, ev=None):
+        cam = cams[k % len(cams)]
+        for v in grad_views:
+            v.zero_()
+        loss_map.zero_()
+        grad_image.zero_()
+        if ev is not None:
+            ev[0].record(stream)
+        counts[:] = ref.forward(g, cam, image, fp16)
+        if ev is not None:
+            ev[1].record(stream)
+        tgt = targets[k % n_targets]
+        refpy.l1(fp16, W, H, image, tgt, loss_map, grad_image, 0.8 * GRAD_SCALER)
+        ref.ssim(fp16, W, H, image, tgt, loss_map, grad_image, 0.2 * GRAD_SCALER)
+        if ev is not None:
+            ev[2].record(stream)
+        ref.backward(g, cam, image, grad_image, gr, fp16)
+        if ev is not None:
+            ev[3].record(stream)
+        adam.step(1.0 / GRAD_SCALER)
+        if ev is not None:
+            ev[4].record(stream)
+
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    sampler.start()
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.steps):
+        step(args.warmup + k)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    rows = []
+    for k in range(max(3, min(args.steps, 5))):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        step(args.warmup + args.steps + k, ev)
+        torch.cuda.synchronize()
+        rows.append({"forward": ev[0].elapsed_time(ev[1]), "loss": ev[1].elapsed_time(ev[2]),
+                     "backward": ev[2].elapsed_time(ev[3]), "adam": ev[3].elapsed_time(ev[4])})
+    stages = {nm: round(statistics.median(r[nm] for r in rows), 4) for nm in ("forward", "loss", "backward", "adam")}
+    if not torch.isfinite(adam.param("means")).all():
+        stages["non_finite_parameters"] = True
+    value = 1e3 / ms_step
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "iters/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 raster / f32 params+grads+Adam" if fp16 else "f32", "data": "synthetic",
+            "config": workload(cfg, len(cams), 1),
+            "cpu_baseline": {"value": value, "unit": "iters/s", "cores": 1, "kind": "reference",
+                             "sample": (f"{args.steps} full training steps of the reference's own CUDA kernels "
+                                        f"(oracle/_ref, built unchanged from its sources) on one B200, driven by "
+                                        f"one host thread")},
+            "e2e": {"value": value, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "stages_ms": stages,
+            "counts": {"visible": counts[0], "instances": counts[1], "buckets": counts[2]},
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    ref.close()
+    adam.close()
+
+
+def run_reference_cpu(args):
+    """The CPU restatement of the reference's algorithm (the oracle), timed
+    on the host cores: the reference arm where oracle/_ref is not built."""
     from tinygs_b200 import scenes
 
     cfg = scene_config(args.config, args.n)
@@ -315,8 +455,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "iters/s", "n_gpus": 0,
             "steps": steps_run, "warmup": 0, "ms_per_step": sec * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.config}", "gaussians": cfg.n, "width": cfg.width, "height": cfg.height,
-                       "sh_degree": cfg.sh_degree, "parallelism": "cpu"},
+            "config": workload(cfg, len(scenes.cameras(cfg)), 1),
             "cpu_baseline": {"value": value, "unit": "iters/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "stages_s": r["stages_s"]}
@@ -643,11 +782,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 raster / f32 params+grads+Adam" if fp16 else "f32",
             "data": "synthetic",
-            "config": {"workload": f"{args.config}: {cfg.n} Gaussians SH{cfg.sh_degree}, {cfg.dtype} rasterizer, "
-                                   f"{W}x{H}, {len(cams)}-view orbit r={cfg.cam_distance}",
-                       "gaussians": cfg.n, "width": W, "height": H, "sh_degree": cfg.sh_degree,
-                       "views_per_gpu_step": 1, "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (parameters+gradients+moments 2.8 GB per step)"},
+            "config": workload(cfg, len(cams), world),
             "e2e": {"value": world * 1e3 / e2e_ms, "unit": "iters/s",
                     "h2d_bytes_per_step": int(up_bufs[0].numel() * up_bufs[0].element_size()),
                     "d2h_bytes_per_step": 4},

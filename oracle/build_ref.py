@@ -16,10 +16,12 @@ google-benchmark over the network (cmake/dependencies.cmake:5-62); its
 kernels need only a handful of names from the headers that pull those in, so
 ``oracle/refshim/`` stands in for exactly those headers.  The flags are the
 reference's release flags for CUDA (tinygs/CMakeLists.txt: --use_fast_math,
-C++20, NDEBUG), for sm_100a.  Not built: tinygs/src/optim/simple_adam.cu,
-whose SimpleAdam class needs the glm vector types, GPUGaussian3d (thrust
-containers, core/gpu_gaussian.cu) and the json-configured OptimizerBase
-(optim/optim.cu).
+C++20, NDEBUG), for sm_100a.  The reference's SimpleAdam
+(tinygs/src/optim/simple_adam.cu) is built too, with stand-ins for the glm
+vector types and the GPUGaussian3d container and the config plumbing of
+optim/optim.cu restated in oracle/ref/ref_adam.cu; it needs nlohmann/json,
+found vendored in an installed Python package (when none is, the optimizer
+is left out).
 
 Built only where the reference sources are present (this container); the
 GPU box runs the prebuilt library, which travels with the repository.
@@ -40,8 +42,22 @@ LIB = OUT / "libtgs_ref.so"
 REFERENCE = Path(os.environ.get("TGS_REFERENCE_ROOT", "/root/reference")) / "tinygs"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "--use_fast_math", "-std=c++20", "-DNDEBUG", "-Xcompiler", "-fPIC", "-w", "-I", str(SHIM),
-         "-I", str(HARNESS)]
+FLAGS = ["-O3", "--use_fast_math", "-std=c++20", "-DNDEBUG", "--extended-lambda", "-Xcompiler", "-fPIC", "-w",
+         "-I", str(SHIM), "-I", str(HARNESS)]
+
+
+def json_include() -> list[str]:
+    """nlohmann/json (a header-only third-party library the reference's
+    optimizer configuration uses), from a copy vendored in an installed
+    Python package; empty when none is found."""
+    import glob
+    import site
+
+    roots = site.getsitepackages() + [site.getusersitepackages()]
+    for root in roots:
+        for hit in glob.glob(f"{root}/**/nlohmann/json.hpp", recursive=True):
+            return ["-I", str(Path(hit).parents[1])]
+    return []
 
 
 def units() -> list[tuple[Path, list[str]]]:
@@ -49,7 +65,9 @@ def units() -> list[tuple[Path, list[str]]]:
     raster = ["-I", str(REFERENCE / "src" / "rasterizer")]
     inc = ["-I", str(REFERENCE / "include")]
     src = REFERENCE / "src"
-    return [
+    js = json_include()
+    adam = [(src / "optim" / "simple_adam.cu", inc + js), (HARNESS / "ref_adam.cu", inc + js)] if js else []
+    return adam + [
         (src / "rasterizer" / "fastgs_ours" / "forward.cu", []),
         (src / "rasterizer" / "fastgs_ours" / "backward.cu", []),
         (src / "rasterizer" / "fastgs_ours_fp16" / "forward.cu", []),
@@ -92,6 +110,9 @@ def build(force: bool = False, verbose: bool = False) -> Path | None:
             failed.append(f"--- {src} ---\n{out.decode(errors='replace')}")
     if failed:
         raise RuntimeError("reference build failed:\n" + "\n".join(failed))
+    for stale in OUT.glob("*.o"):
+        if stale not in objs:
+            stale.unlink()
     if force or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
         if verbose:

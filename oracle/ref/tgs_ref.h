@@ -91,6 +91,17 @@ int tgsref_l1(int32_t fp16, int32_t width, int32_t height, const void* pred, con
 int tgsref_ssim(void* handle, int32_t fp16, int32_t width, int32_t height, const void* pred, const void* target,
                 void* loss, void* grad, float scale, void* stream);
 
+/* The reference's SimpleAdam (tinygs/src/optim/simple_adam.cu) over its own
+ * parameter and gradient containers of n Gaussians (zero-filled; fill them
+ * through the pointers tgsref_adam_arrays returns).  config_json: the
+ * optimizer's JSON configuration (GaussianOptimizationParams and
+ * SimpleAdamParameters keys), or NULL for the defaults. */
+int tgsref_adam_create(int64_t n, int32_t sh_degree, const char* config_json, void** handle);
+void tgsref_adam_destroy(void* handle);
+int tgsref_adam_arrays(void* handle, TgsRefGaussians* params, TgsRefGaussians* grads);
+/* SimpleAdam::step(gradient_scale, stream). */
+int tgsref_adam_step(void* handle, float gradient_scale, void* stream);
+
 const char* tgsref_last_error(void);
 
 #ifdef __cplusplus

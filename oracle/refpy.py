@@ -146,3 +146,55 @@ def l1(fp16, width, height, pred, target, loss, grad, scale, stream=None):
     _check(load().tgsref_l1(int(fp16), int(width), int(height), c_void_p(pred.data_ptr()),
                             c_void_p(target.data_ptr()), c_void_p(loss.data_ptr()), c_void_p(grad.data_ptr()),
                             c_float(scale), c_void_p(_stream(stream))), "tgsref_l1")
+
+
+class RefAdam:
+    """The reference's SimpleAdam over its own parameter and gradient
+    containers (thrust vectors of n Gaussians, the reference's SoA layout)."""
+
+    SEGMENTS = ("means", "opacities", "rotations", "scales", "sh0", "sh_rest")
+    WIDTHS = {"means": 3, "opacities": 1, "rotations": 4, "scales": 3, "sh0": 3, "sh_rest": 45}
+
+    def __init__(self, n: int, sh_degree: int, config: dict | None = None):
+        import json
+
+        self.lib = load()
+        self.n = int(n)
+        h = c_void_p()
+        cfg = json.dumps(config or {}).encode()
+        _check(self.lib.tgsref_adam_create(c_int64(self.n), c_int32(sh_degree), ctypes.c_char_p(cfg),
+                                           ctypes.byref(h)), "tgsref_adam_create")
+        self.h = h
+        self.params, self.grads = RefGaussians(), RefGaussians()
+        _check(self.lib.tgsref_adam_arrays(self.h, ctypes.byref(self.params), ctypes.byref(self.grads)),
+               "tgsref_adam_arrays")
+
+    def close(self):
+        if getattr(self, "h", None) is not None and self.h.value:
+            self.lib.tgsref_adam_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _view(self, s: RefGaussians, name: str):
+        import torch
+
+        from tinygs_b200.runtime import _DeviceView
+
+        count = self.n * self.WIDTHS[name]
+        return torch.as_tensor(_DeviceView(getattr(s, name), count, "<f4"), device="cuda")
+
+    def param(self, name: str):
+        """Device tensor view of a parameter array (flat, float32)."""
+        return self._view(self.params, name)
+
+    def grad(self, name: str):
+        return self._view(self.grads, name)
+
+    def step(self, gradient_scale: float, stream=None) -> None:
+        _check(self.lib.tgsref_adam_step(self.h, c_float(gradient_scale), c_void_p(_stream(stream))),
+               "tgsref_adam_step")

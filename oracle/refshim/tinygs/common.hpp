@@ -1,6 +1,7 @@
 // Stand-in for tinygs/include/tinygs/common.hpp: only the names the
 // reference's hot-path kernels use.  Test infrastructure (oracle/_ref build).
 #pragma once
+#include <cfloat>
 #include <cstddef>
 #include <cstdint>
 #include <cmath>
@@ -32,9 +33,19 @@
 #define TINYGS_PRAGMA_NO_UNROLL
 #endif
 
+#if __has_include(<nlohmann/json.hpp>)
+#include <nlohmann/json.hpp>
+namespace tinygs {
+using json = nlohmann::json;
+}
+#endif
+
 namespace tinygs {
 
 using float16_t = __half;
+// core/gaussian.hpp: SH storage is always 16 coefficients (degree 3).
+constexpr int kMaxSphericalHarmonicsDegree = 3;
+constexpr int kMaxSphericalHarmonicsCoefficients = 16;
 constexpr uint32_t WARP_SIZE = 32;
 
 // common.hpp:358-364: sigmoid and its inverse (input clamped to [1e-9, 1-1e-9]).

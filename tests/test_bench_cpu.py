@@ -1,5 +1,6 @@
-"""bench.py's reference arm (the CPU restatement on the host cores) prints
-one JSON line with the contract's keys, on the small cfg0 scene."""
+"""bench.py's reference arm prints one JSON line with the contract's keys,
+on the small cfg0 scene (without a GPU the arm times the CPU restatement on
+the host cores; on a GPU box it times the reference's own CUDA kernels)."""
 import json
 import subprocess
 import sys

@@ -397,6 +397,59 @@ TGS_API int tgs_raster_backward_adam(TgsRaster* r, const TgsGaussians* params,
  * tinygs/src/orchestrator.cu:351-353). */
 TGS_API int tgs_gaussians_zero(const TgsGaussians* g, tgs_stream_t stream);
 
+/* ------------------------------------------------------ rows of a set
+ * Row operations on a set of Gaussian arrays (parameters, gradients or an
+ * Adam moment).  None allocates; sets may not overlap unless stated. */
+
+/* dst row i <- src row idx[i] for every array, i < n (idx on the device).
+ * Replaces GPUGaussian3d::reorder (tinygs/src/core/gpu_gaussian.cu:273-311)
+ * and SimpleAdam::reorder (tinygs/src/optim/simple_adam.cu:1036-1099),
+ * which gather into newly allocated vectors; here into a caller-owned set. */
+TGS_API int tgs_arena_gather(const TgsGaussians* src, TgsGaussians* dst, const uint32_t* idx, int64_t n,
+                             tgs_stream_t stream);
+
+/* Workspace of tgs_arena_keep_index / tgs_arena_compact for n rows. */
+TGS_API int tgs_arena_compact_workspace_bytes(int64_t n, size_t* bytes);
+
+/* Indices of the rows with keep[i] != 0, in increasing order, into idx_out;
+ * their number into *n_kept (device).  The mapping step of
+ * GPUGaussian3d::remove / SimpleAdam::remove (thrust::copy_if over a
+ * counting iterator, gpu_gaussian.cu:117-160, simple_adam.cu:841-903). */
+TGS_API int tgs_arena_keep_index(const uint8_t* keep, int64_t n, void* workspace, size_t workspace_bytes,
+                                 uint32_t* idx_out, uint32_t* n_kept, tgs_stream_t stream);
+
+/* Stable compaction: dst rows 0..*n_kept-1 <- the src rows with
+ * keep[i] != 0, in order; *n_kept (device) receives their number.
+ * Replaces GPUGaussian3d::remove and SimpleAdam::remove (same lines), which
+ * reallocate every array; no host synchronisation. */
+TGS_API int tgs_arena_compact(const TgsGaussians* src, TgsGaussians* dst, const uint8_t* keep, int64_t n,
+                              void* workspace, size_t workspace_bytes, uint32_t* n_kept, tgs_stream_t stream);
+
+/* Rows rows[0..count) of every array (segment == -1) or of one array
+ * (segment 0..5: means, opacities, rotations, scales, sh0, sh_rest) set to
+ * `value`.  SimpleAdam::reset(indices, n) zeroes both moments' rows
+ * (simple_adam.cu:944-982); SimpleAdam::reset_opacity zeroes the opacity
+ * moments (simple_adam.cu:984-987, a fill of segment 1). */
+TGS_API int tgs_arena_fill_rows(TgsGaussians* set, const int32_t* rows, int64_t count, float value,
+                                int32_t segment, tgs_stream_t stream);
+
+/* dst[i] <- src[idx[i]] of the densification records (the gather of
+ * Orchestrator::reorder_gaussians, tinygs/src/orchestrator.cu:1024-1036). */
+TGS_API int tgs_dens_gather(const TgsDensificationInfo* src, TgsDensificationInfo* dst, const uint32_t* idx,
+                            int64_t n, tgs_stream_t stream);
+
+/* Workspace of tgs_morton_order for n Gaussians. */
+TGS_API int tgs_morton_workspace_bytes(int64_t n, size_t* bytes);
+
+/* The reference's Morton order (reorder(), tinygs/src/orchestrator.cu:26-100):
+ * bounding box of the means, inverse extents 1/max(max-min, 1e-8) in IEEE
+ * float, each coordinate normalised, clamped to [0, 1] and truncated to 10
+ * bits (x 1023), a 30-bit Morton code (x in bits 3i, y 3i+1, z 3i+2), and a
+ * stable sort by code.  perm[i] is the index of the Gaussian that moves to
+ * row i (apply with tgs_arena_gather / tgs_dens_gather).  means: [n][3]. */
+TGS_API int tgs_morton_order(const float* means, int64_t n, void* workspace, size_t workspace_bytes,
+                             uint32_t* perm, tgs_stream_t stream);
+
 /* Human-readable text for a status code (static storage). */
 TGS_API const char* tgs_status_string(int status);
 

@@ -433,3 +433,12 @@ def densify_step(n: int, params: dict, grads: dict | None, m: dict, v: dict, den
     cap = params["means"].shape[0]
     return int(lib.orc_densify_step(n, cap, _set_of(params), _set_of(grads), _set_of(m), _set_of(v),
                                     _p(dens), ctypes.byref(cfg), step, ctypes.byref(rng)))
+
+
+def morton_order(means: np.ndarray) -> np.ndarray:
+    """The reference's Morton order of the means (orchestrator.cu:26-100)."""
+    lib = load()
+    m = np.ascontiguousarray(means, dtype=np.float32).reshape(-1, 3)
+    perm = np.zeros(max(m.shape[0], 1), np.uint32)
+    lib.orc_morton_order(c_int64(m.shape[0]), _p(m), _p(perm))
+    return perm[: m.shape[0]]

@@ -10,6 +10,7 @@
  */
 #include "tgs_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -1788,4 +1789,58 @@ int64_t orc_densify_step(int64_t n, int64_t capacity, OrcSet params, OrcSet grad
         if (exp_avg_sq.opacities) memset(exp_avg_sq.opacities, 0, sizeof(float) * (size_t)n);
     }
     return n;
+}
+
+/* ------------------------------------------------------------ Morton order */
+
+typedef struct { uint32_t code, idx; } MortonPair;
+
+static int morton_cmp(const void* a, const void* b) {
+    const MortonPair* x = (const MortonPair*)a;
+    const MortonPair* y = (const MortonPair*)b;
+    if (x->code != y->code) return x->code < y->code ? -1 : 1;
+    return x->idx < y->idx ? -1 : (x->idx > y->idx ? 1 : 0);
+}
+
+/* bit i of v (i < 10) to bit 3i */
+static uint32_t spread10(uint32_t v) {
+    uint32_t out = 0;
+    for (int i = 0; i < 10; ++i) out |= ((v >> i) & 1u) << (3 * i);
+    return out;
+}
+
+/* reorder(), tinygs/src/orchestrator.cu:26-100: bounding box of the means,
+ * inverse extents 1 / max(max - min, 1e-8) (std::max semantics), 10-bit
+ * quantisation of each normalised, clamped coordinate (x 1023, truncated),
+ * the 30-bit Morton code (x -> bit 3i, y -> 3i+1, z -> 3i+2) and a stable
+ * sort by code (CUB's radix sort is stable: equal codes keep index order). */
+void orc_morton_order(int64_t n, const float* means, uint32_t* perm) {
+    if (n <= 0) return;
+    float lo[3] = {FLT_MAX, FLT_MAX, FLT_MAX}, hi[3] = {-FLT_MAX, -FLT_MAX, -FLT_MAX};
+    for (int64_t i = 0; i < n; ++i)
+        for (int c = 0; c < 3; ++c) {
+            lo[c] = fminf(lo[c], means[3 * i + c]);
+            hi[c] = fmaxf(hi[c], means[3 * i + c]);
+        }
+    float inv[3];
+    for (int c = 0; c < 3; ++c) {
+        float d = hi[c] - lo[c];
+        float e = d < 1e-8f ? 1e-8f : d;
+        inv[c] = 1.0f / e;
+    }
+    MortonPair* pairs = (MortonPair*)malloc(sizeof(MortonPair) * (size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        uint32_t q[3];
+        for (int c = 0; c < 3; ++c) {
+            float v = (means[3 * i + c] - lo[c]) * inv[c];
+            float u = fminf(fmaxf(v, 0.0f), 1.0f);
+            float s = u * 1023.0f;
+            q[c] = (uint32_t)s;
+        }
+        pairs[i].code = spread10(q[0]) | (spread10(q[1]) << 1) | (spread10(q[2]) << 2);
+        pairs[i].idx = (uint32_t)i;
+    }
+    qsort(pairs, (size_t)n, sizeof(MortonPair), morton_cmp);
+    for (int64_t i = 0; i < n; ++i) perm[i] = pairs[i].idx;
+    free(pairs);
 }

@@ -241,6 +241,10 @@ void orc_set_fragile_f16(float rel);
 uint16_t orc_f2h(float f);
 float orc_h2f(uint16_t h);
 
+/* Morton order of the means (tinygs/src/orchestrator.cu:26-100): perm[i] is
+ * the Gaussian that moves to row i. */
+void orc_morton_order(int64_t n, const float* means, uint32_t* perm);
+
 #ifdef __cplusplus
 }
 #endif

@@ -336,3 +336,31 @@ def test_adam_oracle_formula(oracle):
             ref[k] -= mh * lrs[k] / den
     for k in ref:
         np.testing.assert_allclose(p[k], ref[k], rtol=1e-5, atol=1e-6, err_msg=k)
+
+
+def _morton_numpy(means):
+    """Independent numpy restatement of the reference's Morton order
+    (orchestrator.cu:26-100), float32 arithmetic throughout."""
+    m = np.asarray(means, np.float32)
+    lo, hi = m.min(0), m.max(0)
+    d = (hi - lo).astype(np.float32)
+    inv = (np.float32(1.0) / np.where(d < np.float32(1e-8), np.float32(1e-8), d)).astype(np.float32)
+    u = np.clip(((m - lo).astype(np.float32) * inv).astype(np.float32), np.float32(0), np.float32(1))
+    q = (u * np.float32(1023.0)).astype(np.float32).astype(np.uint32)
+    code = np.zeros(m.shape[0], np.uint64)
+    for b in range(10):
+        for c in range(3):
+            code |= ((q[:, c].astype(np.uint64) >> np.uint64(b)) & np.uint64(1)) << np.uint64(3 * b + c)
+    return np.argsort(code, kind="stable").astype(np.uint32)
+
+
+def test_oracle_morton_order_matches_numpy(oracle):
+    rng = np.random.default_rng(3)
+    means = rng.normal(0, 1.5, (20000, 3)).astype(np.float32)
+    means[100:200] = means[100]  # equal codes keep index order
+    np.testing.assert_array_equal(oracle.morton_order(means), _morton_numpy(means))
+    flat = means.copy()
+    flat[:, 2] = 0.25  # a degenerate axis: extent clamped to 1e-8
+    np.testing.assert_array_equal(oracle.morton_order(flat), _morton_numpy(flat))
+    assert oracle.morton_order(means[:1]).tolist() == [0]
+    assert oracle.morton_order(np.zeros((0, 3), np.float32)).size == 0

@@ -128,6 +128,15 @@ PROTOTYPES = {
     "tgs_densify_step": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
                                    POINTER(TgsGaussians), _P, POINTER(TgsDensifyConfig), c_int32, POINTER(TgsPcg32),
                                    POINTER(c_int64), _P]),
+    "tgs_arena_gather": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), _P, c_int64, _P]),
+    "tgs_arena_compact_workspace_bytes": (c_int32, [c_int64, POINTER(c_size_t)]),
+    "tgs_arena_keep_index": (c_int32, [_P, c_int64, _P, c_size_t, _P, _P, _P]),
+    "tgs_arena_compact": (c_int32, [POINTER(TgsGaussians), POINTER(TgsGaussians), _P, c_int64, _P, c_size_t, _P,
+                                    _P]),
+    "tgs_arena_fill_rows": (c_int32, [POINTER(TgsGaussians), _P, c_int64, c_float, c_int32, _P]),
+    "tgs_dens_gather": (c_int32, [_P, _P, _P, c_int64, _P]),
+    "tgs_morton_workspace_bytes": (c_int32, [c_int64, POINTER(c_size_t)]),
+    "tgs_morton_order": (c_int32, [_P, c_int64, _P, c_size_t, _P, _P]),
     "tgs_status_string": (c_char_p, [c_int32]),
     "tgs_loss_set_accumulate": (c_int32, [c_void_p, c_int32]),
     "tgs_version": (c_char_p, []),

@@ -813,28 +813,37 @@ __global__ void __launch_bounds__(32 * kEmitWarps)
 
 template <typename K>
 void radix_sort(K* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, const DevCounts* counts,
-                int64_t capacity, int total_bits, int& result, const RasterState& s, cudaStream_t stream) {
+                int64_t capacity, int total_bits, int& result, const SortScratch& ss, cudaStream_t stream) {
   const uint32_t tiles = static_cast<uint32_t>((capacity + kSortTile - 1) / kSortTile);
-  const uint32_t resident = static_cast<uint32_t>(s.num_sms) * 8u;
+  const uint32_t resident = static_cast<uint32_t>(ss.num_sms) * 8u;
   const uint32_t blocks = tiles < resident ? tiles : resident;
-  const uint32_t max_blocks = static_cast<uint32_t>(s.sort_max_blocks);
+  const uint32_t max_blocks = static_cast<uint32_t>(ss.max_blocks);
   int cur = 0;
   for (int shift = 0; shift < total_bits; shift += kRadixBits) {
     const int bits = min(kRadixBits, total_bits - shift);
     if (blocks > 0) {
       pdl_launch(k_radix_hist<K>, blocks, kSortThreads, 0, stream, keys[cur], count_ptr, counts, shift, bits,
-                 s.sort_hist, max_blocks);
-      pdl_launch(k_radix_scan, kRadix, kSortThreads, 0, stream, s.sort_hist, count_ptr, counts, max_blocks,
-                 s.sort_digit_total);
+                 ss.hist, max_blocks);
+      pdl_launch(k_radix_scan, kRadix, kSortThreads, 0, stream, ss.hist, count_ptr, counts, max_blocks,
+                 ss.digit_total);
       pdl_launch(k_radix_scatter<K>, blocks, kSortThreads, 0, stream, keys[cur], vals[cur], keys[1 - cur],
-                 vals[1 - cur], count_ptr, counts, shift, bits, s.sort_hist, max_blocks, s.sort_digit_total);
+                 vals[1 - cur], count_ptr, counts, shift, bits, ss.hist, max_blocks, ss.digit_total);
     }
     cur = 1 - cur;
   }
   result = cur;
 }
 
+SortScratch sort_scratch(const RasterState& s) {
+  return SortScratch{s.sort_hist, s.sort_digit_total, s.sort_max_blocks, s.num_sms};
+}
+
 }  // namespace
+
+void sort_pairs_u32(uint32_t* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, int64_t capacity,
+                    int total_bits, int& result, const SortScratch& ss, cudaStream_t stream) {
+  radix_sort<uint32_t>(keys, vals, count_ptr, nullptr, capacity, total_bits, result, ss, stream);
+}
 
 void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16, cudaStream_t stream) {
   const uint32_t n = static_cast<uint32_t>(n64);
@@ -849,7 +858,8 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
     pdl_launch(k_compact_visible, n_blocks, kScanBlock, 0, stream, s.bounds, s.depth_key, s.block_sums, n,
                s.vis_key[0], s.vis_idx[0]);
   // 2. depth sort (32-bit keys)
-  radix_sort<uint32_t>(s.vis_key, s.vis_idx, &counts->n_visible, nullptr, n64, 32, s.depth_result, s, stream);
+  radix_sort<uint32_t>(s.vis_key, s.vis_idx, &counts->n_visible, nullptr, n64, 32, s.depth_result,
+                       sort_scratch(s), stream);
   const uint32_t* sorted = s.vis_idx[s.depth_result];
   // 3. super-tile entries in depth order, sorted by super-tile
   if (n_blocks > 0) {
@@ -862,7 +872,7 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
   int super_bits = 1;
   while ((1u << super_bits) < n_super) ++super_bits;
   radix_sort<uint16_t>(s.ent_key, s.ent_prim, &counts->n_entries, counts, s.cap_entries, super_bits, s.ent_result,
-                       s, stream);
+                       sort_scratch(s), stream);
   const uint16_t* ent_key = s.ent_key[s.ent_result];
   const uint32_t* ent_prim = s.ent_prim[s.ent_result];
   // 4. chunks of each super-tile's entry list

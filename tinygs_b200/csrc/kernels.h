@@ -91,6 +91,22 @@ struct RasterState {
 DevCamera make_camera(int width, int height, float fx, float fy, float cx, float cy,
                       float near_plane, float far_plane, const float w2c[16]);
 
+// Scratch of the stable LSD radix sort (binning.cu): per-digit block counts
+// [256][max_blocks] (max_blocks = ceil(capacity / kSortTileItems)) and the
+// 256 digit totals.
+struct SortScratch {
+  uint32_t* hist;
+  uint32_t* digit_total;
+  int64_t max_blocks;
+  int num_sms;
+};
+
+// Stable sort of (key, value) pairs by the low `total_bits` bits of the
+// keys, 8 bits per pass; *count_ptr (device) pairs of at most `capacity`.
+// The sorted pairs end in keys[result], vals[result].
+void sort_pairs_u32(uint32_t* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, int64_t capacity,
+                    int total_bits, int& result, const SortScratch& ss, cudaStream_t stream);
+
 // forward stages (preprocess.cu, binning.cu, blend.cu)
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam,
                        int fp16, float4* dens, cudaStream_t stream);

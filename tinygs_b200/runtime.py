@@ -109,6 +109,83 @@ class GaussianSet:
         s.sh_degree = self.sh_degree
         return s
 
+    # ---- row operations (GPUGaussian3d::reorder / remove / append,
+    # tinygs/src/core/gpu_gaussian.cu:117-171, 273-311)
+    def _replace_with(self, other: "GaussianSet", n: int) -> None:
+        self.storage.copy_(other.storage)
+        self.resize(n)
+
+    def reorder(self, idx: torch.Tensor, stream=None) -> None:
+        """Row i <- row idx[i] (idx: int32/uint32 device tensor of n)."""
+        tmp = GaussianSet(self.n, self.sh_degree, self.storage.device, capacity=self.capacity)
+        src, dst = self.abi(), tmp.abi()
+        check(load_library().tgs_arena_gather(ctypes.byref(src), ctypes.byref(dst), idx.data_ptr(), self.n,
+                                              _stream_handle(stream)), "tgs_arena_gather")
+        self._replace_with(tmp, self.n)
+
+    def remove(self, keep: torch.Tensor, stream=None) -> int:
+        """Keeps the rows with keep[i] != 0 (uint8 device tensor of n), in
+        order; returns the new count (one host synchronisation)."""
+        lib = load_library()
+        ws_bytes = ctypes.c_size_t()
+        check(lib.tgs_arena_compact_workspace_bytes(self.n, ctypes.byref(ws_bytes)), "workspace")
+        ws = torch.empty(max(int(ws_bytes.value), 1), dtype=torch.uint8, device=self.storage.device)
+        n_kept = torch.zeros(1, dtype=torch.int32, device=self.storage.device)
+        tmp = GaussianSet(self.n, self.sh_degree, self.storage.device, capacity=self.capacity)
+        src, dst = self.abi(), tmp.abi()
+        check(lib.tgs_arena_compact(ctypes.byref(src), ctypes.byref(dst), keep.data_ptr(), self.n, ws.data_ptr(),
+                                    ws.numel(), n_kept.data_ptr(), _stream_handle(stream)), "tgs_arena_compact")
+        kept = int(n_kept.item())
+        self._replace_with(tmp, kept)
+        return kept
+
+    def append(self, count: int) -> None:
+        """count zero rows at the end (within the capacity)."""
+        n = self.n
+        self.resize(n + int(count))
+        for name in SEGMENTS:
+            self.full[name][n:n + int(count)].zero_()
+
+    def fill_rows(self, rows: torch.Tensor, value: float = 0.0, segment: int = -1, stream=None) -> None:
+        s = self.abi()
+        check(load_library().tgs_arena_fill_rows(ctypes.byref(s), rows.data_ptr(), rows.numel(), float(value),
+                                                  int(segment), _stream_handle(stream)), "tgs_arena_fill_rows")
+
+
+def morton_order(g: GaussianSet, stream=None) -> torch.Tensor:
+    """The reference's Morton order of the Gaussians' means
+    (tinygs/src/orchestrator.cu:26-100): int32 device tensor perm with row i
+    of the reordered set = row perm[i] (tgs_morton_order)."""
+    lib = load_library()
+    n = g.n
+    ws_bytes = ctypes.c_size_t()
+    check(lib.tgs_morton_workspace_bytes(n, ctypes.byref(ws_bytes)), "tgs_morton_workspace_bytes")
+    ws = torch.empty(int(ws_bytes.value), dtype=torch.uint8, device=g.storage.device)
+    perm = torch.empty(max(n, 1), dtype=torch.int32, device=g.storage.device)
+    check(lib.tgs_morton_order(g.full["means"].data_ptr(), n, ws.data_ptr(), ws.numel(), perm.data_ptr(),
+                               _stream_handle(stream)), "tgs_morton_order")
+    return perm[:n]
+
+
+def reorder_gaussians(params: GaussianSet, grads: GaussianSet | None = None, optimizer=None,
+                      densification_info: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Orchestrator::reorder_gaussians (tinygs/src/orchestrator.cu:1038-1060):
+    Morton-sorts the Gaussians and applies the same permutation to the
+    gradients, the optimizer's moments and the densification records.
+    Returns the permutation."""
+    perm = morton_order(params, stream)
+    params.reorder(perm, stream)
+    if grads is not None:
+        grads.reorder(perm, stream)
+    if optimizer is not None:
+        optimizer.reorder(perm, stream)
+    if densification_info is not None and params.n > 0:
+        tmp = torch.empty_like(densification_info[: params.n])
+        check(load_library().tgs_dens_gather(densification_info.data_ptr(), tmp.data_ptr(), perm.data_ptr(),
+                                             params.n, _stream_handle(stream)), "tgs_dens_gather")
+        densification_info[: params.n].copy_(tmp)
+    return perm
+
 
 def make_camera(cam: dict) -> TgsCamera:
     c = TgsCamera()
@@ -354,6 +431,34 @@ class SimpleAdam:
                                                 ctypes.byref(m), ctypes.byref(v), ctypes.byref(cfg),
                                                 self.global_steps, float(scale), _ptr(ctx.densification_info),
                                                 _stream_handle(ctx.stream)), "tgs_raster_backward_adam")
+
+    # ---- OptimizerBase row hooks (tinygs/include/tinygs/optim/optim.hpp:61-76,
+    # SimpleAdam: tinygs/src/optim/simple_adam.cu:841-1099)
+    def remove(self, keep: torch.Tensor, stream=None) -> int:
+        """Compacts both moments to the kept rows."""
+        self.exp_avg.remove(keep, stream)
+        return self.exp_avg_sq.remove(keep, stream)
+
+    def duplicate(self, indices=None, new_indices=None, count: int = 0) -> None:
+        """New Gaussians get zero moments (the reference only grows its
+        moment vectors to the new size; the indices are unused)."""
+        for m in (self.exp_avg, self.exp_avg_sq):
+            m.append(count)
+
+    def reset(self, indices: torch.Tensor, stream=None) -> None:
+        """Zeroes both moments of the given rows."""
+        for m in (self.exp_avg, self.exp_avg_sq):
+            m.fill_rows(indices, 0.0, -1, stream)
+
+    def reset_opacity(self, stream=None) -> None:
+        """Zeroes the opacity moments of every row."""
+        rows = torch.arange(self.params.n, dtype=torch.int32, device=self.params.storage.device)
+        for m in (self.exp_avg, self.exp_avg_sq):
+            m.fill_rows(rows, 0.0, 1, stream)
+
+    def reorder(self, idx: torch.Tensor, stream=None) -> None:
+        for m in (self.exp_avg, self.exp_avg_sq):
+            m.reorder(idx, stream)
 
     def step(self, scale: float, stream=None, zero_grads: bool = False) -> None:
         self.global_steps += 1

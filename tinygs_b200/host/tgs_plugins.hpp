@@ -8,7 +8,9 @@
 //   OptimizerBase / SimpleAdam               tinygs/include/tinygs/optim/optim.hpp:8-92,
 //                                            tinygs/include/tinygs/optim/simple_adam.hpp:8-89
 //   GPUGaussian3d                            tinygs/include/tinygs/core/gpu_gaussian.hpp:9-73
-//   train_step()                             tinygs/src/orchestrator.cu:335-439
+//   StrategyBase / DefaultStrategy           tinygs/include/tinygs/strategy/strategy.hpp:9-70,
+//                                            tinygs/src/strategy/default.cu:17-69
+//   train_step(), reorder_gaussians()        tinygs/src/orchestrator.cu:335-439, 1038-1060
 // Camera matrices are taken in the reference's glm convention (column-major
 // K and w2c, fx = K[0][0], fy = K[1][1], cx = K[2][0], cy = K[2][1]).
 // Errors are reported as std::runtime_error, as the reference does; the C
@@ -19,6 +21,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -60,29 +63,31 @@ struct Image {
 
 // SoA parameter arrays in one device allocation: 59 floats per Gaussian,
 // every segment padded to a multiple of four Gaussians (16-byte aligned).
+// The allocation holds `capacity` Gaussians; size() of them are live, so
+// densification and row operations change the count without reallocating.
 class GPUGaussian3d {
  public:
   static constexpr int kWidths[6] = {3, 1, 4, 3, 3, 45};
 
-  GPUGaussian3d(int64_t n, int sh_degree) : m_n(n), m_sh_degree(sh_degree) {
-    m_npad = (n + 3) / 4 * 4;
-    check_cuda(cudaMalloc(&m_arena, sizeof(float) * 59 * static_cast<size_t>(m_npad > 0 ? m_npad : 1)),
-               "GPUGaussian3d: cudaMalloc");
-    check_cuda(cudaMemset(m_arena, 0, sizeof(float) * 59 * static_cast<size_t>(m_npad > 0 ? m_npad : 1)),
-               "GPUGaussian3d: cudaMemset");
+  GPUGaussian3d(int64_t n, int sh_degree, int64_t capacity = 0) : m_n(n), m_sh_degree(sh_degree) {
+    m_cap = std::max<int64_t>(capacity, n);
+    m_npad = (m_cap + 3) / 4 * 4;
+    m_arena = alloc_arena(m_npad);
   }
   ~GPUGaussian3d() { cudaFree(m_arena); }
   GPUGaussian3d(const GPUGaussian3d&) = delete;
   GPUGaussian3d& operator=(const GPUGaussian3d&) = delete;
 
   int64_t size() const { return m_n; }
+  int64_t capacity() const { return m_cap; }
   int get_sh_degree() const { return m_sh_degree; }
   void set_sh_degree(int d) { m_sh_degree = d; }
-  float* segment(int k) const {
-    size_t off = 0;
-    for (int i = 0; i < k; ++i) off += size_t(kWidths[i]) * static_cast<size_t>(m_npad);
-    return m_arena + off;
+  // live count within the capacity (densification moves it)
+  void resize(int64_t n) {
+    if (n < 0 || n > m_cap) throw std::runtime_error("GPUGaussian3d::resize: beyond the capacity");
+    m_n = n;
   }
+  float* segment(int k) const { return segment_of(m_arena, m_npad, k); }
   float* means() const { return segment(0); }
   float* opacities() const { return segment(1); }
   float* rotations() const { return segment(2); }
@@ -92,18 +97,7 @@ class GPUGaussian3d {
   float* arena() const { return m_arena; }
   size_t arena_floats() const { return 59 * static_cast<size_t>(m_npad); }
 
-  TgsGaussians abi() const {
-    TgsGaussians g{};
-    g.means = means();
-    g.opacities = opacities();
-    g.rotations = rotations();
-    g.scales = scales();
-    g.sh0 = sh_coefficient_0();
-    g.sh_rest = sh_coefficients_rest();
-    g.n = m_n;
-    g.sh_degree = m_sh_degree;
-    return g;
-  }
+  TgsGaussians abi() const { return abi_of(m_arena, m_npad); }
 
   // host data per segment in the reference layout (means [n][3], ...)
   void copy_from_host(int k, const float* src, cudaStream_t s = nullptr) {
@@ -120,8 +114,91 @@ class GPUGaussian3d {
     check_cuda(cudaMemsetAsync(m_arena, value, sizeof(float) * arena_floats(), s), "GPUGaussian3d::memset");
   }
 
+  // GPUGaussian3d::reorder (gpu_gaussian.cu:273-311): row i <- row
+  // indices[i] (device indices), through a second arena that then becomes
+  // this one's.
+  void reorder(const uint32_t* indices, cudaStream_t s = nullptr) {
+    float* other = alloc_arena(m_npad);
+    TgsGaussians src = abi(), dst = abi_of(other, m_npad);
+    const int st = tgs_arena_gather(&src, &dst, indices, m_n, s);
+    swap_in(other, s);
+    check(st, "GPUGaussian3d::reorder");
+  }
+
+  // GPUGaussian3d::remove (gpu_gaussian.cu:117-160): keeps the rows whose
+  // kept_flag (device, one byte per live row) is non-zero, in order;
+  // num_kept is their number.
+  void remove(const char* kept_flag, int64_t num_kept, cudaStream_t s = nullptr) {
+    size_t ws_bytes = 0;
+    check(tgs_arena_compact_workspace_bytes(m_n, &ws_bytes), "GPUGaussian3d::remove");
+    void* ws = nullptr;
+    check_cuda(cudaMalloc(&ws, ws_bytes + 256), "GPUGaussian3d::remove: workspace");
+    float* other = alloc_arena(m_npad);
+    TgsGaussians src = abi(), dst = abi_of(other, m_npad);
+    uint32_t* count = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + ws_bytes);
+    const int st = tgs_arena_compact(&src, &dst, reinterpret_cast<const uint8_t*>(kept_flag), m_n, ws, ws_bytes,
+                                     count, s);
+    swap_in(other, s);
+    cudaFree(ws);
+    check(st, "GPUGaussian3d::remove");
+    m_n = num_kept;
+  }
+
+  // GPUGaussian3d::append (gpu_gaussian.cu:162-171): num_dup zero rows at the
+  // end, growing the allocation if the capacity is too small.
+  void append(int64_t num_dup, cudaStream_t s = nullptr) {
+    if (m_n + num_dup > m_cap) {
+      const int64_t cap = std::max<int64_t>(m_n + num_dup, m_cap * 3 / 2);
+      const int64_t npad = (cap + 3) / 4 * 4;
+      float* other = alloc_arena(npad);
+      for (int k = 0; k < 6; ++k)
+        check_cuda(cudaMemcpyAsync(segment_of(other, npad, k), segment(k),
+                                   sizeof(float) * kWidths[k] * static_cast<size_t>(m_n), cudaMemcpyDeviceToDevice, s),
+                   "GPUGaussian3d::append");
+      check_cuda(cudaStreamSynchronize(s), "GPUGaussian3d::append");
+      cudaFree(m_arena);
+      m_arena = other;
+      m_cap = cap;
+      m_npad = npad;
+    }
+    for (int k = 0; k < 6; ++k)
+      check_cuda(cudaMemsetAsync(segment(k) + kWidths[k] * m_n, 0, sizeof(float) * kWidths[k] * size_t(num_dup), s),
+                 "GPUGaussian3d::append");
+    m_n += num_dup;
+  }
+
  private:
-  int64_t m_n = 0, m_npad = 0;
+  static float* alloc_arena(int64_t npad) {
+    float* a = nullptr;
+    const size_t bytes = sizeof(float) * 59 * static_cast<size_t>(npad > 0 ? npad : 1);
+    check_cuda(cudaMalloc(&a, bytes), "GPUGaussian3d: cudaMalloc");
+    check_cuda(cudaMemset(a, 0, bytes), "GPUGaussian3d: cudaMemset");
+    return a;
+  }
+  static float* segment_of(float* arena, int64_t npad, int k) {
+    size_t off = 0;
+    for (int i = 0; i < k; ++i) off += size_t(kWidths[i]) * static_cast<size_t>(npad);
+    return arena + off;
+  }
+  TgsGaussians abi_of(float* arena, int64_t npad) const {
+    TgsGaussians g{};
+    g.means = segment_of(arena, npad, 0);
+    g.opacities = segment_of(arena, npad, 1);
+    g.rotations = segment_of(arena, npad, 2);
+    g.scales = segment_of(arena, npad, 3);
+    g.sh0 = segment_of(arena, npad, 4);
+    g.sh_rest = segment_of(arena, npad, 5);
+    g.n = m_n;
+    g.sh_degree = m_sh_degree;
+    return g;
+  }
+  void swap_in(float* other, cudaStream_t s) {
+    check_cuda(cudaStreamSynchronize(s), "GPUGaussian3d: sync");
+    cudaFree(m_arena);
+    m_arena = other;
+  }
+
+  int64_t m_n = 0, m_cap = 0, m_npad = 0;
   int m_sh_degree = 0;
   float* m_arena = nullptr;
 };
@@ -308,9 +385,17 @@ class OptimizerBase {
       : m_gaussians(std::move(g)), m_gaussians_grad(std::move(grad)) {}
   virtual ~OptimizerBase() = default;
   virtual void step(float scale, cudaStream_t stream) = 0;
+  // optim.hpp:61-76: row hooks the strategy and the reorder call
+  virtual void remove(char* /*kept_flag*/, int /*num_kept*/) {}
+  virtual void duplicate(int* /*indices*/, int* /*new_indices*/, int /*num_duplicate*/) {}
+  virtual void reset(int* indices, int num_reset) = 0;
+  virtual void reset_opacity() = 0;
+  virtual void reorder(uint32_t* indices) = 0;
   void set_lr(float lr) { m_global_lr = lr; }
   float get_lr() const { return m_global_lr; }
   GaussianOptimizationParams& params() { return m_params; }
+  std::shared_ptr<GPUGaussian3d> get_gaussians() const { return m_gaussians; }
+  std::shared_ptr<GPUGaussian3d> get_gaussians_grad() const { return m_gaussians_grad; }
 
  protected:
   std::shared_ptr<GPUGaussian3d> m_gaussians, m_gaussians_grad;
@@ -322,12 +407,15 @@ class SimpleAdam final : public OptimizerBase {
  public:
   SimpleAdam(std::shared_ptr<GPUGaussian3d> g, std::shared_ptr<GPUGaussian3d> grad)
       : OptimizerBase(g, grad),
-        m_first(std::make_shared<GPUGaussian3d>(g->size(), g->get_sh_degree())),
-        m_second(std::make_shared<GPUGaussian3d>(g->size(), g->get_sh_degree())) {}
+        m_first(std::make_shared<GPUGaussian3d>(g->size(), g->get_sh_degree(), g->capacity())),
+        m_second(std::make_shared<GPUGaussian3d>(g->size(), g->get_sh_degree(), g->capacity())) {}
 
   SimpleAdamParameters& adam_params() { return m_adam; }
   void set_scene_scale(float s) { m_scene_scale = s; }
   void set_zero_grads_after_step(bool z) { m_zero_grads = z; }
+  void set_stream(cudaStream_t s) { m_stream = s; }
+  GPUGaussian3d& first() { return *m_first; }
+  GPUGaussian3d& second() { return *m_second; }
 
   void step(float scale, cudaStream_t stream) override {
     ++m_global_steps;
@@ -342,13 +430,187 @@ class SimpleAdam final : public OptimizerBase {
           "SimpleAdam::step");
   }
 
+  // SimpleAdam::remove (simple_adam.cu:841-903): both moments compacted to
+  // the kept rows.
+  void remove(char* kept_flag, int num_kept) override {
+    m_first->remove(kept_flag, num_kept, m_stream);
+    m_second->remove(kept_flag, num_kept, m_stream);
+  }
+  // SimpleAdam::duplicate (simple_adam.cu:905-924): the moments grow to the
+  // new size with zero rows (the indices are not used).
+  void duplicate(int*, int*, int num_duplicate) override {
+    if (num_duplicate <= 0) return;
+    m_first->append(num_duplicate, m_stream);
+    m_second->append(num_duplicate, m_stream);
+  }
+  // SimpleAdam::reset (simple_adam.cu:944-982): both moments of the rows
+  // zeroed (indices on the device).
+  void reset(int* indices, int num_reset) override {
+    if (num_reset <= 0) return;
+    for (auto* m : {m_first.get(), m_second.get()}) {
+      TgsGaussians a = m->abi();
+      check(tgs_arena_fill_rows(&a, indices, num_reset, 0.0f, -1, m_stream), "SimpleAdam::reset");
+    }
+  }
+  // SimpleAdam::reset_opacity (simple_adam.cu:984-987): every opacity moment
+  // zeroed.
+  void reset_opacity() override {
+    for (auto* m : {m_first.get(), m_second.get()})
+      check_cuda(cudaMemsetAsync(m->opacities(), 0, sizeof(float) * static_cast<size_t>(m->size()), m_stream),
+                 "SimpleAdam::reset_opacity");
+  }
+  // SimpleAdam::reorder (simple_adam.cu:1036-1099): both moments gathered.
+  void reorder(uint32_t* indices) override {
+    m_first->reorder(indices, m_stream);
+    m_second->reorder(indices, m_stream);
+  }
+  // live count of both moments (after an in-place densification)
+  void resize(int64_t n) {
+    m_first->resize(n);
+    m_second->resize(n);
+  }
+
  private:
   SimpleAdamParameters m_adam;
   std::shared_ptr<GPUGaussian3d> m_first, m_second;
   uint32_t m_global_steps = 0;
   float m_scene_scale = 1.0f;
   bool m_zero_grads = false;
+  cudaStream_t m_stream = nullptr;
 };
+
+// tinygs::StrategyParams (tinygs/include/tinygs/strategy/strategy.hpp:9-29)
+// with the reference defaults.
+struct StrategyParams {
+  float pruning_opacity_threshold = 0.005f;
+  float pruning_scale_threshold = 0.1f;
+  float max_screen_size = 10.0f;
+  float duplicate_grad_threshold = 0.0002f;
+  float duplicate_scale_threshold = 0.01f;
+  bool absgrad = false;
+  int refine_every = 100;
+  int start_refine = 500;
+  int end_refine = 15000;
+  int64_t max_num_gaussians = 10000000;
+  int reset_every = 3000;
+  uint64_t seed = 42;
+};
+
+// tinygs::StrategyBase / DefaultStrategy (strategy.hpp:31-70,
+// tinygs/src/strategy/default.cu:17-69, strategy.cpp:20-46).  The reference
+// reallocates every array through on_remove / on_duplicate; here the whole
+// refine (clone, split, prune, opacity reset) runs in place through
+// tgs_densify_step over the parameters, gradients and both Adam moments,
+// which therefore need spare capacity (GPUGaussian3d's capacity argument).
+class StrategyBase {
+ public:
+  StrategyBase(std::shared_ptr<GPUGaussian3d> g, std::shared_ptr<GPUGaussian3d> grad, std::shared_ptr<SimpleAdam> opt)
+      : m_gaussians(std::move(g)), m_gaussians_grad(std::move(grad)), m_optimizer(std::move(opt)) {}
+  virtual ~StrategyBase() = default;
+  // strategy.cpp:9-12: one step of the strategy after the optimizer step
+  void step(RasterizeContext& ctx) {
+    step_impl(ctx);
+    ++m_step_count;
+  }
+  int64_t this_step() const { return m_step_count; }
+
+ protected:
+  virtual void step_impl(RasterizeContext& ctx) = 0;
+  std::shared_ptr<GPUGaussian3d> m_gaussians, m_gaussians_grad;
+  std::shared_ptr<SimpleAdam> m_optimizer;
+  int64_t m_step_count = 0;
+};
+
+class DefaultStrategyB200 final : public StrategyBase {
+ public:
+  DefaultStrategyB200(std::shared_ptr<GPUGaussian3d> g, std::shared_ptr<GPUGaussian3d> grad,
+                      std::shared_ptr<SimpleAdam> opt, StrategyParams p = {}, float scene_scale = 1.0f)
+      : StrategyBase(std::move(g), std::move(grad), std::move(opt)), m_params(p), m_scene_scale(scene_scale) {
+    check(tgs_densify_create(m_gaussians->capacity(), &m_handle), "DefaultStrategyB200: tgs_densify_create");
+    tgs_pcg32_seed(&m_rng, m_params.seed, 1);
+    check_cuda(cudaMalloc(&m_dens, sizeof(TgsDensificationInfo) * static_cast<size_t>(m_gaussians->capacity())),
+               "DefaultStrategyB200: densification records");
+    check_cuda(cudaMemset(m_dens, 0, sizeof(TgsDensificationInfo) * static_cast<size_t>(m_gaussians->capacity())),
+               "DefaultStrategyB200: densification records");
+  }
+  ~DefaultStrategyB200() override {
+    if (m_handle) tgs_densify_destroy(m_handle);
+    cudaFree(m_dens);
+  }
+  // the records the rasterizer accumulates into (RasterizeContext::densification_info)
+  TgsDensificationInfo* densification_info() const { return m_dens; }
+
+ protected:
+  void step_impl(RasterizeContext& ctx) override {
+    TgsDensifyConfig c{};
+    c.duplicate_grad_threshold = m_params.duplicate_grad_threshold;
+    c.duplicate_scale_threshold = m_params.duplicate_scale_threshold;
+    c.pruning_opacity_threshold = m_params.pruning_opacity_threshold;
+    c.pruning_scale_threshold = m_params.pruning_scale_threshold;
+    c.max_screen_size = m_params.max_screen_size;
+    c.scene_scale = m_scene_scale;
+    c.grad_scaler = ctx.grad_scaler;
+    c.absgrad = m_params.absgrad ? 1 : 0;
+    c.refine_every = m_params.refine_every;
+    c.start_refine = m_params.start_refine;
+    c.end_refine = m_params.end_refine;
+    c.reset_every = m_params.reset_every;
+    c.image_width = static_cast<int32_t>(ctx.fwd_input.width);
+    c.image_height = static_cast<int32_t>(ctx.fwd_input.height);
+    c.max_num_gaussians = m_params.max_num_gaussians;
+    TgsGaussians p = m_gaussians->abi(), m = m_optimizer->first().abi(), v = m_optimizer->second().abi();
+    TgsGaussians g{};
+    if (m_gaussians_grad) g = m_gaussians_grad->abi();
+    int64_t n = m_gaussians->size();
+    check(tgs_densify_step(m_handle, &p, m_gaussians_grad ? &g : nullptr, &m, &v, m_dens, &c,
+                           static_cast<int32_t>(m_step_count), &m_rng, &n, ctx.stream),
+          "DefaultStrategyB200::step");
+    m_gaussians->resize(n);
+    if (m_gaussians_grad) m_gaussians_grad->resize(n);
+    m_optimizer->resize(n);
+    ctx.densification_info = m_dens;
+  }
+
+ private:
+  StrategyParams m_params;
+  float m_scene_scale;
+  TgsDensifier* m_handle = nullptr;
+  TgsPcg32 m_rng{};
+  TgsDensificationInfo* m_dens = nullptr;
+};
+
+// Orchestrator::reorder_gaussians (tinygs/src/orchestrator.cu:1038-1060):
+// Morton order of the means, applied to the parameters, the gradients, the
+// optimizer's moments and the densification records.
+inline void reorder_gaussians(GPUGaussian3d& g, GPUGaussian3d* grad, OptimizerBase* opt,
+                              TgsDensificationInfo* dens, cudaStream_t s) {
+  const int64_t n = g.size();
+  if (n == 0) return;
+  size_t ws_bytes = 0;
+  check(tgs_morton_workspace_bytes(n, &ws_bytes), "reorder_gaussians");
+  void* ws = nullptr;
+  uint32_t* perm = nullptr;
+  check_cuda(cudaMalloc(&ws, ws_bytes), "reorder_gaussians: workspace");
+  check_cuda(cudaMalloc(&perm, sizeof(uint32_t) * static_cast<size_t>(n)), "reorder_gaussians: permutation");
+  int st = tgs_morton_order(g.means(), n, ws, ws_bytes, perm, s);
+  if (st == TGS_OK) {
+    g.reorder(perm, s);
+    if (grad) grad->reorder(perm, s);
+    if (opt) opt->reorder(perm);
+    if (dens) {
+      TgsDensificationInfo* tmp = nullptr;
+      check_cuda(cudaMalloc(&tmp, sizeof(TgsDensificationInfo) * static_cast<size_t>(n)), "reorder_gaussians");
+      st = tgs_dens_gather(dens, tmp, perm, n, s);
+      cudaMemcpyAsync(dens, tmp, sizeof(TgsDensificationInfo) * static_cast<size_t>(n), cudaMemcpyDeviceToDevice, s);
+      cudaStreamSynchronize(s);
+      cudaFree(tmp);
+    }
+  }
+  cudaStreamSynchronize(s);
+  cudaFree(ws);
+  cudaFree(perm);
+  check(st, "reorder_gaussians");
+}
 
 // One Orchestrator::train_step (orchestrator.cu:335-439) without the data
 // loader, pose optimisation and strategy: zero the gradient and image
@@ -366,6 +628,11 @@ class TrainStep {
       : m_g(std::move(g)), m_grad(std::move(grad)), m_rast(rast), m_opt(opt), m_grad_scaler(grad_scaler) {}
 
   void add_loss(std::unique_ptr<LossBase> l, float w) { m_losses.push_back({std::move(l), w}); }
+  // the densification strategy stepped after the optimizer
+  void set_strategy(StrategyBase* s) { m_strategy = s; }
+  // OrchestratorConfig::reorder_gaussians_interval (0: never)
+  void set_reorder_interval(int k) { m_reorder_every = k; }
+  int64_t current_step() const { return m_step; }
 
   void run(RasterizeContext& ctx, const Image& target, const Image& loss_map) {
     m_grad->memset(0, ctx.stream);
@@ -378,6 +645,10 @@ class TrainStep {
     for (auto& wl : m_losses) wl.loss->evaluate(lc, wl.weight * m_grad_scaler);
     m_rast.backward(ctx);
     m_opt.step(1.0f / m_grad_scaler, ctx.stream);
+    if (m_strategy) m_strategy->step(ctx);
+    if (m_step > 0 && m_reorder_every > 0 && m_step % m_reorder_every == 0)
+      reorder_gaussians(*m_g, m_grad.get(), &m_opt, ctx.densification_info, ctx.stream);
+    ++m_step;
   }
 
  private:
@@ -386,6 +657,9 @@ class TrainStep {
   OptimizerBase& m_opt;
   float m_grad_scaler;
   std::vector<WeightedLoss> m_losses;
+  StrategyBase* m_strategy = nullptr;
+  int m_reorder_every = 0;
+  int64_t m_step = 0;
 };
 
 // Factory in the shape of create_rasterizer (rasterizer.cpp:44-53).

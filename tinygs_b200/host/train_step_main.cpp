@@ -5,15 +5,20 @@
 //
 // Usage: tgs_train_step <scene.bin> <out_params.bin>
 // scene.bin (little endian):
-//   char[4] "TGSB"; int32 version (1); int64 n; int32 sh_degree;
+//   char[4] "TGSB"; int32 version (1 or 2); int64 n; int32 sh_degree;
 //   int32 width, height; int32 dtype (0 fp32, 1 fp16); int32 steps;
 //   float grad_scaler; float max_grad_1;
+//   version 2 only: int64 capacity; int32 densify (0/1); int32 refine_every,
+//     start_refine, reset_every, reorder_every; float grad_threshold
+//     (DefaultStrategy run after every optimizer step, Morton reorder every
+//     reorder_every steps; 0 = never);
 //   float params[59 * n]  segments means, opacities, rotations, scales,
 //                         sh0, sh_rest in the reference layout;
 //   float K[9], w2c[16]   glm column-major; float near, far;
 //   target image          3 * Wp * Hp elements of dtype, 8x8-tiled CHW.
-// out_params.bin: float params[59 * n] in the same segment layout.
-// Prints one line per step: "step <k> loss <sum of the loss map>".
+// out_params.bin: version 1: float params[59 * n]; version 2: int64 n_final
+// then float params[59 * n_final], in the same segment layout.
+// Prints one line per step: "step <k> loss <sum of the loss map> n <count>".
 #include <cstdio>
 #include <fstream>
 #include <iostream>
@@ -68,7 +73,20 @@ int main(int argc, char** argv) {
     read_pod(f, steps);
     read_pod(f, grad_scaler);
     read_pod(f, max_grad_1);
-    if (version != 1 || n <= 0 || (dtype != 0 && dtype != 1)) throw std::runtime_error("bad scene header");
+    int64_t capacity = 0;
+    int32_t densify = 0, refine_every = 100, start_refine = 500, reset_every = 3000, reorder_every = 0;
+    float grad_threshold = 0.0002f;
+    if (version == 2) {
+      read_pod(f, capacity);
+      read_pod(f, densify);
+      read_pod(f, refine_every);
+      read_pod(f, start_refine);
+      read_pod(f, reset_every);
+      read_pod(f, reorder_every);
+      read_pod(f, grad_threshold);
+    }
+    if ((version != 1 && version != 2) || n <= 0 || (dtype != 0 && dtype != 1))
+      throw std::runtime_error("bad scene header");
     std::vector<float> params(59 * static_cast<size_t>(n));
     f.read(reinterpret_cast<char*>(params.data()), sizeof(float) * params.size());
     GPUBatchInput in;
@@ -87,8 +105,8 @@ int main(int argc, char** argv) {
 
     cudaStream_t stream;
     check_cuda(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
-    auto g = std::make_shared<GPUGaussian3d>(n, sh);
-    auto grad = std::make_shared<GPUGaussian3d>(n, sh);
+    auto g = std::make_shared<GPUGaussian3d>(n, sh, capacity);
+    auto grad = std::make_shared<GPUGaussian3d>(n, sh, capacity);
     size_t off = 0;
     for (int k = 0; k < 6; ++k) {
       g->copy_from_host(k, params.data() + off, stream);
@@ -101,9 +119,22 @@ int main(int argc, char** argv) {
 
     auto rast = create_rasterizer("fastgs_b200");
     rast->set_gaussians(g);
-    SimpleAdam adam(g, grad);
-    adam.params().max_grad_1 = max_grad_1;
-    TrainStep train(g, grad, *rast, adam, grad_scaler);
+    auto adam = std::make_shared<SimpleAdam>(g, grad);
+    adam->params().max_grad_1 = max_grad_1;
+    adam->set_stream(stream);
+    TrainStep train(g, grad, *rast, *adam, grad_scaler);
+    std::unique_ptr<DefaultStrategyB200> strategy;
+    if (densify) {
+      StrategyParams sp;
+      sp.refine_every = refine_every;
+      sp.start_refine = start_refine;
+      sp.reset_every = reset_every;
+      sp.duplicate_grad_threshold = grad_threshold;
+      sp.max_num_gaussians = capacity > 0 ? capacity : n;
+      strategy = std::make_unique<DefaultStrategyB200>(g, grad, adam, sp);
+      train.set_strategy(strategy.get());
+    }
+    train.set_reorder_interval(reorder_every);
     // the reference's default loss mix (configs/default.json:30-39)
     train.add_loss(create_loss("l1"), 0.8f);
     train.add_loss(create_loss("fused_ssim"), 0.2f);
@@ -112,6 +143,7 @@ int main(int argc, char** argv) {
     ctx.stream = stream;
     ctx.grad_scaler = grad_scaler;
     ctx.fwd_input = in;
+    if (strategy) ctx.densification_info = strategy->densification_info();
     Image out = img, gimg = img, target = img, loss = img;
     out.data = d_image;
     gimg.data = d_grad;
@@ -129,15 +161,18 @@ int main(int argc, char** argv) {
       for (size_t i = 0; i < cnt; ++i)
         sum += dtype ? half_to_float(reinterpret_cast<uint16_t*>(loss_host.data())[i])
                      : reinterpret_cast<float*>(loss_host.data())[i];
-      std::printf("step %d loss %.9g\n", s, sum);
+      std::printf("step %d loss %.9g n %lld\n", s, sum, static_cast<long long>(g->size()));
     }
+    const int64_t n_final = g->size();
+    params.assign(59 * static_cast<size_t>(n_final), 0.0f);
     off = 0;
     for (int k = 0; k < 6; ++k) {
       g->copy_to_host(k, params.data() + off, stream);
-      off += size_t(GPUGaussian3d::kWidths[k]) * static_cast<size_t>(n);
+      off += size_t(GPUGaussian3d::kWidths[k]) * static_cast<size_t>(n_final);
     }
     check_cuda(cudaStreamSynchronize(stream), "sync");
     std::ofstream o(argv[2], std::ios::binary);
+    if (version == 2) o.write(reinterpret_cast<const char*>(&n_final), sizeof(n_final));
     o.write(reinterpret_cast<const char*>(params.data()), sizeof(float) * params.size());
     for (void* p : {d_image, d_grad, d_target, d_loss}) cudaFree(p);
     cudaStreamDestroy(stream);

@@ -335,6 +335,16 @@ TGS_API int tgs_loss_l1_ssim_noalloc(int32_t dtype, int32_t width,
                                      float scale_ssim, float* loss_sum,
                                      tgs_stream_t stream);
 
+/* PSNR of pred against target, left on the device: out[0] = MSE over the
+ * 3 W H real values (pred saturated to [0, 1]), out[1] = -10 log10(MSE) (100
+ * for MSE 0).  Replaces PsnrMetric::evaluate (tinygs/src/loss/psnr.cu:72-128),
+ * which allocates, reduces with thrust and returns the value to the host;
+ * this call allocates nothing and does not synchronise.  workspace: 8 bytes
+ * of device memory (a double accumulator).  dtype TGS_FLOAT32 / TGS_FLOAT16,
+ * images in the tiled layout with zero padding. */
+TGS_API int tgs_metric_psnr(int32_t dtype, int32_t width, int32_t height, const void* pred,
+                            const void* target, void* workspace, float* out, tgs_stream_t stream);
+
 /* -------------------------------------------------------------- optimizer */
 
 /* Hyper-parameters, reference GaussianOptimizationParams + SimpleAdamParameters

@@ -137,6 +137,7 @@ PROTOTYPES = {
     "tgs_dens_gather": (c_int32, [_P, _P, _P, c_int64, _P]),
     "tgs_morton_workspace_bytes": (c_int32, [c_int64, POINTER(c_size_t)]),
     "tgs_morton_order": (c_int32, [_P, c_int64, _P, c_size_t, _P, _P]),
+    "tgs_metric_psnr": (c_int32, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P]),
     "tgs_status_string": (c_char_p, [c_int32]),
     "tgs_loss_set_accumulate": (c_int32, [c_void_p, c_int32]),
     "tgs_version": (c_char_p, []),

@@ -152,6 +152,17 @@ class GaussianSet:
                                                   int(segment), _stream_handle(stream)), "tgs_arena_fill_rows")
 
 
+def psnr(pred: torch.Tensor, target: torch.Tensor, width: int, height: int, stream=None) -> torch.Tensor:
+    """PsnrMetric::evaluate (tinygs/src/loss/psnr.cu:72-128) left on the
+    device: a float32 tensor [MSE, PSNR] (tgs_metric_psnr; no host sync)."""
+    out = torch.empty(2, dtype=torch.float32, device=pred.device)
+    ws = torch.empty(1, dtype=torch.float64, device=pred.device)
+    dtype = _abi.TGS_FLOAT16 if pred.dtype == torch.float16 else _abi.TGS_FLOAT32
+    check(load_library().tgs_metric_psnr(dtype, int(width), int(height), _ptr(pred), _ptr(target), _ptr(ws),
+                                         _ptr(out), _stream_handle(stream)), "tgs_metric_psnr")
+    return out
+
+
 def morton_order(g: GaussianSet, stream=None) -> torch.Tensor:
     """The reference's Morton order of the Gaussians' means
     (tinygs/src/orchestrator.cu:26-100): int32 device tensor perm with row i

@@ -53,7 +53,7 @@ TRAFFIC_BWD_ADAM_PER_GAUSSIAN = 1476.7
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="cfg2")
@@ -65,7 +65,11 @@ def parse():
                          "accumulation + Adam + parameter broadcast in one kernel (inbox); accumulation + Adam in "
                          "one kernel through NVLink SHARP (multicast) or over peer memory (peer); or an NCCL "
                          "all-reduce followed by Adam on every rank (nccl, the baseline); auto = inbox")
-    return ap.parse_args()
+    args = ap.parse_args()
+    args.steps_given = args.steps is not None
+    if args.steps is None:
+        args.steps = 20
+    return args
 
 
 # ----------------------------------------------------------------- clocks
@@ -724,6 +728,14 @@ def run_ours(args):
     counts = rast.counts()
     # Gaussians that touch a tile (the backward reads their screen gradients)
     touched_v = int((rast.debug_array(0, torch.int32, cfg.n) > 0).sum())
+    # evaluated (pixel, Gaussian) pairs of the last view: forward = the
+    # per-pixel contributor counts (Gaussians walked up to the last one that
+    # contributed); backward = 32 x 256 per bucket (every bucket sweeps its
+    # tile's 256 pixels past its 32 Gaussians)
+    plane = rt.image_numel(W, H) // 3
+    ncon = rast.debug_array(4, torch.int16 if fp16 else torch.int32, plane)
+    fwd_pairs = int((ncon.to(torch.int64) & (0xFFFF if fp16 else 0xFFFFFFFF)).sum())
+    bwd_pairs = int(counts.n_buckets) * 32 * 256
     ms_step = ms_dev / args.steps
     value = world * 1e3 / ms_step
     e2e_ms = ms_e2e / args.steps
@@ -787,6 +799,11 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(up_bufs[0].numel() * up_bufs[0].element_size()),
                     "d2h_bytes_per_step": 4},
             "render_mpix_s": W * H / (render_ms * 1e-3) / 1e6,
+            "blend_pairs": {"forward_pairs": fwd_pairs, "backward_pairs": bwd_pairs,
+                            "forward_gpairs_per_s": fwd_pairs / (stages["blend_forward"] * 1e-3) / 1e9,
+                            "backward_gpairs_per_s": bwd_pairs / (stages["blend_backward"] * 1e-3) / 1e9,
+                            "unit": "evaluated (pixel, Gaussian) pairs of one view; forward = sum of the per-pixel "
+                                    "contributor counts, backward = buckets x 32 x 256"},
             "stages_ms": {k: round(v, 4) for k, v in stages.items()},
             "roofline": {"bound": "hbm", "kernel": kernel, "achieved": kernel_gbs, "peak": hbm_peak,
                          "unit": "GB/s", "frac": kernel_gbs / hbm_peak, "peak_source": peak_src, "traffic": kernel_traffic,
@@ -837,10 +854,103 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_cfg3(args):
+    """BASELINE config 3, the densification-heavy run: 1M Gaussians (SH3,
+    fp32, 1280x720, 60-view orbit) trained for `steps` iterations (3000 by
+    default) with DefaultStrategy refining every 100 steps from step 100
+    (clone/split where the mean 2D gradient norm exceeds 2e-4, prune below
+    opacity 0.005, growth while below 3M -- the reference's soft cap,
+    default.cu:53), no opacity reset inside the run.  The whole run is timed
+    (refines and their two host synchronisations included); the line reports
+    iterations per second over it, the Gaussian count after each refine and
+    the refine times.  One GPU."""
+    import numpy as np
+    import torch
+
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    torch.cuda.set_device(0)
+    cfg = scene_config("cfg3", args.n)
+    W, H = cfg.width, cfg.height
+    iters = args.steps if args.steps_given else 3000
+    cap_soft = 3 * cfg.n
+    capacity = int(cap_soft * 1.5)
+    params = scenes.gaussian_params(cfg.n, cfg.sh_degree, cfg.means, cfg.seed)
+    g = rt.GaussianSet.from_numpy(params, cfg.sh_degree, capacity=capacity)
+    del params
+    opt = rt.SimpleAdam(g, g.zeros_like(), rt.AdamParams(max_grad_1=0.3))
+    dens = rt.Densifier(g, None, opt, rt.DensifyParams(refine_every=100, start_refine=100, end_refine=iters,
+                                                       reset_every=0, duplicate_grad_threshold=2e-4,
+                                                       pruning_opacity_threshold=0.005,
+                                                       max_num_gaussians=cap_soft))
+    cams = scenes.cameras(cfg)
+    targets = [torch.from_numpy(scenes.target_image(W, H, cfg.seed + 100 + k).reshape(-1)).cuda() for k in range(4)]
+    image = torch.zeros(rt.image_numel(W, H), dtype=torch.float32, device="cuda")
+    grad_image, loss_map = torch.zeros_like(image), torch.zeros_like(image)
+    loss = rt.FusedLoss(W, H)
+    loss.set_accumulate(False)
+    rast = rt.FastGSB200Rasterizer(capacity, W, H, 24 * capacity)
+    rast.set_gaussians(g)
+    stream = torch.cuda.current_stream()
+    ctx = rt.RasterizeContext(stream=stream, grad_scaler=GRAD_SCALER, fwd_output_image=image,
+                              grad_output_image=grad_image, gaussians_grad=None, accumulate=False)
+    refine_ms, counts = [], []
+
+    def step(k, timed_refines=False):
+        ctx.fwd_input = cams[k % len(cams)]
+        ctx.densification_info = dens.densification_info
+        rast.forward(ctx)
+        loss.evaluate(image, targets[k % 4], loss_map, grad_image, W, H, grad_scaler=GRAD_SCALER, stream=stream)
+        opt.fused_backward_step(rast, ctx, 1.0 / GRAD_SCALER)
+        refine = dens.step_count % 100 == 0 and 100 <= dens.step_count <= iters
+        if refine and timed_refines:
+            r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            r0.record(stream)
+        n_before = g.n
+        dens.step(ctx)
+        if refine and timed_refines:
+            r1.record(stream)
+            r1.synchronize()
+            refine_ms.append(r0.elapsed_time(r1))
+            counts.append((dens.step_count - 1, n_before, g.n))
+
+    sampler = ClockSampler(0)
+    sampler.start()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(iters):
+        step(k, timed_refines=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    c = rast.counts()
+    if c.overflow:
+        raise SystemExit("capacity overflow during the cfg3 run")
+    ms = e0.elapsed_time(e1)
+    line = {"metric": "train iters/s over the densification-heavy run (cfg3)", "value": iters * 1e3 / ms,
+            "unit": "iters/s", "n_gpus": 1, "steps": iters, "warmup": 0, "ms_per_step": ms / iters,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"cfg3: {cfg.n} Gaussians at start, SH{cfg.sh_degree}, fp32, {W}x{H}, "
+                                   f"{len(cams)}-view orbit; refine every 100 from 100 (grad 2e-4, prune opacity "
+                                   f"0.005), soft cap {cap_soft}", "gaussians_start": cfg.n,
+                       "gaussians_final": g.n, "capacity": capacity, "parallelism": "dp1"},
+            "refines": [{"step": s_, "n_in": a, "n_out": b, "ms": round(t, 3)}
+                        for (s_, a, b), t in zip(counts, refine_ms)],
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    rast.close()
+    loss.close()
+    dens.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "cfg3" and args.gpus == 1:
+        run_cfg3(args)
     else:
         run_ours(args)
 

@@ -524,6 +524,56 @@ TGS_API int tgs_raster_backward_routed(TgsRaster* r, const TgsGaussians* params,
                                        float* const* inbox_per_rank, int64_t slice_pad, int32_t world,
                                        int32_t rank, TgsDensificationInfo* dens, tgs_stream_t stream);
 
+/* ---- owner-split data parallelism (no counterpart in the reference; its
+ * accumulate_grad_steps = world, orchestrator.cu:343-403, with the views of
+ * one optimizer step rendered on `world` GPUs).  Rank r owns the Gaussians
+ * [first_r, last_r) -- their parameters and Adam moments -- and renders view
+ * r.  Per step: every owner preprocesses its slice for every rank's view and
+ * stores the screen-space records into that rank's handle
+ * (tgs_raster_preprocess_views); after a collective, every rank bins and
+ * blends its view from the records of all n Gaussians
+ * (tgs_raster_forward_gathered), evaluates the loss and runs the blend
+ * backward into its handle (tgs_raster_backward_screen); after a second
+ * collective, every owner runs the per-Gaussian backward of its slice for
+ * every view, reading the screen-space gradients from the views' handles,
+ * sums them in view order and applies Adam (tgs_raster_backward_views_adam).
+ * Only screen-space records and gradients cross NVLink, and nothing is
+ * broadcast.  Every handle must have the same capacities; slice starts are
+ * multiples of 256. */
+
+/* Exports the handle's device memory for the other ranks (CUDA IPC; open it
+ * with tgs_shared_open). */
+TGS_API int tgs_raster_share(TgsRaster* r, TgsIpcHandle* out);
+/* The handle's device memory in this process (for rank == this rank). */
+TGS_API int tgs_raster_arena(TgsRaster* r, void** arena);
+/* arenas[k]: rank k's handle memory valid in this process (this rank's own
+ * from tgs_raster_arena, the others' from tgs_shared_open). */
+TGS_API int tgs_raster_attach_views(TgsRaster* r, void* const* arenas, int32_t world, int32_t rank);
+/* Preprocess of the Gaussians [first, last) for the `world` views cams[k],
+ * each into rank k's handle (peer stores); dens (this owner's records,
+ * may be NULL) takes the maximum screen radius over the views. */
+TGS_API int tgs_raster_preprocess_views(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cams,
+                                        int32_t dtype, int64_t first, int64_t last, TgsDensificationInfo* dens,
+                                        tgs_stream_t stream);
+/* Binning and blending of this rank's view from the records of all n
+ * Gaussians that the owners stored into this handle. */
+TGS_API int tgs_raster_forward_gathered(TgsRaster* r, int64_t n, const TgsCamera* cam, int32_t dtype,
+                                        void* image, void* alpha, tgs_stream_t stream);
+/* Blend backward of this rank's view: per-Gaussian screen-space gradients
+ * into this handle (absgrad != 0: also the absolute-gradient sums). */
+TGS_API int tgs_raster_backward_screen(TgsRaster* r, const TgsCamera* cam, int32_t dtype, const void* image,
+                                       const void* grad_image, int32_t absgrad, tgs_stream_t stream);
+/* Per-Gaussian backward of the Gaussians [first, last) for the `world`
+ * views (screen-space gradients read from the views' handles), summed in
+ * view order into `grads` (full-size scratch set), then the Adam step of
+ * tgs_adam_step on those rows of params / exp_avg / exp_avg_sq with the
+ * gradient sum.  dens (may be NULL) accumulates over the views. */
+TGS_API int tgs_raster_backward_views_adam(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cams,
+                                           int64_t first, int64_t last, TgsGaussians* grads,
+                                           const TgsGaussians* exp_avg, const TgsGaussians* exp_avg_sq,
+                                           const TgsAdamConfig* cfg, uint32_t step, float gradient_scale,
+                                           TgsDensificationInfo* dens, tgs_stream_t stream);
+
 /* The owner's half of the routed exchange: the slice's gradients are the sum
  * of this rank's inbox slots (local memory, rank order), then the Adam step
  * and the parameter stores into every rank as in tgs_dp_reduce_adam. */

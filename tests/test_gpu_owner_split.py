@@ -1,0 +1,98 @@
+"""The owner-split data-parallel step emulated on ONE GPU: N rasterizer
+handles stand for N ranks (their arenas all local), one shared parameter /
+moment arena of which each emulated owner touches only its slice.  One step
+must equal the reference's accumulate_grad_steps = N on one GPU
+(orchestrator.cu:343-403: N views rendered in turn, their gradients added in
+view order, one Adam step with gradient scale 1/(grad_scaler * N)):
+  * every view's image bit-identical to a plain forward of that view (the
+    forward is deterministic and the gathered records are the same bytes);
+  * the densification records' radii (maximum over the views) and counters
+    identical;
+  * the parameters after Adam equal up to the float-atomic order of the blend
+    backward (which Adam's per-coordinate normalisation can amplify only for
+    gradients at that noise level)."""
+import numpy as np
+import pytest
+import torch
+
+from tinygs_b200 import dp as dpm
+from tinygs_b200 import runtime as rt
+from tinygs_b200 import scenes
+
+from gpu_helpers import scene
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("fp16", [False, True], ids=["fp32", "fp16"])
+def test_owner_split_step_equals_accumulated_views(cuda_lib, world, fp16):
+    cfg, params, sh, _ = scene("cfg1", n=60_001)
+    cams = scenes.cameras(cfg)[:world]
+    W, H = cfg.width, cfg.height
+    n = params["means"].shape[0]
+    dt = torch.float16 if fp16 else torch.float32
+    dtype = rt._abi.TGS_FLOAT16 if fp16 else rt._abi.TGS_FLOAT32
+    acfg = rt.AdamParams(max_grad_1=0.3)
+    scale = 1.0 / (10.0 * world)
+    targets = [torch.from_numpy(scenes.target_image(W, H, 500 + v).reshape(-1)).to(dt).cuda() for v in range(world)]
+    numel = rt.image_numel(W, H)
+    loss = rt.FusedLoss(W, H)
+
+    # reference: one GPU, the N views accumulated, one Adam step
+    g_ref = rt.GaussianSet.from_numpy(params, sh)
+    grads_ref = g_ref.zeros_like()
+    opt_ref = rt.SimpleAdam(g_ref, grads_ref, acfg)
+    dens_ref = torch.zeros(n, 4, device="cuda")
+    rast_ref = rt.FastGSB200Rasterizer(n, W, H)
+    rast_ref.set_gaussians(g_ref)
+    ref_images = []
+    for v in range(world):
+        img, gimg, lmap = (torch.zeros(numel, dtype=dt, device="cuda") for _ in range(3))
+        ctx = rt.RasterizeContext(fwd_input=cams[v], fwd_output_image=img, grad_output_image=gimg,
+                                  gaussians_grad=grads_ref, densification_info=dens_ref, accumulate=v > 0)
+        rast_ref.forward(ctx)
+        loss.evaluate(img, targets[v], lmap, gimg, W, H, grad_scaler=10.0)
+        rast_ref.backward(ctx)
+        ref_images.append(img)
+    opt_ref.step(scale)
+
+    # N emulated owners on this GPU
+    g = rt.GaussianSet.from_numpy(params, sh)
+    rasts = [rt.FastGSB200Rasterizer(n, W, H) for _ in range(world)]
+    arenas = [r.arena() for r in rasts]
+    for r, ra in enumerate(rasts):
+        ra.attach_views(arenas, r)
+    grads, m, v_ = g.zeros_like(), g.zeros_like(), g.zeros_like()
+    dens = torch.zeros(n, 4, device="cuda")
+    slices = [dpm.owner_slice(n, world, r) for r in range(world)]
+    assert slices[0][0] == 0 and slices[-1][1] == n and all(a % 256 == 0 for a, _ in slices)
+    for r, ra in enumerate(rasts):
+        ra.preprocess_views(g, cams, dtype, *slices[r], dens)
+    images = []
+    for r, ra in enumerate(rasts):
+        img, gimg, lmap = (torch.zeros(numel, dtype=dt, device="cuda") for _ in range(3))
+        ra.forward_gathered(n, cams[r], img)
+        loss.evaluate(img, targets[r], lmap, gimg, W, H, grad_scaler=10.0)
+        ra.backward_screen(cams[r], img, gimg)
+        images.append(img)
+    for r, ra in enumerate(rasts):
+        ra.backward_views_adam(g, cams, *slices[r], grads, m, v_, acfg, 1, scale, dens)
+    torch.cuda.synchronize()
+
+    for v in range(world):
+        assert torch.equal(images[v], ref_images[v]), v
+    d, dr = dens.cpu().numpy(), dens_ref.cpu().numpy()
+    np.testing.assert_array_equal(d[:, 3], dr[:, 3])  # max screen radius over the views
+    np.testing.assert_array_equal(d[:, 0], dr[:, 0])  # views in which a Gaussian touched a tile
+    np.testing.assert_allclose(d[:, 1], dr[:, 1], rtol=1e-4, atol=1e-9)
+    got, want = g.to_numpy(), g_ref.to_numpy()
+    for k in want:
+        a, b = got[k].ravel(), want[k].ravel()
+        close = np.abs(a - b) <= 1e-6 + 1e-5 * np.abs(b)
+        assert close.mean() > 0.999, (k, close.mean())
+        assert np.abs(a - b).max() <= 2.5e-2, k
+    for ra in rasts:
+        ra.close()
+    rast_ref.close()
+    loss.close()

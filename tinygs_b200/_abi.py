@@ -138,6 +138,16 @@ PROTOTYPES = {
     "tgs_morton_workspace_bytes": (c_int32, [c_int64, POINTER(c_size_t)]),
     "tgs_morton_order": (c_int32, [_P, c_int64, _P, c_size_t, _P, _P]),
     "tgs_metric_psnr": (c_int32, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P]),
+    "tgs_raster_share": (c_int32, [_P, POINTER(TgsIpcHandle)]),
+    "tgs_raster_arena": (c_int32, [_P, POINTER(c_void_p)]),
+    "tgs_raster_attach_views": (c_int32, [_P, POINTER(c_void_p), c_int32, c_int32]),
+    "tgs_raster_preprocess_views": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int32, c_int64,
+                                              c_int64, _P, _P]),
+    "tgs_raster_forward_gathered": (c_int32, [_P, c_int64, POINTER(TgsCamera), c_int32, _P, _P, _P]),
+    "tgs_raster_backward_screen": (c_int32, [_P, POINTER(TgsCamera), c_int32, _P, _P, c_int32, _P]),
+    "tgs_raster_backward_views_adam": (c_int32, [_P, POINTER(TgsGaussians), POINTER(TgsCamera), c_int64, c_int64,
+                                                 POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                                 POINTER(TgsAdamConfig), c_uint32, c_float, _P, _P]),
     "tgs_status_string": (c_char_p, [c_int32]),
     "tgs_loss_set_accumulate": (c_int32, [c_void_p, c_int32]),
     "tgs_version": (c_char_p, []),

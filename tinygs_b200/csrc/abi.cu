@@ -70,6 +70,10 @@ struct TgsRaster {
   void* arena = nullptr;
   size_t arena_bytes = 0;
   int device = 0;
+  // owner-split data parallelism: the arenas of every rank's handle (same
+  // capacities, hence the same layout), valid in this process
+  char* peer_arena[kMaxDpRanks] = {};
+  int world = 1, rank = 0;
   // stage timing (profiling only): events between the stages
   bool timing = false;
   cudaEvent_t ev[7] = {};
@@ -697,6 +701,143 @@ int tgs_dp_inbox_adam(const TgsGaussians* params_per_rank, const float* inbox, i
   adam_segments(cfg, n, step, gradient_scale, &a);
   launch_dp_adam(p, g, world, rank, to_ptrs(exp_avg), to_ptrs(exp_avg_sq), a, static_cast<cudaStream_t>(stream),
                  true);
+  return cuda_status(cudaGetLastError());
+}
+
+
+// ------------------------------------------------------- owner-split views
+
+namespace {
+// The handle state of rank k's view: every scratch pointer rebased onto
+// rank k's arena (identical capacities give identical carving).
+RasterState view_state(const TgsRaster* r, int k) {
+  RasterState v = r->s;
+  size_t bytes = 0;
+  carve(v, r->peer_arena[k], bytes);
+  return v;
+}
+
+bool slice_ok(const TgsRaster* r, const TgsGaussians* params, int64_t first, int64_t last) {
+  return first >= 0 && first <= last && last <= params->n && first % 256 == 0 && params->n <= r->s.cap_n;
+}
+}  // namespace
+
+int tgs_raster_share(TgsRaster* r, TgsIpcHandle* out) {
+  if (r == nullptr || out == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, r->arena) != cudaSuccess) {
+    cudaGetLastError();
+    return TGS_ERR_CUDA;
+  }
+  std::memcpy(out->bytes, &h, sizeof(h));
+  return TGS_OK;
+}
+
+int tgs_raster_arena(TgsRaster* r, void** arena) {
+  if (r == nullptr || arena == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  *arena = r->arena;
+  return TGS_OK;
+}
+
+int tgs_raster_attach_views(TgsRaster* r, void* const* arenas, int32_t world, int32_t rank) {
+  if (r == nullptr || arenas == nullptr || world < 1 || world > kMaxDpRanks || rank < 0 || rank >= world)
+    return TGS_ERR_INVALID_ARGUMENT;
+  for (int k = 0; k < world; ++k) {
+    if (arenas[k] == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+    r->peer_arena[k] = static_cast<char*>(arenas[k]);
+  }
+  for (int k = world; k < kMaxDpRanks; ++k) r->peer_arena[k] = nullptr;
+  r->world = world;
+  r->rank = rank;
+  return TGS_OK;
+}
+
+int tgs_raster_preprocess_views(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cams, int32_t dtype,
+                                int64_t first, int64_t last, TgsDensificationInfo* dens, tgs_stream_t stream) {
+  if (r == nullptr || !gaussians_ok(params) || cams == nullptr || (dtype != TGS_FLOAT32 && dtype != TGS_FLOAT16) ||
+      r->peer_arena[0] == nullptr || !slice_ok(r, params, first, last))
+    return TGS_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const GaussianPtrs g = to_ptrs(params);
+  for (int k = 0; k < r->world; ++k) {
+    const TgsCamera* c = &cams[k];
+    if (!camera_ok(c) || c->width > r->s.max_w || c->height > r->s.max_h) return TGS_ERR_INVALID_ARGUMENT;
+    const DevCamera dc = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane,
+                                     c->w2c);
+    if (last > first) launch_preprocess(view_state(r, k), g, dc, dtype == TGS_FLOAT16,
+                                        reinterpret_cast<float4*>(dens), st, first, last);
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+int tgs_raster_forward_gathered(TgsRaster* r, int64_t n, const TgsCamera* cam, int32_t dtype, void* image,
+                                void* alpha, tgs_stream_t stream) {
+  if (r == nullptr || n < 0 || !camera_ok(cam) || image == nullptr || (dtype != TGS_FLOAT32 && dtype != TGS_FLOAT16))
+    return TGS_ERR_INVALID_ARGUMENT;
+  RasterState& s = r->s;
+  if (n > s.cap_n || cam->width > s.max_w || cam->height > s.max_h) return TGS_ERR_CAPACITY;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const DevCamera dc = make_camera(cam->width, cam->height, cam->fx, cam->fy, cam->cx, cam->cy, cam->near_plane,
+                                   cam->far_plane, cam->w2c);
+  cudaMemsetAsync(s.counts, 0, sizeof(DevCounts), st);
+  s.have_forward = 0;
+  mark(r, 0, st);
+  mark(r, 1, st);
+  launch_binning(s, n, dc, dtype == TGS_FLOAT16, st);
+  mark(r, 2, st);
+  launch_blend_forward(s, dc, dtype == TGS_FLOAT16, image, alpha, st);
+  mark(r, 3, st);
+  r->fwd_timed = r->timing;
+  if (cudaGetLastError() != cudaSuccess) return TGS_ERR_CUDA;
+  s.have_forward = 1;
+  s.last_dtype = dtype;
+  s.last_n = n;
+  return TGS_OK;
+}
+
+int tgs_raster_backward_screen(TgsRaster* r, const TgsCamera* cam, int32_t dtype, const void* image,
+                               const void* grad_image, int32_t absgrad, tgs_stream_t stream) {
+  if (r == nullptr || !camera_ok(cam) || image == nullptr || grad_image == nullptr) return TGS_ERR_INVALID_ARGUMENT;
+  RasterState& s = r->s;
+  if (!s.have_forward || s.last_dtype != dtype) return TGS_ERR_NO_FORWARD;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const DevCamera dc = make_camera(cam->width, cam->height, cam->fx, cam->fy, cam->cx, cam->cy, cam->near_plane,
+                                   cam->far_plane, cam->w2c);
+  mark(r, 4, st);
+  launch_blend_backward(s, dc, dtype == TGS_FLOAT16, image, grad_image, absgrad != 0, st);
+  mark(r, 5, st);
+  mark(r, 6, st);
+  r->bwd_timed = r->timing;
+  return cuda_status(cudaGetLastError());
+}
+
+int tgs_raster_backward_views_adam(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cams, int64_t first,
+                                   int64_t last, TgsGaussians* grads, const TgsGaussians* exp_avg,
+                                   const TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg, uint32_t step,
+                                   float gradient_scale, TgsDensificationInfo* dens, tgs_stream_t stream) {
+  if (r == nullptr || !gaussians_ok(params) || cams == nullptr || !gaussians_ok(grads) || !gaussians_ok(exp_avg) ||
+      !gaussians_ok(exp_avg_sq) || cfg == nullptr || step == 0 || r->peer_arena[0] == nullptr ||
+      !slice_ok(r, params, first, last) || grads->n != params->n || exp_avg->n != params->n ||
+      exp_avg_sq->n != params->n)
+    return TGS_ERR_INVALID_ARGUMENT;
+  if (last == first) return TGS_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const GaussianPtrs g = to_ptrs(params), gr = to_ptrs(grads), m = to_ptrs(exp_avg), v = to_ptrs(exp_avg_sq);
+  AdamStepArgs a{};
+  adam_segments(cfg, params->n, step, gradient_scale, &a);
+  float4* d = reinterpret_cast<float4*>(dens);
+  for (int k = 0; k < r->world; ++k) {
+    const TgsCamera* c = &cams[k];
+    if (!camera_ok(c)) return TGS_ERR_INVALID_ARGUMENT;
+    const DevCamera dc = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane,
+                                     c->w2c);
+    const RasterState vs = view_state(r, k);
+    if (k + 1 < r->world)  // views 0 .. world-2 summed into `grads`, in view order
+      launch_preprocess_backward(vs, g, gr, dc, k > 0 ? 1 : 0, d, st, nullptr, nullptr, nullptr, nullptr, first,
+                                 last);
+    else  // the last view: its gradients plus the sum so far, then Adam
+      launch_preprocess_backward(vs, g, gr, dc, r->world > 1 ? 1 : 0, d, st, &m, &v, &a, nullptr, first, last);
+  }
   return cuda_status(cudaGetLastError());
 }
 

@@ -109,7 +109,7 @@ void sort_pairs_u32(uint32_t* keys[2], uint32_t* vals[2], const uint32_t* count_
 
 // forward stages (preprocess.cu, binning.cu, blend.cu)
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam,
-                       int fp16, float4* dens, cudaStream_t stream);
+                       int fp16, float4* dens, cudaStream_t stream, int64_t first = 0, int64_t last = -1);
 void launch_binning(RasterState& s, int64_t n, const DevCamera& cam, int fp16, cudaStream_t stream);
 void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, void* image,
                           void* alpha, cudaStream_t stream);
@@ -133,7 +133,7 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g,
                                 const GaussianPtrs& grads, const DevCamera& cam, int accumulate,
                                 float4* dens, cudaStream_t stream, const GaussianPtrs* exp_avg = nullptr,
                                 const GaussianPtrs* exp_avg_sq = nullptr, const AdamStepArgs* adam = nullptr,
-                                const GradRoute* route = nullptr);
+                                const GradRoute* route = nullptr, int64_t first = 0, int64_t last = -1);
 
 // losses (loss.cu)
 void launch_l1(int fp16, int width, int height, const void* pred, const void* target,

@@ -145,11 +145,13 @@ __global__ void __launch_bounds__(kPreBlock)
                  float2* __restrict__ mean2d, float4* __restrict__ conic_opacity,
                  PrimInfo16* __restrict__ prim_info, float* __restrict__ color,
                  float4* __restrict__ helpers,
-                 uint32_t* __restrict__ block_visible, int rest_vec) {
+                 uint32_t* __restrict__ block_visible, int rest_vec, uint32_t first_block) {
   // higher-order SH rows of the warp's 32 Gaussians, loaded coalesced (one
   // row per lane would touch 32 cache lines per load instruction)
   __shared__ __align__(16) float s_rest[kPreBlock / 32][32 * 45];
-  const uint32_t i = blockIdx.x * kPreBlock + threadIdx.x;
+  // first_block: the launch covers Gaussians from first_block * kPreBlock
+  // (a slice of the model whose records go to another rank's view)
+  const uint32_t i = (first_block + blockIdx.x) * kPreBlock + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   // start the copy of the warp's SH rows now; it lands while the projection
   // below is computed (rows of culled Gaussians are copied too)
@@ -294,7 +296,7 @@ __global__ void __launch_bounds__(kPreBlock)
   }
   // number of candidates of this block, for the compaction scan
   const uint32_t vis = __syncthreads_count(candidate);
-  if (threadIdx.x == 0) block_visible[blockIdx.x] = vis;
+  if (threadIdx.x == 0) block_visible[first_block + blockIdx.x] = vis;
 }
 
 // --------------------------------------------------------------- backward
@@ -673,8 +675,14 @@ __device__ __forceinline__ ChunkRef chunk_ref(const SegPtrs& params, const SegPt
   return r;
 }
 
+// accumulate: `r.g` holds the gradient sum of the views before this one;
+// the step uses that sum plus this view's gradient and leaves `r.g` as is
 __device__ __forceinline__ void adam_chunk(const ChunkRef& r, float4 t, float4 m, float4 v, float4 gv,
-                                           const AdamArgs& adam) {
+                                           const AdamArgs& adam, int accumulate) {
+  if (accumulate) {
+    const float4 o = *reinterpret_cast<const float4*>(r.g);
+    gv = make_float4(o.x + gv.x, o.y + gv.y, o.z + gv.z, o.w + gv.w);
+  }
   adam_element(t.x, gv.x, m.x, v.x, r.lr, r.kind, r.decay, adam);
   adam_element(t.y, gv.y, m.y, v.y, r.lr, r.kind, r.decay, adam);
   adam_element(t.z, gv.z, m.z, v.z, r.lr, r.kind, r.decay, adam);
@@ -682,16 +690,18 @@ __device__ __forceinline__ void adam_chunk(const ChunkRef& r, float4 t, float4 m
   *reinterpret_cast<float4*>(r.p) = t;
   *reinterpret_cast<float4*>(r.m) = m;
   *reinterpret_cast<float4*>(r.v) = v;
-  if (r.g != nullptr) *reinterpret_cast<float4*>(r.g) = gv;
+  if (r.g != nullptr && !accumulate) *reinterpret_cast<float4*>(r.g) = gv;
 }
 
 template <int kLo, int kHi>
 __device__ __forceinline__ void geom_round(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
                                            const SegPtrs& exp_avg_sq, const AdamArgs& adam, const float* th,
-                                           const float* g, uint32_t first, uint32_t c, float4 m, float4 v) {
+                                           const float* g, uint32_t first, uint32_t c, float4 m, float4 v,
+                                           int accumulate) {
   if (c >= seg_chunk0(5)) return;
   const ChunkRef r = chunk_ref<kLo, kHi>(params, grads, exp_avg, exp_avg_sq, adam, first, c);
-  adam_chunk(r, reinterpret_cast<const float4*>(th)[c], m, v, reinterpret_cast<const float4*>(g)[c], adam);
+  adam_chunk(r, reinterpret_cast<const float4*>(th)[c], m, v, reinterpret_cast<const float4*>(g)[c], adam,
+             accumulate);
 }
 
 __device__ __forceinline__ float4 rest_grad4(const float* sb, uint32_t e4) {
@@ -700,8 +710,9 @@ __device__ __forceinline__ float4 rest_grad4(const float* sb, uint32_t e4) {
 }
 
 __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
-                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, const float* th,
-                                               const float* g, const float* sb, uint32_t first, uint32_t lane) {
+                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, int accumulate,
+                                               const float* th, const float* g, const float* sb, uint32_t first,
+                                               uint32_t lane) {
   constexpr uint32_t kRestChunks = 45u * kWarpGaussians / 4u;  // 360
   constexpr int kBatch = 4;
   constexpr uint32_t kRestRounds = (kRestChunks + 31u) / 32u;  // 12 (the last one: lanes < 8)
@@ -728,10 +739,10 @@ __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegP
     rm[q] = reinterpret_cast<const float4*>(RM)[e4];
     rv[q] = reinterpret_cast<const float4*>(RV)[e4];
   }
-  geom_round<0, 1>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, lane, gm[0], gvv[0]);
-  geom_round<2, 2>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 32u + lane, gm[1], gvv[1]);
-  geom_round<3, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 64u + lane, gm[2], gvv[2]);
-  geom_round<4, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 96u + lane, gm[3], gvv[3]);
+  geom_round<0, 1>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, lane, gm[0], gvv[0], accumulate);
+  geom_round<2, 2>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 32u + lane, gm[1], gvv[1], accumulate);
+  geom_round<3, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 64u + lane, gm[2], gvv[2], accumulate);
+  geom_round<4, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 96u + lane, gm[3], gvv[3], accumulate);
   // sh_rest
   ChunkRef rr;
   rr.lr = adam.lr[5];
@@ -759,7 +770,8 @@ __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegP
         rr.m = exp_avg.p[5] + rest_base + 4u * e4;
         rr.v = exp_avg_sq.p[5] + rest_base + 4u * e4;
         rr.g = grads.p[5] != nullptr ? grads.p[5] + rest_base + 4u * e4 : nullptr;
-        adam_chunk(rr, reinterpret_cast<const float4*>(ts)[e4], rm[q], rv[q], rest_grad4(sb, e4), adam);
+        adam_chunk(rr, reinterpret_cast<const float4*>(ts)[e4], rm[q], rv[q], rest_grad4(sb, e4), adam,
+                   accumulate);
       }
     }
     if (b0 + kBatch < kRestRounds) {
@@ -810,8 +822,13 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
         float4 t = reinterpret_cast<const float4*>(ts)[e4];
         float4 m = reinterpret_cast<const float4*>(M)[e4];
         float4 v = reinterpret_cast<const float4*>(V)[e4];
-        const float4 gv = make_float4(slice_grad<k>(g, sb, 4 * e4), slice_grad<k>(g, sb, 4 * e4 + 1),
-                                      slice_grad<k>(g, sb, 4 * e4 + 2), slice_grad<k>(g, sb, 4 * e4 + 3));
+        float4 gv = make_float4(slice_grad<k>(g, sb, 4 * e4), slice_grad<k>(g, sb, 4 * e4 + 1),
+                                slice_grad<k>(g, sb, 4 * e4 + 2), slice_grad<k>(g, sb, 4 * e4 + 3));
+        if (accumulate) {
+          // the views before this one, summed in order in `grads`
+          const float4 o = reinterpret_cast<const float4*>(G)[e4];
+          gv = make_float4(o.x + gv.x, o.y + gv.y, o.z + gv.z, o.w + gv.w);
+        }
         adam_element(t.x, gv.x, m.x, v.x, lr, kind, decay, adam);
         adam_element(t.y, gv.y, m.y, v.y, lr, kind, decay, adam);
         adam_element(t.z, gv.z, m.z, v.z, lr, kind, decay, adam);
@@ -819,17 +836,17 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
         reinterpret_cast<float4*>(P)[e4] = t;
         reinterpret_cast<float4*>(M)[e4] = m;
         reinterpret_cast<float4*>(V)[e4] = v;
-        if (G != nullptr) reinterpret_cast<float4*>(G)[e4] = gv;
+        if (G != nullptr && !accumulate) reinterpret_cast<float4*>(G)[e4] = gv;
       }
     } else {
       for (uint32_t e = lane; e < count; e += 32) {
         float t = ts[e], m = M[e], v = V[e];
-        const float gv = slice_grad<k>(g, sb, e);
+        const float gv = accumulate ? G[e] + slice_grad<k>(g, sb, e) : slice_grad<k>(g, sb, e);
         adam_element(t, gv, m, v, lr, kind, decay, adam);
         P[e] = t;
         M[e] = m;
         V[e] = v;
-        if (G != nullptr) G[e] = gv;
+        if (G != nullptr && !accumulate) G[e] = gv;
       }
     }
   } else {
@@ -865,17 +882,19 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
     k_preprocess_backward(SegPtrs params, SegPtrs grads, SegPtrs exp_avg, SegPtrs exp_avg_sq, AdamArgs adam,
                           int accumulate, int vec, int active_bases, uint32_t n, DevCamera cam,
                           const uint32_t* __restrict__ n_touched, const float4* __restrict__ helpers,
-                          float4* __restrict__ dens, const DevCounts* __restrict__ counts, RouteArgs route) {
+                          float4* __restrict__ dens, const DevCounts* __restrict__ counts, RouteArgs route,
+                          uint32_t base) {
   __shared__ __align__(16) float smem[kBwdWarps * kWarpFloats];
   const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   uint32_t wi = blockIdx.x * kBwdWarps + warp;
-  const uint32_t n_warps = (n + kWarpGaussians - 1) / kWarpGaussians;
+  // Gaussians [base, n): base is a multiple of 32
+  const uint32_t n_warps = (n - base + kWarpGaussians - 1) / kWarpGaussians;
   if (wi >= n_warps) return;
   if constexpr (kRoute) {
     wi += route.warp_shift;
     if (wi >= n_warps) wi -= n_warps;
   }
-  const uint32_t first = wi * kWarpGaussians;
+  const uint32_t first = base + wi * kWarpGaussians;
   const uint32_t cnt = min(static_cast<uint32_t>(kWarpGaussians), n - first);
   const bool v16 = vec != 0 && cnt == kWarpGaussians;
   float* th = smem + warp * kWarpFloats;
@@ -885,8 +904,10 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
     if (v16) {
 #pragma unroll
       for (int k = 0; k < 6; ++k) {
-        if (lane == static_cast<uint32_t>(k) || lane == static_cast<uint32_t>(k + 6)) {
-          const float* ptr = (lane < 6u ? exp_avg.p[k] : exp_avg_sq.p[k]) + static_cast<size_t>(first) * seg_width(k);
+        if (lane == static_cast<uint32_t>(k) || lane == static_cast<uint32_t>(k + 6) ||
+            (accumulate && lane == static_cast<uint32_t>(k + 12))) {
+          const float* ptr = (lane < 6u ? exp_avg.p[k] : lane < 12u ? exp_avg_sq.p[k] : grads.p[k]) +
+                             static_cast<size_t>(first) * seg_width(k);
           const uint32_t bytes = 4u * kWarpGaussians * seg_width(k);
           asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(ptr), "r"(bytes) : "memory");
         }
@@ -935,7 +956,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
   if (kRoute && v16) {
     route_warp_bulk(route, th, g, sb, first, lane);
   } else if (kAdam && v16) {
-    adam_slice_v16(params, grads, exp_avg, exp_avg_sq, adam, th, g, sb, first, lane);
+    adam_slice_v16(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, lane);
   } else {
     write_segment<kAdam, 0, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
                                       lane, v16, route);
@@ -958,33 +979,38 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
 }  // namespace
 
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam, int fp16,
-                       float4* dens, cudaStream_t stream) {
-  const uint32_t n = static_cast<uint32_t>(g.n);
+                       float4* dens, cudaStream_t stream, int64_t first, int64_t last) {
+  // Gaussians [first, last) (last < 0: to g.n); first is a multiple of the
+  // block size so every block's candidate count has one writer
+  const uint32_t n = static_cast<uint32_t>(last < 0 ? g.n : last);
+  const uint32_t first_block = static_cast<uint32_t>(first / kPreBlock);
   const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
-  const uint32_t blocks = (n + kPreBlock - 1) / kPreBlock;
+  const uint32_t blocks = n > first_block * kPreBlock ? (n - first_block * kPreBlock + kPreBlock - 1) / kPreBlock : 0;
   if (blocks == 0) return;
   const int rest_vec = (reinterpret_cast<uintptr_t>(g.sh_rest) & 15u) == 0;
   if (fp16)
     k_preprocess<1><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
+        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block);
   else
     k_preprocess<0><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec);
+        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block);
 }
 
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, const GaussianPtrs& grads,
                                 const DevCamera& cam, int accumulate, float4* dens, cudaStream_t stream,
                                 const GaussianPtrs* exp_avg, const GaussianPtrs* exp_avg_sq,
-                                const AdamStepArgs* adam, const GradRoute* route) {
-  const uint32_t n = static_cast<uint32_t>(g.n);
-  if (n == 0) return;
+                                const AdamStepArgs* adam, const GradRoute* route, int64_t first, int64_t last) {
+  // Gaussians [first, last) (last < 0: to g.n); first is a multiple of 32
+  const uint32_t n = static_cast<uint32_t>(last < 0 ? g.n : last);
+  const uint32_t base = static_cast<uint32_t>(first);
+  if (n <= base) return;
   const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
   const uint32_t per_block = kBwdWarps * kWarpGaussians;
-  const uint32_t blocks = (n + per_block - 1) / per_block;
+  const uint32_t blocks = (n - base + per_block - 1) / per_block;
   auto segs = [](const GaussianPtrs& x) {
     SegPtrs p{{x.means, x.opacities, x.rotations, x.scales, x.sh0, x.sh_rest}};
     return p;
@@ -1013,8 +1039,8 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, con
     v = segs(*exp_avg_sq);
     const int vec = aligned(segs(g)) && aligned(m) && aligned(v) && aligned(segs(grads));
     k_preprocess_backward<true><<<blocks, 32 * kBwdWarps, 0, stream>>>(
-        segs(g), segs(grads), m, v, a, 0, vec, active_bases, n, cam, s.n_touched,
-        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{});
+        segs(g), segs(grads), m, v, a, accumulate, vec, active_bases, n, cam, s.n_touched,
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{}, base);
   } else if (route != nullptr) {
     RouteArgs r{};
     bool vec = aligned(segs(g));
@@ -1032,12 +1058,12 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, con
     vec = vec && route->slice_pad % 4 == 0;
     k_preprocess_backward<false, true><<<blocks, 32 * kBwdWarps, 0, stream>>>(
         segs(g), segs(grads), m, v, a, 0, vec ? 1 : 0, active_bases, n, cam, s.n_touched,
-        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, r);
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, r, base);
   } else {
     const int vec = aligned(segs(g)) && aligned(segs(grads));
     k_preprocess_backward<false><<<blocks, 32 * kBwdWarps, 0, stream>>>(
         segs(g), segs(grads), m, v, a, accumulate, vec, active_bases, n, cam, s.n_touched,
-        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{});
+        reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{}, base);
   }
 }
 

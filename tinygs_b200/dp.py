@@ -371,3 +371,94 @@ class InboxAdam:
         for p in self.opened:
             self.lib.tgs_shared_close(ctypes.c_void_p(p))
         self.opened = []
+
+
+# ------------------------------------------------------------------------
+# Owner-split step: every rank owns a slice of the Gaussians (parameters and
+# Adam moments) and renders one view.  Only screen-space records (owner ->
+# view) and screen-space gradients (view -> owner) cross NVLink; nothing is
+# broadcast, and the per-Gaussian backward + Adam work is split N ways.
+
+def owner_slice(n: int, world: int, r: int) -> tuple[int, int]:
+    """Rank r's Gaussians [first, last): starts on multiples of 256 (one
+    preprocess block has one owner)."""
+    def begin(k):
+        return n if k >= world else (n * k // world) // 256 * 256
+    return begin(r), begin(r + 1)
+
+
+class OwnerSplit:
+    """Owner-split data-parallel training step over the ranks of `dp`
+    (tgs_raster_preprocess_views / forward_gathered / backward_screen /
+    backward_views_adam).  Per step:
+
+        opt.forward(cams_of_all_ranks, image)        # records to the views, barrier, bin + blend
+        (loss into grad_image)
+        opt.backward_adam(cams_of_all_ranks, image, grad_image, scale)
+
+    Every rank holds the full parameter arena, but only its slice's rows are
+    read (preprocess, backward) and updated (Adam); the moments likewise."""
+
+    def __init__(self, dp: DataParallel, rast: "rt.FastGSB200Rasterizer", params: "rt.GaussianSet",
+                 cfg: "rt.AdamParams", dtype: int):
+        self.dp, self.rast, self.params, self.cfg, self.dtype = dp, rast, params, cfg, dtype
+        self.lib = load_library()
+        self.first, self.last = owner_slice(params.n, dp.world, dp.rank)
+        self.grads = params.zeros_like()
+        self.exp_avg, self.exp_avg_sq = params.zeros_like(), params.zeros_like()
+        self.global_steps = 0
+        self.flag = torch.zeros(1, device=params.storage.device)
+        mine = rast.share()
+        handles = [mine] * dp.world
+        if dp.world > 1:
+            handles = [None] * dp.world
+            dist.all_gather_object(handles, mine, group=dp.group)
+        self.opened: list[int] = []
+        arenas = []
+        for r, h in enumerate(handles):
+            if r == dp.rank:
+                arenas.append(rast.arena())
+                continue
+            p = ctypes.c_void_p()
+            check(self.lib.tgs_shared_open(ctypes.byref(TgsIpcHandle.from_raw(h)), ctypes.byref(p)),
+                  "tgs_shared_open")
+            self.opened.append(p.value)
+            arenas.append(p.value)
+        rast.attach_views(arenas, dp.rank)
+
+    def barrier(self, stream=None) -> None:
+        if self.dp.world > 1:
+            with torch.cuda.stream(_as_torch_stream(stream)):
+                dist.all_reduce(self.flag, group=self.dp.group)
+
+    def forward(self, cams: list[dict], image: torch.Tensor, dens: torch.Tensor | None = None, stream=None,
+                events=None) -> None:
+        """This rank's slice preprocessed for every view, then (after every
+        owner's records have landed) this rank's view binned and blended."""
+        self.rast.preprocess_views(self.params, cams, self.dtype, self.first, self.last, dens, stream)
+        if events is not None:
+            events[0].record(_as_torch_stream(stream))
+        self.barrier(stream)
+        if events is not None:
+            events[1].record(_as_torch_stream(stream))
+        self.rast.forward_gathered(self.params.n, cams[self.dp.rank], image, stream=stream)
+
+    def backward_adam(self, cams: list[dict], image: torch.Tensor, grad_image: torch.Tensor,
+                      gradient_scale: float, dens: torch.Tensor | None = None, stream=None, events=None) -> None:
+        """Blend backward of this rank's view, then (after every view's
+        screen-space gradients are in place) this rank's slice: per-Gaussian
+        backward for every view, summed in view order, and Adam."""
+        self.global_steps += 1
+        self.rast.backward_screen(cams[self.dp.rank], image, grad_image, False, stream)
+        if events is not None:
+            events[0].record(_as_torch_stream(stream))
+        self.barrier(stream)
+        if events is not None:
+            events[1].record(_as_torch_stream(stream))
+        self.rast.backward_views_adam(self.params, cams, self.first, self.last, self.grads, self.exp_avg,
+                                      self.exp_avg_sq, self.cfg, self.global_steps, gradient_scale, dens, stream)
+
+    def close(self) -> None:
+        for p in self.opened:
+            self.lib.tgs_shared_close(ctypes.c_void_p(p))
+        self.opened = []

@@ -297,6 +297,54 @@ class FastGSB200Rasterizer:
                                                   _ptr(ctx.densification_info), _stream_handle(ctx.stream)),
               "tgs_raster_backward_routed")
 
+    # ---- owner-split data parallelism (tgs_raster_preprocess_views & co.)
+    def share(self) -> bytes:
+        """The handle's device memory as a CUDA IPC handle (64 bytes)."""
+        h = _abi.TgsIpcHandle()
+        check(self.lib.tgs_raster_share(self.handle, ctypes.byref(h)), "tgs_raster_share")
+        return bytes(h.bytes)
+
+    def arena(self) -> int:
+        p = ctypes.c_void_p()
+        check(self.lib.tgs_raster_arena(self.handle, ctypes.byref(p)), "tgs_raster_arena")
+        return p.value
+
+    def attach_views(self, arenas: list[int], rank: int) -> None:
+        arr = (ctypes.c_void_p * len(arenas))(*arenas)
+        check(self.lib.tgs_raster_attach_views(self.handle, arr, len(arenas), rank), "tgs_raster_attach_views")
+
+    def preprocess_views(self, params: GaussianSet, cams: list[dict], dtype: int, first: int, last: int,
+                         dens: torch.Tensor | None = None, stream=None) -> None:
+        g = params.abi()
+        cs = (TgsCamera * len(cams))(*[make_camera(c) for c in cams])
+        check(self.lib.tgs_raster_preprocess_views(self.handle, ctypes.byref(g), cs, dtype, int(first), int(last),
+                                                   _ptr(dens), _stream_handle(stream)), "tgs_raster_preprocess_views")
+
+    def forward_gathered(self, n: int, cam: dict, image: torch.Tensor, alpha: torch.Tensor | None = None,
+                         stream=None) -> None:
+        c = make_camera(cam)
+        check(self.lib.tgs_raster_forward_gathered(self.handle, int(n), ctypes.byref(c), self._dtype(image),
+                                                   _ptr(image), _ptr(alpha), _stream_handle(stream)),
+              "tgs_raster_forward_gathered")
+
+    def backward_screen(self, cam: dict, image: torch.Tensor, grad_image: torch.Tensor, absgrad: bool = False,
+                        stream=None) -> None:
+        c = make_camera(cam)
+        check(self.lib.tgs_raster_backward_screen(self.handle, ctypes.byref(c), self._dtype(image), _ptr(image),
+                                                  _ptr(grad_image), 1 if absgrad else 0, _stream_handle(stream)),
+              "tgs_raster_backward_screen")
+
+    def backward_views_adam(self, params: GaussianSet, cams: list[dict], first: int, last: int, grads: GaussianSet,
+                            exp_avg: GaussianSet, exp_avg_sq: GaussianSet, cfg: "AdamParams", step: int,
+                            gradient_scale: float, dens: torch.Tensor | None = None, stream=None) -> None:
+        p, gr, m, v = params.abi(), grads.abi(), exp_avg.abi(), exp_avg_sq.abi()
+        cs = (TgsCamera * len(cams))(*[make_camera(c) for c in cams])
+        c = cfg.abi()
+        check(self.lib.tgs_raster_backward_views_adam(self.handle, ctypes.byref(p), cs, int(first), int(last),
+                                                      ctypes.byref(gr), ctypes.byref(m), ctypes.byref(v),
+                                                      ctypes.byref(c), int(step), float(gradient_scale), _ptr(dens),
+                                                      _stream_handle(stream)), "tgs_raster_backward_views_adam")
+
     def set_stage_timing(self, enable: bool) -> None:
         check(self.lib.tgs_raster_set_stage_timing(self.handle, 1 if enable else 0), "tgs_raster_set_stage_timing")
 

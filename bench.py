@@ -60,8 +60,11 @@ def parse():
     ap.add_argument("--n", type=int, default=0, help="override the Gaussian count (profiling small cases)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=25.0, help="seconds of CPU work for the baseline sample")
-    ap.add_argument("--dp", choices=["auto", "inbox", "multicast", "peer", "nccl"], default="auto",
-                    help="several GPUs: gradients stored into their owners' inboxes by the backward, then "
+    ap.add_argument("--dp", choices=["auto", "owner", "inbox", "multicast", "peer", "nccl"], default="auto",
+                    help="several GPUs: each rank preprocesses and back-propagates its own slice of the Gaussians "
+                         "for every rank's view, with the records and screen-space gradients exchanged through "
+                         "the ranks' arenas over NVLink, and Adam on its slice (owner); gradients stored into "
+                         "their owners' inboxes by the backward, then "
                          "accumulation + Adam + parameter broadcast in one kernel (inbox); accumulation + Adam in "
                          "one kernel through NVLink SHARP (multicast) or over peer memory (peer); or an NCCL "
                          "all-reduce followed by Adam on every rank (nccl, the baseline); auto = inbox")
@@ -468,10 +471,11 @@ def run_reference_cpu(args):
 
 # ------------------------------------------------------------------- ours
 
-def kernels_per_step(width: int, height: int, world: int) -> int:
+def kernels_per_step(width: int, height: int, world: int, owner: bool = False) -> int:
     """Launches of this library's kernels in one training step (what
     launch_preprocess / launch_binning / launch_blend_* / the loss and the
-    backward enqueue)."""
+    backward enqueue).  owner: the owner split launches the preprocess and
+    the per-Gaussian backward once per view."""
     grid_w, grid_h = (width + 15) // 16, (height + 15) // 16
     n_super = ((grid_w + 7) // 8) * ((grid_h + 3) // 4)
     entry_passes = max(1, ((max(1, n_super - 1)).bit_length() + 7) // 8)
@@ -485,6 +489,8 @@ def kernels_per_step(width: int, height: int, world: int) -> int:
                + 1)  # blend forward
     # loss forward + backward; blend backward; per-Gaussian backward fused
     # with Adam (one GPU) or routed backward + accumulation/Adam kernel
+    if owner:
+        return forward + (world - 1) + 2 + 1 + world
     return forward + 2 + 1 + (1 if world == 1 else 2)
 
 
@@ -516,6 +522,14 @@ def run_ours(args):
     peer = world > 1 and args.dp != "nccl"
     dp_impl = args.dp if world > 1 else "none"
     opt = None
+    owner = None
+    if peer and args.dp == "owner":
+        # every rank keeps the whole parameter arena but reads and updates only
+        # its own slice; the split object is made once the rasterizer exists
+        g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+        grads = None
+        opt = "owner"
+        dp_impl = "owner"
     if peer and args.dp in ("auto", "inbox"):
         # parameters the other ranks map (CUDA IPC) and a gradient inbox per
         # rank: the backward stores each Gaussian's gradients into the inbox
@@ -584,6 +598,14 @@ def run_ours(args):
             raise SystemExit("instance capacity too small for the sizing pass")
     rast.close()
     rast = make_raster(int(max_inst * 1.5) + 1024)
+    if dp_impl == "owner":
+        owner = dpm.OwnerSplit(dp, rast, g, rt.AdamParams(max_grad_1=0.3),
+                               rt._abi.TGS_FLOAT16 if fp16 else rt._abi.TGS_FLOAT32)
+        opt = owner
+
+    def views_of(step):
+        # the views of all ranks at `step`, in rank order
+        return [cams[(step * world + r) % len(cams)] for r in range(world)]
 
     def view_of(step):
         return cams[dp.view_index(step, len(cams))]
@@ -604,7 +626,14 @@ def run_ours(args):
         ctx.fwd_input = view_of(k)
         if e2e and k + 1 < last:
             upload(k + 1)  # overlaps this step's forward
-        rast.forward(ctx)
+        if owner is not None:
+            # preprocess of this rank's slice for all views (ev[7]..ev[8]),
+            # barrier, binning + blend of this rank's view
+            if ev is not None:
+                ev[7].record(stream)
+            owner.forward(views_of(k), image, stream=stream, events=None if ev is None else ev[8:10])
+        else:
+            rast.forward(ctx)
         if ev is not None:
             ev[0].record(stream)
         if e2e:
@@ -620,6 +649,13 @@ def run_ours(args):
             ev[1].record(stream)
         if fused:
             opt.fused_backward_step(rast, ctx, 1.0 / GRAD_SCALER)
+        elif owner is not None:
+            # blend backward (ev[1]..ev[5]), barrier (..ev[6]), per-Gaussian
+            # backward of the slice over all views + Adam (..ev[2])
+            owner.backward_adam(views_of(k), image, grad_image, dp.gradient_scale(GRAD_SCALER), stream=stream,
+                                events=None if ev is None else ev[5:7])
+            if ev is not None:
+                ev[2].record(stream)
         elif dp_impl == "inbox":
             rast.backward_routed(ctx, *opt.route())
             if ev is not None:
@@ -692,7 +728,7 @@ def run_ours(args):
     rast.set_stage_timing(True)
     rows = []
     for k in range(n_stage):
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(10)]
         step(args.warmup + 2 * args.steps + k, False, evs)
         torch.cuda.synchronize()
         t = rast.stage_times()
@@ -700,6 +736,12 @@ def run_ours(args):
                "blend_backward": t[3]}
         if fused:
             row["gaussian_backward_adam"] = t[4]
+        elif owner is not None:
+            row["preprocess"] = evs[7].elapsed_time(evs[8])
+            row["forward_barrier"] = evs[8].elapsed_time(evs[9])
+            row["blend_backward"] = evs[1].elapsed_time(evs[5])
+            row["backward_barrier"] = evs[5].elapsed_time(evs[6])
+            row["gaussian_backward_adam"] = evs[6].elapsed_time(evs[2])
         elif peer:
             row["gaussian_backward"] = t[4]
             row["peer_reduce_adam"] = evs[2].elapsed_time(evs[3])
@@ -739,7 +781,17 @@ def run_ours(args):
     ms_step = ms_dev / args.steps
     value = world * 1e3 / ms_step
     e2e_ms = ms_e2e / args.steps
-    if fused:
+    if owner is not None:
+        # k_preprocess_backward over this rank's slice, once per view (the
+        # last one fused with Adam): parameters read per view, the gradient
+        # sum written and re-read between views, moments read and written
+        # once, touched-tile counts and screen gradients read per view
+        nl = owner.last - owner.first
+        kernel = ("k_preprocess_backward over the rank's slice for every view (N-1 accumulating launches, then "
+                  "the launch fused with Adam)")
+        kernel_bytes = (nl * world * (236 + 4 + 48) + nl * (world - 1) * 236 * 2 + nl * 4 * 236)
+        kernel_ms = stages["gaussian_backward_adam"]
+    elif fused:
         # k_preprocess_backward<true>: parameters, both moments read and
         # written, the touched-tile counts, and the 48-byte screen-space
         # gradients of the visible Gaussians
@@ -809,7 +861,7 @@ def run_ours(args):
                          "unit": "GB/s", "frac": kernel_gbs / hbm_peak, "peak_source": peak_src, "traffic": kernel_traffic,
                          "algorithmic_bytes_per_launch": kernel_bytes, "avg_launch_ms": kernel_ms},
             "counts": {"visible": counts.n_visible, "instances": counts.n_instances, "buckets": counts.n_buckets},
-            "gpu_launches": kernels_per_step(W, H, world) * args.steps,
+            "gpu_launches": kernels_per_step(W, H, world, owner is not None) * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
@@ -817,7 +869,15 @@ def run_ours(args):
             line["densify"] = dens_row
         if world > 1:
             line["config"]["dp_impl"] = dp_impl
-        if peer:
+        if owner is not None:
+            line["owner_split"] = {
+                "slice": [owner.first, owner.last],
+                "preprocess_ms": stages["preprocess"], "forward_barrier_ms": stages["forward_barrier"],
+                "backward_barrier_ms": stages["backward_barrier"],
+                "gaussian_backward_adam_ms": stages["gaussian_backward_adam"],
+                "note": "records (preprocess) stored into the view ranks' arenas and screen-space gradients "
+                        "read back over NVLink; no gradient all-reduce"}
+        elif peer:
             # NVLink bytes into each GPU (and the same out of it) per step.
             # peer: its slice's gradients loaded from the other ranks plus the
             # other ranks' new parameters stored into it, 2 * 236 B * n/N *
@@ -845,10 +905,11 @@ def run_ours(args):
             if dp_impl == "inbox":
                 line["peer_reduce_adam"]["routed_gradient_bytes_each_way_per_gpu"] = slice_bytes * (world - 1)
         print(json.dumps(line), flush=True)
+    if peer:
+        opt.close()  # peer mappings closed on every rank before any owner frees its memory
+        dist.barrier()
     rast.close()
     loss.close()
-    if peer:
-        opt.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -929,6 +990,14 @@ def run_cfg3(args):
     if c.overflow:
         raise SystemExit("capacity overflow during the cfg3 run")
     ms = e0.elapsed_time(e1)
+    # the statistic the refines test, over the steps after the last refine
+    # (accumulated, not yet consumed): how many Gaussians pass the threshold
+    info = dens.densification_info[: g.n].float()
+    seen = info[:, 0] > 0
+    mean_grad = info[seen, 1] / info[seen, 0]
+    q = torch.quantile(mean_grad[: 1 << 24], torch.tensor([0.5, 0.99, 0.999], device=mean_grad.device))
+    grad_stats = {"seen": int(seen.sum()), "above_threshold": int((mean_grad > 2e-4).sum()),
+                  "median": float(q[0]), "p99": float(q[1]), "p999": float(q[2]), "max": float(mean_grad.max())}
     line = {"metric": "train iters/s over the densification-heavy run (cfg3)", "value": iters * 1e3 / ms,
             "unit": "iters/s", "n_gpus": 1, "steps": iters, "warmup": 0, "ms_per_step": ms / iters,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -938,6 +1007,7 @@ def run_cfg3(args):
                        "gaussians_final": g.n, "capacity": capacity, "parallelism": "dp1"},
             "refines": [{"step": s_, "n_in": a, "n_out": b, "ms": round(t, 3)}
                         for (s_, a, b), t in zip(counts, refine_ms)],
+            "mean_grad2d_after_last_refine": grad_stats,
             "clocks": clocks}
     print(json.dumps(line), flush=True)
     rast.close()

@@ -178,3 +178,107 @@ def test_routed_training_step_two_gpus(tmp_path):
     for k in ref:
         close = np.abs(r0[k] - ref[k]) <= 1e-6 + 1e-5 * np.abs(ref[k])
         assert close.mean() > 0.999, (k, close.mean())
+
+
+def _owner_worker(rank: int, port: int, out_dir: str, dtype_name: str) -> None:
+    """Two owner-split training steps per rank (rank r renders view 2s + r)."""
+    import torch.distributed as dist
+
+    from tinygs_b200 import dp as dpm
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        dp = dpm.DataParallel.from_env()
+        cfg = scenes.CONFIGS["cfg1"]
+        n = 20_001
+        params = scenes.gaussian_params(n, cfg.sh_degree, cfg.means, 9)
+        cams = scenes.cameras(cfg)
+        W, H = cams[0]["width"], cams[0]["height"]
+        fp16 = dtype_name == "fp16"
+        dt = torch.float16 if fp16 else torch.float32
+        g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+        rast = rt.FastGSB200Rasterizer(n, W, H)
+        rast.set_gaussians(g)
+        opt = dpm.OwnerSplit(dp, rast, g, rt.AdamParams(max_grad_1=0.3),
+                             rt._abi.TGS_FLOAT16 if fp16 else rt._abi.TGS_FLOAT32)
+        img = torch.zeros(rt.image_numel(W, H), dtype=dt, device="cuda")
+        gimg, lmap = torch.zeros_like(img), torch.zeros_like(img)
+        loss = rt.FusedLoss(W, H)
+        images = []
+        for s in range(2):
+            views = [cams[2 * s + r] for r in range(2)]
+            tgt = torch.from_numpy(scenes.target_image(W, H, 3 + 2 * s + rank).reshape(-1)).to(dt).cuda()
+            opt.forward(views, img)
+            loss.evaluate(img, tgt, lmap, gimg, W, H, grad_scaler=10.0)
+            opt.backward_adam(views, img, gimg, dp.gradient_scale(10.0))
+            images.append(img.float().cpu().numpy())
+        torch.cuda.synchronize()
+        out = {k: v[opt.first:opt.last] for k, v in g.to_numpy().items()}
+        np.savez(os.path.join(out_dir, f"owner{rank}.npz"), first=opt.first, last=opt.last, img0=images[0],
+                 img1=images[1], **out)
+        opt.barrier()
+        opt.close()
+        dist.barrier()
+        rast.close()
+        loss.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("dtype_name", ["fp32", "fp16"])
+def test_owner_split_two_gpus(tmp_path, dtype_name):
+    """Each rank's slice after two owner-split steps equals one GPU
+    accumulating the same two views per step and stepping Adam, up to the
+    float-atomic order noise of the blend backward; the first step's images
+    are those of one GPU rendering the view."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    from tinygs_b200 import runtime as rt
+    from tinygs_b200 import scenes
+
+    mp.start_processes(_owner_worker, args=(_free_port(), str(tmp_path), dtype_name), nprocs=2,
+                       start_method="spawn")
+    rk = [np.load(tmp_path / f"owner{k}.npz") for k in range(2)]
+    assert int(rk[0]["first"]) == 0 and int(rk[0]["last"]) == int(rk[1]["first"])
+    cfg = scenes.CONFIGS["cfg1"]
+    n = 20_001
+    assert int(rk[1]["last"]) == n
+    params = scenes.gaussian_params(n, cfg.sh_degree, cfg.means, 9)
+    cams = scenes.cameras(cfg)
+    W, H = cams[0]["width"], cams[0]["height"]
+    fp16 = dtype_name == "fp16"
+    dt = torch.float16 if fp16 else torch.float32
+    g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
+    grads = g.zeros_like()
+    opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
+    rast = rt.FastGSB200Rasterizer(n, W, H)
+    rast.set_gaussians(g)
+    loss = rt.FusedLoss(W, H)
+    img = torch.zeros(rt.image_numel(W, H), dtype=dt, device="cuda")
+    gimg, lmap = torch.zeros_like(img), torch.zeros_like(img)
+    for s in range(2):
+        for r in range(2):
+            ctx = rt.RasterizeContext(fwd_input=cams[2 * s + r], fwd_output_image=img, grad_output_image=gimg,
+                                      gaussians_grad=grads, grad_scaler=10.0, accumulate=r > 0)
+            rast.forward(ctx)
+            if s == 0:
+                np.testing.assert_array_equal(rk[r]["img0"], img.float().cpu().numpy())
+            tgt = torch.from_numpy(scenes.target_image(W, H, 3 + 2 * s + r).reshape(-1)).to(dt).cuda()
+            loss.evaluate(img, tgt, lmap, gimg, W, H, grad_scaler=10.0)
+            rast.backward(ctx)
+        opt.step(1.0 / (10.0 * 2))
+    ref = g.to_numpy()
+    rast.close()
+    loss.close()
+    for k in ref:
+        got = np.concatenate([rk[0][k], rk[1][k]])
+        close = np.abs(got - ref[k]) <= 1e-6 + 1e-5 * np.abs(ref[k])
+        assert close.mean() > 0.999, (k, close.mean())

@@ -57,6 +57,11 @@ extern "C" {
 /* Image / rasterizer arithmetic type (reference tinygs::DataType, image.hpp:6-11). */
 #define TGS_FLOAT32 0
 #define TGS_FLOAT16 1
+#define TGS_UINT8   2  /* image data path only */
+
+/* Layouts of 8-bit host images (tgs_image_from_u8). */
+#define TGS_IMAGE_TILED_CHW 0  /* channel planes of 8x8 tiles, padded to multiples of 8 (Image, image.hpp) */
+#define TGS_IMAGE_HWC       1  /* decoded rows, 3 (RGB) or 4 (RGBA) bytes per pixel, no padding */
 
 /* Opaque stream handle: a cudaStream_t passed through as a pointer. */
 typedef void* tgs_stream_t;
@@ -344,6 +349,43 @@ TGS_API int tgs_loss_l1_ssim_noalloc(int32_t dtype, int32_t width,
  * images in the tiled layout with zero padding. */
 TGS_API int tgs_metric_psnr(int32_t dtype, int32_t width, int32_t height, const void* pred,
                             const void* target, void* workspace, float* out, tgs_stream_t stream);
+
+/* ------------------------------------------------------------- data path */
+
+/* An 8-bit image already on the device (src) into the rasterizer's tiled
+ * layout in dst_dtype (TGS_FLOAT32 / TGS_FLOAT16: value / 255, fp16 rounded
+ * to nearest; TGS_UINT8: the bytes).
+ *   layout TGS_IMAGE_TILED_CHW: src holds src_channels (3 or 4) padded tiled
+ *     planes, converted element for element, padding included; src and dst
+ *     16-byte aligned.  Replaces the same-shape branch of
+ *     DataLoaderBase::transfer_gpu (tinygs/src/dataloader/dataloader.cu:
+ *     257-297) and its kernels (:26-104).
+ *   layout TGS_IMAGE_HWC: src holds height rows of width pixels of
+ *     src_channels bytes (RGB or RGBA; alpha is dropped); dst receives 3
+ *     padded tiled planes, padding zero.  This is the reorder that
+ *     PngFolderDataset does on the host while loading
+ *     (tinygs/src/dataset/png_folder.cpp:60-69), moved to the device.
+ * Asynchronous on `stream`; nothing is allocated. */
+TGS_API int tgs_image_from_u8(const uint8_t* src, int32_t layout, int32_t src_channels, int32_t width,
+                              int32_t height, void* dst, int32_t dst_dtype, tgs_stream_t stream);
+
+/* A tiled 8-bit image of src_width x src_height with `channels` (3 or 4)
+ * planes resized into dst (TGS_FLOAT32 / TGS_FLOAT16, dst_width x
+ * dst_height, padding written as zero).  blur_state NULL: nearest source
+ * pixel (dataloader.cu:107-120).  Otherwise the stochastic blur of the
+ * reference's resize branch (dataloader.cu:122-186, 299-322): each
+ * destination element draws its source pixel from the block it covers with
+ * its own PCG32 state, blur_state[c * plane + tiled index] (at least
+ * channels x padded destination plane entries), which is advanced in place.
+ * Asynchronous on `stream`. */
+TGS_API int tgs_image_resize_u8(const uint8_t* src, int32_t src_width, int32_t src_height, int32_t channels,
+                                void* dst, int32_t dst_dtype, int32_t dst_width, int32_t dst_height,
+                                uint64_t* blur_state, tgs_stream_t stream);
+
+/* blur_state[i] = (a << 32) | b, a and b the outputs 2i and 2i + 1 of
+ * pcg32(seed, 1): DataLoaderBase::reset's initialisation (dataloader.cu:
+ * 361-378, seed 0 there), computed in parallel by jumping ahead. */
+TGS_API int tgs_image_blur_state_init(uint64_t* blur_state, int64_t n, uint64_t seed, tgs_stream_t stream);
 
 /* -------------------------------------------------------------- optimizer */
 

@@ -27,6 +27,9 @@ TGS_ERR_DEVICE_TIMEOUT = 7
 
 TGS_FLOAT32 = 0
 TGS_FLOAT16 = 1
+TGS_UINT8 = 2
+TGS_IMAGE_TILED_CHW = 0
+TGS_IMAGE_HWC = 1
 TGS_NOALLOC_MAX_PIXELS = 262144
 
 
@@ -138,6 +141,9 @@ PROTOTYPES = {
     "tgs_morton_workspace_bytes": (c_int32, [c_int64, POINTER(c_size_t)]),
     "tgs_morton_order": (c_int32, [_P, c_int64, _P, c_size_t, _P, _P]),
     "tgs_metric_psnr": (c_int32, [c_int32, c_int32, c_int32, _P, _P, _P, _P, _P]),
+    "tgs_image_from_u8": (c_int32, [_P, c_int32, c_int32, c_int32, c_int32, _P, c_int32, _P]),
+    "tgs_image_resize_u8": (c_int32, [_P, c_int32, c_int32, c_int32, _P, c_int32, c_int32, c_int32, _P, _P]),
+    "tgs_image_blur_state_init": (c_int32, [_P, c_int64, c_uint64, _P]),
     "tgs_raster_share": (c_int32, [_P, POINTER(TgsIpcHandle)]),
     "tgs_raster_arena": (c_int32, [_P, POINTER(c_void_p)]),
     "tgs_raster_attach_views": (c_int32, [_P, POINTER(c_void_p), c_int32, c_int32]),

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstring>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -119,6 +120,50 @@ struct DevCounts {
   uint32_t n_entries;       // (Gaussian, super-tile) entries
   uint32_t n_chunks;        // chunks of the super-tile entry lists
   uint32_t pad;
+};
+
+// ------------------------------------------------------------------ PCG32
+// The random stream of the reference (include/tinygs/random/pcg32.hpp):
+// M. E. O'Neill 2014, 64-bit LCG state, XSH-RR output; jump-ahead by the
+// LCG's affine map composed by repeated squaring (F. B. Brown 1994).
+constexpr uint64_t kPcgMult = 0x5851f42d4c957f2dULL;
+
+struct Pcg {
+  uint64_t state, inc;
+  // pcg32(initstate, initseq)
+  __host__ __device__ static Pcg seeded(uint64_t initstate, uint64_t initseq) {
+    Pcg g{0u, (initseq << 1u) | 1u};
+    g.next_uint();
+    g.state += initstate;
+    g.next_uint();
+    return g;
+  }
+  __host__ __device__ uint32_t next_uint() {
+    const uint64_t old = state;
+    state = old * kPcgMult + inc;
+    const uint32_t xorshifted = static_cast<uint32_t>(((old >> 18u) ^ old) >> 27u);
+    const uint32_t rot = static_cast<uint32_t>(old >> 59u);
+    return (xorshifted >> rot) | (xorshifted << ((~rot + 1u) & 31u));
+  }
+  __host__ __device__ float next_float() {
+    const uint32_t u = (next_uint() >> 9) | 0x3f800000u;
+    float f;
+    memcpy(&f, &u, 4);
+    return f - 1.0f;
+  }
+  __host__ __device__ void advance(uint64_t delta) {
+    uint64_t cur_mult = kPcgMult, cur_plus = inc, acc_mult = 1u, acc_plus = 0u;
+    while (delta > 0) {
+      if (delta & 1u) {
+        acc_mult *= cur_mult;
+        acc_plus = acc_plus * cur_mult + cur_plus;
+      }
+      cur_plus = (cur_mult + 1u) * cur_plus;
+      cur_mult *= cur_mult;
+      delta >>= 1u;
+    }
+    state = acc_mult * state + acc_plus;
+  }
 };
 
 }  // namespace tgs

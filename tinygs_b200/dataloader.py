@@ -191,6 +191,8 @@ class DataLoaderBase:
         self.dataset = dataset
         self.data_type = data_type
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.out_w, self.out_h = dataset.width, dataset.height
         self.rng = Pcg32(seed, 1)
         self._blur: torch.Tensor | None = None

@@ -387,6 +387,48 @@ TGS_API int tgs_image_resize_u8(const uint8_t* src, int32_t src_width, int32_t s
  * 361-378, seed 0 there), computed in parallel by jumping ahead. */
 TGS_API int tgs_image_blur_state_init(uint64_t* blur_state, int64_t n, uint64_t seed, tgs_stream_t stream);
 
+/* ---------------------------------------------------- checkpoint / resume */
+
+/* Counters that a resumed run needs besides the arrays. */
+typedef struct TgsTrainState {
+    uint64_t step;           /* training steps done (TrainingState::current_step) */
+    uint64_t adam_step;      /* SimpleAdam's step count (bias correction) */
+    uint64_t strategy_step;  /* the densification strategy's step count */
+    TgsPcg32 rng;            /* the strategy's random stream */
+} TgsTrainState;
+
+/* Write the live rows (params->n) of the parameters, of both Adam moments
+ * (exp_avg and exp_avg_sq both given, or both NULL) and of the
+ * densification statistics (dens, may be NULL), with *state, to `path` (a
+ * temporary file renamed over it when complete).  Device memory is read on
+ * `stream`, which is synchronised.  The reference offers only a callback
+ * hook for this (Orchestrator::set_checkpoint_callback,
+ * tinygs/src/orchestrator.cu:291-293,433-435) and a PLY export of the
+ * parameters (core/pointcloud.cpp:111); with this file a resumed run
+ * continues bit for bit. */
+TGS_API int tgs_checkpoint_save(const char* path, const TgsGaussians* params, const TgsGaussians* exp_avg,
+                                const TgsGaussians* exp_avg_sq, const TgsDensificationInfo* dens,
+                                const TgsTrainState* state, tgs_stream_t stream);
+
+/* Header of a checkpoint: Gaussian count, SH degree, flags (bit 0 moments,
+ * bit 1 densification statistics) and the counters.  Any pointer may be
+ * NULL.  TGS_ERR_INVALID_ARGUMENT for a missing or foreign file. */
+TGS_API int tgs_checkpoint_info(const char* path, int64_t* n, int32_t* sh_degree, uint32_t* flags,
+                                TgsTrainState* state);
+
+/* Read a checkpoint into arrays with room for `capacity` Gaussians
+ * (TGS_ERR_CAPACITY if the file holds more).  exp_avg / exp_avg_sq / dens
+ * may be NULL to skip those arrays; asking for arrays the file does not hold
+ * is TGS_ERR_UNSUPPORTED.  The whole file is read and its hash checked
+ * before device memory is written: a truncated or damaged file returns
+ * TGS_ERR_INVALID_ARGUMENT and leaves the arrays as they were.  On success
+ * params->n (and the moments' n) and params->sh_degree are set from the
+ * file and *state (may be NULL) receives the counters; `stream` is
+ * synchronised. */
+TGS_API int tgs_checkpoint_load(const char* path, int64_t capacity, TgsGaussians* params, TgsGaussians* exp_avg,
+                                TgsGaussians* exp_avg_sq, TgsDensificationInfo* dens, TgsTrainState* state,
+                                tgs_stream_t stream);
+
 /* -------------------------------------------------------------- optimizer */
 
 /* Hyper-parameters, reference GaussianOptimizationParams + SimpleAdamParameters

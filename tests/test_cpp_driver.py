@@ -185,3 +185,54 @@ def test_cpp_strategy_and_reorder_match_python_binding(tmp_path):
     from oracle import pyoracle as O
 
     np.testing.assert_array_equal(O.morton_order(means), np.arange(n_final))
+
+
+def test_cpp_checkpoint_resume(tmp_path):
+    """The C++ driver saves a checkpoint after 3 of 6 densifying steps
+    (save_checkpoint over tgs_checkpoint_save); the Python binding reads it
+    (the format is shared); a second C++ run resumed from it ends where the
+    uninterrupted run does (same Gaussian count and losses, parameters up to
+    float-atomic order noise)."""
+    from tinygs_b200 import checkpoint as ck
+
+    assert DRIVER.exists(), "tgs_train_step is built by __graft_entry__.build()"
+    cfg = scenes.CONFIGS["cfg0"]
+    n, sh, steps, cap = 6000, 1, 6, 60000
+    params = scenes.gaussian_params(n, sh, cfg.means, 97)
+    cam = scenes.cameras(cfg)[0]
+    W, H = cam["width"], cam["height"]
+    target = scenes.target_image(W, H, 96).reshape(-1).astype(np.float32)
+    scene = tmp_path / "scene.bin"
+    _write_scene_v2(scene, params, sh, cam, target, steps, cap, 2, 0, 5, 5e-5)
+    ckpt, out_a, out_b = tmp_path / "run.ckpt", tmp_path / "a.bin", tmp_path / "b.bin"
+    ra = subprocess.run([str(DRIVER), str(scene), str(out_a), "--save-at", "3", str(ckpt)], capture_output=True,
+                        text=True, timeout=120)
+    assert ra.returncode == 0, ra.stderr
+    info = ck.checkpoint_info(ckpt)
+    rows_a = [line.split() for line in ra.stdout.splitlines() if line.startswith("step")]
+    assert (info.step, info.adam_step, info.strategy_step) == (3, 3, 3)
+    assert info.n == int(rows_a[2][5]) and info.has_moments and info.has_densification
+    # the Python binding reads the C++ checkpoint
+    g = rt.GaussianSet(0, sh, capacity=cap)
+    grads = g.zeros_like()
+    opt = rt.SimpleAdam(g, grads, rt.AdamParams(max_grad_1=0.3))
+    dens = rt.Densifier(g, grads, opt, rt.DensifyParams())
+    assert ck.load_checkpoint(ckpt, g, opt, dens) == 3
+    assert g.n == info.n and opt.global_steps == 3 and dens.step_count == 3
+    assert np.isfinite(g.to_numpy()["means"]).all()
+    dens.close()
+
+    rb = subprocess.run([str(DRIVER), str(scene), str(out_b), "--resume", str(ckpt)], capture_output=True,
+                        text=True, timeout=120)
+    assert rb.returncode == 0, rb.stderr
+    rows_b = [line.split() for line in rb.stdout.splitlines() if line.startswith("step")]
+    assert [int(x[1]) for x in rows_b] == [3, 4, 5]
+    for x, y in zip(rows_a[3:], rows_b):
+        assert abs(int(x[5]) - int(y[5])) <= max(3, 1e-3 * int(x[5])), (rows_a, rows_b)
+        assert abs(float(x[3]) - float(y[3])) <= 1e-2 * abs(float(x[3]))
+    fa, fb = np.fromfile(out_a, np.uint8), np.fromfile(out_b, np.uint8)
+    na, nb = int(fa[:8].view(np.int64)[0]), int(fb[:8].view(np.int64)[0])
+    if na == nb:
+        a, b = fa[8:].view(np.float32), fb[8:].view(np.float32)
+        close = np.abs(a - b) <= 1e-5 + 1e-4 * np.abs(a)
+        assert close.mean() > 0.99, close.mean()

@@ -74,6 +74,10 @@ class TgsPcg32(ctypes.Structure):
     _fields_ = [("state", c_uint64), ("inc", c_uint64)]
 
 
+class TgsTrainState(ctypes.Structure):
+    _fields_ = [("step", c_uint64), ("adam_step", c_uint64), ("strategy_step", c_uint64), ("rng", TgsPcg32)]
+
+
 class TgsIpcHandle(ctypes.Structure):
     _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
@@ -144,6 +148,12 @@ PROTOTYPES = {
     "tgs_image_from_u8": (c_int32, [_P, c_int32, c_int32, c_int32, c_int32, _P, c_int32, _P]),
     "tgs_image_resize_u8": (c_int32, [_P, c_int32, c_int32, c_int32, _P, c_int32, c_int32, c_int32, _P, _P]),
     "tgs_image_blur_state_init": (c_int32, [_P, c_int64, c_uint64, _P]),
+    "tgs_checkpoint_save": (c_int32, [c_char_p, POINTER(TgsGaussians), POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                      _P, POINTER(TgsTrainState), _P]),
+    "tgs_checkpoint_info": (c_int32, [c_char_p, POINTER(c_int64), POINTER(c_int32), POINTER(c_uint32),
+                                      POINTER(TgsTrainState)]),
+    "tgs_checkpoint_load": (c_int32, [c_char_p, c_int64, POINTER(TgsGaussians), POINTER(TgsGaussians),
+                                      POINTER(TgsGaussians), _P, POINTER(TgsTrainState), _P]),
     "tgs_raster_share": (c_int32, [_P, POINTER(TgsIpcHandle)]),
     "tgs_raster_arena": (c_int32, [_P, POINTER(c_void_p)]),
     "tgs_raster_attach_views": (c_int32, [_P, POINTER(c_void_p), c_int32, c_int32]),

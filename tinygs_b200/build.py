@@ -27,7 +27,7 @@ HOST_DIR = HERE / "host"
 DRIVER = HERE / "tgs_train_step"
 CUDA_HOME = Path("/usr/local/cuda")
 
-SOURCES = ["abi.cu", "preprocess.cu", "binning.cu", "blend.cu", "loss.cu", "adam.cu", "densify.cu", "arena.cu", "metrics.cu", "image.cu", "noalloc.cu"]
+SOURCES = ["abi.cu", "preprocess.cu", "binning.cu", "blend.cu", "loss.cu", "adam.cu", "densify.cu", "arena.cu", "metrics.cu", "image.cu", "checkpoint.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "--use_fast_math", "-std=c++20", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr", "-I", str(INCLUDE),

@@ -469,6 +469,9 @@ class SimpleAdam final : public OptimizerBase {
     m_first->resize(n);
     m_second->resize(n);
   }
+  // Adam's step count (bias correction); restored by a resume
+  uint32_t global_steps() const { return m_global_steps; }
+  void set_global_steps(uint32_t s) { m_global_steps = s; }
 
  private:
   SimpleAdamParameters m_adam;
@@ -513,6 +516,7 @@ class StrategyBase {
     ++m_step_count;
   }
   int64_t this_step() const { return m_step_count; }
+  void set_this_step(int64_t s) { m_step_count = s; }
 
  protected:
   virtual void step_impl(RasterizeContext& ctx) = 0;
@@ -539,6 +543,9 @@ class DefaultStrategyB200 final : public StrategyBase {
   }
   // the records the rasterizer accumulates into (RasterizeContext::densification_info)
   TgsDensificationInfo* densification_info() const { return m_dens; }
+  // the random stream of the splits; saved and restored with a checkpoint
+  TgsPcg32 rng() const { return m_rng; }
+  void set_rng(TgsPcg32 r) { m_rng = r; }
 
  protected:
   void step_impl(RasterizeContext& ctx) override {
@@ -633,6 +640,7 @@ class TrainStep {
   // OrchestratorConfig::reorder_gaussians_interval (0: never)
   void set_reorder_interval(int k) { m_reorder_every = k; }
   int64_t current_step() const { return m_step; }
+  void set_current_step(int64_t s) { m_step = s; }
 
   void run(RasterizeContext& ctx, const Image& target, const Image& loss_map) {
     m_grad->memset(0, ctx.stream);
@@ -661,6 +669,57 @@ class TrainStep {
   int m_reorder_every = 0;
   int64_t m_step = 0;
 };
+
+// Checkpoint of a run (tgs_checkpoint_save): the parameters, the optimizer's
+// moments and step count, the strategy's statistics, step count and random
+// stream, and the training step.  The reference has only the callback hook
+// (Orchestrator::set_checkpoint_callback, orchestrator.cu:291-293,433-435).
+inline void save_checkpoint(const std::string& path, GPUGaussian3d& g, SimpleAdam* opt,
+                            DefaultStrategyB200* strategy, int64_t step, cudaStream_t s) {
+  TgsTrainState st{};
+  st.step = static_cast<uint64_t>(step);
+  const TgsGaussians p = g.abi();
+  TgsGaussians m{}, v{};
+  if (opt) {
+    st.adam_step = opt->global_steps();
+    m = opt->first().abi();
+    v = opt->second().abi();
+  }
+  if (strategy) {
+    st.strategy_step = static_cast<uint64_t>(strategy->this_step());
+    st.rng = strategy->rng();
+  }
+  check(tgs_checkpoint_save(path.c_str(), &p, opt ? &m : nullptr, opt ? &v : nullptr,
+                            strategy ? strategy->densification_info() : nullptr, &st, s),
+        "save_checkpoint");
+}
+
+// Resume from a checkpoint written by save_checkpoint (or by the Python
+// binding): every array moves to the saved count; returns the saved step.
+inline int64_t load_checkpoint(const std::string& path, GPUGaussian3d& g, GPUGaussian3d* grad, SimpleAdam* opt,
+                               DefaultStrategyB200* strategy, cudaStream_t s) {
+  TgsTrainState st{};
+  TgsGaussians p = g.abi(), m{}, v{};
+  if (opt) {
+    m = opt->first().abi();
+    v = opt->second().abi();
+  }
+  check(tgs_checkpoint_load(path.c_str(), g.capacity(), &p, opt ? &m : nullptr, opt ? &v : nullptr,
+                            strategy ? strategy->densification_info() : nullptr, &st, s),
+        "load_checkpoint");
+  g.resize(p.n);
+  g.set_sh_degree(p.sh_degree);
+  if (grad) grad->resize(p.n);
+  if (opt) {
+    opt->resize(p.n);
+    opt->set_global_steps(static_cast<uint32_t>(st.adam_step));
+  }
+  if (strategy) {
+    strategy->set_this_step(static_cast<int64_t>(st.strategy_step));
+    strategy->set_rng(st.rng);
+  }
+  return static_cast<int64_t>(st.step);
+}
 
 // Factory in the shape of create_rasterizer (rasterizer.cpp:44-53).
 inline std::unique_ptr<RasterizerBase> create_rasterizer(const std::string& type) {

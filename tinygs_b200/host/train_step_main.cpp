@@ -3,7 +3,11 @@
 // config_train loop (examples/config_train.cpp:240-288 ->
 // Orchestrator::train_step, orchestrator.cu:335-439) on one resident view.
 //
-// Usage: tgs_train_step <scene.bin> <out_params.bin>
+// Usage: tgs_train_step <scene.bin> <out_params.bin> [--save-at K ckpt]
+//                       [--resume ckpt]
+//   --save-at K ckpt: write a checkpoint after K steps (and carry on);
+//   --resume ckpt:    start from a checkpoint and run the steps left of the
+//                     scene's step count.
 // scene.bin (little endian):
 //   char[4] "TGSB"; int32 version (1 or 2); int64 n; int32 sh_degree;
 //   int32 width, height; int32 dtype (0 fp32, 1 fp16); int32 steps;
@@ -20,8 +24,10 @@
 // then float params[59 * n_final], in the same segment layout.
 // Prints one line per step: "step <k> loss <sum of the loss map> n <count>".
 #include <cstdio>
+#include <cstdlib>
 #include <fstream>
 #include <iostream>
+#include <string>
 #include <vector>
 
 #include "tgs_plugins.hpp"
@@ -52,8 +58,22 @@ float half_to_float(uint16_t h) {
 }  // namespace
 
 int main(int argc, char** argv) {
-  if (argc != 3) {
-    std::fprintf(stderr, "usage: %s scene.bin out_params.bin\n", argv[0]);
+  int save_at = -1;
+  std::string save_path, resume_path;
+  for (int a = 3; a < argc; ++a) {
+    const std::string arg = argv[a];
+    if (arg == "--save-at" && a + 2 < argc) {
+      save_at = std::atoi(argv[a + 1]);
+      save_path = argv[a + 2];
+      a += 2;
+    } else if (arg == "--resume" && a + 1 < argc) {
+      resume_path = argv[++a];
+    } else {
+      argc = 0;
+    }
+  }
+  if (argc < 3) {
+    std::fprintf(stderr, "usage: %s scene.bin out_params.bin [--save-at K ckpt] [--resume ckpt]\n", argv[0]);
     return 2;
   }
   try {
@@ -152,7 +172,14 @@ int main(int argc, char** argv) {
     ctx.fwd_output_image = out;
     ctx.grad_output_image = gimg;
     std::vector<char> loss_host(img.bytes());
-    for (int s = 0; s < steps; ++s) {
+    int first_step = 0;
+    if (!resume_path.empty()) {
+      first_step = static_cast<int>(load_checkpoint(resume_path, *g, grad.get(), adam.get(), strategy.get(), stream));
+      train.set_current_step(first_step);
+      rast->set_gaussians(g);
+    }
+    for (int s = first_step; s < steps; ++s) {
+      if (s == save_at) save_checkpoint(save_path, *g, adam.get(), strategy.get(), s, stream);
       train.run(ctx, target, loss);
       check_cuda(cudaMemcpyAsync(loss_host.data(), d_loss, img.bytes(), cudaMemcpyDeviceToHost, stream), "loss");
       check_cuda(cudaStreamSynchronize(stream), "sync");
@@ -163,6 +190,7 @@ int main(int argc, char** argv) {
                      : reinterpret_cast<float*>(loss_host.data())[i];
       std::printf("step %d loss %.9g n %lld\n", s, sum, static_cast<long long>(g->size()));
     }
+    if (save_at == steps) save_checkpoint(save_path, *g, adam.get(), strategy.get(), steps, stream);
     const int64_t n_final = g->size();
     params.assign(59 * static_cast<size_t>(n_final), 0.0f);
     off = 0;

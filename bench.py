@@ -490,7 +490,7 @@ def kernels_per_step(width: int, height: int, world: int, owner: bool = False) -
     # loss forward + backward; blend backward; per-Gaussian backward fused
     # with Adam (one GPU) or routed backward + accumulation/Adam kernel
     if owner:
-        return forward + (world - 1) + 2 + 1 + world
+        return forward + (world - 1) + 2 + 1 + 1
     return forward + 2 + 1 + (1 if world == 1 else 2)
 
 
@@ -798,14 +798,14 @@ def run_ours(args):
     value = world * 1e3 / ms_step
     e2e_ms = ms_e2e / args.steps
     if owner is not None:
-        # k_preprocess_backward over this rank's slice, once per view (the
-        # last one fused with Adam): parameters read per view, the gradient
-        # sum written and re-read between views, moments read and written
-        # once, touched-tile counts and screen gradients read per view
+        # k_views_backward_adam over this rank's slice: parameters read and
+        # written, both moments read and written (6 x 236 B), and per view
+        # the touched-tile count and the 48-byte screen gradients (peer
+        # memory for the other ranks' views)
         nl = owner.last - owner.first
-        kernel = ("k_preprocess_backward over the rank's slice for every view (N-1 accumulating launches, then "
-                  "the launch fused with Adam)")
-        kernel_bytes = (nl * world * (236 + 4 + 48) + nl * (world - 1) * 236 * 2 + nl * 4 * 236)
+        kernel = ("k_views_backward_adam (the rank's slice back-propagated through every rank's view, summed "
+                  "on chip, Adam in the same pass)")
+        kernel_bytes = nl * (6 * 236 + world * (4 + 48))
         kernel_ms = stages["gaussian_backward_adam"]
     elif fused:
         # k_preprocess_backward<true>: parameters, both moments read and

@@ -649,9 +649,10 @@ TGS_API int tgs_raster_backward_screen(TgsRaster* r, const TgsCamera* cam, int32
                                        const void* grad_image, int32_t absgrad, tgs_stream_t stream);
 /* Per-Gaussian backward of the Gaussians [first, last) for the `world`
  * views (screen-space gradients read from the views' handles), summed in
- * view order into `grads` (full-size scratch set), then the Adam step of
- * tgs_adam_step on those rows of params / exp_avg / exp_avg_sq with the
- * gradient sum.  dens (may be NULL) accumulates over the views. */
+ * view order on chip, then the Adam step of tgs_adam_step on those rows of
+ * params / exp_avg / exp_avg_sq with the gradient sum -- one pass over the
+ * slice.  grads (may be NULL) receives the sums of those rows.  dens (may
+ * be NULL) accumulates over the views. */
 TGS_API int tgs_raster_backward_views_adam(TgsRaster* r, const TgsGaussians* params, const TgsCamera* cams,
                                            int64_t first, int64_t last, TgsGaussians* grads,
                                            const TgsGaussians* exp_avg, const TgsGaussians* exp_avg_sq,

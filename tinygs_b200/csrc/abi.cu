@@ -815,29 +815,29 @@ int tgs_raster_backward_views_adam(TgsRaster* r, const TgsGaussians* params, con
                                    int64_t last, TgsGaussians* grads, const TgsGaussians* exp_avg,
                                    const TgsGaussians* exp_avg_sq, const TgsAdamConfig* cfg, uint32_t step,
                                    float gradient_scale, TgsDensificationInfo* dens, tgs_stream_t stream) {
-  if (r == nullptr || !gaussians_ok(params) || cams == nullptr || !gaussians_ok(grads) || !gaussians_ok(exp_avg) ||
-      !gaussians_ok(exp_avg_sq) || cfg == nullptr || step == 0 || r->peer_arena[0] == nullptr ||
-      !slice_ok(r, params, first, last) || grads->n != params->n || exp_avg->n != params->n ||
-      exp_avg_sq->n != params->n)
+  if (r == nullptr || !gaussians_ok(params) || cams == nullptr || (grads != nullptr && !gaussians_ok(grads)) ||
+      !gaussians_ok(exp_avg) || !gaussians_ok(exp_avg_sq) || cfg == nullptr || step == 0 ||
+      r->peer_arena[0] == nullptr || !slice_ok(r, params, first, last) ||
+      (grads != nullptr && grads->n != params->n) || exp_avg->n != params->n || exp_avg_sq->n != params->n)
     return TGS_ERR_INVALID_ARGUMENT;
   if (last == first) return TGS_OK;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const GaussianPtrs g = to_ptrs(params), gr = to_ptrs(grads), m = to_ptrs(exp_avg), v = to_ptrs(exp_avg_sq);
-  AdamStepArgs a{};
-  adam_segments(cfg, params->n, step, gradient_scale, &a);
-  float4* d = reinterpret_cast<float4*>(dens);
+  RasterState vs[kMaxDpRanks];
+  const RasterState* vp[kMaxDpRanks];
+  DevCamera dc[kMaxDpRanks];
   for (int k = 0; k < r->world; ++k) {
     const TgsCamera* c = &cams[k];
     if (!camera_ok(c)) return TGS_ERR_INVALID_ARGUMENT;
-    const DevCamera dc = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane,
-                                     c->w2c);
-    const RasterState vs = view_state(r, k);
-    if (k + 1 < r->world)  // views 0 .. world-2 summed into `grads`, in view order
-      launch_preprocess_backward(vs, g, gr, dc, k > 0 ? 1 : 0, d, st, nullptr, nullptr, nullptr, nullptr, first,
-                                 last);
-    else  // the last view: its gradients plus the sum so far, then Adam
-      launch_preprocess_backward(vs, g, gr, dc, r->world > 1 ? 1 : 0, d, st, &m, &v, &a, nullptr, first, last);
+    dc[k] = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane, c->w2c);
+    vs[k] = view_state(r, k);
+    vp[k] = &vs[k];
   }
+  AdamStepArgs a{};
+  adam_segments(cfg, params->n, step, gradient_scale, &a);
+  const GaussianPtrs g = to_ptrs(params), m = to_ptrs(exp_avg), v = to_ptrs(exp_avg_sq);
+  GaussianPtrs gr{};
+  if (grads != nullptr) gr = to_ptrs(grads);
+  launch_views_backward_adam(vp, dc, r->world, g, grads != nullptr ? &gr : nullptr, m, v, a,
+                             reinterpret_cast<float4*>(dens), static_cast<cudaStream_t>(stream), first, last);
   return cuda_status(cudaGetLastError());
 }
 

@@ -134,6 +134,13 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g,
                                 float4* dens, cudaStream_t stream, const GaussianPtrs* exp_avg = nullptr,
                                 const GaussianPtrs* exp_avg_sq = nullptr, const AdamStepArgs* adam = nullptr,
                                 const GradRoute* route = nullptr, int64_t first = 0, int64_t last = -1);
+// Owner split: Gaussians [first, last) back-propagated through the views of
+// all `world` ranks (views[k]: rank k's handle state, cams[k] its camera),
+// summed in view order, then Adam; grads (may be null) receives the sums.
+void launch_views_backward_adam(const RasterState* const* views, const DevCamera* cams, int world,
+                                const GaussianPtrs& g, const GaussianPtrs* grads, const GaussianPtrs& exp_avg,
+                                const GaussianPtrs& exp_avg_sq, const AdamStepArgs& adam, float4* dens,
+                                cudaStream_t stream, int64_t first, int64_t last);
 
 // losses (loss.cu)
 void launch_l1(int fp16, int width, int height, const void* pred, const void* target,

@@ -675,14 +675,8 @@ __device__ __forceinline__ ChunkRef chunk_ref(const SegPtrs& params, const SegPt
   return r;
 }
 
-// accumulate: `r.g` holds the gradient sum of the views before this one;
-// the step uses that sum plus this view's gradient and leaves `r.g` as is
 __device__ __forceinline__ void adam_chunk(const ChunkRef& r, float4 t, float4 m, float4 v, float4 gv,
-                                           const AdamArgs& adam, int accumulate) {
-  if (accumulate) {
-    const float4 o = *reinterpret_cast<const float4*>(r.g);
-    gv = make_float4(o.x + gv.x, o.y + gv.y, o.z + gv.z, o.w + gv.w);
-  }
+                                           const AdamArgs& adam) {
   adam_element(t.x, gv.x, m.x, v.x, r.lr, r.kind, r.decay, adam);
   adam_element(t.y, gv.y, m.y, v.y, r.lr, r.kind, r.decay, adam);
   adam_element(t.z, gv.z, m.z, v.z, r.lr, r.kind, r.decay, adam);
@@ -690,18 +684,16 @@ __device__ __forceinline__ void adam_chunk(const ChunkRef& r, float4 t, float4 m
   *reinterpret_cast<float4*>(r.p) = t;
   *reinterpret_cast<float4*>(r.m) = m;
   *reinterpret_cast<float4*>(r.v) = v;
-  if (r.g != nullptr && !accumulate) *reinterpret_cast<float4*>(r.g) = gv;
+  if (r.g != nullptr) *reinterpret_cast<float4*>(r.g) = gv;
 }
 
 template <int kLo, int kHi>
 __device__ __forceinline__ void geom_round(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
                                            const SegPtrs& exp_avg_sq, const AdamArgs& adam, const float* th,
-                                           const float* g, uint32_t first, uint32_t c, float4 m, float4 v,
-                                           int accumulate) {
+                                           const float* g, uint32_t first, uint32_t c, float4 m, float4 v) {
   if (c >= seg_chunk0(5)) return;
   const ChunkRef r = chunk_ref<kLo, kHi>(params, grads, exp_avg, exp_avg_sq, adam, first, c);
-  adam_chunk(r, reinterpret_cast<const float4*>(th)[c], m, v, reinterpret_cast<const float4*>(g)[c], adam,
-             accumulate);
+  adam_chunk(r, reinterpret_cast<const float4*>(th)[c], m, v, reinterpret_cast<const float4*>(g)[c], adam);
 }
 
 __device__ __forceinline__ float4 rest_grad4(const float* sb, uint32_t e4) {
@@ -709,10 +701,12 @@ __device__ __forceinline__ float4 rest_grad4(const float* sb, uint32_t e4) {
                      slice_grad<5>(nullptr, sb, 4 * e4 + 2), slice_grad<5>(nullptr, sb, 4 * e4 + 3));
 }
 
+// kSum: the higher-band SH gradients are read from `sb` as a plain slice
+// segment (the multi-view sum) instead of being formed from basis x colour.
+template <bool kSum = false>
 __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
-                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, int accumulate,
-                                               const float* th, const float* g, const float* sb, uint32_t first,
-                                               uint32_t lane) {
+                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, const float* th,
+                                               const float* g, const float* sb, uint32_t first, uint32_t lane) {
   constexpr uint32_t kRestChunks = 45u * kWarpGaussians / 4u;  // 360
   constexpr int kBatch = 4;
   constexpr uint32_t kRestRounds = (kRestChunks + 31u) / 32u;  // 12 (the last one: lanes < 8)
@@ -739,10 +733,10 @@ __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegP
     rm[q] = reinterpret_cast<const float4*>(RM)[e4];
     rv[q] = reinterpret_cast<const float4*>(RV)[e4];
   }
-  geom_round<0, 1>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, lane, gm[0], gvv[0], accumulate);
-  geom_round<2, 2>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 32u + lane, gm[1], gvv[1], accumulate);
-  geom_round<3, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 64u + lane, gm[2], gvv[2], accumulate);
-  geom_round<4, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 96u + lane, gm[3], gvv[3], accumulate);
+  geom_round<0, 1>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, lane, gm[0], gvv[0]);
+  geom_round<2, 2>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 32u + lane, gm[1], gvv[1]);
+  geom_round<3, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 64u + lane, gm[2], gvv[2]);
+  geom_round<4, 4>(params, grads, exp_avg, exp_avg_sq, adam, th, g, first, 96u + lane, gm[3], gvv[3]);
   // sh_rest
   ChunkRef rr;
   rr.lr = adam.lr[5];
@@ -770,8 +764,8 @@ __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegP
         rr.m = exp_avg.p[5] + rest_base + 4u * e4;
         rr.v = exp_avg_sq.p[5] + rest_base + 4u * e4;
         rr.g = grads.p[5] != nullptr ? grads.p[5] + rest_base + 4u * e4 : nullptr;
-        adam_chunk(rr, reinterpret_cast<const float4*>(ts)[e4], rm[q], rv[q], rest_grad4(sb, e4), adam,
-                   accumulate);
+        adam_chunk(rr, reinterpret_cast<const float4*>(ts)[e4], rm[q], rv[q],
+                   kSum ? reinterpret_cast<const float4*>(sb)[e4] : rest_grad4(sb, e4), adam);
       }
     }
     if (b0 + kBatch < kRestRounds) {
@@ -784,7 +778,18 @@ __device__ __forceinline__ void adam_slice_v16(const SegPtrs& params, const SegP
   }
 }
 
-template <bool kAdam, int k, bool kRoute = false>
+// Gradient element e of segment k: kSum reads the higher-band SH gradients
+// from `sb` as a plain segment (the multi-view sum).
+template <int k, bool kSum>
+__device__ __forceinline__ float grad_of(const float* __restrict__ g, const float* __restrict__ sb, uint32_t e) {
+  if constexpr (kSum && k == 5) {
+    return sb[e];
+  } else {
+    return slice_grad<k>(g, sb, e);
+  }
+}
+
+template <bool kAdam, int k, bool kRoute = false, bool kSum = false>
 __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPtrs& grads, const SegPtrs& exp_avg,
                                               const SegPtrs& exp_avg_sq, const AdamArgs& adam, int accumulate,
                                               const float* __restrict__ th, const float* __restrict__ g,
@@ -822,13 +827,8 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
         float4 t = reinterpret_cast<const float4*>(ts)[e4];
         float4 m = reinterpret_cast<const float4*>(M)[e4];
         float4 v = reinterpret_cast<const float4*>(V)[e4];
-        float4 gv = make_float4(slice_grad<k>(g, sb, 4 * e4), slice_grad<k>(g, sb, 4 * e4 + 1),
-                                slice_grad<k>(g, sb, 4 * e4 + 2), slice_grad<k>(g, sb, 4 * e4 + 3));
-        if (accumulate) {
-          // the views before this one, summed in order in `grads`
-          const float4 o = reinterpret_cast<const float4*>(G)[e4];
-          gv = make_float4(o.x + gv.x, o.y + gv.y, o.z + gv.z, o.w + gv.w);
-        }
+        const float4 gv = make_float4(grad_of<k, kSum>(g, sb, 4 * e4), grad_of<k, kSum>(g, sb, 4 * e4 + 1),
+                                      grad_of<k, kSum>(g, sb, 4 * e4 + 2), grad_of<k, kSum>(g, sb, 4 * e4 + 3));
         adam_element(t.x, gv.x, m.x, v.x, lr, kind, decay, adam);
         adam_element(t.y, gv.y, m.y, v.y, lr, kind, decay, adam);
         adam_element(t.z, gv.z, m.z, v.z, lr, kind, decay, adam);
@@ -836,17 +836,17 @@ __device__ __forceinline__ void write_segment(const SegPtrs& params, const SegPt
         reinterpret_cast<float4*>(P)[e4] = t;
         reinterpret_cast<float4*>(M)[e4] = m;
         reinterpret_cast<float4*>(V)[e4] = v;
-        if (G != nullptr && !accumulate) reinterpret_cast<float4*>(G)[e4] = gv;
+        if (G != nullptr) reinterpret_cast<float4*>(G)[e4] = gv;
       }
     } else {
       for (uint32_t e = lane; e < count; e += 32) {
         float t = ts[e], m = M[e], v = V[e];
-        const float gv = accumulate ? G[e] + slice_grad<k>(g, sb, e) : slice_grad<k>(g, sb, e);
+        const float gv = grad_of<k, kSum>(g, sb, e);
         adam_element(t, gv, m, v, lr, kind, decay, adam);
         P[e] = t;
         M[e] = m;
         V[e] = v;
-        if (G != nullptr && !accumulate) G[e] = gv;
+        if (G != nullptr) G[e] = gv;
       }
     }
   } else {
@@ -904,10 +904,8 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
     if (v16) {
 #pragma unroll
       for (int k = 0; k < 6; ++k) {
-        if (lane == static_cast<uint32_t>(k) || lane == static_cast<uint32_t>(k + 6) ||
-            (accumulate && lane == static_cast<uint32_t>(k + 12))) {
-          const float* ptr = (lane < 6u ? exp_avg.p[k] : lane < 12u ? exp_avg_sq.p[k] : grads.p[k]) +
-                             static_cast<size_t>(first) * seg_width(k);
+        if (lane == static_cast<uint32_t>(k) || lane == static_cast<uint32_t>(k + 6)) {
+          const float* ptr = (lane < 6u ? exp_avg.p[k] : exp_avg_sq.p[k]) + static_cast<size_t>(first) * seg_width(k);
           const uint32_t bytes = 4u * kWarpGaussians * seg_width(k);
           asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(ptr), "r"(bytes) : "memory");
         }
@@ -956,7 +954,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
   if (kRoute && v16) {
     route_warp_bulk(route, th, g, sb, first, lane);
   } else if (kAdam && v16) {
-    adam_slice_v16(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, lane);
+    adam_slice_v16(params, grads, exp_avg, exp_avg_sq, adam, th, g, sb, first, lane);
   } else {
     write_segment<kAdam, 0, kRoute>(params, grads, exp_avg, exp_avg_sq, adam, accumulate, th, g, sb, first, cnt,
                                       lane, v16, route);
@@ -974,6 +972,145 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 4)
   // (routed stores: the kernel's completion orders them before the
   // collective that the owners wait on; no per-warp system fence, which
   // would hold every warp until its stores crossed NVLink)
+}
+
+// Owner-split backward: one rank's slice of Gaussians, the per-Gaussian
+// backward of every rank's view, summed in view order, then Adam.
+struct ViewsArgs {
+  DevCamera cam[kMaxDpRanks];
+  const uint32_t* n_touched[kMaxDpRanks];
+  const float4* helpers[kMaxDpRanks];
+  const DevCounts* counts[kMaxDpRanks];
+  int world;
+};
+// per warp: the slice staging, one view's gradients, and the running sum of
+// the 45 higher-band SH gradients of its 32 Gaussians (the 14 others are
+// summed in registers, one Gaussian per lane)
+constexpr int kViewsWarpFloats = kWarpFloats + 45 * kWarpGaussians;  // 4384
+constexpr size_t kViewsSmemBytes = sizeof(float) * kViewsWarpFloats * kBwdWarps;
+
+// Position of geometry gradient j (0..13: means 3, opacity, rotation 4,
+// scales 3, sh0 3) of `lane`'s Gaussian in the warp's gradient slice.
+__device__ __forceinline__ uint32_t geom_pos(int j, uint32_t lane) {
+  return j < 3 ? seg_off(0) + 3u * lane + j
+       : j < 4 ? seg_off(1) + lane
+       : j < 8 ? seg_off(2) + 4u * lane + (j - 4)
+       : j < 11 ? seg_off(3) + 3u * lane + (j - 8)
+                : seg_off(4) + 3u * lane + (j - 11);
+}
+
+// The sum runs as acc = g_0, acc = acc + g_1, ..., the order in which
+// tgs_raster_backward(accumulate) over the views in turn would add the
+// gradients into one arena, so the Adam step sees the same sums; the
+// screen-space inputs of view k + 1 (peer memory in a multi-GPU run) are
+// loaded while view k is computed.
+__global__ void __launch_bounds__(32 * kBwdWarps, 3)
+    k_views_backward_adam(SegPtrs params, SegPtrs grads, SegPtrs exp_avg, SegPtrs exp_avg_sq, AdamArgs adam,
+                          int vec, int active_bases, uint32_t n, uint32_t base, float4* __restrict__ dens,
+                          ViewsArgs views) {
+  extern __shared__ __align__(16) float vsmem[];
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  const uint32_t wi = blockIdx.x * kBwdWarps + warp;
+  const uint32_t n_warps = (n - base + kWarpGaussians - 1) / kWarpGaussians;
+  if (wi >= n_warps) return;
+  const uint32_t first = base + wi * kWarpGaussians;
+  const uint32_t cnt = min(static_cast<uint32_t>(kWarpGaussians), n - first);
+  const bool v16 = vec != 0 && cnt == kWarpGaussians;
+  float* th = vsmem + warp * kViewsWarpFloats;
+  float* g = th + kSliceFloats;
+  float* sb = g + kGeomFloats;
+  float* rest_sum = sb + kShFloats;
+  if (v16) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) {
+      if (lane == static_cast<uint32_t>(k) || lane == static_cast<uint32_t>(k + 6)) {
+        const float* ptr = (lane < 6u ? exp_avg.p[k] : exp_avg_sq.p[k]) + static_cast<size_t>(first) * seg_width(k);
+        const uint32_t bytes = 4u * kWarpGaussians * seg_width(k);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(ptr), "r"(bytes) : "memory");
+      }
+    }
+  }
+  stage_slice(params, th, first, cnt, lane, v16);
+  cp_async_commit();
+  const uint32_t i = first + lane;
+  const bool live = lane < cnt;
+  uint32_t nt = 0;
+  float4 h0{}, h1{}, h2{}, d{};
+  if (live) {
+    nt = views.n_touched[0][i];
+    h0 = views.helpers[0][3 * i];
+    h1 = views.helpers[0][3 * i + 1];
+    h2 = views.helpers[0][3 * i + 2];
+    if (dens != nullptr) d = dens[i];
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+  float* my_sb = sb + kShStride * lane;
+  float acc[14];
+  bool any_touched = false;
+  for (int k = 0; k < views.world; ++k) {
+    uint32_t nt_next = 0;
+    float4 n0{}, n1{}, n2{};
+    if (k + 1 < views.world && live) {
+      nt_next = views.n_touched[k + 1][i];
+      n0 = views.helpers[k + 1][3 * i];
+      n1 = views.helpers[k + 1][3 * i + 1];
+      n2 = views.helpers[k + 1][3 * i + 2];
+    }
+    const bool touched = views.counts[k]->overflow == 0u && live && nt > 0;
+    if (touched) {
+      const DevCamera& cam = views.cam[k];
+      gaussian_backward(th, g, my_sb, lane, h0, h1, h2, active_bases, cam);
+      if (dens != nullptr) {
+        d.x += 1.0f;
+        const float ux = h0.x * (0.5f * cam.w), uy = h0.y * (0.5f * cam.h);
+        d.y += sqrtf(ux * ux + uy * uy);
+        const float vx = h0.z * (0.5f * cam.w), vy = h0.w * (0.5f * cam.h);
+        d.z += sqrtf(vx * vx + vy * vy);
+      }
+      any_touched = true;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 14; ++j) g[geom_pos(j, lane)] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 18; ++c) my_sb[c] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 14; ++j) {
+      const float x = g[geom_pos(j, lane)];
+      acc[j] = k == 0 ? x : acc[j] + x;
+    }
+    __syncwarp();  // every lane's basis and colour gradients are in place
+    for (uint32_t e = lane; e < 45u * kWarpGaussians; e += 32) {
+      const float x = slice_grad<5>(g, sb, e);
+      rest_sum[e] = k == 0 ? x : rest_sum[e] + x;
+    }
+    __syncwarp();  // sb is rewritten by the next view
+    nt = nt_next;
+    h0 = n0;
+    h1 = n1;
+    h2 = n2;
+  }
+#pragma unroll
+  for (int j = 0; j < 14; ++j) g[geom_pos(j, lane)] = acc[j];
+  if (dens != nullptr && any_touched) dens[i] = d;
+  __syncwarp();
+  if (v16) {
+    adam_slice_v16<true>(params, grads, exp_avg, exp_avg_sq, adam, th, g, rest_sum, first, lane);
+  } else {
+    write_segment<true, 0, false, true>(params, grads, exp_avg, exp_avg_sq, adam, 0, th, g, rest_sum, first, cnt,
+                                        lane, false, RouteArgs{});
+    write_segment<true, 1, false, true>(params, grads, exp_avg, exp_avg_sq, adam, 0, th, g, rest_sum, first, cnt,
+                                        lane, false, RouteArgs{});
+    write_segment<true, 2, false, true>(params, grads, exp_avg, exp_avg_sq, adam, 0, th, g, rest_sum, first, cnt,
+                                        lane, false, RouteArgs{});
+    write_segment<true, 3, false, true>(params, grads, exp_avg, exp_avg_sq, adam, 0, th, g, rest_sum, first, cnt,
+                                        lane, false, RouteArgs{});
+    write_segment<true, 4, false, true>(params, grads, exp_avg, exp_avg_sq, adam, 0, th, g, rest_sum, first, cnt,
+                                        lane, false, RouteArgs{});
+    write_segment<true, 5, false, true>(params, grads, exp_avg, exp_avg_sq, adam, 0, th, g, rest_sum, first, cnt,
+                                        lane, false, RouteArgs{});
+  }
 }
 
 }  // namespace
@@ -1039,7 +1176,7 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, con
     v = segs(*exp_avg_sq);
     const int vec = aligned(segs(g)) && aligned(m) && aligned(v) && aligned(segs(grads));
     k_preprocess_backward<true><<<blocks, 32 * kBwdWarps, 0, stream>>>(
-        segs(g), segs(grads), m, v, a, accumulate, vec, active_bases, n, cam, s.n_touched,
+        segs(g), segs(grads), m, v, a, 0, vec, active_bases, n, cam, s.n_touched,
         reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{}, base);
   } else if (route != nullptr) {
     RouteArgs r{};
@@ -1065,6 +1202,58 @@ void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, con
         segs(g), segs(grads), m, v, a, accumulate, vec, active_bases, n, cam, s.n_touched,
         reinterpret_cast<const float4*>(s.helpers), dens, s.counts, RouteArgs{}, base);
   }
+}
+
+void launch_views_backward_adam(const RasterState* const* views, const DevCamera* cams, int world,
+                                const GaussianPtrs& g, const GaussianPtrs* grads, const GaussianPtrs& exp_avg,
+                                const GaussianPtrs& exp_avg_sq, const AdamStepArgs& adam, float4* dens,
+                                cudaStream_t stream, int64_t first, int64_t last) {
+  const uint32_t n = static_cast<uint32_t>(last);
+  const uint32_t base = static_cast<uint32_t>(first);
+  if (n <= base || world < 1 || world > kMaxDpRanks) return;
+  static const bool attr_set = [] {
+    return cudaFuncSetAttribute(k_views_backward_adam, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kViewsSmemBytes)) == cudaSuccess;
+  }();
+  (void)attr_set;
+  auto segs = [](const GaussianPtrs& x) {
+    SegPtrs p{{x.means, x.opacities, x.rotations, x.scales, x.sh0, x.sh_rest}};
+    return p;
+  };
+  auto aligned = [](const SegPtrs& p) {
+    for (float* q : p.p)
+      if (q != nullptr && (reinterpret_cast<uintptr_t>(q) & 15u) != 0) return false;
+    return true;
+  };
+  AdamArgs a{};
+  for (int k = 0; k < 6; ++k) {
+    a.lr[k] = adam.lr[k];
+    a.decay[k] = adam.decay[k];
+    a.kind[k] = adam.kind[k];
+  }
+  a.beta1 = adam.beta1;
+  a.beta2 = adam.beta2;
+  a.eps = adam.eps;
+  a.gscale = adam.gradient_scale;
+  a.bc1 = adam.bc1;
+  a.bc2_sqrt = adam.bc2_sqrt;
+  a.max_g = adam.max_grad_1;
+  ViewsArgs va{};
+  for (int k = 0; k < world; ++k) {
+    va.cam[k] = cams[k];
+    va.n_touched[k] = views[k]->n_touched;
+    va.helpers[k] = reinterpret_cast<const float4*>(views[k]->helpers);
+    va.counts[k] = views[k]->counts;
+  }
+  va.world = world;
+  const SegPtrs gr = grads != nullptr ? segs(*grads) : SegPtrs{};
+  const SegPtrs m = segs(exp_avg), v = segs(exp_avg_sq);
+  const int vec = aligned(segs(g)) && aligned(m) && aligned(v) && aligned(gr);
+  const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
+  const uint32_t per_block = kBwdWarps * kWarpGaussians;
+  const uint32_t blocks = (n - base + per_block - 1) / per_block;
+  k_views_backward_adam<<<blocks, 32 * kBwdWarps, kViewsSmemBytes, stream>>>(segs(g), gr, m, v, a, vec,
+                                                                           active_bases, n, base, dens, va);
 }
 
 }  // namespace tgs

@@ -764,8 +764,10 @@ int tgs_raster_preprocess_views(TgsRaster* r, const TgsGaussians* params, const 
     if (!camera_ok(c) || c->width > r->s.max_w || c->height > r->s.max_h) return TGS_ERR_INVALID_ARGUMENT;
     const DevCamera dc = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane,
                                      c->w2c);
+    // the backward accumulators are cleared by the view's rank
+    // (tgs_raster_forward_gathered), not across NVLink
     if (last > first) launch_preprocess(view_state(r, k), g, dc, dtype == TGS_FLOAT16,
-                                        reinterpret_cast<float4*>(dens), st, first, last);
+                                        reinterpret_cast<float4*>(dens), st, first, last, 0);
   }
   return cuda_status(cudaGetLastError());
 }
@@ -780,6 +782,7 @@ int tgs_raster_forward_gathered(TgsRaster* r, int64_t n, const TgsCamera* cam, i
   const DevCamera dc = make_camera(cam->width, cam->height, cam->fx, cam->fy, cam->cx, cam->cy, cam->near_plane,
                                    cam->far_plane, cam->w2c);
   cudaMemsetAsync(s.counts, 0, sizeof(DevCounts), st);
+  cudaMemsetAsync(s.helpers, 0, sizeof(float) * kHelperFloats * static_cast<size_t>(n), st);
   s.have_forward = 0;
   mark(r, 0, st);
   mark(r, 1, st);

@@ -108,8 +108,11 @@ void sort_pairs_u32(uint32_t* keys[2], uint32_t* vals[2], const uint32_t* count_
                     int total_bits, int& result, const SortScratch& ss, cudaStream_t stream);
 
 // forward stages (preprocess.cu, binning.cu, blend.cu)
+// zero_helpers == 0: the backward accumulators of the candidates are left
+// for the caller to clear (the owner split clears them on the view's rank)
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam,
-                       int fp16, float4* dens, cudaStream_t stream, int64_t first = 0, int64_t last = -1);
+                       int fp16, float4* dens, cudaStream_t stream, int64_t first = 0, int64_t last = -1,
+                       int zero_helpers = 1);
 void launch_binning(RasterState& s, int64_t n, const DevCamera& cam, int fp16, cudaStream_t stream);
 void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, void* image,
                           void* alpha, cudaStream_t stream);

@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(kPreBlock)
                  float2* __restrict__ mean2d, float4* __restrict__ conic_opacity,
                  PrimInfo16* __restrict__ prim_info, float* __restrict__ color,
                  float4* __restrict__ helpers,
-                 uint32_t* __restrict__ block_visible, int rest_vec, uint32_t first_block) {
+                 uint32_t* __restrict__ block_visible, int rest_vec, uint32_t first_block, int zero_helpers) {
   // higher-order SH rows of the warp's 32 Gaussians, loaded coalesced (one
   // row per lane would touch 32 cache lines per load instruction)
   __shared__ __align__(16) float s_rest[kPreBlock / 32][32 * 45];
@@ -252,11 +252,14 @@ __global__ void __launch_bounds__(kPreBlock)
                           : make_ushort4(0, 0, 0, 0);
     if (candidate) {
       depth_key[i] = __float_as_uint(depth);
-      // the blend backward accumulates into these
-      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-      helpers[3 * i] = z;
-      helpers[3 * i + 1] = z;
-      helpers[3 * i + 2] = z;
+      // the blend backward accumulates into these (zero_helpers == 0: the
+      // view's own rank clears them locally instead)
+      if (zero_helpers) {
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        helpers[3 * i] = z;
+        helpers[3 * i + 1] = z;
+        helpers[3 * i + 2] = z;
+      }
       mean2d[i] = m2;
       // view-dependent colour
       float3 col = make_float3(0.5f + 0.28209479177387814f * sh0[3 * i],
@@ -1116,7 +1119,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 3)
 }  // namespace
 
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam, int fp16,
-                       float4* dens, cudaStream_t stream, int64_t first, int64_t last) {
+                       float4* dens, cudaStream_t stream, int64_t first, int64_t last, int zero_helpers) {
   // Gaussians [first, last) (last < 0: to g.n); first is a multiple of the
   // block size so every block's candidate count has one writer
   const uint32_t n = static_cast<uint32_t>(last < 0 ? g.n : last);
@@ -1129,12 +1132,14 @@ void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCam
     k_preprocess<1><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block);
+        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block,
+        zero_helpers);
   else
     k_preprocess<0><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
         active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block);
+        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block,
+        zero_helpers);
 }
 
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, const GaussianPtrs& grads,

@@ -210,6 +210,7 @@ def _owner_worker(rank: int, port: int, out_dir: str, dtype_name: str) -> None:
         img = torch.zeros(rt.image_numel(W, H), dtype=dt, device="cuda")
         gimg, lmap = torch.zeros_like(img), torch.zeros_like(img)
         loss = rt.FusedLoss(W, H)
+        loss.set_accumulate(False)  # each evaluation overwrites the loss map and gradient image
         images = []
         for s in range(2):
             views = [cams[2 * s + r] for r in range(2)]
@@ -262,6 +263,7 @@ def test_owner_split_two_gpus(tmp_path, dtype_name):
     rast = rt.FastGSB200Rasterizer(n, W, H)
     rast.set_gaussians(g)
     loss = rt.FusedLoss(W, H)
+    loss.set_accumulate(False)
     img = torch.zeros(rt.image_numel(W, H), dtype=dt, device="cuda")
     gimg, lmap = torch.zeros_like(img), torch.zeros_like(img)
     for s in range(2):

@@ -404,7 +404,6 @@ class OwnerSplit:
         self.dp, self.rast, self.params, self.cfg, self.dtype = dp, rast, params, cfg, dtype
         self.lib = load_library()
         self.first, self.last = owner_slice(params.n, dp.world, dp.rank)
-        self.grads = params.zeros_like()
         self.exp_avg, self.exp_avg_sq = params.zeros_like(), params.zeros_like()
         self.global_steps = 0
         self.flag = torch.zeros(1, device=params.storage.device)
@@ -455,7 +454,7 @@ class OwnerSplit:
         self.barrier(stream)
         if events is not None:
             events[1].record(_as_torch_stream(stream))
-        self.rast.backward_views_adam(self.params, cams, self.first, self.last, self.grads, self.exp_avg,
+        self.rast.backward_views_adam(self.params, cams, self.first, self.last, None, self.exp_avg,
                                       self.exp_avg_sq, self.cfg, self.global_steps, gradient_scale, dens, stream)
 
     def close(self) -> None:

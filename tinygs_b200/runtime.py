@@ -334,14 +334,17 @@ class FastGSB200Rasterizer:
                                                   _ptr(grad_image), 1 if absgrad else 0, _stream_handle(stream)),
               "tgs_raster_backward_screen")
 
-    def backward_views_adam(self, params: GaussianSet, cams: list[dict], first: int, last: int, grads: GaussianSet,
+    def backward_views_adam(self, params: GaussianSet, cams: list[dict], first: int, last: int,
+                            grads: GaussianSet | None,
                             exp_avg: GaussianSet, exp_avg_sq: GaussianSet, cfg: "AdamParams", step: int,
                             gradient_scale: float, dens: torch.Tensor | None = None, stream=None) -> None:
-        p, gr, m, v = params.abi(), grads.abi(), exp_avg.abi(), exp_avg_sq.abi()
+        p, m, v = params.abi(), exp_avg.abi(), exp_avg_sq.abi()
+        gr = grads.abi() if grads is not None else None
         cs = (TgsCamera * len(cams))(*[make_camera(c) for c in cams])
         c = cfg.abi()
         check(self.lib.tgs_raster_backward_views_adam(self.handle, ctypes.byref(p), cs, int(first), int(last),
-                                                      ctypes.byref(gr), ctypes.byref(m), ctypes.byref(v),
+                                                      ctypes.byref(gr) if gr is not None else None,
+                                                      ctypes.byref(m), ctypes.byref(v),
                                                       ctypes.byref(c), int(step), float(gradient_scale), _ptr(dens),
                                                       _stream_handle(stream)), "tgs_raster_backward_views_adam")
 

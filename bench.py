@@ -67,7 +67,7 @@ def parse():
                          "their owners' inboxes by the backward, then "
                          "accumulation + Adam + parameter broadcast in one kernel (inbox); accumulation + Adam in "
                          "one kernel through NVLink SHARP (multicast) or over peer memory (peer); or an NCCL "
-                         "all-reduce followed by Adam on every rank (nccl, the baseline); auto = inbox")
+                         "all-reduce followed by Adam on every rank (nccl, the baseline); auto = owner")
     args = ap.parse_args()
     args.steps_given = args.steps is not None
     if args.steps is None:
@@ -523,14 +523,14 @@ def run_ours(args):
     dp_impl = args.dp if world > 1 else "none"
     opt = None
     owner = None
-    if peer and args.dp == "owner":
+    if peer and args.dp in ("auto", "owner"):
         # every rank keeps the whole parameter arena but reads and updates only
         # its own slice; the split object is made once the rasterizer exists
         g = rt.GaussianSet.from_numpy(params, cfg.sh_degree)
         grads = None
         opt = "owner"
         dp_impl = "owner"
-    if peer and args.dp in ("auto", "inbox"):
+    if peer and opt is None and args.dp == "inbox":
         # parameters the other ranks map (CUDA IPC) and a gradient inbox per
         # rank: the backward stores each Gaussian's gradients into the inbox
         # of the rank that owns its slice (no local gradient arena)

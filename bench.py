@@ -480,10 +480,10 @@ def kernels_per_step(width: int, height: int, world: int, owner: bool = False) -
     n_super = ((grid_w + 7) // 8) * ((grid_h + 3) // 4)
     entry_passes = max(1, ((max(1, n_super - 1)).bit_length() + 7) // 8)
     forward = (1  # preprocess
-               + 1  # candidate compaction (look-back scan)
-               + 2 + 4  # depth sort: state reset, digit counts, 4 one-sweep passes
-               + 1  # entry creation (look-back scan)
-               + 2 + entry_passes  # entry sort by super-tile
+               + 2  # candidate compaction: block-sum scan, compaction
+               + 4 * 3  # depth sort: 4 passes of histogram, scan, scatter
+               + 3  # per-block entry counts, their scan, entry creation
+               + 3 * entry_passes  # entry sort by super-tile
                + (1 if entry_passes > 1 else 0) + 1  # super-tile ranges (multi-pass sort only), chunk table
                + 4  # tile tests, chunk prefix, tile offsets, emission
                + 1)  # blend forward

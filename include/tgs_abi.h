@@ -126,10 +126,8 @@ typedef struct TgsRasterCaps {
  * tgs_raster_counts().  n_visible counts the Gaussians that passed culling
  * with a non-empty tile rectangle (a superset of those that touch a tile,
  * whose per-Gaussian tile counts are debug buffer 0).  `overflow` != 0 means
- * the outputs of that forward are invalid: bits 1, 2, 4 = a capacity bound
- * (instances, buckets, super-tile entries) was hit (grow the caps and rerun);
- * bit 8 = a wait of the binning's scans on another block gave up (not
- * expected; rerun). */
+ * a capacity bound was hit and the outputs of that forward are invalid (grow
+ * the caps and rerun). */
 typedef struct TgsRasterCounts {
     uint32_t n_visible;
     uint32_t n_instances;

@@ -169,11 +169,9 @@ void carve(RasterState& s, char* base, size_t& bytes) {
   s.chunk_counts = c.take<uint32_t>(static_cast<size_t>(s.cap_chunks) * kSuperTiles);
   s.sub_offsets = c.take<uint32_t>(static_cast<size_t>(s.cap_chunks) * kSubChunks * kSuperTiles);
   s.tile_total = c.take<uint32_t>(nt);
-  s.sort_max_tiles = static_cast<int64_t>((std::max(n, ne) + kSortTileItems - 1) / kSortTileItems);
-  s.sort_state = c.take<uint32_t>(kSortStateWords);
-  s.sort_look = c.take<unsigned long long>(256 * static_cast<size_t>(s.sort_max_tiles));
-  s.scan_look_half = static_cast<int64_t>(n / 1024 + 1);
-  s.scan_look = c.take<unsigned long long>(2 * static_cast<size_t>(s.scan_look_half));
+  s.sort_max_blocks = static_cast<int64_t>((std::max(n, ne) + kSortTileItems - 1) / kSortTileItems);
+  s.sort_hist = c.take<uint32_t>(256 * static_cast<size_t>(s.sort_max_blocks));
+  s.sort_digit_total = c.take<uint32_t>(256);
   s.ranges = c.take<uint2>(nt);
   s.bucket_offsets = c.take<uint32_t>(nt);
   s.tile_max_contrib = c.take<uint32_t>(nt);
@@ -273,13 +271,7 @@ int tgs_raster_create(const TgsRasterCaps* caps, TgsRaster** out) {
   r->arena = mem;
   r->arena_bytes = bytes;
   carve(s, static_cast<char*>(mem), bytes);
-  // the look-back words and sort state start zeroed (never cleared again)
-  if (cudaMemset(s.counts, 0, sizeof(DevCounts)) != cudaSuccess ||
-      cudaMemset(s.sort_state, 0, sizeof(uint32_t) * kSortStateWords) != cudaSuccess ||
-      cudaMemset(s.sort_look, 0, sizeof(unsigned long long) * 256 * static_cast<size_t>(s.sort_max_tiles)) !=
-          cudaSuccess ||
-      cudaMemset(s.scan_look, 0, sizeof(unsigned long long) * 2 * static_cast<size_t>(s.scan_look_half)) !=
-          cudaSuccess) {
+  if (cudaMemset(s.counts, 0, sizeof(DevCounts)) != cudaSuccess) {
     cudaFree(mem);
     delete r;
     return TGS_ERR_CUDA;

@@ -21,6 +21,7 @@
 namespace tgs {
 namespace {
 
+constexpr int kWidths[6] = {3, 1, 4, 3, 3, 45};
 constexpr int kRowThreads = 256;
 constexpr int kKeepBlock = 1024;
 constexpr int kBBoxBlocks = 256;
@@ -248,8 +249,8 @@ bool set_ok(const TgsGaussians* g) {
   return g != nullptr && g->means && g->opacities && g->rotations && g->scales && g->sh0 && g->sh_rest;
 }
 
-// Morton workspace layout: codes[2][n], idx[2][n], sort look-back words
-// [max_tiles][256], sort state, bbox partials[6][kBBoxBlocks], bbox[8], count.
+// Morton workspace layout: codes[2][n], idx[2][n], hist[256][max_blocks],
+// digit totals[256], bbox partials[6][kBBoxBlocks], bbox[8], count.
 struct MortonLayout {
   size_t codes0, codes1, idx0, idx1, hist, digit, partial, bbox, count, total;
   int64_t max_blocks;
@@ -265,8 +266,8 @@ MortonLayout morton_layout(int64_t n) {
   l.codes1 = off; off += up(4 * nn);
   l.idx0 = off; off += up(4 * nn);
   l.idx1 = off; off += up(4 * nn);
-  l.hist = off; off += up(8 * 256 * static_cast<size_t>(l.max_blocks));
-  l.digit = off; off += up(4 * kSortStateWords);
+  l.hist = off; off += up(4 * 256 * static_cast<size_t>(l.max_blocks));
+  l.digit = off; off += up(4 * 256);
   l.partial = off; off += up(4 * 6 * kBBoxBlocks);
   l.bbox = off; off += up(4 * 8);
   l.count = off; off += up(4);
@@ -384,11 +385,8 @@ int tgs_morton_order(const float* means, int64_t n, void* workspace, size_t work
   k_bbox_partial<<<bb, 256, 0, s>>>(means, un, partial);
   k_bbox_final<<<1, 32, 0, s>>>(partial, bb, bbox);
   k_morton_codes<<<(un + 255) / 256, 256, 0, s>>>(means, un, bbox, keys[0], vals[0], count);
-  // the caller's workspace holds anything: the sort's state and look-back
-  // words are cleared on every call
-  cudaMemsetAsync(w + l.hist, 0, l.digit + 4 * kSortStateWords - l.hist, s);
-  const SortScratch ss{reinterpret_cast<uint32_t*>(w + l.digit), reinterpret_cast<unsigned long long*>(w + l.hist),
-                       sms};
+  const SortScratch ss{reinterpret_cast<uint32_t*>(w + l.hist), reinterpret_cast<uint32_t*>(w + l.digit),
+                       l.max_blocks, sms};
   int result = 0;
   sort_pairs_u32(keys, vals, count, n, 30, result, ss, s);
   cudaMemcpyAsync(perm, vals[result], sizeof(uint32_t) * static_cast<size_t>(n), cudaMemcpyDeviceToDevice, s);

@@ -39,7 +39,7 @@ namespace {
 
 constexpr int kScanBlock = 256;
 constexpr int kSortThreads = 256;
-constexpr int kSortItems = 16;
+constexpr int kSortItems = 8;
 constexpr int kSortTile = kSortThreads * kSortItems;  // items per sort block
 static_assert(kSortTile == kSortTileItems, "scratch sizing in abi.cu uses kSortTileItems");
 constexpr int kRadixBits = 8;
@@ -95,305 +95,239 @@ __device__ __forceinline__ void for_run(const uint32_t* src, uint32_t begin, uin
   }
 }
 
-// 2./4. stable LSD radix sort over a device-resident count, one kernel per
-// 8-bit pass (one-sweep: A. Adinets and D. Merrill, "Onesweep: A Faster
-// Least Significant Digit Radix Sort for GPUs", 2022).
-//   k_sort_init     one block: bumps the sort's epoch, clears the tickets and
-//                   the global digit counts;
-//   k_sort_upsweep  the global digit counts of every pass from one read of
-//                   the keys;
-//   k_onesweep      per pass: each block takes the next 4096-item tile by
-//                   ticket, ranks its items per digit, publishes its digit
-//                   counts, finds the exclusive prefix of every digit over
-//                   the earlier tiles by decoupled look-back, and writes its
-//                   items out as contiguous runs per digit.
-// Look-back words are 64 bits: the tag (epoch * 8 + pass) in the high half,
-// so that words of an earlier pass or sort call read as "not yet published"
-// and nothing has to be cleared between calls, and in the low half a 2-bit
-// state (1 = this tile's count, 2 = inclusive prefix) over a 30-bit count.
-// Tiles publish in ticket order and a block takes its ticket when it starts,
-// so every tile a block waits on belongs to a running or finished block; the
-// wait is bounded all the same: after kLookbackSpins polls the block raises
-// `wait_bit` in *error and carries on (its output is then invalid and the
-// raised flag says so).
-constexpr uint32_t kLookAggregate = 1u << 30;
-constexpr uint32_t kLookInclusive = 2u << 30;
-constexpr uint32_t kLookCountMask = (1u << 30) - 1u;
-constexpr uint32_t kLookbackSpins = 1u << 22;
-
-__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__global__ void __launch_bounds__(1024) k_sort_init(uint32_t* __restrict__ state) {
+// Exclusive scan of `count` block sums in place (one block of 1024 threads);
+// the grand total goes to *total_out.  Optional capacity check raises
+// `overflow_bit` in counts->overflow.
+__global__ void __launch_bounds__(1024)
+    k_scan_sums(uint32_t* __restrict__ sums, uint32_t count, uint32_t* __restrict__ total_out,
+                DevCounts* __restrict__ counts, uint32_t cap, uint32_t overflow_bit) {
   pdl_entry();
+  __shared__ uint32_t warp_sums[32];
   const uint32_t t = threadIdx.x;
-  if (t == 0) state[kSortStateEpoch] += 1u;
-  else if (t <= kSortMaxPasses) state[kSortStateTicket + t - 1] = 0u;
-  state[kSortStateHist + t] = 0u;  // kSortMaxPasses * 256 == 1024 words
-}
-
-template <typename K>
-__global__ void __launch_bounds__(kSortThreads)
-    k_sort_upsweep(const K* __restrict__ keys, const uint32_t* __restrict__ count_ptr,
-                   const DevCounts* __restrict__ counts, int total_bits, uint32_t* __restrict__ state) {
-  pdl_entry();
-  __shared__ uint32_t h[kSortMaxPasses * kRadix];
-  const uint32_t t = threadIdx.x, lane = t & 31u;
-  const int passes = (total_bits + kRadixBits - 1) / kRadixBits;
-  for (uint32_t i = t; i < kSortMaxPasses * kRadix; i += kSortThreads) h[i] = 0;
-  __syncthreads();
-  const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
-  const uint32_t stride = gridDim.x * kSortThreads;
-  // whole warps iterate together (the digit groups are formed per warp)
-  for (uint32_t base = blockIdx.x * kSortThreads + (t & ~31u); base < n; base += stride) {
-    const uint32_t idx = base + lane;
-    const bool valid = idx < n;
-    const uint32_t k = valid ? static_cast<uint32_t>(keys[idx]) : 0u;
+  const uint32_t per = (count + 1023u) / 1024u;
+  const uint32_t begin = min(count, t * per), end = min(count, begin + per);
+  uint32_t local = 0;
+  for_run(sums, begin, end, [&](uint32_t, uint32_t v) { local += v; });
+  // block scan of `local`
+  const uint32_t lane = t & 31u, warp = t >> 5;
+  uint32_t x = local;
 #pragma unroll
-    for (int p = 0; p < kSortMaxPasses; ++p) {
-      if (p < passes) {
-        const int bits = min(kRadixBits, total_bits - p * kRadixBits);
-        const uint32_t d = (k >> (p * kRadixBits)) & ((1u << bits) - 1u);
-        // one shared atomic per digit group of the warp (few distinct high
-        // digits would otherwise serialise on one address)
-        const uint32_t peers = __match_any_sync(0xffffffffu, valid ? d : 0xffffffffu);
-        if (valid && lane == static_cast<uint32_t>(__ffs(peers) - 1)) atomicAdd(&h[p * kRadix + d], __popc(peers));
-      }
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= static_cast<uint32_t>(o)) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= static_cast<uint32_t>(o)) w += y;
     }
+    warp_sums[lane] = w;
   }
   __syncthreads();
-  for (uint32_t i = t; i < static_cast<uint32_t>(passes) * kRadix; i += kSortThreads)
-    if (h[i]) atomicAdd(&state[kSortStateHist + i], h[i]);
-}
-
-template <typename K>
-__global__ void __launch_bounds__(kSortThreads)
-    k_onesweep(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, K* __restrict__ keys_out,
-               uint32_t* __restrict__ vals_out, const uint32_t* __restrict__ count_ptr,
-               const DevCounts* __restrict__ counts, int pass, int shift, int bits, uint32_t* __restrict__ state,
-               unsigned long long* __restrict__ look, uint32_t* __restrict__ error, uint32_t wait_bit) {
-  pdl_entry();
-  constexpr int kWarps = kSortThreads / 32;
-  constexpr int kPerWarp = kSortTile / kWarps;
-  __shared__ uint32_t s_cnt[kWarps][kRadix];  // running counts, then per-warp offsets
-  __shared__ uint32_t s_start[kRadix];        // block-local start of each digit
-  __shared__ uint32_t s_global[kRadix];       // global start of this tile's digit run
-  __shared__ K s_keys[kSortTile];
-  __shared__ uint32_t s_vals[kSortTile];
-  __shared__ uint32_t s_tile;
-  const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
-  if (blockIdx.x * kSortTile >= n) return;  // the grid is sized by the capacity
-  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
-  if (t == 0) s_tile = atomicAdd(&state[kSortStateTicket + pass], 1u);
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) s_cnt[w][t] = 0;
-  const unsigned long long tag = static_cast<unsigned long long>(state[kSortStateEpoch] * 8u + pass) << 32;
-  uint32_t all_digits;
-  const uint32_t smaller = block_exclusive_scan(state[kSortStateHist + pass * kRadix + t], all_digits);
-  const uint32_t tile = s_tile;
-  const uint32_t base = tile * kSortTile;
-  const uint32_t mask_bits = (1u << bits) - 1u;
-  const uint32_t lt = lanemask_lt();
-  K key[kSortItems];
-  uint32_t val[kSortItems];
-  uint32_t rank[kSortItems];
-  const uint32_t wbase = base + warp * kPerWarp;
-#pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    const uint32_t idx = wbase + r * 32 + lane;
-    key[r] = idx < n ? keys_in[idx] : K(0);
-    val[r] = idx < n ? vals_in[idx] : 0u;
-  }
-  // each warp ranks its items (rounds of 32, item order preserved) against
-  // warp-private running digit counters
-#pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    const bool valid = wbase + r * 32 + lane < n;
-    const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
-    uint32_t peers = __ballot_sync(0xffffffffu, valid);
-#pragma unroll
-    for (int bt = 0; bt < kRadixBits; ++bt) {
-      if (bt < bits) {
-        const uint32_t m = __ballot_sync(0xffffffffu, (digit >> bt) & 1u);
-        peers &= ((digit >> bt) & 1u) ? m : ~m;
-      }
-    }
-    const int leader = __ffs(peers) - 1;
-    uint32_t before = 0;
-    if (valid && static_cast<int>(lane) == leader) {
-      before = s_cnt[warp][digit];
-      s_cnt[warp][digit] = before + __popc(peers);
-    }
-    before = __shfl_sync(0xffffffffu, before, leader < 0 ? 0 : leader);
-    rank[r] = valid ? before + __popc(peers & lt) : 0xffffffffu;
-    __syncwarp();
-  }
-  __syncthreads();
-  // thread t = digit t: per-warp offsets and the tile's count of the digit
-  uint32_t run = 0;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const uint32_t c = s_cnt[w][t];
-    s_cnt[w][t] = run;
-    run += c;
-  }
-  unsigned long long* mine = look + static_cast<size_t>(tile) * kRadix + t;
-  uint32_t excl = 0;
-  if (tile == 0) {
-    st_relaxed_u64(mine, tag | kLookInclusive | run);
-  } else {
-    st_relaxed_u64(mine, tag | kLookAggregate | run);
-    uint32_t j = tile - 1, spins = 0;
-    for (;;) {
-      const unsigned long long v = ld_relaxed_u64(look + static_cast<size_t>(j) * kRadix + t);
-      const uint32_t lo = static_cast<uint32_t>(v);
-      if ((v & 0xffffffff00000000ull) == tag && (lo & ~kLookCountMask) != 0u) {
-        excl += lo & kLookCountMask;
-        if ((lo & ~kLookCountMask) == kLookInclusive || j == 0u) break;
-        --j;
-      } else if (++spins >= kLookbackSpins) {
-        atomicOr(error, wait_bit);
-        break;
-      }
-    }
-    st_relaxed_u64(mine, tag | kLookInclusive | ((excl + run) & kLookCountMask));
-  }
-  s_global[t] = smaller + excl;
-  uint32_t block_total;
-  const uint32_t start = block_exclusive_scan(run, block_total);
-  s_start[t] = start;
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    if (rank[r] != 0xffffffffu) {
-      const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
-      const uint32_t pos = s_start[digit] + s_cnt[warp][digit] + rank[r];
-      s_keys[pos] = key[r];
-      s_vals[pos] = val[r];
-    }
-  }
-  __syncthreads();
-  // consecutive items of the same digit go to consecutive global addresses
-  for (uint32_t i = t; i < block_total; i += kSortThreads) {
-    const K k = s_keys[i];
-    const uint32_t digit = (static_cast<uint32_t>(k) >> shift) & mask_bits;
-    const uint32_t g = s_global[digit] + (i - s_start[digit]);
-    keys_out[g] = k;
-    vals_out[g] = s_vals[i];
+  uint32_t run = (warp == 0 ? 0u : warp_sums[warp - 1]) + x - local;
+  for_run(sums, begin, end, [&](uint32_t k, uint32_t v) {
+    sums[k] = run;
+    run += v;
+  });
+  if (t == 1023) {
+    const uint32_t total = warp_sums[31];
+    *total_out = total;
+    if (counts != nullptr && total > cap) atomicOr(&counts->overflow, overflow_bit);
   }
 }
 
-// Decoupled look-back over one counter per tile (the scans of the candidate
-// compaction and of the entry creation): the calling warp publishes the
-// tile's aggregate, then sums the published counts of the tiles before it,
-// 32 at a time, back to the nearest inclusive prefix; it publishes its own
-// inclusive prefix and returns the exclusive one (every lane).  The words and
-// the bounded wait are those of the sort's per-digit look-back.
-__device__ __forceinline__ uint32_t warp_lookback(unsigned long long* __restrict__ words, uint32_t tile,
-                                                  uint32_t aggregate, unsigned long long tag,
-                                                  uint32_t* __restrict__ error, uint32_t wait_bit) {
-  const unsigned full = 0xffffffffu;
-  const uint32_t lane = threadIdx.x & 31u;
-  if (tile == 0u) {
-    if (lane == 0) st_relaxed_u64(words, tag | kLookInclusive | aggregate);
-    return 0u;
-  }
-  if (lane == 0) st_relaxed_u64(words + tile, tag | kLookAggregate | aggregate);
-  uint32_t excl = 0, spins = 0;
-  int64_t j = static_cast<int64_t>(tile) - 1;  // the window is [j - 31, j], lane 0 nearest
-  for (;;) {
-    const int64_t idx = j - static_cast<int64_t>(lane);
-    uint32_t lo = kLookInclusive;  // before tile 0: an inclusive prefix of 0
-    bool ready = true;
-    if (idx >= 0) {
-      const unsigned long long v = ld_relaxed_u64(words + idx);
-      lo = static_cast<uint32_t>(v);
-      ready = (v & 0xffffffff00000000ull) == tag && (lo & ~kLookCountMask) != 0u;
-    }
-    if (!__all_sync(full, ready)) {
-      if (++spins >= kLookbackSpins) {
-        if (lane == 0) atomicOr(error, wait_bit);
-        break;
-      }
-      continue;
-    }
-    const uint32_t incl = __ballot_sync(full, (lo & ~kLookCountMask) == kLookInclusive);
-    const int first = incl ? __ffs(incl) - 1 : 32;
-    excl += __reduce_add_sync(full, static_cast<int>(lane) <= first ? lo & kLookCountMask : 0u);
-    if (incl) break;
-    j -= 32;
-  }
-  if (lane == 0) st_relaxed_u64(words + tile, tag | kLookInclusive | ((excl + aggregate) & kLookCountMask));
-  return excl;
-}
-
-// Takes the block's tile by ticket (tiles are then published in ticket
-// order, see k_onesweep); the block holding the last of the n_tiles tickets
-// resets the counter for the next call, since every other ticket is taken.
-__device__ __forceinline__ uint32_t take_tile(uint32_t* __restrict__ ticket, uint32_t n_tiles) {
-  __shared__ uint32_t s_tile;
-  if (threadIdx.x == 0) {
-    const uint32_t tk = atomicAdd(ticket, 1u);
-    if (tk == n_tiles - 1u) atomicExch(ticket, 0u);
-    s_tile = tk;
-  }
-  __syncthreads();
-  return s_tile;
-}
-
-// 1. candidate list in index order: 1024 Gaussians (four preprocess blocks)
-// per tile; the tile's candidate count is the sum of the four preprocess
-// block counts, so it is published before the bounds are read.
-constexpr uint32_t kCompactTile = 4 * kScanBlock;
+// 1. candidate list in index order
 __global__ void __launch_bounds__(kScanBlock)
     k_compact_visible(const ushort4* __restrict__ bounds, const uint32_t* __restrict__ depth_key,
-                      const uint32_t* __restrict__ block_visible, uint32_t n, uint32_t* __restrict__ out_key,
-                      uint32_t* __restrict__ out_idx, DevCounts* __restrict__ counts, uint32_t* __restrict__ state,
-                      unsigned long long* __restrict__ words) {
+                      const uint32_t* __restrict__ block_offsets, uint32_t n, uint32_t* __restrict__ out_key,
+                      uint32_t* __restrict__ out_idx) {
   pdl_entry();
-  __shared__ uint32_t s_base;
-  const uint32_t n_tiles = (n + kCompactTile - 1) / kCompactTile;
-  if (blockIdx.x >= n_tiles) return;
-  const uint32_t tile = take_tile(state + kSortStateTicketCompact, n_tiles);
-  const uint32_t t = threadIdx.x;
-  if (t < 32) {
-    const unsigned long long tag = static_cast<unsigned long long>(state[kSortStateEpoch] * 8u + 4u) << 32;
-    const uint32_t nb = (n + kScanBlock - 1) / kScanBlock, b = tile * 4u + t;
-    const uint32_t agg = __reduce_add_sync(0xffffffffu, t < 4u && b < nb ? block_visible[b] : 0u);
-    const uint32_t excl = warp_lookback(words, tile, agg, tag, &counts->overflow, kOverflowSortWait);
-    if (t == 0) {
-      s_base = excl;
-      if (tile == n_tiles - 1u) counts->n_visible = excl + agg;
-    }
+  const uint32_t i = blockIdx.x * kScanBlock + threadIdx.x;
+  bool vis = false;
+  if (i < n) {
+    const ushort4 b = bounds[i];
+    vis = b.x < b.y && b.z < b.w;
   }
-  bool vis[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const uint32_t i = tile * kCompactTile + r * kScanBlock + t;
-    vis[r] = false;
-    if (i < n) {
-      const ushort4 b = bounds[i];
-      vis[r] = b.x < b.y && b.z < b.w;
-    }
+  uint32_t total;
+  const uint32_t pos = block_exclusive_scan(vis ? 1u : 0u, total) + block_offsets[blockIdx.x];
+  if (vis) {
+    out_key[pos] = depth_key[i];
+    out_idx[pos] = i;
   }
-  __syncthreads();
-  uint32_t run = s_base;
+}
+
+// 2./4. stable LSD radix sort over a device-resident count.
+// Per-block digit counts; thread t counts the 8 consecutive items t*8.. of
+// the block's tile (one or two 16-byte loads) into its warp's histogram.
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads)
+    k_radix_hist(const K* __restrict__ keys, const uint32_t* __restrict__ count_ptr,
+                 const DevCounts* __restrict__ counts, int shift, int bits, uint32_t* __restrict__ hist,
+                 uint32_t max_blocks) {
+  pdl_entry();
+  constexpr int kWarps = kSortThreads / 32;
+  __shared__ uint32_t h[kWarps][kRadix];
+  const uint32_t mask = (1u << bits) - 1u;
+  const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
+  const uint32_t t = threadIdx.x, warp = t >> 5;
+  // grid-stride over the 2048-item tiles (the grid is sized by the resident
+  // blocks, not by the capacity)
+  for (uint32_t tb = blockIdx.x; tb * kSortTile < n; tb += gridDim.x) {
+    const uint32_t base = tb * kSortTile;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const uint32_t i = tile * kCompactTile + r * kScanBlock + t;
-    uint32_t total;
-    const uint32_t pos = block_exclusive_scan(vis[r] ? 1u : 0u, total) + run;
-    run += total;
-    if (vis[r]) {
-      out_key[pos] = depth_key[i];
-      out_idx[pos] = i;
+    for (int w = 0; w < kWarps; ++w) h[w][t] = 0;
+    __syncthreads();
+    const uint32_t first = base + t * kSortItems;
+    K k[kSortItems];
+    if (base + kSortTile <= n) {
+      constexpr int kVec = kSortItems * sizeof(K) / 16;
+      const uint4* src = reinterpret_cast<const uint4*>(keys + first);
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) {
+        const uint4 q = src[v];
+        memcpy(&k[v * (16 / sizeof(K))], &q, 16);
+      }
+#pragma unroll
+      for (int j = 0; j < kSortItems; ++j) atomicAdd(&h[warp][(static_cast<uint32_t>(k[j]) >> shift) & mask], 1u);
+    } else {
+#pragma unroll
+      for (int j = 0; j < kSortItems; ++j)
+        if (first + j < n) atomicAdd(&h[warp][(static_cast<uint32_t>(keys[first + j]) >> shift) & mask], 1u);
     }
+    __syncthreads();
+    uint32_t c = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) c += h[w][t];
+    hist[t * max_blocks + tb] = c;
+    __syncthreads();  // h is cleared again for the next tile
+  }
+}
+
+// One block per digit: exclusive scan of the digit's per-block counts in
+// place, and the digit's total (the scatter adds the totals of the smaller
+// digits).  Thread t owns a contiguous run of blocks.
+__global__ void __launch_bounds__(kSortThreads)
+    k_radix_scan(uint32_t* __restrict__ hist, const uint32_t* __restrict__ count_ptr,
+                 const DevCounts* __restrict__ counts, uint32_t max_blocks, uint32_t* __restrict__ digit_total) {
+  pdl_entry();
+  const uint32_t d = blockIdx.x;
+  const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
+  const uint32_t nb = (n + kSortTile - 1) / kSortTile;
+  uint32_t* row = hist + static_cast<size_t>(d) * max_blocks;
+  const uint32_t per = (nb + kSortThreads - 1) / kSortThreads;
+  const uint32_t begin = min(nb, threadIdx.x * per), end = min(nb, begin + per);
+  uint32_t local = 0;
+  for_run(row, begin, end, [&](uint32_t, uint32_t v) { local += v; });
+  uint32_t total;
+  uint32_t run = block_exclusive_scan(local, total);
+  for_run(row, begin, end, [&](uint32_t b, uint32_t v) {
+    row[b] = run;
+    run += v;
+  });
+  if (threadIdx.x == 0) digit_total[d] = total;
+}
+
+// Scatter of one LSD pass.  Each warp ranks its 256 items (8 rounds of 32,
+// item order preserved) against warp-private running digit counters in
+// shared memory -- no block barrier per round.  The block then turns the
+// per-warp counts into block-local digit offsets, reorders its 2048 items by
+// digit in shared memory and writes them out as contiguous runs per digit.
+template <typename K>
+__global__ void __launch_bounds__(kSortThreads)
+    k_radix_scatter(const K* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+                    K* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
+                    const uint32_t* __restrict__ count_ptr, const DevCounts* __restrict__ counts, int shift,
+                    int bits, const uint32_t* __restrict__ hist, uint32_t max_blocks,
+                    const uint32_t* __restrict__ digit_total) {
+  pdl_entry();
+  constexpr int kWarps = kSortThreads / 32;
+  constexpr int kPerWarp = kSortTile / kWarps;  // 256
+  __shared__ uint32_t s_cnt[kWarps][kRadix];    // running counts, then per-warp offsets
+  __shared__ uint32_t s_start[kRadix];          // block-local start of each digit
+  __shared__ uint32_t s_global[kRadix];         // global start of this block's digit run
+  __shared__ K s_keys[kSortTile];
+  __shared__ uint32_t s_vals[kSortTile];
+  const uint32_t n = (counts != nullptr && counts->overflow) ? 0u : *count_ptr;
+  if (blockIdx.x * kSortTile >= n) return;
+  const uint32_t t = threadIdx.x, lane = t & 31u, warp = t >> 5;
+  const uint32_t mask_bits = (1u << bits) - 1u;
+  uint32_t all_digits;
+  const uint32_t smaller = block_exclusive_scan(digit_total[t], all_digits);
+  // grid-stride over the 2048-item tiles (the grid is sized by the resident
+  // blocks, not by the capacity)
+  for (uint32_t tb = blockIdx.x; tb * kSortTile < n; tb += gridDim.x) {
+    const uint32_t base = tb * kSortTile;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s_cnt[w][t] = 0;
+    s_global[t] = smaller + hist[t * max_blocks + tb];
+    __syncthreads();
+    const uint32_t lt = lanemask_lt();
+    K key[kSortItems];
+    uint32_t val[kSortItems];
+    uint32_t rank[kSortItems];
+    const uint32_t wbase = base + warp * kPerWarp;
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const uint32_t idx = wbase + r * 32 + lane;
+      const bool valid = idx < n;
+      key[r] = valid ? keys_in[idx] : K(0);
+      val[r] = valid ? vals_in[idx] : 0u;
+      const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
+      uint32_t peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+      for (int bt = 0; bt < kRadixBits; ++bt) {
+        if (bt < bits) {
+          const uint32_t m = __ballot_sync(0xffffffffu, (digit >> bt) & 1u);
+          peers &= ((digit >> bt) & 1u) ? m : ~m;
+        }
+      }
+      // the lowest lane of each digit group advances the warp's counter
+      const int leader = __ffs(peers) - 1;
+      uint32_t before = 0;
+      if (valid && static_cast<int>(lane) == leader) {
+        before = s_cnt[warp][digit];
+        s_cnt[warp][digit] = before + __popc(peers);
+      }
+      before = __shfl_sync(0xffffffffu, before, leader < 0 ? 0 : leader);
+      rank[r] = valid ? before + __popc(peers & lt) : 0xffffffffu;
+      __syncwarp();
+    }
+    __syncthreads();
+    // per-digit offsets of each warp and block-local digit starts
+    uint32_t run = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const uint32_t c = s_cnt[w][t];
+      s_cnt[w][t] = run;
+      run += c;
+    }
+    uint32_t block_total;
+    const uint32_t start = block_exclusive_scan(run, block_total);
+    s_start[t] = start;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      if (rank[r] != 0xffffffffu) {
+        const uint32_t digit = (static_cast<uint32_t>(key[r]) >> shift) & mask_bits;
+        const uint32_t pos = s_start[digit] + s_cnt[warp][digit] + rank[r];
+        s_keys[pos] = key[r];
+        s_vals[pos] = val[r];
+      }
+    }
+    __syncthreads();
+    // consecutive items of the same digit go to consecutive global addresses
+    for (uint32_t i = t; i < block_total; i += kSortThreads) {
+      const K k = s_keys[i];
+      const uint32_t digit = (static_cast<uint32_t>(k) >> shift) & mask_bits;
+      const uint32_t g = s_global[digit] + (i - s_start[digit]);
+      keys_out[g] = k;
+      vals_out[g] = s_vals[i];
+    }
+    __syncthreads();  // shared state is rebuilt for the next tile
   }
 }
 
@@ -413,83 +347,69 @@ __device__ __forceinline__ SuperRect super_rect(ushort4 b) {
   return r;
 }
 
-// 3. entry emission in depth order: (super-tile id, Gaussian id), 1024
-// depth-sorted candidates (four rounds of 256) per tile, the tile's first
-// slot found by look-back.  A tile whose entries would pass the capacity
-// writes none of them and raises the overflow flag.
-constexpr uint32_t kEntryTile = 4 * kScanBlock;
+// 3a. per-block sums of super-tile entry counts over the depth-sorted list
+__global__ void __launch_bounds__(kScanBlock)
+    k_entry_block_sums(const uint32_t* __restrict__ sorted_idx, const ushort4* __restrict__ bounds,
+                       const DevCounts* __restrict__ counts, uint32_t* __restrict__ sums) {
+  pdl_entry();
+  const uint32_t k = blockIdx.x * kScanBlock + threadIdx.x;
+  uint32_t v = 0;
+  if (k < counts->n_visible) {
+    const SuperRect r = super_rect(bounds[sorted_idx[k]]);
+    v = r.nsx * r.nsy;
+  }
+  const uint32_t s = __reduce_add_sync(0xffffffffu, v);
+  __shared__ uint32_t ws[kScanBlock / 32];
+  if ((threadIdx.x & 31u) == 0) ws[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t tot = 0;
+    for (int w = 0; w < kScanBlock / 32; ++w) tot += ws[w];
+    sums[blockIdx.x] = tot;
+  }
+}
+
+// 3b. entry emission in depth order: (super-tile id, Gaussian id)
 __global__ void __launch_bounds__(kScanBlock)
     k_create_entries(const uint32_t* __restrict__ sorted_idx, const ushort4* __restrict__ bounds,
-                     DevCounts* __restrict__ counts, uint32_t super_w, uint16_t* __restrict__ ent_key,
-                     uint32_t* __restrict__ ent_prim, uint32_t cap, uint32_t* __restrict__ state,
-                     unsigned long long* __restrict__ words) {
+                     const uint32_t* __restrict__ block_offsets, const DevCounts* __restrict__ counts,
+                     uint32_t super_w, uint16_t* __restrict__ ent_key, uint32_t* __restrict__ ent_prim) {
   pdl_entry();
-  __shared__ uint32_t s_base;
-  const uint32_t n = counts->overflow ? 0u : counts->n_visible;
-  const uint32_t n_tiles = (n + kEntryTile - 1) / kEntryTile;
-  if (blockIdx.x >= n_tiles) return;
-  const uint32_t tile = take_tile(state + kSortStateTicketEntries, n_tiles);
-  const uint32_t t = threadIdx.x;
-  uint32_t prim[4];
-  SuperRect rect[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const uint32_t k = tile * kEntryTile + r * kScanBlock + t;
-    prim[r] = 0;
-    rect[r] = SuperRect{0, 0, 0, 0};
-    if (k < n) {
-      prim[r] = sorted_idx[k];
-      rect[r] = super_rect(bounds[prim[r]]);
-    }
+  const uint32_t k = blockIdx.x * kScanBlock + threadIdx.x;
+  const bool active = k < counts->n_visible && counts->overflow == 0u;
+  uint32_t prim = 0;
+  SuperRect r{0, 0, 0, 0};
+  if (active) {
+    prim = sorted_idx[k];
+    r = super_rect(bounds[prim]);
   }
-  uint32_t off[4], round_total[4], aggregate = 0;
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    off[r] = block_exclusive_scan(rect[r].nsx * rect[r].nsy, round_total[r]) + aggregate;
-    aggregate += round_total[r];
-  }
-  if (t < 32) {
-    const unsigned long long tag = static_cast<unsigned long long>(state[kSortStateEpoch] * 8u + 5u) << 32;
-    const uint32_t excl = warp_lookback(words, tile, aggregate, tag, &counts->overflow, kOverflowSortWait);
-    if (t == 0) {
-      const uint64_t end = static_cast<uint64_t>(excl) + aggregate;
-      s_base = end > cap ? 0xffffffffu : excl;
-      if (end > cap) atomicOr(&counts->overflow, kOverflowEntries);
-      if (tile == n_tiles - 1u) counts->n_entries = static_cast<uint32_t>(end);
-    }
-  }
-  __syncthreads();
-  const uint32_t tile_base = s_base;
-  if (tile_base == 0xffffffffu) return;
-  // each warp's entries of a round laid end to end (they are contiguous in
-  // the output): lane j writes entry base + j of each group of 32, so every
-  // store is coalesced; the owner of an entry is the number of Gaussian
-  // starts up to it minus one (Gaussians with no entry start nowhere)
+  uint32_t total;
+  const uint32_t cnt = r.nsx * r.nsy;
+  const uint32_t off = block_exclusive_scan(cnt, total) + block_offsets[blockIdx.x];
+  // the warp's entries laid end to end (they are contiguous in the output):
+  // lane j writes entry base + j of each round of 32, so every store is
+  // coalesced; the owner of an entry is the number of Gaussian starts up to
+  // it minus one (Gaussians with no entry start nowhere)
   const unsigned full = 0xffffffffu;
-  const uint32_t lane = t & 31u;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t w_off = __shfl_sync(full, off, 0);
+  const uint32_t start = off - w_off;
+  const uint32_t w_total = __shfl_sync(full, start + cnt, 31);
   const uint32_t lt = lanemask_lt();
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const SuperRect rr = rect[r];
-    const uint32_t cnt = rr.nsx * rr.nsy;
-    const uint32_t w_off = __shfl_sync(full, off[r], 0);
-    const uint32_t start = off[r] - w_off;
-    const uint32_t w_total = __shfl_sync(full, start + cnt, 31);
-    uint32_t starts_before = 0;
-    for (uint32_t base = 0; base < w_total; base += 32u) {
-      const uint32_t sbit = cnt > 0u && start >= base && start < base + 32u ? 1u << (start - base) : 0u;
-      const uint32_t starts = __reduce_or_sync(full, sbit);
-      const uint32_t owner = (starts_before + __popc(starts & (lt | (1u << lane))) - 1u) & 31u;
-      starts_before += __popc(starts);
-      const uint32_t o_prim = __shfl_sync(full, prim[r], owner), o_start = __shfl_sync(full, start, owner);
-      const uint32_t o_x0 = __shfl_sync(full, rr.sx0, owner), o_y0 = __shfl_sync(full, rr.sy0, owner);
-      const uint32_t o_w = __shfl_sync(full, rr.nsx, owner);
-      const uint32_t e = base + lane;
-      if (e < w_total) {
-        const uint32_t q = e - o_start, ty = q / o_w, tx = q - ty * o_w;
-        ent_key[tile_base + w_off + e] = static_cast<uint16_t>((o_y0 + ty) * super_w + o_x0 + tx);
-        ent_prim[tile_base + w_off + e] = o_prim;
-      }
+  uint32_t starts_before = 0;
+  for (uint32_t base = 0; base < w_total; base += 32u) {
+    const uint32_t sbit = cnt > 0u && start >= base && start < base + 32u ? 1u << (start - base) : 0u;
+    const uint32_t starts = __reduce_or_sync(full, sbit);
+    const uint32_t owner = (starts_before + __popc(starts & (lt | (1u << lane))) - 1u) & 31u;
+    starts_before += __popc(starts);
+    const uint32_t o_prim = __shfl_sync(full, prim, owner), o_start = __shfl_sync(full, start, owner);
+    const uint32_t o_x0 = __shfl_sync(full, r.sx0, owner), o_y0 = __shfl_sync(full, r.sy0, owner);
+    const uint32_t o_w = __shfl_sync(full, r.nsx, owner);
+    const uint32_t e = base + lane;
+    if (e < w_total) {
+      const uint32_t t = e - o_start, ty = t / o_w, tx = t - ty * o_w;
+      ent_key[w_off + e] = static_cast<uint16_t>((o_y0 + ty) * super_w + o_x0 + tx);
+      ent_prim[w_off + e] = o_prim;
     }
   }
 }
@@ -598,13 +518,8 @@ __device__ __forceinline__ uint32_t warp_transpose_bits(uint32_t row, uint32_t l
 }
 
 // 5a. per chunk: hit mask of every entry (exact tile tests of its rectangle
-// inside the super-tile), per-tile hit counts of the chunk, and each
-// Gaussian's touched-tile total.  Each thread tests all tiles of one entry;
-// the block's 256 entries are first ordered by rectangle size (a counting
-// sort over the 33 sizes in shared memory), so that the 32 entries of a warp
-// have equal numbers of tests and the lanes do not idle.  Everything written
-// is independent of that order: the mask goes to the entry's own slot, and
-// the counts are integer sums.
+// inside the super-tile, the warp's (entry, tile) pairs tested 32 at a time),
+// per-tile hit counts of the chunk, and each Gaussian's touched-tile total.
 template <int kFp16>
 __global__ void __launch_bounds__(kScanBlock)
     k_chunk_hits(const uint4* __restrict__ chunks, const uint32_t* __restrict__ ent_prim,
@@ -615,25 +530,25 @@ __global__ void __launch_bounds__(kScanBlock)
                  uint32_t* __restrict__ n_touched) {
   pdl_entry();
   static_assert(kSubChunk == kScanBlock, "one block pass per emission sub-chunk");
-  constexpr uint32_t kSizes = kSuperTiles + 1;  // rectangle sizes 0..32
   __shared__ uint32_t s_cnt[kSubChunks * kSuperTiles];
-  __shared__ uint32_t s_size[kSizes + 1];
-  __shared__ uint4 s_work[kScanBlock];  // (entry, Gaussian, x0 | y0 << 16, w | h << 8 | magic << 16)
+  // each entry's test inputs and rectangle, read by the lanes that test its
+  // tiles (48 bytes used of 64-byte records)
+  __shared__ float4 s_rec[kScanBlock / 32][32][4];
   const unsigned full = 0xffffffffu;
   const uint32_t n_chunks = counts->overflow ? 0u : counts->n_chunks;
-  const uint32_t t = threadIdx.x, lane = t & 31u;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t lt = lanemask_lt();
   for (uint32_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
     const uint4 ch = chunks[c];
     const uint32_t tx0 = (ch.x % super_w) * kSuperW, ty0 = (ch.x / super_w) * kSuperH;
-    if (t < kSubChunks * kSuperTiles) s_cnt[t] = 0;
+    if (threadIdx.x < kSubChunks * kSuperTiles) s_cnt[threadIdx.x] = 0;
+    __syncthreads();
     for (uint32_t e0 = ch.y; e0 < ch.z; e0 += kScanBlock) {
       uint32_t* sub_cnt = s_cnt + (e0 - ch.y) / kScanBlock * kSuperTiles;
-      const uint32_t n_valid = min(ch.z - e0, static_cast<uint32_t>(kScanBlock));
-      if (t < kSizes) s_size[t] = 0;
-      __syncthreads();  // also: the previous pass has read its work records
-      const uint32_t e = e0 + t;
-      const bool valid = t < n_valid;
-      uint32_t prim = 0, x0 = 0, y0 = 0, w = 0, h = 0;
+      const uint32_t e = e0 + threadIdx.x;
+      const bool valid = e < ch.z;
+      uint32_t prim = 0, x0 = 0, y0 = 0, w = 0, h = 0, magic = 0;
+      TileTest tt{};
       if (valid) {
         prim = ent_prim[e];
         const ushort4 b = bounds[prim];
@@ -641,45 +556,82 @@ __global__ void __launch_bounds__(kScanBlock)
         y0 = max(static_cast<uint32_t>(b.z), ty0);
         w = min(static_cast<uint32_t>(b.y), tx0 + kSuperW) - x0;
         h = min(static_cast<uint32_t>(b.w), ty0 + kSuperH) - y0;
+        magic = 255u / w + 1u;  // t / w == (t * magic) >> 8 for t < 33, w <= 8
+        tt = tile_test_of<kFp16>(prim, mean2d, conic_opacity, prim_info);
       }
-      const uint32_t size = w * h;  // 1..32 for an entry
-      const uint32_t rank = valid ? atomicAdd(&s_size[size], 1u) : 0u;
-      __syncthreads();
-      if (t < 32) {
-        // exclusive scan of the 33 size counts (lane 31 also carries size 32)
-        const uint32_t v = s_size[t] + (t == 31 ? s_size[32] : 0u);
-        uint32_t incl = v;
+      const uint32_t total = w * h;  // <= 32
+      // lay the lanes' rectangles end to end; lane j tests pair base + j
+      uint32_t incl = total;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(full, incl, o);
-          if (lane >= static_cast<uint32_t>(o)) incl += y;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(full, incl, o);
+        if (lane >= static_cast<uint32_t>(o)) incl += y;
+      }
+      const uint32_t start = incl - total;
+      const uint32_t pairs = __shfl_sync(full, incl, 31);
+      {
+        float4* rec = s_rec[threadIdx.x >> 5][lane];
+        rec[0] = make_float4(tt.ca, tt.cb, tt.cc, tt.thr);
+        rec[1] = make_float4(kFp16 ? tt.xs : tt.mx, kFp16 ? tt.ys : tt.my,
+                             __uint_as_float(*reinterpret_cast<const uint32_t*>(&tt.c_xy)),
+                             __uint_as_float(*reinterpret_cast<const uint32_t*>(&tt.c_yz)));
+        rec[2] = make_float4(__uint_as_float(*reinterpret_cast<const uint32_t*>(&tt.den)),
+                             __uint_as_float(start), __uint_as_float(x0 | (y0 << 16)),
+                             __uint_as_float(w | (magic << 8)));
+      }
+      __syncwarp();
+      uint32_t local = 0;  // hits in rectangle order (bit t = row t / w, column t % w)
+      // owners are lanes 0 .. (valid entries - 1), every one with total >= 1,
+      // so the owner of a slot is the number of rectangle starts up to it - 1
+      uint32_t starts_before = 0;
+      for (uint32_t base = 0; base < pairs; base += 32u) {
+        const uint32_t slot = base + lane;
+        const uint32_t sbit = total > 0u && start >= base && start < base + 32u ? 1u << (start - base) : 0u;
+        const uint32_t starts = __reduce_or_sync(full, sbit);
+        const uint32_t owner = (starts_before + __popc(starts & (lt | (1u << lane))) - 1u) & 31u;
+        starts_before += __popc(starts);
+        const float4* orec = s_rec[threadIdx.x >> 5][owner];
+        const float4 r0 = orec[0], r1 = orec[1], r2 = orec[2];
+        TileTest q;
+        q.ca = r0.x;
+        q.cb = r0.y;
+        q.cc = r0.z;
+        q.thr = r0.w;
+        if constexpr (kFp16) {
+          q.xs = r1.x;
+          q.ys = r1.y;
+          const uint32_t cxy = __float_as_uint(r1.z), cyz = __float_as_uint(r1.w), den = __float_as_uint(r2.x);
+          q.c_xy = *reinterpret_cast<const __half2*>(&cxy);
+          q.c_yz = *reinterpret_cast<const __half2*>(&cyz);
+          q.den = *reinterpret_cast<const __half2*>(&den);
+        } else {
+          q.mx = r1.x;
+          q.my = r1.y;
         }
-        const uint32_t s31 = s_size[31];
-        __syncwarp();
-        s_size[t] = incl - v;
-        if (t == 31) s_size[32] = incl - v + s31;
+        const uint32_t o_start = __float_as_uint(r2.y), o_xy = __float_as_uint(r2.z), o_wm = __float_as_uint(r2.w);
+        const uint32_t o_x = o_xy & 0xffffu, o_y = o_xy >> 16, o_w = o_wm & 0xffu, o_magic = o_wm >> 8;
+        const uint32_t t = slot - o_start;
+        const uint32_t row = (t * o_magic) >> 8;
+        const bool hit = slot < pairs && overlaps<kFp16>(q, o_x + (t - row * o_w), o_y + row);
+        const uint32_t m = __ballot_sync(full, hit);
+        // this lane's pairs within the round are one run of ballot bits
+        const uint32_t lo = max(start, base), hi = min(start + total, base + 32u);
+        if (lo < hi) {
+          const uint32_t len = hi - lo;
+          const uint32_t bits = (m >> (lo - base)) & (len == 32u ? full : ((1u << len) - 1u));
+          local |= bits << (lo - start);
+        }
       }
-      __syncthreads();
-      if (valid) {
-        const uint32_t magic = 255u / w + 1u;  // q / w == (q * magic) >> 8 for q < 33, w <= 8
-        s_work[s_size[size] + rank] = make_uint4(e, prim, x0 | (y0 << 16), w | (h << 8) | (magic << 16));
-      }
-      __syncthreads();
+      __syncwarp();  // the records are rewritten by the next pass
+      // rectangle order -> super-tile bits (row * 8 + column)
       uint32_t mask = 0;
-      if (t < n_valid) {
-        const uint4 wk = s_work[t];
-        const uint32_t me = wk.x, mp = wk.y;
-        const uint32_t mx0 = wk.z & 0xffffu, my0 = wk.z >> 16;
-        const uint32_t mw = wk.w & 0xffu, mh = (wk.w >> 8) & 0xffu, mmagic = wk.w >> 16;
-        const TileTest tt = tile_test_of<kFp16>(mp, mean2d, conic_opacity, prim_info);
-        const uint32_t n_tests = mw * mh;
-        const uint32_t bit0 = (my0 - ty0) * kSuperW + (mx0 - tx0);
-        for (uint32_t q = 0; q < n_tests; ++q) {
-          const uint32_t row = (q * mmagic) >> 8, col = q - row * mw;
-          if (overlaps<kFp16>(tt, mx0 + col, my0 + row)) mask |= 1u << (bit0 + row * kSuperW + col);
-        }
-        masks[me] = mask;
-        if (mask != 0u) atomicAdd(&n_touched[mp], static_cast<uint32_t>(__popc(mask)));
+      const uint32_t row_bits = w == 32u ? full : ((1u << w) - 1u);
+#pragma unroll
+      for (uint32_t r = 0; r < kSuperH; ++r)
+        if (r < h) mask |= ((local >> (r * w)) & row_bits) << ((y0 - ty0 + r) * kSuperW + (x0 - tx0));
+      if (valid) {
+        masks[e] = mask;
+        if (mask != 0u) atomicAdd(&n_touched[prim], static_cast<uint32_t>(__popc(mask)));
       }
       // per-tile counts: transpose the warp's 32 x 32 bit matrix of masks
       // (rows = entries, columns = tiles) across the lanes, so that lane j
@@ -861,68 +813,72 @@ __global__ void __launch_bounds__(32 * kEmitWarps)
 
 template <typename K>
 void radix_sort(K* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, const DevCounts* counts,
-                int64_t capacity, int total_bits, int& result, const SortScratch& ss, cudaStream_t stream,
-                uint32_t* error, uint32_t wait_bit) {
+                int64_t capacity, int total_bits, int& result, const SortScratch& ss, cudaStream_t stream) {
   const uint32_t tiles = static_cast<uint32_t>((capacity + kSortTile - 1) / kSortTile);
-  const uint32_t up_blocks = std::min<uint32_t>(tiles > 0 ? tiles : 1u, static_cast<uint32_t>(ss.num_sms) * 4u);
-  pdl_launch(k_sort_init, 1, 1024, 0, stream, ss.state);
-  pdl_launch(k_sort_upsweep<K>, up_blocks, kSortThreads, 0, stream, keys[0], count_ptr, counts, total_bits,
-             ss.state);
+  const uint32_t resident = static_cast<uint32_t>(ss.num_sms) * 8u;
+  const uint32_t blocks = tiles < resident ? tiles : resident;
+  const uint32_t max_blocks = static_cast<uint32_t>(ss.max_blocks);
   int cur = 0;
-  int pass = 0;
-  for (int shift = 0; shift < total_bits; shift += kRadixBits, ++pass) {
+  for (int shift = 0; shift < total_bits; shift += kRadixBits) {
     const int bits = min(kRadixBits, total_bits - shift);
-    if (tiles > 0)
-      pdl_launch(k_onesweep<K>, tiles, kSortThreads, 0, stream, keys[cur], vals[cur], keys[1 - cur], vals[1 - cur],
-                 count_ptr, counts, pass, shift, bits, ss.state, ss.look, error, wait_bit);
+    if (blocks > 0) {
+      pdl_launch(k_radix_hist<K>, blocks, kSortThreads, 0, stream, keys[cur], count_ptr, counts, shift, bits,
+                 ss.hist, max_blocks);
+      pdl_launch(k_radix_scan, kRadix, kSortThreads, 0, stream, ss.hist, count_ptr, counts, max_blocks,
+                 ss.digit_total);
+      pdl_launch(k_radix_scatter<K>, blocks, kSortThreads, 0, stream, keys[cur], vals[cur], keys[1 - cur],
+                 vals[1 - cur], count_ptr, counts, shift, bits, ss.hist, max_blocks, ss.digit_total);
+    }
     cur = 1 - cur;
   }
   result = cur;
 }
 
 SortScratch sort_scratch(const RasterState& s) {
-  return SortScratch{s.sort_state, s.sort_look, s.num_sms};
+  return SortScratch{s.sort_hist, s.sort_digit_total, s.sort_max_blocks, s.num_sms};
 }
 
 }  // namespace
 
 void sort_pairs_u32(uint32_t* keys[2], uint32_t* vals[2], const uint32_t* count_ptr, int64_t capacity,
                     int total_bits, int& result, const SortScratch& ss, cudaStream_t stream) {
-  radix_sort<uint32_t>(keys, vals, count_ptr, nullptr, capacity, total_bits, result, ss, stream,
-                       ss.state + kSortStateError, 1u);
+  radix_sort<uint32_t>(keys, vals, count_ptr, nullptr, capacity, total_bits, result, ss, stream);
 }
 
 void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16, cudaStream_t stream) {
   const uint32_t n = static_cast<uint32_t>(n64);
+  const uint32_t n_blocks = (n + kScanBlock - 1) / kScanBlock;
   const uint32_t n_tiles = cam.grid_w * cam.grid_h;
   const uint32_t super_w = (cam.grid_w + kSuperW - 1) / kSuperW, super_h = (cam.grid_h + kSuperH - 1) / kSuperH;
   const uint32_t n_super = super_w * super_h;
   DevCounts* counts = s.counts;
-  // 1. compaction (the preprocess kernel wrote each 256-Gaussian block's
-  // candidate count)
-  const uint32_t compact_tiles = (n + kCompactTile - 1) / kCompactTile;
-  if (compact_tiles > 0)
-    pdl_launch(k_compact_visible, compact_tiles, kScanBlock, 0, stream, s.bounds, s.depth_key, s.block_sums, n,
-               s.vis_key[0], s.vis_idx[0], counts, s.sort_state, s.scan_look);
+  // 1. compaction (block sums were written by the preprocess kernel)
+  pdl_launch(k_scan_sums, 1, 1024, 0, stream, s.block_sums, n_blocks, &counts->n_visible, nullptr, 0, 0);
+  if (n_blocks > 0)
+    pdl_launch(k_compact_visible, n_blocks, kScanBlock, 0, stream, s.bounds, s.depth_key, s.block_sums, n,
+               s.vis_key[0], s.vis_idx[0]);
   // 2. depth sort (32-bit keys)
-  radix_sort<uint32_t>(s.vis_key, s.vis_idx, &counts->n_visible, counts, n64, 32, s.depth_result,
-                       sort_scratch(s), stream, &counts->overflow, kOverflowSortWait);
+  radix_sort<uint32_t>(s.vis_key, s.vis_idx, &counts->n_visible, nullptr, n64, 32, s.depth_result,
+                       sort_scratch(s), stream);
   const uint32_t* sorted = s.vis_idx[s.depth_result];
   // 3. super-tile entries in depth order, sorted by super-tile
-  if (compact_tiles > 0)
-    pdl_launch(k_create_entries, compact_tiles, kScanBlock, 0, stream, sorted, s.bounds, counts, super_w,
-               s.ent_key[0], s.ent_prim[0], static_cast<uint32_t>(s.cap_entries), s.sort_state,
-               s.scan_look + s.scan_look_half);
+  if (n_blocks > 0) {
+    pdl_launch(k_entry_block_sums, n_blocks, kScanBlock, 0, stream, sorted, s.bounds, counts, s.block_sums);
+    pdl_launch(k_scan_sums, 1, 1024, 0, stream, s.block_sums, n_blocks, &counts->n_entries, counts,
+               static_cast<uint32_t>(s.cap_entries), kOverflowEntries);
+    pdl_launch(k_create_entries, n_blocks, kScanBlock, 0, stream, sorted, s.bounds, s.block_sums, counts, super_w,
+               s.ent_key[0], s.ent_prim[0]);
+  }
   int super_bits = 1;
   while ((1u << super_bits) < n_super) ++super_bits;
   radix_sort<uint16_t>(s.ent_key, s.ent_prim, &counts->n_entries, counts, s.cap_entries, super_bits, s.ent_result,
-                       sort_scratch(s), stream, &counts->overflow, kOverflowSortWait);
+                       sort_scratch(s), stream);
   const uint16_t* ent_key = s.ent_key[s.ent_result];
   const uint32_t* ent_prim = s.ent_prim[s.ent_result];
   // 4. chunks of each super-tile's entry list
   if (super_bits <= kRadixBits) {
     // one pass: its digit totals are the super-tiles' entry counts
-    pdl_launch(k_chunk_table, 1, 1024, 0, stream, s.super_ranges, s.sort_state + kSortStateHist, n_super, s.chunks,
+    pdl_launch(k_chunk_table, 1, 1024, 0, stream, s.super_ranges, s.sort_digit_total, n_super, s.chunks,
                s.super_chunk, counts);
   } else {
     cudaMemsetAsync(s.super_ranges, 0, sizeof(uint2) * n_super, stream);

@@ -48,18 +48,7 @@ constexpr float kMinAlpha = 1.0f / 255.0f;
 constexpr float kMaxAlphaF32 = 0.999f;
 constexpr float kMaxAlphaF16 = 0.99f;
 constexpr float kMinTransmittance = 1e-4f;
-constexpr int kSortTileItems = 4096;  // items per radix-sort tile (one block)
-// radix-sort state words: epoch, per-pass tile tickets, the tickets of the
-// two look-back scans, error word, then the global digit counts of up to four
-// 8-bit passes
-constexpr int kSortMaxPasses = 4;
-constexpr int kSortStateEpoch = 0;
-constexpr int kSortStateTicket = 1;         // [1, 1 + kSortMaxPasses)
-constexpr int kSortStateTicketCompact = 5;  // tile tickets of the candidate compaction
-constexpr int kSortStateTicketEntries = 6;  // tile tickets of the entry creation
-constexpr int kSortStateError = 8;
-constexpr int kSortStateHist = 256;  // [256 + pass * 256 + digit]
-constexpr int kSortStateWords = kSortStateHist + kSortMaxPasses * 256;
+constexpr int kSortTileItems = 2048;  // items per radix-sort block
 // binning works on super-tiles of 8x4 tiles (one bit per tile in a 32-bit
 // mask) and cuts each super-tile's depth-ordered list into chunks
 constexpr uint32_t kSuperW = 8;
@@ -120,7 +109,6 @@ struct alignas(16) PrimInfo16 {
 constexpr uint32_t kOverflowInstances = 1u;
 constexpr uint32_t kOverflowBuckets = 2u;
 constexpr uint32_t kOverflowEntries = 4u;  // (Gaussian, super-tile) entries
-constexpr uint32_t kOverflowSortWait = 8u; // a look-back wait of a scan or sort gave up
 
 // Device counters of one forward, kept in one 32-byte record.
 struct DevCounts {

@@ -61,11 +61,9 @@ struct RasterState {
   // instance follows from the tile ranges)
   uint32_t* inst_prim[2] = {nullptr, nullptr};  // only [0] is allocated
   // radix sort scratch
-  uint32_t* sort_state = nullptr;            // [kSortStateWords]
-  unsigned long long* sort_look = nullptr;  // [sort_max_tiles][256]
-  int64_t sort_max_tiles = 0;
-  unsigned long long* scan_look = nullptr;  // look-back words of the compaction, then of the entry creation
-  int64_t scan_look_half = 0;
+  uint32_t* sort_hist = nullptr;    // [256][sort_max_blocks]
+  uint32_t* sort_digit_total = nullptr;  // [256]
+  int64_t sort_max_blocks = 0;
   // per tile
   uint2* ranges = nullptr;
   uint32_t* tile_total = nullptr;
@@ -93,14 +91,13 @@ struct RasterState {
 DevCamera make_camera(int width, int height, float fx, float fy, float cx, float cy,
                       float near_plane, float far_plane, const float w2c[16]);
 
-// Scratch of the stable LSD radix sort (binning.cu): the state words (sort
-// epoch, per-pass tile tickets, per-pass global digit counts, error word) and
-// the look-back words [max_tiles][256] (max_tiles = ceil(capacity /
-// kSortTileItems)).  Both must be zeroed once before the first sort; after
-// that nothing is cleared between calls.
+// Scratch of the stable LSD radix sort (binning.cu): per-digit block counts
+// [256][max_blocks] (max_blocks = ceil(capacity / kSortTileItems)) and the
+// 256 digit totals.
 struct SortScratch {
-  uint32_t* state;
-  unsigned long long* look;
+  uint32_t* hist;
+  uint32_t* digit_total;
+  int64_t max_blocks;
   int num_sms;
 };
 

@@ -25,7 +25,8 @@ def _set(n, seed, sh=3):
     return params, rt.GaussianSet.from_numpy(params, sh)
 
 
-@pytest.mark.parametrize("n", [1, 1000, 1_000_003])
+# 4096 / 4097 / 12288: whole 2048-item sort tiles, one item past them, six tiles
+@pytest.mark.parametrize("n", [1, 1000, 4096, 4097, 12288, 1_000_003])
 def test_morton_order_matches_oracle(oracle, cuda_lib, n):
     params, g = _set(n, 11)
     perm = rt.morton_order(g).cpu().numpy().view(np.uint32)

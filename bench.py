@@ -896,6 +896,27 @@ def run_ours(args):
                 "gaussian_backward_adam_ms": stages["gaussian_backward_adam"],
                 "note": "records (preprocess) stored into the view ranks' arenas and screen-space gradients "
                         "read back over NVLink; no gradient all-reduce"}
+            # NVLink bytes per GPU per step, estimated from this rank's view
+            # (its candidate and touched fractions stand for every view's):
+            # out during the preprocess, per other view, the touched-count
+            # and bounds words of every slice Gaussian (12 B) plus the depth
+            # key, mean2d and primitive record of each candidate (28 B fp16,
+            # 40 B fp32); in during the backward, per other view, the touched
+            # counts (4 B) plus the 48-byte screen gradients of each touched
+            # Gaussian.  Peak: the recipe's measured peer copy (770 GB/s per
+            # direction per GPU).
+            nl = owner.last - owner.first
+            others = world - 1
+            rec_bytes = others * nl * (12 + (28 if fp16 else 40) * counts.n_visible / cfg.n)
+            grad_bytes = others * nl * (4 + 48 * touched_v / cfg.n)
+            pre_ms, bwd_ms = stages["preprocess"], stages["gaussian_backward_adam"]
+            line["owner_split"]["nvlink"] = {
+                "records_out_bytes": rec_bytes, "records_out_gbs": rec_bytes / (pre_ms * 1e-3) / 1e9,
+                "screen_grads_in_bytes": grad_bytes, "screen_grads_in_gbs": grad_bytes / (bwd_ms * 1e-3) / 1e9,
+                "peak_gbs_each_way": 770.0,
+                "link_floor_ms": max(rec_bytes, grad_bytes) / 770e9 * 1e3,
+                "peak_source": "peer copy per direction measured on this pool (profiling recipe), not re-measured here",
+                "estimate": "per-view candidate/touched fractions taken from this rank's view"}
         elif peer:
             # NVLink bytes into each GPU (and the same out of it) per step.
             # peer: its slice's gradients loaded from the other ranks plus the

@@ -21,7 +21,6 @@
 namespace tgs {
 namespace {
 
-constexpr int kWidths[6] = {3, 1, 4, 3, 3, 45};
 constexpr int kRowThreads = 256;
 constexpr int kKeepBlock = 1024;
 constexpr int kBBoxBlocks = 256;

@@ -886,18 +886,25 @@ void launch_binning(RasterState& s, int64_t n64, const DevCamera& cam, int fp16,
     pdl_launch(k_chunk_table, 1, 1024, 0, stream, s.super_ranges, nullptr, n_super, s.chunks, s.super_chunk, counts);
   }
   // 5. hit masks and counts, then every (chunk, tile)'s first slot
-  const int persistent = s.num_sms * 8;
+  // tile tests: one block per chunk (capacity-sized grid; blocks past the
+  // live chunk count exit at once): the hardware hands chunks of uneven
+  // length to SMs as they free up, where a grid-stride loop over resident
+  // blocks left a tail of blocks with one chunk more than the others (cfg2:
+  // 212 against 236 us)
+  const int chunk_grid = static_cast<int>(s.cap_chunks > 0 ? s.cap_chunks : 1);
   if (fp16)
-    pdl_launch(k_chunk_hits<1>, persistent, kScanBlock, 0, stream, s.chunks, ent_prim, s.bounds, s.mean2d,
+    pdl_launch(k_chunk_hits<1>, chunk_grid, kScanBlock, 0, stream, s.chunks, ent_prim, s.bounds, s.mean2d,
                s.conic_opacity, s.prim_info, counts, super_w, s.masks, s.chunk_counts, s.sub_offsets, s.n_touched);
   else
-    pdl_launch(k_chunk_hits<0>, persistent, kScanBlock, 0, stream, s.chunks, ent_prim, s.bounds, s.mean2d,
+    pdl_launch(k_chunk_hits<0>, chunk_grid, kScanBlock, 0, stream, s.chunks, ent_prim, s.bounds, s.mean2d,
                s.conic_opacity, s.prim_info, counts, super_w, s.masks, s.chunk_counts, s.sub_offsets, s.n_touched);
   pdl_launch(k_chunk_prefix, (n_super * kSuperTiles + 255) / 256, 256, 0, stream, s.super_ranges, s.super_chunk,
              n_super, super_w, cam.grid_w, cam.grid_h, counts, s.chunk_counts, s.tile_total);
   pdl_launch(k_tile_offsets, 1, 1024, 0, stream, s.tile_total, n_tiles, s.ranges, s.bucket_offsets, counts,
              static_cast<uint32_t>(s.cap_inst), static_cast<uint32_t>(s.cap_buckets));
   // 6. instances at their final slots
+  // (the emission keeps a grid-stride loop over resident blocks: one block
+  // per chunk measured 104 against 90 us at cfg2)
   pdl_launch(k_emit_instances, s.num_sms * 16, 32 * kEmitWarps, 0, stream, s.chunks, ent_prim, s.masks,
              s.chunk_counts, s.sub_offsets, s.ranges, counts, super_w, cam.grid_w, cam.grid_h, s.inst_prim[0]);
   s.tile_result = 0;

@@ -418,7 +418,8 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
                      const float* __restrict__ color, const PrimInfo16* __restrict__ prim_info,
                      const void* __restrict__ image_v, const void* __restrict__ grad_v,
                      const void* __restrict__ n_contrib_v, const void* __restrict__ ckpt_v,
-                     const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ helpers) {
+                     const DevCounts* __restrict__ counts, DevCamera cam, float* __restrict__ helpers,
+                     uint32_t* __restrict__ work) {
   // Two pixel streams per lane (pixels 0..127 and 128..255 of the tile),
   // evaluated together with packed fp32 pairs.  Per warp, the pixel pairs of
   // the current and the previous 32-step chunk sit in a ring of 64 records:
@@ -446,7 +447,25 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
   if constexpr (!kFp16) s_last[warp][lane] = s_last[warp][32 + lane] = make_uint2(0u, 0u);
   __syncwarp();
 
-  for (uint32_t item = blockIdx.x * kBwdWarps + warp; item < n_live; item += stride) {
+  // Buckets differ in cost (a bucket late in its tile sweeps pixels that
+  // have mostly stopped), so a fixed share per warp leaves a tail of warps
+  // still busy after the others ran out.  The first three quarters of the
+  // list are dealt out by stride; the rest is taken kGrab buckets at a time
+  // from the counter *work (zeroed before the launch), by whichever warps are
+  // free.
+  constexpr uint32_t kGrab = 4;
+  const uint32_t n_static = n_live - n_live / 4;
+  uint32_t item = blockIdx.x * kBwdWarps + warp, grab_end = 0;
+  for (;;) {
+    if (item >= n_static) {
+      if (item >= grab_end) {
+        uint32_t b = 0;
+        if (lane == 0) b = atomicAdd(work, kGrab);
+        item = n_static + __shfl_sync(0xffffffffu, b, 0);
+        grab_end = item + kGrab;
+      }
+      if (item >= n_live) break;
+    }
     const uint2 lb = live_buckets[item];
     const uint32_t tile = lb.x, tb = lb.y;
     const uint2 r = ranges[tile];
@@ -606,6 +625,7 @@ __global__ void __launch_bounds__(32 * kBwdWarps)
       atomicAdd(h + 9, gc1);
       atomicAdd(h + 10, gc2);
     }
+    item += item < n_static ? stride : 1u;
   }
 }
 
@@ -621,9 +641,10 @@ void run_blend_backward(const RasterState& s, const DevCamera& cam, const void* 
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, k_blend_backward<kFp16, kAbs>, 32 * kBwdWarps, 0);
     if (bps <= 0) bps = 1;
   }
+  cudaMemsetAsync(s.bwd_work, 0, sizeof(uint32_t), stream);
   k_blend_backward<kFp16, kAbs><<<s.num_sms * bps, 32 * kBwdWarps, 0, stream>>>(
       s.ranges, s.bucket_offsets, s.live_buckets, s.inst_prim[s.tile_result], s.mean2d, s.conic_opacity, s.color,
-      s.prim_info, image, grad_image, s.n_contrib, s.ckpt, s.counts, cam, s.helpers);
+      s.prim_info, image, grad_image, s.n_contrib, s.ckpt, s.counts, cam, s.helpers, s.bwd_work);
 }
 
 }  // namespace

@@ -474,8 +474,8 @@ def run_reference_cpu(args):
 def kernels_per_step(width: int, height: int, world: int, owner: bool = False) -> int:
     """Launches of this library's kernels in one training step (what
     launch_preprocess / launch_binning / launch_blend_* / the loss and the
-    backward enqueue).  owner: the owner split launches the preprocess and
-    the per-Gaussian backward once per view."""
+    backward enqueue).  owner: the owner split's preprocess covers every
+    view in one launch and its per-Gaussian backward + Adam is one launch."""
     grid_w, grid_h = (width + 15) // 16, (height + 15) // 16
     n_super = ((grid_w + 7) // 8) * ((grid_h + 3) // 4)
     entry_passes = max(1, ((max(1, n_super - 1)).bit_length() + 7) // 8)
@@ -490,7 +490,7 @@ def kernels_per_step(width: int, height: int, world: int, owner: bool = False) -
     # loss forward + backward; blend backward; per-Gaussian backward fused
     # with Adam (one GPU) or routed backward + accumulation/Adam kernel
     if owner:
-        return forward + (world - 1) + 2 + 1 + 1
+        return forward + 2 + 1 + 1
     return forward + 2 + 1 + (1 if world == 1 else 2)
 
 

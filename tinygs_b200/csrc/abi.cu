@@ -763,20 +763,25 @@ int tgs_raster_preprocess_views(TgsRaster* r, const TgsGaussians* params, const 
     const TgsCamera* c = &cams[k];
     if (!camera_ok(c) || c->width > r->s.max_w || c->height > r->s.max_h) return TGS_ERR_INVALID_ARGUMENT;
   }
-  // every rank starts with the next rank's view and ends with its own, so
-  // that at any moment the ranks' record stores go to different GPUs (in
-  // view order every rank would store into rank 0's arena first); the
-  // records of different views are disjoint, so the order changes nothing
-  for (int j = 0; j < r->world; ++j) {
-    const int k = (r->rank + 1 + j) % r->world;
+  // one launch for all views (the slice's parameters are read once); every
+  // rank starts with the next rank's view and ends with its own, so that at
+  // any moment the ranks' record stores go to different GPUs (in view order
+  // every rank would store into rank 0's arena first); the records of
+  // different views are disjoint, so the order changes nothing.  The views'
+  // backward accumulators are cleared by their ranks
+  // (tgs_raster_forward_gathered), not across NVLink.
+  RasterState vs[kMaxDpRanks];
+  DevCamera dcs[kMaxDpRanks];
+  int order[kMaxDpRanks];
+  for (int k = 0; k < r->world; ++k) {
     const TgsCamera* c = &cams[k];
-    const DevCamera dc = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane,
-                                     c->w2c);
-    // the backward accumulators are cleared by the view's rank
-    // (tgs_raster_forward_gathered), not across NVLink
-    if (last > first) launch_preprocess(view_state(r, k), g, dc, dtype == TGS_FLOAT16,
-                                        reinterpret_cast<float4*>(dens), st, first, last, 0);
+    vs[k] = view_state(r, k);
+    dcs[k] = make_camera(c->width, c->height, c->fx, c->fy, c->cx, c->cy, c->near_plane, c->far_plane, c->w2c);
+    order[k] = (r->rank + 1 + k) % r->world;
   }
+  if (last > first)
+    launch_preprocess_views(vs, dcs, order, r->world, g, dtype == TGS_FLOAT16, reinterpret_cast<float4*>(dens), st,
+                            first, last, 0);
   return cuda_status(cudaGetLastError());
 }
 

@@ -113,6 +113,13 @@ void sort_pairs_u32(uint32_t* keys[2], uint32_t* vals[2], const uint32_t* count_
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam,
                        int fp16, float4* dens, cudaStream_t stream, int64_t first = 0, int64_t last = -1,
                        int zero_helpers = 1);
+// Gaussians [first, last) projected into `count` views (cams[k], records
+// into views[k]'s arena), taken in `order`; parameters read once.
+// zero_helpers == 0 leaves the views' backward accumulators to their ranks
+// (the owner split).  launch_preprocess is the one-view case.
+void launch_preprocess_views(const RasterState* views, const DevCamera* cams, const int* order, int count,
+                             const GaussianPtrs& g, int fp16, float4* dens, cudaStream_t stream, int64_t first,
+                             int64_t last, int zero_helpers);
 void launch_binning(RasterState& s, int64_t n, const DevCamera& cam, int fp16, cudaStream_t stream);
 void launch_blend_forward(const RasterState& s, const DevCamera& cam, int fp16, void* image,
                           void* alpha, cudaStream_t stream);

@@ -135,61 +135,56 @@ __device__ __forceinline__ uint32_t clamp_bound(int v, uint32_t hi) {
   return min(hi, static_cast<uint32_t>(max(0, v)));
 }
 
-template <int kFp16>
-__global__ void __launch_bounds__(kPreBlock)
-    k_preprocess(const float* __restrict__ means, const float* __restrict__ opacities,
-                 const float4* __restrict__ rotations, const float* __restrict__ scales,
-                 const float* __restrict__ sh0, const float* __restrict__ sh_rest, int active_bases,
-                 uint32_t n, DevCamera cam, float4* __restrict__ dens, uint32_t* __restrict__ n_touched,
-                 uint32_t* __restrict__ depth_key, ushort4* __restrict__ bounds,
-                 float2* __restrict__ mean2d, float4* __restrict__ conic_opacity,
-                 PrimInfo16* __restrict__ prim_info, float* __restrict__ color,
-                 float4* __restrict__ helpers,
-                 uint32_t* __restrict__ block_visible, int rest_vec, uint32_t first_block, int zero_helpers) {
-  // higher-order SH rows of the warp's 32 Gaussians, loaded coalesced (one
-  // row per lane would touch 32 cache lines per load instruction)
-  __shared__ __align__(16) float s_rest[kPreBlock / 32][32 * 45];
-  // first_block: the launch covers Gaussians from first_block * kPreBlock
-  // (a slice of the model whose records go to another rank's view)
-  const uint32_t i = (first_block + blockIdx.x) * kPreBlock + threadIdx.x;
-  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  // start the copy of the warp's SH rows now; it lands while the projection
-  // below is computed (rows of culled Gaussians are copied too)
-  const uint32_t first = i - lane;
-  const bool stage_rest = active_bases > 1 && first < n;
-  if (stage_rest) {
-    const uint32_t cnt = min(32u, n - first);
-    const float* src = sh_rest + 45 * static_cast<size_t>(first);
-    float* dst = s_rest[warp];
-    if (rest_vec && cnt == 32u) {
-      for (uint32_t e = lane; e < 32u * 45u / 4u; e += 32u) cp_async16(dst + 4 * e, src + 4 * e);
-    } else {
-      for (uint32_t e = lane; e < cnt * 45u; e += 32u) cp_async4(dst + e, src + e);
-    }
-  }
-  cp_async_commit();
-  const bool in_range = i < n;
-  const uint32_t gi = in_range ? i : (n > 0 ? n - 1 : 0);
+// Per-view outputs of the preprocess (one view's arena, possibly a peer's).
+struct PreOut {
+  uint32_t* n_touched;
+  uint32_t* depth_key;
+  ushort4* bounds;
+  float2* mean2d;
+  float4* conic_opacity;
+  PrimInfo16* prim_info;
+  float* color;
+  float4* helpers;
+  uint32_t* block_visible;
+};
 
+// One Gaussian's view-independent inputs, loaded once per thread.
+struct PreIn {
+  float mx3, my3, mz3, logit, s0, s1, s2;
+  float4 q;
+};
+
+// Projection, culling, colour and records of Gaussian i for one camera, with
+// the reference's operation order (fastgs_ours*/kernels_forward.cuh:157-412).
+// Every thread of the block calls it (the candidate count is a block
+// reduction).  The warp's SH rows are in `rest_rows` once the pending
+// cp.async group has landed (waited for after the projection, so the copy
+// overlaps it on the first call).
+template <int kFp16>
+__device__ __forceinline__ void preprocess_view(const PreIn& in, bool in_range, uint32_t i, uint32_t gi,
+                                                const DevCamera& cam, const PreOut& o, float4* __restrict__ dens,
+                                                const float* __restrict__ sh0, const float* rest_rows,
+                                                int active_bases, uint32_t block_slot, int zero_helpers) {
+  const uint32_t lane = threadIdx.x & 31u;
   // culling checks before the reference's first warp-level exit
-  const float mx3 = means[3 * gi], my3 = means[3 * gi + 1], mz3 = means[3 * gi + 2];
+  const float mx3 = in.mx3, my3 = in.my3, mz3 = in.mz3;
   const float depth = cam.r3.x * mx3 + cam.r3.y * my3 + cam.r3.z * mz3 + cam.r3.w;
   bool active = in_range && !(depth < cam.near_plane || depth > cam.far_plane);
   float opacity;
   __half opacity_h = __float2half_rn(0.0f);
   if constexpr (kFp16) {
     // fp16 path: logit rounded to half, sigmoid in fp32, stored as half
-    const __half raw = active ? __float2half_rn(opacities[gi]) : __float2half_rn(0.0f);
+    const __half raw = active ? __float2half_rn(in.logit) : __float2half_rn(0.0f);
     opacity = 1.0f / (1.0f + __expf(-__half2float(raw)));
     if (opacity < kMinAlpha) active = false;
     opacity_h = __float2half_rn(opacity);
   } else {
-    opacity = 1.0f / (1.0f + __expf(-opacities[gi]));
+    opacity = 1.0f / (1.0f + __expf(-in.logit));
     if (opacity < kMinAlpha) active = false;
   }
-  const float s0 = scales[3 * gi], s1 = scales[3 * gi + 1], s2 = scales[3 * gi + 2];
-  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (!kFp16 || active) q = rotations[gi];
+  const float s0 = in.s0, s1 = in.s1, s2 = in.s2;
+  // (the fp16 reference reads the rotation of active Gaussians only)
+  const float4 q = (!kFp16 || active) ? in.q : make_float4(0.f, 0.f, 0.f, 0.f);
   const float qn = q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w;
   if (qn < 1e-8f) active = false;
   const bool warp_alive = __ballot_sync(0xffffffffu, active) != 0u;
@@ -246,21 +241,21 @@ __global__ void __launch_bounds__(kPreBlock)
   __syncwarp();
 
   if (in_range) {
-    n_touched[i] = 0;  // binning adds the hits of each super-tile
-    bounds[i] = candidate ? make_ushort4(static_cast<unsigned short>(rect.x), static_cast<unsigned short>(rect.y),
-                                         static_cast<unsigned short>(rect.z), static_cast<unsigned short>(rect.w))
-                          : make_ushort4(0, 0, 0, 0);
+    o.n_touched[i] = 0;  // binning adds the hits of each super-tile
+    o.bounds[i] = candidate ? make_ushort4(static_cast<unsigned short>(rect.x), static_cast<unsigned short>(rect.y),
+                                           static_cast<unsigned short>(rect.z), static_cast<unsigned short>(rect.w))
+                            : make_ushort4(0, 0, 0, 0);
     if (candidate) {
-      depth_key[i] = __float_as_uint(depth);
+      o.depth_key[i] = __float_as_uint(depth);
       // the blend backward accumulates into these (zero_helpers == 0: the
       // view's own rank clears them locally instead)
       if (zero_helpers) {
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-        helpers[3 * i] = z;
-        helpers[3 * i + 1] = z;
-        helpers[3 * i + 2] = z;
+        o.helpers[3 * i] = z;
+        o.helpers[3 * i + 1] = z;
+        o.helpers[3 * i + 2] = z;
       }
-      mean2d[i] = m2;
+      o.mean2d[i] = m2;
       // view-dependent colour
       float3 col = make_float3(0.5f + 0.28209479177387814f * sh0[3 * i],
                                0.5f + 0.28209479177387814f * sh0[3 * i + 1],
@@ -270,7 +265,7 @@ __global__ void __launch_bounds__(kPreBlock)
         const float inv = rsqrtf(dx * dx + dy * dy + dz * dz);
         float b[15] = {};
         const int nb = sh_basis(dx * inv, dy * inv, dz * inv, active_bases, b);
-        const float* rest = s_rest[warp] + 45 * lane;  // 45 words apart: no bank conflicts
+        const float* rest = rest_rows + 45 * lane;  // 45 words apart: no bank conflicts
 #pragma unroll
         for (int k = 0; k < 15; ++k) {
           if (k < nb) {
@@ -288,18 +283,85 @@ __global__ void __launch_bounds__(kPreBlock)
                                   static_cast<unsigned char>(sat(col.y) * 255.0f),
                                   static_cast<unsigned char>(sat(col.z) * 255.0f), 0);
         rec.pad = 0;
-        prim_info[i] = rec;
+        o.prim_info[i] = rec;
       } else {
-        conic_opacity[i] = make_float4(conic.x, conic.y, conic.z, opacity);
-        color[3 * i] = col.x;
-        color[3 * i + 1] = col.y;
-        color[3 * i + 2] = col.z;
+        o.conic_opacity[i] = make_float4(conic.x, conic.y, conic.z, opacity);
+        o.color[3 * i] = col.x;
+        o.color[3 * i + 1] = col.y;
+        o.color[3 * i + 2] = col.z;
       }
     }
   }
   // number of candidates of this block, for the compaction scan
   const uint32_t vis = __syncthreads_count(candidate);
-  if (threadIdx.x == 0) block_visible[first_block + blockIdx.x] = vis;
+  if (threadIdx.x == 0) o.block_visible[block_slot] = vis;
+}
+
+// Loads of Gaussian i (clamped to a valid index) and the start of the
+// coalesced copy of its warp's higher-order SH rows into `rows` (one row per
+// lane would touch 32 cache lines per load instruction; rows of culled
+// Gaussians are copied too).
+__device__ __forceinline__ PreIn preprocess_load(const float* __restrict__ means, const float* __restrict__ opacities,
+                                                 const float4* __restrict__ rotations,
+                                                 const float* __restrict__ scales, const float* __restrict__ sh_rest,
+                                                 int active_bases, uint32_t n, uint32_t i, int rest_vec, float* rows,
+                                                 uint32_t& gi) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t first = i - lane;
+  if (active_bases > 1 && first < n) {
+    const uint32_t cnt = min(32u, n - first);
+    const float* src = sh_rest + 45 * static_cast<size_t>(first);
+    if (rest_vec && cnt == 32u) {
+      for (uint32_t e = lane; e < 32u * 45u / 4u; e += 32u) cp_async16(rows + 4 * e, src + 4 * e);
+    } else {
+      for (uint32_t e = lane; e < cnt * 45u; e += 32u) cp_async4(rows + e, src + e);
+    }
+  }
+  cp_async_commit();
+  gi = i < n ? i : (n > 0 ? n - 1 : 0);
+  PreIn in;
+  in.mx3 = means[3 * gi];
+  in.my3 = means[3 * gi + 1];
+  in.mz3 = means[3 * gi + 2];
+  in.logit = opacities[gi];
+  in.s0 = scales[3 * gi];
+  in.s1 = scales[3 * gi + 1];
+  in.s2 = scales[3 * gi + 2];
+  in.q = rotations[gi];
+  return in;
+}
+
+// Preprocess of Gaussians [first_block * kPreBlock, n) for `count` views:
+// one view for a single GPU; every rank's view for the owner split, whose
+// records go to each view's arena (peers' arenas over NVLink).  The
+// parameters and SH rows are read once for all views; the views are taken
+// in `order` (each rank starts with a different one, so the ranks' stores go
+// to different GPUs at any moment).  The single-view and the owner-split
+// paths run this same kernel, so their records are the same bit for bit.
+struct PreViews {
+  DevCamera cam[kMaxDpRanks];
+  PreOut out[kMaxDpRanks];
+  int order[kMaxDpRanks];
+  int count;
+};
+
+template <int kFp16>
+__global__ void __launch_bounds__(kPreBlock)
+    k_preprocess_views(const float* __restrict__ means, const float* __restrict__ opacities,
+                       const float4* __restrict__ rotations, const float* __restrict__ scales,
+                       const float* __restrict__ sh0, const float* __restrict__ sh_rest, int active_bases,
+                       uint32_t n, const __grid_constant__ PreViews views, float4* __restrict__ dens, int rest_vec,
+                       uint32_t first_block, int zero_helpers) {
+  __shared__ __align__(16) float s_rest[kPreBlock / 32][32 * 45];
+  const uint32_t i = (first_block + blockIdx.x) * kPreBlock + threadIdx.x;
+  float* rows = s_rest[threadIdx.x >> 5];
+  uint32_t gi;
+  const PreIn in = preprocess_load(means, opacities, rotations, scales, sh_rest, active_bases, n, i, rest_vec, rows, gi);
+  for (int j = 0; j < views.count; ++j) {
+    const int k = views.order[j];
+    preprocess_view<kFp16>(in, i < n, i, gi, views.cam[k], views.out[k], dens, sh0, rows, active_bases,
+                           first_block + blockIdx.x, zero_helpers);
+  }
 }
 
 // --------------------------------------------------------------- backward
@@ -1116,30 +1178,45 @@ __global__ void __launch_bounds__(32 * kBwdWarps, 3)
   }
 }
 
+PreOut pre_out(const RasterState& s) {
+  return PreOut{s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity, s.prim_info, s.color,
+                reinterpret_cast<float4*>(s.helpers), s.block_sums};
+}
+
 }  // namespace
 
 void launch_preprocess(const RasterState& s, const GaussianPtrs& g, const DevCamera& cam, int fp16,
                        float4* dens, cudaStream_t stream, int64_t first, int64_t last, int zero_helpers) {
   // Gaussians [first, last) (last < 0: to g.n); first is a multiple of the
   // block size so every block's candidate count has one writer
-  const uint32_t n = static_cast<uint32_t>(last < 0 ? g.n : last);
+  const int order = 0;
+  launch_preprocess_views(&s, &cam, &order, 1, g, fp16, dens, stream, first, last < 0 ? g.n : last, zero_helpers);
+}
+
+void launch_preprocess_views(const RasterState* views, const DevCamera* cams, const int* order, int count,
+                             const GaussianPtrs& g, int fp16, float4* dens, cudaStream_t stream, int64_t first,
+                             int64_t last, int zero_helpers) {
+  const uint32_t n = static_cast<uint32_t>(last);
   const uint32_t first_block = static_cast<uint32_t>(first / kPreBlock);
   const int active_bases = (g.sh_degree + 1) * (g.sh_degree + 1);
   const uint32_t blocks = n > first_block * kPreBlock ? (n - first_block * kPreBlock + kPreBlock - 1) / kPreBlock : 0;
-  if (blocks == 0) return;
+  if (blocks == 0 || count <= 0) return;
   const int rest_vec = (reinterpret_cast<uintptr_t>(g.sh_rest) & 15u) == 0;
+  PreViews v{};
+  v.count = count;
+  for (int k = 0; k < count; ++k) {
+    v.cam[k] = cams[k];
+    v.out[k] = pre_out(views[k]);
+    v.order[k] = order[k];
+  }
   if (fp16)
-    k_preprocess<1><<<blocks, kPreBlock, 0, stream>>>(
+    k_preprocess_views<1><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
-        active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block,
-        zero_helpers);
+        active_bases, n, v, dens, rest_vec, first_block, zero_helpers);
   else
-    k_preprocess<0><<<blocks, kPreBlock, 0, stream>>>(
+    k_preprocess_views<0><<<blocks, kPreBlock, 0, stream>>>(
         g.means, g.opacities, reinterpret_cast<const float4*>(g.rotations), g.scales, g.sh0, g.sh_rest,
-        active_bases, n, cam, dens, s.n_touched, s.depth_key, s.bounds, s.mean2d, s.conic_opacity,
-        s.prim_info, s.color, reinterpret_cast<float4*>(s.helpers), s.block_sums, rest_vec, first_block,
-        zero_helpers);
+        active_bases, n, v, dens, rest_vec, first_block, zero_helpers);
 }
 
 void launch_preprocess_backward(const RasterState& s, const GaussianPtrs& g, const GaussianPtrs& grads,

@@ -97,6 +97,15 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: wait (at most 10 s) for its
+        # first sample, so that the sampling covers the timed regions
+        t0 = time.time()
+        while time.time() - t0 < 10.0 and self.proc.poll() is None:
+            self.fh.flush()
+            if self.path.stat().st_size > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.proc is None:

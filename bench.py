@@ -93,7 +93,7 @@ class ClockSampler:
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "50", "-i", str(self.gpu)], stdout=self.fh,
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -729,8 +729,9 @@ def run_ours(args):
             dist.barrier()
         return dp.max_over_ranks(e0.elapsed_time(e1), "cuda")
 
-    # clocks are sampled from the start of the warm-up to the end of both
-    # timed regions (a 50 ms sampling period would miss a short timed region)
+    # clocks are sampled (every 200 ms, as the profiling recipe does: a
+    # tighter loop of driver queries competes with the e2e region's own API
+    # calls) from the start of the warm-up to the end of both timed regions
     sampler = ClockSampler(local)
     sampler.start()
     for k in range(args.warmup):

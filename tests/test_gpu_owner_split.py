@@ -24,7 +24,7 @@ from gpu_helpers import scene
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("fp16", [False, True], ids=["fp32", "fp16"])
 def test_owner_split_step_equals_accumulated_views(cuda_lib, world, fp16):
     cfg, params, sh, _ = scene("cfg1", n=60_001)
